@@ -1,0 +1,339 @@
+"""CPU restatement of UltraQuant's quantization hot path (test oracle).
+
+TEST INFRASTRUCTURE ONLY -- never imported by the product package.
+
+Every function cites the reference file:line it restates.  Floating-point
+operations are written in the same order and precision as the reference so
+that results agree bit-for-bit:
+
+* numpy reductions along a contiguous last axis use numpy's pairwise sum
+  (8 accumulators per block of <=128, halves split at a multiple of 8);
+  the oracle calls numpy the same way, so the order is inherited.
+* the Viterbi recurrence is evaluated with separate sub / square / add
+  tensor ops (no fused multiply-add), min/argmin pick the first index.
+* NEP-50 promotion: a float32 array times a numpy float64 scalar is float64.
+
+Third-party arithmetic on the path (versions recorded in the golden
+fixtures): numpy legacy ``RandomState`` (MT19937) for the sign vector and the
+E8 calibration subsample, ``scipy.stats.norm.ppf`` for the codebook, torch
+``min`` / ``argmin`` tie-breaking.
+"""
+from __future__ import annotations
+
+import numpy as np
+import torch
+
+__all__ = [
+    "next_pow2", "rht_signs", "rht_rows", "irht_rows", "d8_decode", "e8_decode",
+    "entropy_bpw", "q_e8_fast", "E8_SCALE", "wnmse", "codebook", "pred_table",
+    "trellis_quant", "trellis_quant_fast", "trellis_encode", "trellis_decode",
+    "fwht_torch", "irht_torch", "recon_torch", "quant_trellis", "quant_step",
+    "group_rms_f32", "viterbi_segments",
+]
+
+
+# ---------------------------------------------------------------------------
+# Randomized Hadamard transform  (qlab.py:66-98)
+# ---------------------------------------------------------------------------
+def next_pow2(n: int) -> int:
+    """qlab.py:66-69 -- smallest power of two >= n (1 for n <= 1)."""
+    p = 1
+    while p < n:
+        p <<= 1
+    return p
+
+
+def rht_signs(n: int, seed: int = 0) -> np.ndarray:
+    """qlab.py:78 and :96 -- legacy MT19937 ``choice([-1., 1.], n)``."""
+    return np.random.RandomState(seed).choice([-1.0, 1.0], size=n)
+
+
+def _butterflies(x: np.ndarray) -> np.ndarray:
+    """Sylvester stages h = 1, 2, 4, ... n/2 along the last axis (qlab.py:80-84).
+
+    For every pair (i, i+h) inside a block of 2h: new[i] = x[i] + x[i+h],
+    new[i+h] = x[i] - x[i+h].  Stage order matters for rounding.
+    """
+    rows, n = x.shape
+    h = 1
+    while h < n:
+        v = x.reshape(rows, n // (2 * h), 2, h)
+        lo = v[:, :, 0, :]
+        hi = v[:, :, 1, :]
+        x = np.stack([lo + hi, lo - hi], axis=2).reshape(rows, n)
+        h *= 2
+    return x
+
+
+def rht_rows(A: np.ndarray, seed: int = 0) -> np.ndarray:
+    """qlab.py:71-85 -- pad columns to 2^k with zeros, multiply by the sign
+    vector, run the butterflies in fp64, divide by sqrt(n)."""
+    rows, n0 = A.shape
+    n = next_pow2(n0)
+    if n != n0:
+        A = np.concatenate([A, np.zeros((rows, n - n0))], axis=1)
+    d = rht_signs(n, seed)
+    x = _butterflies(A * d)
+    return x / np.sqrt(n)
+
+
+def irht_rows(X: np.ndarray, n0: int, seed: int = 0) -> np.ndarray:
+    """qlab.py:87-98 -- multiply by sqrt(n) (float32 input promotes to fp64),
+    butterflies, then (x / n) * d and crop to n0 columns."""
+    rows, n = X.shape
+    x = X.copy() * np.sqrt(n)
+    x = _butterflies(x)
+    d = rht_signs(n, seed)
+    x = (x / n) * d
+    return x[:, :n0]
+
+
+def wnmse(A: np.ndarray, Ah: np.ndarray) -> float:
+    """qlab.py:53-54 -- sum((A - Ah)^2) / sum(A^2)."""
+    return float(np.sum((A - Ah) ** 2) / np.sum(A ** 2))
+
+
+# ---------------------------------------------------------------------------
+# E8 nearest point  (qlab.py:133-183)
+# ---------------------------------------------------------------------------
+def d8_decode(Y: np.ndarray) -> np.ndarray:
+    """qlab.py:133-142 -- nearest D8 point: round half to even; when the
+    coordinate sum is odd, move the coordinate with the largest rounding error
+    (first on ties) one step towards Y (np.sign, so an error of 0 moves 0)."""
+    f = np.round(Y)
+    parity = f.sum(1).astype(np.int64) % 2
+    rows = np.nonzero(parity != 0)[0]
+    if rows.size:
+        err = Y[rows] - f[rows]
+        k = np.argmax(np.abs(err), axis=1)
+        f[rows, k] += np.sign(err[np.arange(rows.size), k])
+    return f
+
+
+def e8_decode(Y: np.ndarray) -> np.ndarray:
+    """qlab.py:144-149 -- better of D8 and D8 + 1/2 (strict <, pairwise sums)."""
+    a = d8_decode(Y)
+    b = d8_decode(Y - 0.5) + 0.5
+    da = ((Y - a) ** 2).sum(1)
+    db = ((Y - b) ** 2).sum(1)
+    return np.where((db < da)[:, None], b, a)
+
+
+def entropy_bpw(idx_pts: np.ndarray) -> float:
+    """qlab.py:151-156 -- empirical entropy of the 8-tuples 2*pts, / 8."""
+    keys = np.ascontiguousarray((idx_pts * 2).astype(np.int64))
+    keys = keys.view([("", np.int64)] * 8).ravel()
+    _, cnt = np.unique(keys, return_counts=True)
+    p = cnt / cnt.sum()
+    return float(-(p * np.log2(p)).sum()) / 8.0
+
+
+E8_SCALE: dict = {}
+
+
+def q_e8_fast(A, target_bpw=2.0, group=256, calib_key="g", fixed_step=None,
+              cache=None):
+    """qlab.py:159-183 -- per-group RMS normalisation, one global step, E8.
+
+    ``cache`` stands in for the module-global ``_E8_SCALE`` (qlab.py:158)."""
+    cache = E8_SCALE if cache is None else cache
+    flat = A.ravel().astype(np.float64)
+    pad = (-flat.size) % group
+    g = np.concatenate([flat, np.zeros(pad)]).reshape(-1, group)
+    rms = np.sqrt((g ** 2).mean(1, keepdims=True)) + 1e-12
+    gn = (g / rms).reshape(-1, 8)
+    if fixed_step is not None:
+        step = fixed_step
+    else:
+        if calib_key not in cache:
+            ns = min(600_000, gn.shape[0])
+            pick = np.random.RandomState(0).randint(0, gn.shape[0], ns)
+            sub = gn[pick]
+            lo, hi = 0.3, 10.0
+            for _ in range(18):
+                mid = (lo + hi) / 2
+                if entropy_bpw(e8_decode(sub / mid)) > target_bpw:
+                    lo = mid
+                else:
+                    hi = mid
+            cache[calib_key] = (lo + hi) / 2
+        step = cache[calib_key]
+    rec = (e8_decode(gn / step) * step).reshape(-1, group) * rms
+    return rec.ravel()[:A.size].reshape(A.shape)
+
+
+# ---------------------------------------------------------------------------
+# Bitshift trellis  (trellis.py:14-108, qat.py:11-59)
+# ---------------------------------------------------------------------------
+def codebook(L: int, seed: int = 0) -> np.ndarray:
+    """trellis.py:14-19 -- 64-bit mix hash of the state, low 32 bits to
+    u in (0, 1), inverse normal CDF, rounded to float32.  ``seed`` is unused
+    by the reference and therefore here."""
+    from scipy.stats import norm
+    s = np.arange(1 << L, dtype=np.uint64)
+    h = s * np.uint64(2654435761) + np.uint64(0x9E3779B97F4A7C15)
+    h ^= h >> np.uint64(29)
+    h *= np.uint64(0xBF58476D1CE4E5B9)
+    h ^= h >> np.uint64(32)
+    u = ((h & np.uint64(0xFFFFFFFF)).astype(np.float64) + 0.5) / 2 ** 32
+    return norm.ppf(u).astype(np.float32)
+
+
+def pred_table(L: int, R: int) -> np.ndarray:
+    """trellis.py:21-25 -- pred[s, k] = ((s >> R) | (k << (L-R))) & (2^L - 1)."""
+    S = 1 << L
+    s = np.arange(S)[:, None]
+    k = np.arange(1 << R)[None, :]
+    return ((s >> R) | (k << (L - R))) & (S - 1)
+
+
+def group_rms_f32(g: np.ndarray) -> np.ndarray:
+    """trellis.py:75 -- float32 sqrt(mean(g^2)) + 1e-12 along the last axis."""
+    return np.sqrt((g ** 2).mean(-1, keepdims=True)) + 1e-12
+
+
+def viterbi_segments(xn: np.ndarray, L: int, R: int, cw=None, chunk: int = 1 << 16):
+    """trellis.py:84-105 (= qat.py:141-152) -- min-plus Viterbi per row of
+    ``xn`` (nseq, T) float32.  Returns the int64 state path (nseq, T).
+
+    Forward: cost_0[s] = (x_0 - cw[s])^2; for t >= 1
+    m[q] = min_k cost[k*2^(L-R) + q] (first k on ties), bp[t, q] = k,
+    cost[s] = (x_t - cw[s])^2 + m[s >> R].  Backward from the first argmin:
+    s_{t-1} = bp[t, s_t >> R] * 2^(L-R) + (s_t >> R).
+    """
+    cw_t = torch.from_numpy(codebook(L) if cw is None else np.asarray(cw, np.float32))
+    nseq, T = xn.shape
+    Q = 1 << (L - R)
+    K = 1 << R
+    out = np.empty((nseq, T), np.int64)
+    cw2 = cw_t[None, :]
+    for c0 in range(0, nseq, chunk):
+        x = torch.from_numpy(np.ascontiguousarray(xn[c0:c0 + chunk], np.float32))
+        b = x.shape[0]
+        cost = (x[:, 0:1] - cw2) ** 2
+        bp = torch.empty((b, T, Q), dtype=torch.uint8)
+        for t in range(1, T):
+            m, k = cost.view(b, K, Q).min(dim=1)
+            bp[:, t, :] = k.to(torch.uint8)
+            cost = (x[:, t:t + 1] - cw2) ** 2 + m.repeat_interleave(K, dim=1)
+        st = torch.empty((b, T), dtype=torch.long)
+        st[:, T - 1] = cost.argmin(1)
+        rows = torch.arange(b)
+        for t in range(T - 1, 0, -1):
+            q = st[:, t] >> R
+            st[:, t - 1] = bp[rows, t, q].long() * Q + q
+        out[c0:c0 + b] = st.numpy()
+    return out
+
+
+def _flat_normalise(A, seg, scale_group):
+    """trellis.py:69-80 -- float32 flatten, zero-pad to the scale group,
+    per-group RMS, normalise, cut into Viterbi segments."""
+    flat = A.astype(np.float32).ravel()
+    pad = (-flat.size) % scale_group
+    g = np.concatenate([flat, np.zeros(pad, np.float32)]).reshape(-1, scale_group)
+    sc_g = group_rms_f32(g)
+    xn = (g / sc_g).ravel().reshape(-1, seg)
+    return xn, sc_g, flat.size, pad
+
+
+def trellis_quant_fast(A, L=12, R=2, seg=64, scale_group=256, mem_gb=3.0):
+    """trellis.py:62-108 -- segmented Viterbi; returns cw[s] * sc_g (float32)."""
+    del mem_gb  # chunking only bounds memory; numerically irrelevant
+    nrow, ncol = A.shape
+    cw = codebook(L)
+    xn, sc_g, ntot, _ = _flat_normalise(A, seg, scale_group)
+    st = viterbi_segments(xn, L, R, cw)
+    rec = cw[st].ravel()
+    rec = (rec.reshape(-1, scale_group) * sc_g).ravel()
+    return rec[:ntot].reshape(nrow, ncol).astype(np.float32)
+
+
+def trellis_encode(A, L=12, R=2, seg=64, scale_group=256):
+    """qat.py:11-33 -- same Viterbi; returns (states int32, sc_g, cw, meta)."""
+    nrow, ncol = A.shape
+    cw = codebook(L)
+    xn, sc_g, ntot, pad = _flat_normalise(A, seg, scale_group)
+    st = viterbi_segments(xn, L, R, cw).astype(np.int32)
+    meta = dict(nrow=nrow, ncol=ncol, Ntot=ntot, seg=seg, scale_group=scale_group,
+                pad=pad, Nseg=st.shape[0])
+    return st, sc_g.astype(np.float32), cw, meta
+
+
+def trellis_decode(states, cw, sc_g, meta):
+    """trellis.py:104-108 -- cw[states] * sc_g, cropped to Ntot (float32)."""
+    rec = np.asarray(cw, np.float32)[states].ravel()
+    rec = (rec.reshape(-1, meta["scale_group"]) * sc_g).ravel()
+    return rec[:meta["Ntot"]].reshape(meta["nrow"], meta["ncol"]).astype(np.float32)
+
+
+def trellis_quant(A, L=10, R=2, group=256, chunk_rows=512):
+    """trellis.py:27-60 -- full-row Viterbi (one sequence per padded row) with
+    per-(row, group) RMS; returns float32 reconstruction."""
+    del chunk_rows
+    cw = codebook(L)
+    nrow, T = A.shape
+    out = np.empty((nrow, T), np.float32)
+    blk = A.astype(np.float32)
+    Tp = ((T + group - 1) // group) * group
+    pad = np.zeros((nrow, Tp), np.float32)
+    pad[:, :T] = blk
+    g = pad.reshape(nrow, Tp // group, group)
+    sc = group_rms_f32(g)
+    xn = (g / sc).reshape(nrow, Tp)
+    st = viterbi_segments(xn, L, R, cw)
+    rec = (cw[st].reshape(nrow, Tp // group, group) * sc).reshape(nrow, Tp)
+    out[:] = rec[:, :T]
+    return out
+
+
+def fwht_torch(x):
+    """qat.py:35-41 -- differentiable FWHT along the last axis, / sqrt(n)."""
+    n = x.shape[-1]
+    shape = x.shape
+    h = 1
+    while h < n:
+        v = x.reshape(-1, n // (2 * h), 2, h)
+        x = torch.cat([v[:, :, 0, :] + v[:, :, 1, :], v[:, :, 0, :] - v[:, :, 1, :]],
+                      dim=2).reshape(*shape[:-1], n)
+        h *= 2
+    return x / np.sqrt(n)
+
+
+def irht_torch(Xrot, in0, seed=0):
+    """qat.py:43-49 -- fwht_torch(X) * d, cropped to in0."""
+    n = Xrot.shape[1]
+    x = fwht_torch(Xrot)
+    d = torch.tensor(rht_signs(n, seed), dtype=Xrot.dtype, device=Xrot.device)
+    return (x * d)[:, :in0]
+
+
+def recon_torch(states, cw, sc_g, meta, sH, in0):
+    """qat.py:51-59 -- cw[states] * sc_g -> irht_torch -> / sH."""
+    dev = cw.device
+    st = torch.as_tensor(states, device=dev, dtype=torch.long)
+    rec = cw[st].reshape(-1)[:meta["Nseg"] * meta["seg"]]
+    rec = (rec.reshape(-1, meta["scale_group"]) * sc_g).reshape(-1)[:meta["Ntot"]]
+    return irht_torch(rec.reshape(meta["nrow"], meta["ncol"]), in0) / sH
+
+
+# ---------------------------------------------------------------------------
+# Builder recipes around the path  (buildtrellis.py:16-20, buildalloc.py:21-24)
+# ---------------------------------------------------------------------------
+def quant_trellis(W, H, L=12, R=2, seg=64, scale_group=256):
+    """buildtrellis.py:16-20 -- clamp H, A = W*sqrt(H), RHT, trellis, iRHT, /sqrt(H)."""
+    H = np.maximum(H, H.max() * 1e-3)
+    sH = np.sqrt(H)[None, :]
+    A = W * sH
+    in0 = A.shape[1]
+    Ah = irht_rows(trellis_quant_fast(rht_rows(A), L=L, R=R, seg=seg,
+                                      scale_group=scale_group), in0)
+    return (Ah / sH).astype(np.float32)
+
+
+def quant_step(W, H, step):
+    """buildalloc.py:21-24 -- same recipe with E8 at a fixed step."""
+    H = np.maximum(H, H.max() * 1e-3)
+    sH = np.sqrt(H)[None, :]
+    Ah = irht_rows(q_e8_fast(rht_rows(W * sH), fixed_step=step), W.shape[1])
+    return (Ah / sH).astype(np.float32)

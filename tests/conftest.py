@@ -1,0 +1,50 @@
+import os
+import sys
+
+import numpy as np
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+GOLDEN = os.path.join(ROOT, "tests", "golden")
+
+
+def pytest_configure(config):
+    config.addinivalue_line("markers", "gpu: needs a CUDA device (B200, sm_100a)")
+
+
+def load_golden(name):
+    with np.load(os.path.join(GOLDEN, name), allow_pickle=False) as z:
+        return {k: z[k] for k in z.files}
+
+
+@pytest.fixture(scope="session")
+def g_rht():
+    return load_golden("golden_rht.npz")
+
+
+@pytest.fixture(scope="session")
+def g_e8():
+    return load_golden("golden_e8.npz")
+
+
+@pytest.fixture(scope="session")
+def g_trellis():
+    return load_golden("golden_trellis.npz")
+
+
+@pytest.fixture(scope="session")
+def g_pipeline():
+    return load_golden("golden_pipeline.npz")
+
+
+def same_bits(a, b):
+    """Bit-for-bit equality of two float arrays (signed zeros included)."""
+    a = np.ascontiguousarray(a)
+    b = np.ascontiguousarray(b)
+    if a.shape != b.shape or a.dtype != b.dtype:
+        return False
+    iv = {4: np.int32, 8: np.int64, 2: np.int16, 1: np.int8}[a.dtype.itemsize]
+    return bool(np.array_equal(a.view(iv), b.view(iv)))

@@ -1,0 +1,111 @@
+"""Pin the CPU oracle against golden vectors produced by the reference itself."""
+import numpy as np
+import pytest
+
+import oracle as O
+from conftest import same_bits
+
+
+def test_signs(g_rht):
+    for n in [1, 2, 4, 8, 16, 32, 64, 128, 256, 512, 1024, 2048, 4096, 8192, 16384, 32768]:
+        assert np.array_equal(O.rht_signs(n).astype(np.int8), g_rht[f"signs_{n}"])
+    assert np.array_equal(O.rht_signs(1024, 7).astype(np.int8), g_rht["signs_seed7_1024"])
+
+
+@pytest.mark.parametrize("tag", list("abcdefghi"))
+def test_rht_irht(g_rht, tag):
+    A = g_rht[f"rht_{tag}_in"]
+    seed = int(g_rht[f"rht_{tag}_seed"])
+    X = O.rht_rows(A, seed=seed)
+    assert same_bits(X, g_rht[f"rht_{tag}_out"])
+    assert same_bits(O.irht_rows(X, A.shape[1], seed=seed), g_rht[f"irht_{tag}_out"])
+    k = f"irht_{tag}_f32_out"
+    if k in g_rht:
+        assert same_bits(O.irht_rows(X.astype(np.float32), A.shape[1], seed=seed), g_rht[k])
+
+
+def test_d8_e8(g_e8):
+    Y = g_e8["Y"]
+    assert same_bits(O.d8_decode(Y.copy()), g_e8["d8"])
+    assert same_bits(O.e8_decode(Y), g_e8["e8"])
+
+
+def test_entropy(g_e8):
+    assert O.entropy_bpw(g_e8["ent_pts"]) == float(g_e8["ent_bpw"])
+
+
+def test_q_e8_fixed(g_e8):
+    A = g_e8["q_A"]
+    for step in (0.48, 0.25, 0.16, 0.11):
+        assert same_bits(O.q_e8_fast(A, fixed_step=step), g_e8[f"q_fixed_{step}"])
+    A2 = g_e8["q_A2"]
+    assert same_bits(O.q_e8_fast(A2, fixed_step=0.48), g_e8["q_A2_fixed_0.48"])
+    assert same_bits(O.q_e8_fast(A2, group=64, fixed_step=0.25), g_e8["q_A2_g64_fixed_0.25"])
+
+
+@pytest.mark.parametrize("tb", [2.0, 3.0])
+def test_q_e8_calibrated(g_e8, tb):
+    cache = {}
+    rec = O.q_e8_fast(g_e8["q_A3"], target_bpw=tb, calib_key="k", cache=cache)
+    assert cache["k"] == float(g_e8[f"q_cal_{tb}_step"])
+    assert same_bits(rec, g_e8[f"q_cal_{tb}_rec"])
+
+
+def test_codebook(g_trellis):
+    cb = O.codebook(16)
+    assert same_bits(cb, g_trellis["codebook16"])
+    # smaller L are prefixes of the L=16 table (the hash depends on s only)
+    assert same_bits(O.codebook(12), cb[:4096])
+    assert np.array_equal(O.pred_table(8, 2), g_trellis["pred_8_2"])
+
+
+TQ = ["l8r2", "l8r1", "l8r3", "l8r4", "l10r2", "l12r2", "l12r2s64", "l12r3", "l16r2",
+      "l16r3", "pad", "g128"]
+
+
+@pytest.mark.parametrize("tag", TQ)
+def test_trellis_fast_and_encode(g_trellis, tag):
+    A = g_trellis[f"tq_{tag}_in"]
+    L, R, seg, group = (int(v) for v in g_trellis[f"tq_{tag}_cfg"])
+    if L == 16:
+        pytest.importorskip("torch")
+    rec = O.trellis_quant_fast(A, L=L, R=R, seg=seg, scale_group=group)
+    assert same_bits(rec, g_trellis[f"tq_{tag}_rec"])
+    st, sc_g, cw, meta = O.trellis_encode(A, L=L, R=R, seg=seg, scale_group=group)
+    assert np.array_equal(st, g_trellis[f"tq_{tag}_states"])
+    assert same_bits(sc_g, g_trellis[f"tq_{tag}_scg"])
+    assert same_bits(O.trellis_decode(st, cw, sc_g, meta), rec)
+
+
+@pytest.mark.parametrize("tag", ["r8", "r10"])
+def test_trellis_full_row(g_trellis, tag):
+    A = g_trellis[f"tr_{tag}_in"]
+    L, R, group = (int(v) for v in g_trellis[f"tr_{tag}_cfg"])
+    assert same_bits(O.trellis_quant(A, L=L, R=R, group=group), g_trellis[f"tr_{tag}_rec"])
+
+
+def test_selftest_kat(g_trellis):
+    X = np.random.RandomState(0).randn(64, 1024).astype(np.float32)
+    Xh = O.trellis_quant(X, L=8, R=2, group=256)
+    nmse = float(np.sum((X - Xh) ** 2) / np.sum(X ** 2))
+    assert nmse == float(g_trellis["selftest_l8_nmse"])
+    # trellis.py:110-117 / FINDINGS: L=8 R=2 beats memoryless (~0.118), above 2^-4
+    assert 0.0625 < nmse < 0.118
+
+
+def test_pipelines(g_pipeline):
+    import torch
+    W, H = g_pipeline["W"], g_pipeline["H"]
+    for L, R, seg in [(8, 2, 64), (12, 2, 64), (10, 3, 256)]:
+        Wh = O.quant_trellis(W, H, L=L, R=R, seg=seg)
+        assert same_bits(Wh, g_pipeline[f"qt_{L}_{R}_{seg}_What"])
+    for step in (0.48, 0.25):
+        assert same_bits(O.quant_step(W, H, step), g_pipeline[f"qs_{step}_What"])
+    Hc = np.maximum(H, H.max() * 1e-3)
+    sH = np.sqrt(Hc)[None, :]
+    A = O.rht_rows(W * sH).astype(np.float32)
+    st, sc_g, cwn, meta = O.trellis_encode(A, L=8, R=2, seg=64, scale_group=256)
+    assert np.array_equal(st, g_pipeline["qat_states"])
+    Wh = O.recon_torch(st, torch.tensor(cwn), torch.tensor(sc_g), meta,
+                       torch.tensor(sH, dtype=torch.float32), 300)
+    assert same_bits(Wh.numpy(), g_pipeline["qat_recon"])
