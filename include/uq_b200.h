@@ -1,0 +1,198 @@
+/*
+ * uq_b200.h -- C ABI of the B200 (sm_100a) quantization hot path:
+ * randomized Hadamard transform, E8 nearest-point quantizer and the
+ * bitshift-trellis Viterbi encoder / decoder of UltraQuant.
+ *
+ * The reference exposes this path as plain Python module functions on numpy
+ * arrays (qlab.py, trellis.py, qat.py).  Each entry point below names the
+ * reference function it replaces.  The Python package ``ultraquant_b200``
+ * wraps these calls in the reference's exact signatures; a ctypes binding is
+ * shown in INTEGRATION.md.
+ *
+ * Conventions
+ *  - All array pointers are DEVICE pointers unless the name ends in _host.
+ *  - Row-major layouts, explicit leading dimensions (in elements).
+ *  - ``stream`` is a cudaStream_t passed as void* (NULL = legacy default).
+ *  - Every entry point returns a uq_status; on failure uq_last_error()
+ *    returns a message for the calling thread.  No entry point has a CPU
+ *    fallback.
+ *  - Entry points never synchronise the stream unless documented (the E8
+ *    calibration reads scalar results back to the host).
+ *  - dtype codes: UQ_F32 = 0, UQ_F64 = 1.
+ */
+#ifndef UQ_B200_H
+#define UQ_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum uq_status {
+    UQ_OK = 0,
+    UQ_ERR_INVALID = 1,      /* bad shape / argument (reference: numpy ValueError) */
+    UQ_ERR_UNSUPPORTED = 2,  /* valid for the reference but not built here (e.g. L > 16) */
+    UQ_ERR_CUDA = 3,         /* CUDA runtime / launch error */
+    UQ_ERR_WORKSPACE = 4,    /* workspace smaller than the *_workspace_bytes() query */
+    UQ_ERR_TIMEOUT = 5       /* a device wait exceeded its bound */
+};
+
+enum uq_dtype { UQ_F32 = 0, UQ_F64 = 1 };
+
+int uq_version(void);
+const char *uq_status_string(int status);
+const char *uq_last_error(void);
+
+/* ---------------------------------------------------------------------
+ * Randomized Hadamard transform (qlab.py:66-98)
+ * ------------------------------------------------------------------- */
+
+/* qlab.py:78, :96 -- ``np.random.RandomState(seed).choice([-1., 1.], n)``:
+ * legacy MT19937, one 32-bit draw per sign, bit 0 selects +1.  Host output. */
+int uq_rht_signs(uint32_t seed, int64_t n, double *out_host);
+
+/* qlab.py:66-69 -- next power of two >= n0. */
+int64_t uq_next_pow2(int64_t n0);
+
+/* qlab.py:71-85 rht_rows(A, seed): out[rows, n] = FWHT(pad(A) * d) / sqrt(n),
+ * fp64, stages h = 1..n/2 in order (bit-exact with numpy).  A is f32 or f64
+ * (a_dtype), row stride lda >= n0.  signs: device, length n = next_pow2(n0).
+ * n <= 16384 in this build. */
+int uq_rht_rows(const void *A, int a_dtype, int64_t rows, int64_t n0, int64_t lda,
+                const double *signs, double *out, void *stream);
+
+/* qlab.py:87-98 irht_rows(X, n0, seed): out[rows, n0] =
+ * (FWHT(X * sqrt(n)) / n * d)[:, :n0], fp64 (a float32 X is widened exactly,
+ * as numpy 2 promotes it).  X has n (power of two) columns, stride ldx. */
+int uq_irht_rows(const void *X, int x_dtype, int64_t rows, int64_t n, int64_t ldx,
+                 int64_t n0, const double *signs, double *out, void *stream);
+
+/* ---------------------------------------------------------------------
+ * E8 lattice (qlab.py:133-183)
+ * ------------------------------------------------------------------- */
+
+/* qlab.py:133-142 _d8_decode(Y): Y, out are (nvec, 8) fp64. */
+int uq_d8_decode(const double *Y, int64_t nvec, double *out, void *stream);
+
+/* qlab.py:144-149 e8_decode(Y): nearest point of D8 u (D8 + 1/2). */
+int uq_e8_decode(const double *Y, int64_t nvec, double *out, void *stream);
+
+/* qlab.py:159-170, 181-183 q_e8_fast(A, group=group, fixed_step=step) and the
+ * calibrated form once its step is known: per-group RMS (numpy pairwise
+ * order) + 1e-12, gn = g / rms, pts = e8_decode(gn / step),
+ * rec = pts * step * rms, flattened A of `size` elements (zero-padded to the
+ * group).  rec: `size` fp64.  idx (nullable): 2*pts as int16, size rounded up
+ * to a multiple of 8. */
+int uq_e8_quant(const void *A, int a_dtype, int64_t size, int64_t group, double step,
+                double *rec, int16_t *idx, void *stream);
+
+/* qlab.py:151-156 _entropy_bpw(pts): entropy of the distinct 8-tuples
+ * (2*pts truncated to int64) / 8.  pts: (nvec, 8) fp64; result written to
+ * bpw (device, one fp64).  Needs uq_e8_entropy_workspace_bytes(nvec). */
+size_t uq_e8_entropy_workspace_bytes(int64_t nvec);
+int uq_e8_entropy_bpw(const double *pts, int64_t nvec, double *bpw, void *workspace,
+                      size_t workspace_bytes, void *stream);
+
+/* qlab.py:171-180 -- calibrated step of q_e8_fast(A, target_bpw, group):
+ * 600k-vector MT19937 subsample (RandomState(0).randint), 18 bisection steps
+ * on [0.3, 10] of the entropy rate.  Synchronises `stream`; the step is
+ * written to *step_host. */
+size_t uq_e8_calibrate_workspace_bytes(int64_t size, int64_t group);
+int uq_e8_calibrate(const void *A, int a_dtype, int64_t size, int64_t group,
+                    double target_bpw, double *step_host, void *workspace,
+                    size_t workspace_bytes, void *stream);
+
+/* ---------------------------------------------------------------------
+ * Bitshift trellis (trellis.py:14-108, qat.py:11-59)
+ * ------------------------------------------------------------------- */
+
+/* trellis.py:14-19 codebook(L): hashed state -> u -> inverse normal CDF
+ * (Wichura AS241 in fp64) -> float32.  out: 2^L floats, 1 <= L <= 16. */
+int uq_trellis_codebook(int L, float *out, void *stream);
+
+/* trellis.py:69-80 (= qat.py:135-138): flatten `ntot` values (f32 or f64,
+ * rounded to f32), zero-pad to a multiple of `group`, sc[g] = sqrt(mean(g^2))
+ * + 1e-12 in float32 (numpy pairwise order), xn = g / sc.  The padded length
+ * must be a multiple of `seg` (else UQ_ERR_INVALID, as numpy's reshape
+ * fails).  xn: padded length; sc: padded length / group. */
+int uq_trellis_normalize(const void *A, int a_dtype, int64_t ntot, int64_t group,
+                         int64_t seg, float *xn, float *sc, void *stream);
+
+/* trellis.py:35-42 -- per-row variant used by trellis_quant: rows of T values
+ * are padded to Tp = ceil(T / group) * group.  xn: (nrow, Tp), sc:
+ * (nrow, Tp / group). */
+int uq_trellis_normalize_rows(const void *A, int a_dtype, int64_t nrow, int64_t T,
+                              int64_t lda, int64_t group, float *xn, float *sc,
+                              void *stream);
+
+/* trellis.py:84-103, qat.py:141-152 -- min-plus Viterbi over `nseq`
+ * sequences of T normalised values (xn, row-major).  Writes the full L-bit
+ * state of every step: states (nseq, T) int32.  cw: 2^L floats (the
+ * codebook, or a tuned one).  6 <= L <= 16, 1 <= R <= 4, L >= 2R, T >= 1.
+ * Backpointers live in the caller's workspace (uq_trellis_workspace_bytes). */
+size_t uq_trellis_workspace_bytes(int64_t nseq, int T, int L, int R);
+int uq_trellis_viterbi(const float *xn, int64_t nseq, int T, int L, int R, const float *cw,
+                       int32_t *states, void *workspace, size_t workspace_bytes,
+                       void *stream);
+
+/* trellis.py:104-108 -- decoder: out[i] = cw[states[i]] * sc[i / group] for
+ * i < ntot (float32 product). */
+int uq_trellis_decode(const int32_t *states, const float *cw, const float *sc,
+                      int64_t group, int64_t ntot, float *out, void *stream);
+
+/* trellis.py:57-58 -- row decoder of trellis_quant: states (nrow, Tp),
+ * sc (nrow, Tp / group); out (nrow, T) = cw[s] * sc cropped to T. */
+int uq_trellis_decode_rows(const int32_t *states, const float *cw, const float *sc,
+                           int64_t nrow, int64_t T, int64_t Tp, int64_t group,
+                           float *out, void *stream);
+
+/* ---------------------------------------------------------------------
+ * Importance-weighted pipelines (builder recipes around the path)
+ * ------------------------------------------------------------------- */
+
+/* buildtrellis.py:16-20 quant_trellis(W, H): H' = max(H, max(H) * 1e-3),
+ * sH = sqrt(H'), A = W * sH, Arot = rht_rows(A), trellis_quant_fast(Arot, L,
+ * R, seg, group), Ah = irht_rows(., n0), What = float32(Ah / sH).
+ * W: (rows, n0) f32/f64 (stride ldw); H: n0 fp64; signs: n = next_pow2(n0)
+ * fp64; cw: 2^L floats.  Outputs: What (rows, n0) float32; optional states
+ * (rows * n / seg, seg) int32, sc (rows * n / group) float32 and
+ * err[2] fp64 = { sum (A - Ah)^2, sum A^2 } (the weighted NMSE is
+ * err[0] / err[1]). */
+size_t uq_quant_trellis_workspace_bytes(int64_t rows, int64_t n0, int L, int R, int seg,
+                                        int group);
+int uq_quant_trellis(const void *W, int w_dtype, int64_t rows, int64_t n0, int64_t ldw,
+                     const double *H, int L, int R, int seg, int group,
+                     const double *signs, const float *cw, float *What, int32_t *states,
+                     float *sc, double *err, void *workspace, size_t workspace_bytes,
+                     void *stream);
+
+/* buildalloc.py:21-24 quant_step(W, H, step): same recipe with
+ * q_e8_fast(Arot, fixed_step=step, group) in place of the trellis.
+ * idx (nullable): 2*pts int16 of the rotated matrix (rows * n values). */
+size_t uq_quant_e8_workspace_bytes(int64_t rows, int64_t n0, int group);
+int uq_quant_e8(const void *W, int w_dtype, int64_t rows, int64_t n0, int64_t ldw,
+                const double *H, double step, int group, const double *signs,
+                float *What, int16_t *idx, double *err, void *workspace,
+                size_t workspace_bytes, void *stream);
+
+/* ---------------------------------------------------------------------
+ * Instrumentation (no counterpart in the reference; used by bench.py)
+ * ------------------------------------------------------------------- */
+
+/* Count every kernel launch and, when enabled, bracket the launches of the
+ * named hot kernels ("viterbi_fwd", "rht", "e8_quant", "traceback") with
+ * CUDA events on their launch stream. */
+void uq_profile_enable(int on);
+void uq_profile_reset(void);
+int64_t uq_launch_count(void);
+/* Synchronises the recorded events of `kernel`; returns the number of
+ * launches and their summed device time in milliseconds. */
+int uq_profile_read(const char *kernel, double *total_ms, int64_t *launches);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* UQ_B200_H */

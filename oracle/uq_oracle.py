@@ -238,12 +238,14 @@ def _flat_normalise(A, seg, scale_group):
 
 
 def trellis_quant_fast(A, L=12, R=2, seg=64, scale_group=256, mem_gb=3.0):
-    """trellis.py:62-108 -- segmented Viterbi; returns cw[s] * sc_g (float32)."""
-    del mem_gb  # chunking only bounds memory; numerically irrelevant
+    """trellis.py:62-108 -- segmented Viterbi; returns cw[s] * sc_g (float32).
+    ``mem_gb`` bounds the backpointer chunk as in trellis.py:81 (numerically
+    irrelevant)."""
     nrow, ncol = A.shape
     cw = codebook(L)
     xn, sc_g, ntot, _ = _flat_normalise(A, seg, scale_group)
-    st = viterbi_segments(xn, L, R, cw)
+    chunk = max(1, int(mem_gb * 1e9 / (seg * (1 << L))))
+    st = viterbi_segments(xn, L, R, cw, chunk=chunk)
     rec = cw[st].ravel()
     rec = (rec.reshape(-1, scale_group) * sc_g).ravel()
     return rec[:ntot].reshape(nrow, ncol).astype(np.float32)

@@ -1,0 +1,116 @@
+"""GPU parity: RHT / iRHT and the E8 quantizer against the reference goldens
+and the oracle (bit-exact), through the C ABI."""
+import numpy as np
+import pytest
+
+import oracle as O
+from conftest import same_bits
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def uq():
+    import ultraquant_b200.qlab as Q
+    return Q
+
+
+@pytest.mark.parametrize("tag", list("abcdefghi"))
+def test_rht_golden(uq, g_rht, tag):
+    A = g_rht[f"rht_{tag}_in"]
+    seed = int(g_rht[f"rht_{tag}_seed"])
+    X = uq.rht_rows(A, seed=seed)
+    assert same_bits(X, g_rht[f"rht_{tag}_out"])
+    assert same_bits(uq.irht_rows(X, A.shape[1], seed=seed), g_rht[f"irht_{tag}_out"])
+    k = f"irht_{tag}_f32_out"
+    if k in g_rht:
+        assert same_bits(uq.irht_rows(X.astype(np.float32), A.shape[1], seed=seed), g_rht[k])
+
+
+@pytest.mark.parametrize("rows,n0", [(1, 2), (3, 17), (7, 255), (5, 256), (9, 4095), (2, 8191), (3, 8192),
+                                     (4, 12000), (2, 16384), (33, 64)])
+def test_rht_random_vs_oracle(uq, rows, n0):
+    rng = np.random.RandomState(rows * 1000 + n0)
+    A = rng.standard_t(4, size=(rows, n0)) * 0.02
+    X = uq.rht_rows(A)
+    assert same_bits(X, O.rht_rows(A))
+    assert same_bits(uq.irht_rows(X, n0), O.irht_rows(X, n0))
+    X32 = X.astype(np.float32)
+    assert same_bits(uq.irht_rows(X32, n0), O.irht_rows(X32, n0))
+
+
+def test_rht_full_size_roundtrip(uq):
+    """4096 x 4096 (and the ffn_down 14336 -> 16384 width): orthogonality and
+    a bit-exact subsample of rows against the oracle."""
+    import torch
+    rng = np.random.RandomState(3)
+    for rows, n0 in [(4096, 4096), (1024, 14336)]:
+        A = (rng.randn(rows, n0) * 0.02)
+        At = torch.from_numpy(A).cuda()
+        X = uq.rht_rows(At)
+        Ah = uq.irht_rows(X, n0)
+        assert float((Ah - At).abs().max()) < 1e-15
+        nA, nX = float((At ** 2).sum()), float((X ** 2).sum())
+        assert abs(nA - nX) / nA < 1e-12
+        pick = rng.choice(rows, 8, replace=False)
+        assert same_bits(X[pick].cpu().numpy(), O.rht_rows(A[pick]))
+
+
+def test_d8_e8_golden(uq, g_e8):
+    Y = g_e8["Y"]
+    assert same_bits(uq._d8_decode(Y), g_e8["d8"])
+    assert same_bits(uq.e8_decode(Y), g_e8["e8"])
+
+
+def test_e8_random_vs_oracle(uq):
+    rng = np.random.RandomState(5)
+    Y = np.concatenate([rng.randn(50000, 8) * s for s in (0.3, 1.0, 4.0, 30.0)])
+    Y[:1000] = np.round(Y[:1000] * 2) / 2
+    assert same_bits(uq.e8_decode(Y), O.e8_decode(Y))
+    assert same_bits(uq._d8_decode(Y), O.d8_decode(Y.copy()))
+
+
+def test_entropy(uq, g_e8):
+    v = uq._entropy_bpw(g_e8["ent_pts"])
+    ref = float(g_e8["ent_bpw"])
+    assert abs(v - ref) <= 1e-12 * ref
+
+
+def test_q_e8_fixed_golden(uq, g_e8):
+    A = g_e8["q_A"]
+    for step in (0.48, 0.25, 0.16, 0.11):
+        assert same_bits(uq.q_e8_fast(A, fixed_step=step), g_e8[f"q_fixed_{step}"])
+    A2 = g_e8["q_A2"]
+    assert same_bits(uq.q_e8_fast(A2, fixed_step=0.48), g_e8["q_A2_fixed_0.48"])
+    assert same_bits(uq.q_e8_fast(A2, group=64, fixed_step=0.25), g_e8["q_A2_g64_fixed_0.25"])
+
+
+@pytest.mark.parametrize("group", [8, 64, 128, 256, 512, 1024, 96, 200])
+def test_q_e8_groups_vs_oracle(uq, group):
+    rng = np.random.RandomState(group)
+    A = rng.standard_t(4, size=(37, 301)) * 0.015
+    assert same_bits(uq.q_e8_fast(A, group=group, fixed_step=0.48), O.q_e8_fast(A, group=group, fixed_step=0.48))
+
+
+@pytest.mark.parametrize("tb", [2.0, 3.0])
+def test_q_e8_calibrated_golden(uq, g_e8, tb):
+    uq._E8_SCALE.clear()
+    rec = uq.q_e8_fast(g_e8["q_A3"], target_bpw=tb, calib_key="k")
+    assert uq._E8_SCALE["k"] == float(g_e8[f"q_cal_{tb}_step"])
+    assert same_bits(rec, g_e8[f"q_cal_{tb}_rec"])
+    uq._E8_SCALE.clear()
+
+
+def test_q_e8_full_size(uq):
+    """ffn_down-shaped 4096 x 14336 through rht (pad 16384) and E8 at 0.48:
+    rows subsample bit-exact, entropy of the whole index set finite."""
+    import torch
+    rng = np.random.RandomState(9)
+    A = torch.from_numpy(rng.standard_t(4, size=(4096, 14336)) / np.sqrt(2) * 0.015).cuda()
+    X = uq.rht_rows(A)
+    rec = uq.q_e8_fast(X, fixed_step=0.48)
+    pick = [0, 1, 2047, 4095]
+    Xs = X[pick].cpu().numpy()
+    assert same_bits(rec[pick].cpu().numpy(), O.q_e8_fast(Xs, fixed_step=0.48))
+    err = float(((rec - X) ** 2).sum() / (X ** 2).sum())
+    assert 0.0 < err < 0.05

@@ -1,0 +1,144 @@
+"""GPU parity: codebook, Viterbi encoder / decoder and the fused pipelines
+against the reference goldens and the oracle, through the C ABI."""
+import numpy as np
+import pytest
+
+import oracle as O
+from conftest import same_bits
+
+pytestmark = pytest.mark.gpu
+
+TQ = ["l8r2", "l8r1", "l8r3", "l8r4", "l10r2", "l12r2", "l12r2s64", "l12r3", "l16r2", "l16r3", "pad", "g128"]
+
+
+@pytest.fixture(scope="module")
+def T():
+    import ultraquant_b200.trellis as T
+    return T
+
+
+@pytest.fixture(scope="module")
+def Qat():
+    import ultraquant_b200.qat as Qat
+    return Qat
+
+
+def test_codebook_exhaustive(T, g_trellis):
+    """All 2^16 states (smaller L are prefixes) equal scipy's norm.ppf table."""
+    cb = T.codebook(16)
+    ref = g_trellis["codebook16"]
+    bad = np.nonzero(cb.view(np.int32) != ref.view(np.int32))[0]
+    assert bad.size == 0, f"{bad.size} codewords differ, first {bad[:5]}"
+    assert same_bits(T.codebook(12), ref[:4096])
+
+
+@pytest.mark.parametrize("tag", TQ)
+def test_trellis_golden(T, Qat, g_trellis, tag):
+    A = g_trellis[f"tq_{tag}_in"]
+    L, R, seg, group = (int(v) for v in g_trellis[f"tq_{tag}_cfg"])
+    rec = T.trellis_quant_fast(A, L=L, R=R, seg=seg, scale_group=group)
+    assert same_bits(rec, g_trellis[f"tq_{tag}_rec"])
+    st, sc_g, cw, meta = Qat.trellis_encode(A, L=L, R=R, seg=seg, scale_group=group)
+    assert np.array_equal(st, g_trellis[f"tq_{tag}_states"])
+    assert same_bits(sc_g, g_trellis[f"tq_{tag}_scg"])
+
+
+@pytest.mark.parametrize("tag", ["r8", "r10"])
+def test_trellis_full_row_golden(T, g_trellis, tag):
+    A = g_trellis[f"tr_{tag}_in"]
+    L, R, group = (int(v) for v in g_trellis[f"tr_{tag}_cfg"])
+    assert same_bits(T.trellis_quant(A, L=L, R=R, group=group), g_trellis[f"tr_{tag}_rec"])
+
+
+@pytest.mark.parametrize("L,R,seg", [(6, 1, 32), (6, 2, 64), (6, 3, 16), (8, 4, 64), (9, 2, 64), (10, 1, 256),
+                                     (11, 3, 256), (12, 2, 256), (13, 2, 128), (14, 2, 256), (14, 4, 256),
+                                     (15, 2, 64), (15, 3, 256), (16, 1, 256), (16, 2, 256), (16, 3, 256),
+                                     (16, 4, 256), (12, 2, 1), (12, 2, 2), (16, 2, 1)])
+def test_viterbi_states_vs_oracle(T, L, R, seg):
+    """Random sequences (plus exact-valued ones that provoke cost ties)."""
+    import torch
+    rng = np.random.RandomState(L * 100 + R * 10 + seg)
+    nseq = 24 if L >= 15 else 70
+    x = rng.randn(nseq, seg).astype(np.float32)
+    x[:4] = np.round(x[:4] * 2) / 2
+    got = T.viterbi_states(torch.from_numpy(x).cuda(), L, R).cpu().numpy()
+    ref = O.viterbi_segments(x, L, R)
+    assert np.array_equal(got, ref)
+
+
+def test_trellis_fast_full_size_l12(T, Qat):
+    """Config-1 shape: 4096 x 4096, L=12 R=2, T=256 (65,536 sequences).
+    Size-independent checks on all of it, bit-exact oracle on a subsample."""
+    import torch
+    rng = np.random.RandomState(0)
+    W = rng.normal(0, 0.02, size=(4096, 4096))
+    m = rng.random_sample(W.shape) < 0.001
+    W[m] = np.sign(rng.normal(size=m.sum())) * 0.16
+    A = torch.from_numpy(W.astype(np.float32)).cuda()
+    st, sc, ntot, pad = T.encode_segments(A, 12, 2, 256, 256)
+    assert st.shape == (65536, 256) and int(st.min()) >= 0 and int(st.max()) < 4096
+    # bitshift structure: s_t >> R == s_{t-1} & (2^(L-R) - 1)
+    assert bool(((st[:, 1:] >> 2) == (st[:, :-1] & 1023)).all())
+    rec = T.trellis_quant_fast(A, L=12, R=2, seg=256, scale_group=256)
+    nmse = float(((rec - A) ** 2).sum() / (A ** 2).sum())
+    assert 0.05 < nmse < 0.1, nmse
+    pick = np.sort(rng.choice(65536, 48, replace=False))
+    xs = (A.reshape(-1, 256)[pick] / sc[pick].reshape(-1, 1)).cpu().numpy()
+    ref = O.viterbi_segments(xs, 12, 2)
+    assert np.array_equal(st[pick].cpu().numpy(), ref)
+
+
+def test_pipeline_golden(g_pipeline):
+    from ultraquant_b200 import pipeline as P
+    W, H = g_pipeline["W"], g_pipeline["H"]
+    for L, R, seg in [(8, 2, 64), (12, 2, 64), (10, 3, 256)]:
+        res = P.quant_trellis_device(__import__("torch").from_numpy(W).cuda(),
+                                     __import__("torch").from_numpy(H).cuda(), L, R, seg, 256)
+        assert same_bits(res.What.cpu().numpy(), g_pipeline[f"qt_{L}_{R}_{seg}_What"])
+        ref = float(g_pipeline[f"qt_{L}_{R}_{seg}_wnmse"])
+        assert abs(res.wnmse - ref) <= 1e-5 * ref
+    for step in (0.48, 0.25):
+        assert same_bits(P.quant_step(W, H, step), g_pipeline[f"qs_{step}_What"])
+
+
+def test_pipeline_l16_vs_oracle():
+    """Config-2 recipe (L=16, k=2 and k=3, T=256, log-normal imatrix) on a
+    slice of rows: What bit-exact, weighted NMSE within 1e-5 relative."""
+    import torch
+    from ultraquant_b200 import pipeline as P
+    rng = np.random.RandomState(1)
+    W = rng.normal(0, 0.02, size=(4, 4096)).astype(np.float32)
+    H = np.exp(rng.normal(0.0, 1.0, size=4096))
+    for R in (2, 3):
+        res = P.quant_trellis_device(torch.from_numpy(W).cuda(), torch.from_numpy(H).cuda(), 16, R, 256, 256)
+        ref = O.quant_trellis(W.astype(np.float64), H, L=16, R=R, seg=256)
+        assert same_bits(res.What.cpu().numpy(), ref)
+        Hc = np.maximum(H, H.max() * 1e-3)
+        sH = np.sqrt(Hc)[None, :]
+        A = W.astype(np.float64) * sH
+        Ah = O.irht_rows(O.trellis_quant_fast(O.rht_rows(A), L=16, R=R, seg=256), 4096)
+        w = O.wnmse(A, Ah)
+        assert abs(res.wnmse - w) <= 1e-5 * w
+
+
+def test_install_patches_reference_modules(tmp_path, monkeypatch):
+    """install() swaps the hot path into importable qlab / trellis / qat
+    modules (here: stand-ins with the reference's attribute names)."""
+    import sys
+    for name, body in {"qlab": "def rht_rows(A, seed=0): raise AssertionError\n_E8_SCALE = {}\n"
+                               "def load_WH(n): return n\n",
+                       "trellis": "def trellis_quant_fast(*a, **k): raise AssertionError\n",
+                       "qat": "DEV='cuda'\n"}.items():
+        (tmp_path / f"{name}.py").write_text(body)
+    monkeypatch.syspath_prepend(str(tmp_path))
+    for name in ("qlab", "trellis", "qat"):
+        sys.modules.pop(name, None)
+    import ultraquant_b200
+    mods = ultraquant_b200.install()
+    from qlab import rht_rows, load_WH
+    import ultraquant_b200.qlab as Q
+    assert rht_rows is Q.rht_rows and load_WH("x") == "x"
+    A = np.random.RandomState(0).randn(3, 100)
+    assert same_bits(mods["qlab"].rht_rows(A), O.rht_rows(A))
+    for name in ("qlab", "trellis", "qat"):
+        sys.modules.pop(name, None)

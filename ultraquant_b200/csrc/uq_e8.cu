@@ -1,0 +1,439 @@
+// E8 nearest-point quantizer (qlab.py:133-183) for sm_100a.
+//
+// q_e8_fast: per-group RMS in fp64 (numpy pairwise order), gn = g / rms,
+// Y = gn / step, closed-form Conway-Sloane decode of D8 u (D8 + 1/2), then
+// rec = (pts * step) * rms.  All fp64 operations are the reference's, one by
+// one, with IEEE division and no FMA contraction, so points and
+// reconstructions are bit-exact.  The kernel is HBM-bound: a CTA stages a
+// tile of whole groups in shared memory (coalesced), reduces the group RMS
+// cooperatively, then every thread decodes one 8-vector.
+//
+// Entropy (qlab.py:151-156): distinct 8-tuples of 2*pts are counted in an
+// open-addressing hash table (64-bit keys, one byte per coordinate), the
+// rate -sum p log2 p is accumulated in 2^-64 fixed point (order independent,
+// hence deterministic) and divided by 8.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <vector>
+
+#include "uq_common.cuh"
+#include "uq_groupsum.cuh"
+#include "uq_mt19937.h"
+
+namespace {
+
+// ---- D8 / E8 decode on one vector in registers ------------------------------
+__device__ __forceinline__ double sum8_pairwise(const double v[8]) {
+    return d_add(d_add(d_add(v[0], v[1]), d_add(v[2], v[3])), d_add(d_add(v[4], v[5]), d_add(v[6], v[7])));
+}
+
+// qlab.py:133-142: round half to even; odd coordinate sum -> move the first
+// coordinate of largest |error| by sign(error) (0 when the error is 0).
+__device__ __forceinline__ void d8_point(const double y[8], double f[8]) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) f[i] = rint(y[i]);
+    const long long s = (long long)sum8_pairwise(f);
+    if (s % 2 != 0) {
+        int k = 0;
+        double best = fabs(d_sub(y[0], f[0]));
+#pragma unroll
+        for (int i = 1; i < 8; ++i) {
+            const double a = fabs(d_sub(y[i], f[i]));
+            if (a > best) { best = a; k = i; }
+        }
+        double ek = 0.0;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) if (i == k) ek = d_sub(y[i], f[i]);
+        const double sg = ek > 0.0 ? 1.0 : (ek < 0.0 ? -1.0 : 0.0);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) if (i == k) f[i] = d_add(f[i], sg);
+    }
+}
+
+// qlab.py:144-149
+__device__ __forceinline__ void e8_point(const double y[8], double p[8]) {
+    double a[8], b[8], ym[8], da[8], db[8];
+    d8_point(y, a);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) ym[i] = d_sub(y[i], 0.5);
+    d8_point(ym, b);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        b[i] = d_add(b[i], 0.5);
+        const double ea = d_sub(y[i], a[i]), eb = d_sub(y[i], b[i]);
+        da[i] = d_mul(ea, ea);
+        db[i] = d_mul(eb, eb);
+    }
+    const bool use_b = sum8_pairwise(db) < sum8_pairwise(da);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) p[i] = use_b ? b[i] : a[i];
+}
+
+__global__ void d8_kernel(const double *Y, int64_t nvec, double *out, int e8) {
+    for (int64_t v = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; v < nvec;
+         v += int64_t(gridDim.x) * blockDim.x) {
+        double y[8], p[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) y[i] = __ldg(Y + 8 * v + i);
+        if (e8) e8_point(y, p); else d8_point(y, p);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) out[8 * v + i] = p[i];
+    }
+}
+
+// ---- fixed-step quantizer ---------------------------------------------------
+struct E8Args {
+    const void *A;
+    int64_t size;      // valid elements
+    int group;
+    int tile;          // elements per CTA (multiple of group and of 8)
+    double step;
+    double *rec;       // size
+    int16_t *idx;      // padded size, nullable
+    double *rms_out;   // per group, nullable (calibration uses it)
+};
+
+template <typename TIn>
+__global__ void e8_quant_kernel(E8Args a) {
+    extern __shared__ double sm[];
+    double *tile = sm;                       // a.tile
+    const int ng = a.tile / a.group;
+    double *rms = tile + a.tile;             // ng
+    double *scratch = rms + ng;              // ng * 32
+    const int64_t base = int64_t(blockIdx.x) * a.tile;
+    const TIn *A = static_cast<const TIn *>(a.A);
+    for (int i = threadIdx.x; i < a.tile; i += blockDim.x) {
+        const int64_t gi = base + i;
+        tile[i] = gi < a.size ? double(__ldg(A + gi)) : 0.0;
+    }
+    __syncthreads();
+    tile_group_sumsq<double>(tile, ng, a.group, rms, scratch);
+    for (int g = threadIdx.x; g < ng; g += blockDim.x) {
+        // np.sqrt((g**2).mean()) + 1e-12: mean = sum / count in fp64
+        const double r = d_add(sqrt(rms[g] / double(a.group)), 1e-12);
+        rms[g] = r;
+        if (a.rms_out) {
+            const int64_t gg = base / a.group + g;
+            if (gg * a.group < a.size) a.rms_out[gg] = r;
+        }
+    }
+    __syncthreads();
+    if (!a.rec && !a.idx) return;
+    for (int v = threadIdx.x; v < a.tile / 8; v += blockDim.x) {
+        const int64_t e0 = base + 8 * int64_t(v);
+        if (e0 >= a.size) break;
+        const double r = rms[(8 * v) / a.group];
+        double y[8], p[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) y[i] = (tile[8 * v + i] / r) / a.step;
+        e8_point(y, p);
+        if (a.rec) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+                if (e0 + i < a.size) a.rec[e0 + i] = d_mul(d_mul(p[i], a.step), r);
+        }
+        if (a.idx) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) a.idx[e0 + i] = (int16_t)(long long)d_mul(p[i], 2.0);
+        }
+    }
+}
+
+int e8_tile_elems(int group) {
+    if (group >= 2048) return group;
+    int t = group;
+    while (t < 2048) t += group;
+    // keep tile a multiple of 8 vectors' worth of threads
+    return t;
+}
+
+template <typename TIn>
+int launch_e8_quant(const E8Args &a0, cudaStream_t st) {
+    E8Args a = a0;
+    a.tile = e8_tile_elems(a.group);
+    const int ng = a.tile / a.group;
+    const size_t smem = sizeof(double) * (size_t(a.tile) + ng + size_t(ng) * 32);
+    const int threads = std::min(1024, std::max(32, ((a.tile / 8 + 31) / 32) * 32));
+    const int64_t padded = (a.size + a.group - 1) / a.group * a.group;
+    const int64_t grid = (padded + a.tile - 1) / a.tile;
+    auto kern = e8_quant_kernel<TIn>;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess)
+        return uq::check_cuda("e8: set smem attribute");
+    if (grid > 0) { uq::ProfScope _p("e8_quant", st); kern<<<unsigned(grid), threads, smem, st>>>(a); }
+    return uq::check_cuda("e8_quant_kernel launch");
+}
+
+// ---- entropy of lattice indices --------------------------------------------
+// Key: byte i = (2*p_i truncated) + 128, coordinate values must lie in
+// [-127, 127]; byte 0 never occurs, so key 0 marks an empty slot.
+__device__ __forceinline__ unsigned long long mix64(unsigned long long k) {
+    k ^= k >> 33; k *= 0xff51afd7ed558ccdull; k ^= k >> 33; k *= 0xc4ceb9fe1a85ec53ull; k ^= k >> 33;
+    return k;
+}
+
+template <typename Src>
+__global__ void hash_count_kernel(Src src, int64_t nvec, unsigned long long *keys, unsigned *cnt,
+                                  unsigned long long mask, int *overflow) {
+    for (int64_t v = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; v < nvec;
+         v += int64_t(gridDim.x) * blockDim.x) {
+        unsigned long long key = 0;
+        bool bad = false;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const long long c = src(v, i);
+            bad |= (c < -127 || c > 127);
+            key |= (unsigned long long)(c + 128) << (8 * i);
+        }
+        if (bad) { atomicExch(overflow, 1); continue; }
+        unsigned long long h = mix64(key) & mask;
+        for (unsigned long long probe = 0; probe <= mask; ++probe) {
+            const unsigned long long prev = atomicCAS(keys + h, 0ull, key);
+            if (prev == 0ull || prev == key) { atomicAdd(cnt + h, 1u); break; }
+            h = (h + 1) & mask;
+        }
+    }
+}
+
+struct PtsSrc {  // (pts * 2).astype(int64) of an fp64 (nvec, 8) array
+    const double *p;
+    __device__ long long operator()(int64_t v, int i) const { return (long long)d_mul(__ldg(p + 8 * v + i), 2.0); }
+};
+
+// Per-CTA fixed-point sums of -p log2 p (p = cnt / total), 2^-64 units.
+__global__ void entropy_partial_kernel(const unsigned *cnt, int64_t slots, double total,
+                                       unsigned long long *part_hi, unsigned long long *part_lo) {
+    __shared__ unsigned __int128 red[256];
+    unsigned __int128 acc = 0;
+    for (int64_t s = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; s < slots;
+         s += int64_t(gridDim.x) * blockDim.x) {
+        const unsigned c = cnt[s];
+        if (c) {
+            const double p = double(c) / total;
+            const double t = -(p * log2(p));            // in [0, 0.531]
+            acc += (unsigned __int128)(unsigned long long)(t * 18446744073709551616.0);  // * 2^64 < 2^63
+        }
+    }
+    red[threadIdx.x] = acc;
+    __syncthreads();
+    for (int w = blockDim.x / 2; w > 0; w >>= 1) {
+        if (threadIdx.x < w) red[threadIdx.x] += red[threadIdx.x + w];
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) {
+        part_hi[blockIdx.x] = (unsigned long long)(red[0] >> 64);
+        part_lo[blockIdx.x] = (unsigned long long)red[0];
+    }
+}
+
+__global__ void entropy_final_kernel(const unsigned long long *hi, const unsigned long long *lo, int parts,
+                                     double *bpw, const int *overflow) {
+    unsigned __int128 s = 0;
+    for (int i = 0; i < parts; ++i) s += ((unsigned __int128)hi[i] << 64) | lo[i];
+    const double v = double((unsigned long long)(s >> 64)) + double((unsigned long long)s) * 5.421010862427522e-20;
+    *bpw = (*overflow) ? -1.0 : v / 8.0;
+}
+
+constexpr int kEntParts = 296;
+
+struct EntWs {
+    unsigned long long *keys, *hi, *lo;
+    unsigned *cnt;
+    int *overflow;
+    unsigned long long mask;
+};
+
+size_t entropy_ws_bytes(int64_t nvec, EntWs *w, void *base) {
+    unsigned long long slots = 1024;
+    while (slots < (unsigned long long)(2 * nvec)) slots <<= 1;
+    uq::Carver c(base, ~size_t(0));
+    EntWs t;
+    t.keys = c.take<unsigned long long>(slots);
+    t.cnt = c.take<unsigned>(slots);
+    t.hi = c.take<unsigned long long>(kEntParts);
+    t.lo = c.take<unsigned long long>(kEntParts);
+    t.overflow = c.take<int>(1);
+    t.mask = slots - 1;
+    if (w) *w = t;
+    return c.off;
+}
+
+template <typename Src>
+int entropy_run(Src src, int64_t nvec, double *bpw, void *ws, size_t ws_bytes, cudaStream_t st) {
+    EntWs w;
+    const size_t need = entropy_ws_bytes(nvec, &w, ws);
+    if (ws_bytes < need) return uq::fail(UQ_ERR_WORKSPACE, "entropy: workspace %zu < %zu", ws_bytes, need);
+    const size_t slots = size_t(w.mask) + 1;
+    cudaMemsetAsync(w.keys, 0, slots * sizeof(unsigned long long), st);
+    cudaMemsetAsync(w.cnt, 0, slots * sizeof(unsigned), st);
+    cudaMemsetAsync(w.overflow, 0, sizeof(int), st);
+    const int grid = std::max(1, std::min<int>(int((nvec + 255) / 256), uq::num_sms() * 8));
+    if (nvec > 0) { uq::ProfScope _p("hash_count", st); hash_count_kernel<<<grid, 256, 0, st>>>(src, nvec, w.keys, w.cnt, w.mask, w.overflow); }
+    { uq::ProfScope _p("entropy_partial", st); entropy_partial_kernel<<<kEntParts, 256, 0, st>>>(w.cnt, int64_t(slots), double(nvec), w.hi, w.lo); }
+    { uq::ProfScope _p("entropy_final", st); entropy_final_kernel<<<1, 1, 0, st>>>(w.hi, w.lo, kEntParts, bpw, w.overflow); }
+    return uq::check_cuda("entropy kernels");
+}
+
+// ---- calibration (qlab.py:171-180) ------------------------------------------
+// gather the subsampled, normalised vectors: sub[i] = x[8*pick[i] ..] / rms[group]
+template <typename TIn>
+__global__ void gather_gn_kernel(const TIn *A, int64_t size, int group, const double *rms,
+                                 const int64_t *pick, int64_t ns, double *sub) {
+    for (int64_t t = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; t < ns * 8;
+         t += int64_t(gridDim.x) * blockDim.x) {
+        const int64_t v = pick[t >> 3];
+        const int64_t e = 8 * v + (t & 7);
+        const double x = e < size ? double(__ldg(A + e)) : 0.0;
+        sub[t] = x / rms[e / group];
+    }
+}
+
+__global__ void e8_scaled_keys_kernel(const double *sub, int64_t ns, double step, double *pts) {
+    for (int64_t v = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; v < ns;
+         v += int64_t(gridDim.x) * blockDim.x) {
+        double y[8], p[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) y[i] = sub[8 * v + i] / step;
+        e8_point(y, p);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) pts[8 * v + i] = p[i];
+    }
+}
+
+struct CalWs {
+    double *rms, *sub, *pts, *bpw;
+    int64_t *pick;
+    void *ent;
+    size_t ent_bytes;
+};
+
+size_t calib_ws_bytes(int64_t size, int64_t group, CalWs *w, void *base) {
+    const int64_t padded = (size + group - 1) / group * group;
+    const int64_t ngroups = padded / group, nvec = padded / 8;
+    const int64_t ns = nvec < 600000 ? nvec : 600000;
+    uq::Carver c(base, ~size_t(0));
+    CalWs t;
+    t.rms = c.take<double>(ngroups);
+    t.pick = c.take<int64_t>(ns);
+    t.sub = c.take<double>(ns * 8);
+    t.pts = c.take<double>(ns * 8);
+    t.bpw = c.take<double>(1);
+    t.ent_bytes = entropy_ws_bytes(ns, nullptr, nullptr);
+    t.ent = c.take<char>(t.ent_bytes);
+    if (w) *w = t;
+    return c.off;
+}
+
+}  // namespace
+
+namespace uq {
+int e8_quant(const void *A, int a_dtype, int64_t size, int64_t group, double step, double *rec,
+             int16_t *idx, double *rms_out, cudaStream_t st) {
+    E8Args a{};
+    a.A = A; a.size = size; a.group = int(group); a.step = step; a.rec = rec; a.idx = idx; a.rms_out = rms_out;
+    if (a_dtype == UQ_F64) return launch_e8_quant<double>(a, st);
+    if (a_dtype == UQ_F32) return launch_e8_quant<float>(a, st);
+    return fail(UQ_ERR_INVALID, "e8: bad dtype");
+}
+}  // namespace uq
+
+static int e8_check(int64_t size, int64_t group, const char *who) {
+    if (size < 0) return uq::fail(UQ_ERR_INVALID, "%s: negative size", who);
+    if (group < 8 || group % 8 != 0 || group > 8192)
+        return uq::fail(UQ_ERR_UNSUPPORTED, "%s: group %lld must be a multiple of 8 in [8, 8192]", who, (long long)group);
+    return UQ_OK;
+}
+
+extern "C" {
+
+int uq_d8_decode(const double *Y, int64_t nvec, double *out, void *stream) {
+    if (nvec < 0) return uq::fail(UQ_ERR_INVALID, "uq_d8_decode: nvec < 0");
+    if (nvec == 0) return UQ_OK;
+    if (!Y || !out) return uq::fail(UQ_ERR_INVALID, "uq_d8_decode: null pointer");
+    const int grid = std::max(1, std::min<int>(int((nvec + 255) / 256), uq::num_sms() * 16));
+    { uq::ProfScope _p("d8_decode", UQ_STREAM(stream)); d8_kernel<<<grid, 256, 0, UQ_STREAM(stream)>>>(Y, nvec, out, 0); }
+    return uq::check_cuda("d8_kernel launch");
+}
+
+int uq_e8_decode(const double *Y, int64_t nvec, double *out, void *stream) {
+    if (nvec < 0) return uq::fail(UQ_ERR_INVALID, "uq_e8_decode: nvec < 0");
+    if (nvec == 0) return UQ_OK;
+    if (!Y || !out) return uq::fail(UQ_ERR_INVALID, "uq_e8_decode: null pointer");
+    const int grid = std::max(1, std::min<int>(int((nvec + 255) / 256), uq::num_sms() * 16));
+    { uq::ProfScope _p("e8_decode", UQ_STREAM(stream)); d8_kernel<<<grid, 256, 0, UQ_STREAM(stream)>>>(Y, nvec, out, 1); }
+    return uq::check_cuda("e8 decode launch");
+}
+
+int uq_e8_quant(const void *A, int a_dtype, int64_t size, int64_t group, double step, double *rec,
+                int16_t *idx, void *stream) {
+    int rc = e8_check(size, group, "uq_e8_quant");
+    if (rc) return rc;
+    if (!uq::dtype_size(a_dtype)) return uq::fail(UQ_ERR_INVALID, "uq_e8_quant: bad dtype");
+    if (size == 0) return UQ_OK;
+    if (!A || (!rec && !idx)) return uq::fail(UQ_ERR_INVALID, "uq_e8_quant: null pointer");
+    return uq::e8_quant(A, a_dtype, size, group, step, rec, idx, nullptr, UQ_STREAM(stream));
+}
+
+size_t uq_e8_entropy_workspace_bytes(int64_t nvec) { return entropy_ws_bytes(nvec < 0 ? 0 : nvec, nullptr, nullptr); }
+
+int uq_e8_entropy_bpw(const double *pts, int64_t nvec, double *bpw, void *workspace,
+                      size_t workspace_bytes, void *stream) {
+    if (nvec < 1) return uq::fail(UQ_ERR_INVALID, "uq_e8_entropy_bpw: need at least one vector");
+    if (!pts || !bpw || !workspace) return uq::fail(UQ_ERR_INVALID, "uq_e8_entropy_bpw: null pointer");
+    return entropy_run(PtsSrc{pts}, nvec, bpw, workspace, workspace_bytes, UQ_STREAM(stream));
+}
+
+size_t uq_e8_calibrate_workspace_bytes(int64_t size, int64_t group) {
+    if (size < 0 || group < 8) return 0;
+    return calib_ws_bytes(size, group, nullptr, nullptr);
+}
+
+int uq_e8_calibrate(const void *A, int a_dtype, int64_t size, int64_t group, double target_bpw,
+                    double *step_host, void *workspace, size_t workspace_bytes, void *stream) {
+    int rc = e8_check(size, group, "uq_e8_calibrate");
+    if (rc) return rc;
+    if (size < 1 || !A || !step_host || !workspace || !uq::dtype_size(a_dtype))
+        return uq::fail(UQ_ERR_INVALID, "uq_e8_calibrate: bad arguments");
+    cudaStream_t st = UQ_STREAM(stream);
+    CalWs w;
+    const size_t need = calib_ws_bytes(size, group, &w, workspace);
+    if (workspace_bytes < need) return uq::fail(UQ_ERR_WORKSPACE, "uq_e8_calibrate: workspace %zu < %zu", workspace_bytes, need);
+    const int64_t padded = (size + group - 1) / group * group;
+    const int64_t nvec = padded / 8;
+    const int64_t ns = nvec < 600000 ? nvec : 600000;
+    // group RMS of the whole tensor
+    rc = uq::e8_quant(A, a_dtype, size, group, 1.0, nullptr, nullptr, w.rms, st);
+    if (rc) return rc;
+    // RandomState(0).randint(0, nvec, ns)
+    std::vector<int64_t> pick(static_cast<size_t>(ns), 0);
+    uq::MT19937 g;
+    g.seed(0);
+    g.randint(0, nvec, ns, pick.data());
+    if (cudaMemcpyAsync(w.pick, pick.data(), size_t(ns) * sizeof(int64_t), cudaMemcpyHostToDevice, st) != cudaSuccess)
+        return uq::check_cuda("calibrate: copy subsample indices");
+    const int grid = std::max(1, std::min<int>(int((ns * 8 + 255) / 256), uq::num_sms() * 16));
+    uq::count_launch();
+    if (a_dtype == UQ_F64)
+        gather_gn_kernel<double><<<grid, 256, 0, st>>>(static_cast<const double *>(A), size, int(group), w.rms, w.pick, ns, w.sub);
+    else
+        gather_gn_kernel<float><<<grid, 256, 0, st>>>(static_cast<const float *>(A), size, int(group), w.rms, w.pick, ns, w.sub);
+    if ((rc = uq::check_cuda("gather_gn_kernel launch"))) return rc;
+    double lo = 0.3, hi = 10.0;
+    for (int it = 0; it < 18; ++it) {
+        const double mid = (lo + hi) / 2;
+        const int g2 = std::max(1, std::min<int>(int((ns + 127) / 128), uq::num_sms() * 16));
+        { uq::ProfScope _p("e8_scaled_keys", st); e8_scaled_keys_kernel<<<g2, 128, 0, st>>>(w.sub, ns, mid, w.pts); }
+        if ((rc = uq::check_cuda("e8_scaled_keys_kernel launch"))) return rc;
+        if ((rc = entropy_run(PtsSrc{w.pts}, ns, w.bpw, w.ent, w.ent_bytes, st))) return rc;
+        double bpw = 0.0;
+        if (cudaMemcpyAsync(&bpw, w.bpw, sizeof(double), cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+            cudaStreamSynchronize(st) != cudaSuccess)
+            return uq::check_cuda("calibrate: read entropy");
+        if (bpw < 0) return uq::fail(UQ_ERR_UNSUPPORTED, "calibrate: lattice index outside [-127, 127] at step %g", mid);
+        if (bpw > target_bpw) lo = mid; else hi = mid;
+    }
+    *step_host = (lo + hi) / 2;
+    return UQ_OK;
+}
+
+}  // extern "C"

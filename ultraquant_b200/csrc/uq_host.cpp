@@ -1,0 +1,208 @@
+// Host-side pieces of the C ABI: status strings, per-thread error messages
+// and the legacy MT19937 stream that produces the RHT sign vector and the E8
+// calibration subsample exactly as numpy's RandomState does.
+#include <atomic>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include <cuda_runtime.h>
+
+#include "uq_common.cuh"
+#include "uq_mt19937.h"
+
+namespace {
+thread_local char g_err[512] = "";
+
+std::atomic<long long> g_launches{0};
+std::atomic<int> g_prof_on{0};
+std::mutex g_prof_mu;
+struct ProfEntry {
+    std::string kernel;
+    cudaEvent_t a, b;
+};
+std::vector<ProfEntry> g_prof;
+}  // namespace
+
+namespace uq {
+
+int fail(int code, const char *fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_err, sizeof(g_err), fmt, ap);
+    va_end(ap);
+    return code;
+}
+
+int check_cuda(const char *what) {
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return fail(UQ_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+    return UQ_OK;
+}
+
+void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+
+ProfScope::ProfScope(const char *kernel, cudaStream_t s) : st(s) {
+    count_launch();
+    if (!g_prof_on.load(std::memory_order_relaxed)) return;
+    ProfEntry e;
+    e.kernel = kernel;
+    if (cudaEventCreate(&e.a) != cudaSuccess || cudaEventCreate(&e.b) != cudaSuccess) return;
+    cudaEventRecord(e.a, s);
+    std::lock_guard<std::mutex> g(g_prof_mu);
+    slot = int(g_prof.size());
+    g_prof.push_back(e);
+}
+
+ProfScope::~ProfScope() {
+    if (slot < 0) return;
+    std::lock_guard<std::mutex> g(g_prof_mu);
+    cudaEventRecord(g_prof[size_t(slot)].b, st);
+}
+
+int num_sms() {
+    int dev = 0, n = 148;
+    if (cudaGetDevice(&dev) == cudaSuccess)
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    return n > 0 ? n : 148;
+}
+
+// --- MT19937 (Matsumoto & Nishimura 1998), 32-bit output --------------------
+void MT19937::seed(uint32_t s) {
+    // init_genrand: Knuth's multiplier 1812433253 recurrence
+    mt[0] = s;
+    for (int i = 1; i < kN; ++i)
+        mt[i] = 1812433253u * (mt[i - 1] ^ (mt[i - 1] >> 30)) + uint32_t(i);
+    idx = kN;
+}
+
+void MT19937::twist() {
+    const uint32_t upper = 0x80000000u, lower = 0x7fffffffu, matrix = 0x9908b0dfu;
+    for (int i = 0; i < kN; ++i) {
+        uint32_t y = (mt[i] & upper) | (mt[(i + 1) % kN] & lower);
+        uint32_t v = mt[(i + kM) % kN] ^ (y >> 1);
+        if (y & 1u) v ^= matrix;
+        mt[i] = v;
+    }
+    idx = 0;
+}
+
+uint32_t MT19937::next32() {
+    if (idx >= kN) twist();
+    uint32_t y = mt[idx++];
+    y ^= y >> 11;
+    y ^= (y << 7) & 0x9d2c5680u;
+    y ^= (y << 15) & 0xefc60000u;
+    y ^= y >> 18;
+    return y;
+}
+
+uint64_t MT19937::next64() {
+    uint64_t hi = next32();
+    return (hi << 32) | next32();
+}
+
+// numpy legacy randint(low, high) with the masked-rejection bounded draw:
+// rng = high - low - 1, mask = smallest 2^k - 1 >= rng; 32-bit draws when
+// rng fits in 32 bits, otherwise 64-bit draws.
+void MT19937::randint(int64_t low, int64_t high, int64_t count, int64_t *out) {
+    uint64_t rng = uint64_t(high - low - 1);
+    if (rng == 0) {
+        for (int64_t i = 0; i < count; ++i) out[i] = low;
+        return;
+    }
+    uint64_t mask = rng;
+    mask |= mask >> 1; mask |= mask >> 2; mask |= mask >> 4;
+    mask |= mask >> 8; mask |= mask >> 16; mask |= mask >> 32;
+    if (rng <= 0xffffffffull) {
+        if (rng == 0xffffffffull) {
+            for (int64_t i = 0; i < count; ++i) out[i] = low + int64_t(next32());
+            return;
+        }
+        uint32_t m32 = uint32_t(mask), r32 = uint32_t(rng);
+        for (int64_t i = 0; i < count; ++i) {
+            uint32_t v;
+            do { v = next32() & m32; } while (v > r32);
+            out[i] = low + int64_t(v);
+        }
+    } else {
+        for (int64_t i = 0; i < count; ++i) {
+            uint64_t v;
+            if (rng == ~0ull) { v = next64(); }
+            else { do { v = next64() & mask; } while (v > rng); }
+            out[i] = low + int64_t(v);
+        }
+    }
+}
+
+}  // namespace uq
+
+extern "C" {
+
+int uq_version(void) { return 100; }
+
+void uq_profile_enable(int on) { g_prof_on.store(on ? 1 : 0); }
+
+void uq_profile_reset(void) {
+    std::lock_guard<std::mutex> g(g_prof_mu);
+    for (auto &e : g_prof) {
+        cudaEventDestroy(e.a);
+        cudaEventDestroy(e.b);
+    }
+    g_prof.clear();
+    g_launches.store(0);
+}
+
+int64_t uq_launch_count(void) { return g_launches.load(); }
+
+int uq_profile_read(const char *kernel, double *total_ms, int64_t *launches) {
+    std::lock_guard<std::mutex> g(g_prof_mu);
+    double tot = 0.0;
+    int64_t n = 0;
+    for (auto &e : g_prof) {
+        if (kernel && e.kernel != kernel) continue;
+        if (cudaEventSynchronize(e.b) != cudaSuccess) return uq::check_cuda("uq_profile_read");
+        float ms = 0.f;
+        cudaEventElapsedTime(&ms, e.a, e.b);
+        tot += ms;
+        ++n;
+    }
+    if (total_ms) *total_ms = tot;
+    if (launches) *launches = n;
+    return UQ_OK;
+}
+
+const char *uq_status_string(int status) {
+    switch (status) {
+        case UQ_OK: return "ok";
+        case UQ_ERR_INVALID: return "invalid argument";
+        case UQ_ERR_UNSUPPORTED: return "unsupported configuration";
+        case UQ_ERR_CUDA: return "CUDA error";
+        case UQ_ERR_WORKSPACE: return "workspace too small";
+        case UQ_ERR_TIMEOUT: return "device wait timed out";
+        default: return "unknown status";
+    }
+}
+
+const char *uq_last_error(void) { return g_err; }
+
+int64_t uq_next_pow2(int64_t n0) {
+    int64_t p = 1;
+    while (p < n0) p <<= 1;
+    return p;
+}
+
+int uq_rht_signs(uint32_t seed, int64_t n, double *out_host) {
+    if (n < 0 || (n > 0 && !out_host)) return uq::fail(UQ_ERR_INVALID, "uq_rht_signs: bad n / pointer");
+    // choice([-1., 1.], n) == a[randint(0, 2, n)]: rng = 1, mask = 1, one
+    // 32-bit draw per element, never rejected.
+    uq::MT19937 g;
+    g.seed(seed);
+    for (int64_t i = 0; i < n; ++i) out_host[i] = (g.next32() & 1u) ? 1.0 : -1.0;
+    return UQ_OK;
+}
+
+}  // extern "C"

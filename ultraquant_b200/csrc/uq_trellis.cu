@@ -1,0 +1,816 @@
+// Bitshift-trellis Viterbi encoder / decoder (trellis.py:14-108, qat.py:11-59)
+// for sm_100a.
+//
+// Recurrence (state s has L bits, a step appends R bits at the bottom):
+//   cost_0[s]   = (x_0 - cw[s])^2
+//   m_t[q]      = min_k cost_t[k*Q + q],   bp[t+1][q] = first argmin k
+//   cost_{t+1}[s] = (x_{t+1} - cw[s])^2 + m_t[s >> R]
+// with Q = 2^(L-R), K = 2^R.  Written in terms of m only:
+//   m_t[q] = min_k ((x_t - cw[kQ + q])^2 + m_{t-1}[k*Rn + (q >> R)]),  Rn = Q / K.
+// Every term is the reference's separate sub / square / add in float32, so
+// the min-plus values, and hence the decisions, are bit-exact.
+//
+// Work split: a thread owns NQ consecutive q (64 = K * NQ trellis states),
+// keeps their codewords in registers for the whole sequence and, per step,
+//   * reads K * max(NQ/K, 1) values of m_{t-1} from shared memory,
+//   * computes its 64 costs with packed f32x2 sub / mul / add,
+//   * reduces each q's K candidates with fminf and derives the first-index
+//     argmin from the sign bits of f32x2 differences (LOP3 select + funnel
+//     shift: no compare / select chains),
+//   * writes NQ new m values (16-byte stores) and one 32-bit backpointer word.
+// The m array is double buffered in shared memory with an XOR swizzle that
+// makes both the write and the read pattern bank-conflict free.
+// 2^L / 64 threads cover one sequence: a 512-thread CTA holds several
+// sequences for L <= 15; for L = 16 a 2-CTA cluster (2 SMs) shares one
+// sequence and reads the other half of m through distributed shared memory.
+// Two independent sequence sets are interleaved so that the cluster barrier
+// of one set overlaps the arithmetic of the other.
+//
+// Backpointers go to a global workspace; a second kernel walks them back
+// (one thread per sequence) and writes the full L-bit state path.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+
+#include "uq_common.cuh"
+#include "uq_groupsum.cuh"
+
+namespace {
+
+// ---------------------------------------------------------------------------
+// Codebook: trellis.py:14-19.  Inverse normal CDF by Wichura's algorithm
+// AS 241 (PPND16, Applied Statistics 37(3), 1988), fp64, then float32.
+// ---------------------------------------------------------------------------
+__device__ double ppnd16(double p) {
+    const double q = p - 0.5;
+    if (fabs(q) <= 0.425) {
+        const double r = 0.180625 - q * q;
+        const double num = fma(fma(fma(fma(fma(fma(fma(2.5090809287301226727e+3, r, 3.3430575583588128105e+4), r,
+                              6.7265770927008700853e+4), r, 4.5921953931549871457e+4), r,
+                              1.3731693765509461125e+4), r, 1.9715909503065514427e+3), r,
+                              1.3314166789178437745e+2), r, 3.3871328727963666080e+0);
+        const double den = fma(fma(fma(fma(fma(fma(fma(5.2264952788528545610e+3, r, 2.8729085735721942674e+4), r,
+                              3.9307895800092710610e+4), r, 2.1213794301586595867e+4), r,
+                              5.3941960214247511077e+3), r, 6.8718700749205790830e+2), r,
+                              4.2313330701600911252e+1), r, 1.0);
+        return q * num / den;
+    }
+    double r = q < 0 ? p : 1.0 - p;
+    r = sqrt(-log(r));
+    double val;
+    if (r <= 5.0) {
+        r -= 1.6;
+        const double num = fma(fma(fma(fma(fma(fma(fma(7.74545014278341407640e-4, r, 2.27238449892691845833e-2), r,
+                              2.41780725177450611770e-1), r, 1.27045825245236838258e+0), r,
+                              3.64784832476320460504e+0), r, 5.76949722146069140550e+0), r,
+                              4.63033784615654529590e+0), r, 1.42343711074968357734e+0);
+        const double den = fma(fma(fma(fma(fma(fma(fma(1.05075007164441684324e-9, r, 5.47593808499534494600e-4), r,
+                              1.51986665636164571966e-2), r, 1.48103976427480074590e-1), r,
+                              6.89767334985100004550e-1), r, 1.67638483018380384940e+0), r,
+                              2.05319162663775882187e+0), r, 1.0);
+        val = num / den;
+    } else {
+        r -= 5.0;
+        const double num = fma(fma(fma(fma(fma(fma(fma(2.01033439929228813265e-7, r, 2.71155556874348757815e-5), r,
+                              1.24266094738807843860e-3), r, 2.65321895265761230930e-2), r,
+                              2.96560571828504891230e-1), r, 1.78482653991729133580e+0), r,
+                              5.46378491116411436990e+0), r, 6.65790464350110377720e+0);
+        const double den = fma(fma(fma(fma(fma(fma(fma(2.04426310338993978564e-15, r, 1.42151175831644588870e-7), r,
+                              1.84631831751005468180e-5), r, 7.86869131145613259100e-4), r,
+                              1.48753612908506148525e-2), r, 1.36929880922735805310e-1), r,
+                              5.99832206555887937690e-1), r, 1.0);
+        val = num / den;
+    }
+    return q < 0 ? -val : val;
+}
+
+__global__ void codebook_kernel(int L, float *out) {
+    const unsigned S = 1u << L;
+    for (unsigned s = blockIdx.x * blockDim.x + threadIdx.x; s < S; s += gridDim.x * blockDim.x) {
+        unsigned long long h = (unsigned long long)s * 2654435761ull + 0x9E3779B97F4A7C15ull;
+        h ^= h >> 29;
+        h *= 0xBF58476D1CE4E5B9ull;
+        h ^= h >> 32;
+        const double u = (double(h & 0xFFFFFFFFull) + 0.5) / 4294967296.0;
+        out[s] = float(ppnd16(u));
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Normalisation: trellis.py:69-80 (flat) and :35-42 (per row).
+// A CTA stages whole groups in shared memory as float32, reduces the group
+// sum of squares in numpy order, and writes sc and xn = g / sc.
+// ---------------------------------------------------------------------------
+struct NormArgs {
+    const void *A;
+    int dtype;
+    int64_t nrow, T, lda;   // flat mode: nrow = 1, T = ntot, lda = ntot
+    int64_t Tp;             // padded row length (flat: padded total)
+    int group, tile;        // tile: elements per CTA (multiple of group)
+    float *xn, *sc;
+};
+
+__device__ __forceinline__ float load_as_f32(const void *A, int dtype, int64_t i) {
+    return dtype == UQ_F32 ? __ldg(static_cast<const float *>(A) + i)
+                           : float(__ldg(static_cast<const double *>(A) + i));
+}
+
+__global__ void normalize_kernel(NormArgs a) {
+    extern __shared__ float smf[];
+    float *tile = smf;
+    const int ng = a.tile / a.group;
+    float *ss = tile + a.tile;
+    float *scratch = ss + ng;
+    const int64_t base = int64_t(blockIdx.x) * a.tile;   // over nrow * Tp
+    const int64_t total = a.nrow * a.Tp;
+    for (int i = threadIdx.x; i < a.tile; i += blockDim.x) {
+        const int64_t gi = base + i;
+        float v = 0.f;
+        if (gi < total) {
+            const int64_t r = gi / a.Tp, c = gi - r * a.Tp;
+            if (c < a.T) v = load_as_f32(a.A, a.dtype, r * a.lda + c);
+        }
+        tile[i] = v;
+    }
+    __syncthreads();
+    tile_group_sumsq<float>(tile, ng, a.group, ss, scratch);
+    for (int g = threadIdx.x; g < ng; g += blockDim.x) {
+        const int64_t gg = base / a.group + g;
+        const float s = __fadd_rn(sqrtf(ss[g] / float(a.group)), 1e-12f);
+        ss[g] = s;
+        if (gg * a.group < total) a.sc[gg] = s;
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < a.tile; i += blockDim.x) {
+        const int64_t gi = base + i;
+        if (gi < total) a.xn[gi] = tile[i] / ss[i / a.group];
+    }
+}
+
+int launch_normalize(NormArgs a, cudaStream_t st) {
+    int t = a.group;
+    while (t < 2048) t += a.group;
+    a.tile = t;
+    const int ng = a.tile / a.group;
+    const size_t smem = sizeof(float) * (size_t(a.tile) + ng + size_t(ng) * 32);
+    const int64_t total = a.nrow * a.Tp;
+    const int64_t grid = (total + a.tile - 1) / a.tile;
+    if (cudaFuncSetAttribute(normalize_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess)
+        return uq::check_cuda("normalize: set smem attribute");
+    if (grid > 0) { uq::ProfScope _p("normalize", st); normalize_kernel<<<unsigned(grid), 256, smem, st>>>(a); }
+    return uq::check_cuda("normalize_kernel launch");
+}
+
+// ---------------------------------------------------------------------------
+// Viterbi forward
+// ---------------------------------------------------------------------------
+constexpr int kThreads = 512;
+
+typedef unsigned long long u64;
+
+__device__ __forceinline__ u64 pk2(float lo, float hi) {
+    u64 r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
+}
+__device__ __forceinline__ void up2(u64 v, float &lo, float &hi) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ u64 sub2(u64 a, u64 b) {
+    u64 r;
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ u64 mul2(u64 a, u64 b) {
+    u64 r;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ u64 add2(u64 a, u64 b) {
+    u64 r;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+// bitwise select by the mask word: (m & a) | (~m & b); only bit 31 is used.
+__device__ __forceinline__ unsigned sel_bits(unsigned m, unsigned a, unsigned b) {
+    unsigned r;
+    asm("lop3.b32 %0, %1, %2, %3, 0xCA;" : "=r"(r) : "r"(m), "r"(a), "r"(b));
+    return r;
+}
+// (word << 1) | (src >> 31)
+__device__ __forceinline__ unsigned shift_in_sign(unsigned word, unsigned src) {
+    unsigned r;
+    asm("shf.l.wrap.b32 %0, %1, %2, 1;" : "=r"(r) : "r"(src), "r"(word));
+    return r;
+}
+
+__device__ __forceinline__ void cluster_arrive() { asm volatile("barrier.cluster.arrive.release;\n" ::: "memory"); }
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.acquire;\n" ::: "memory"); }
+__device__ __forceinline__ unsigned cluster_rank() {
+    unsigned r;
+    asm("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ unsigned mapa_shared(unsigned addr, unsigned rank) {
+    unsigned r;
+    asm("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+    return r;
+}
+__device__ __forceinline__ float4 lds4(unsigned addr, bool cluster) {
+    float4 v;
+    if (cluster)
+        asm volatile("ld.shared::cluster.v4.f32 {%0,%1,%2,%3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr));
+    else
+        asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr));
+    return v;
+}
+__device__ __forceinline__ float lds1(unsigned addr, bool cluster) {
+    float v;
+    if (cluster) asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr));
+    else asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(addr));
+    return v;
+}
+__device__ __forceinline__ void sts4(unsigned addr, float a, float b, float c, float d) {
+    asm volatile("st.shared.v4.f32 [%0], {%1,%2,%3,%4};" :: "r"(addr), "f"(a), "f"(b), "f"(c), "f"(d) : "memory");
+}
+
+template <int R> struct Swz;
+template <> struct Swz<1> { static constexpr int A = 3, M = 7; };
+template <> struct Swz<2> { static constexpr int A = 2, M = 7; };
+template <> struct Swz<3> { static constexpr int A = 1, M = 7; };
+template <> struct Swz<4> { static constexpr int A = 1, M = 0; };
+
+template <int R> __device__ __forceinline__ unsigned swz_chunk(unsigned c) {
+    return c ^ ((c >> Swz<R>::A) & Swz<R>::M);
+}
+
+struct VitArgs {
+    const float *xn;        // (nseq, T) normalised values
+    int64_t seq0, nbatch;   // sequences [seq0, seq0 + nbatch) in this launch
+    int T;
+    const float *cw;        // 2^L
+    uint32_t *bp;           // (nbatch, T-1, TPS)
+    int32_t *fin;           // (nbatch)
+};
+
+template <int L_, int R_, int CL_> struct VitCfg {
+    static constexpr int L = L_, R = R_, CL = CL_;
+    static constexpr int K = 1 << R;
+    static constexpr int NQ = 64 / K;                    // q per thread (64 states)
+    static constexpr int NP = NQ / 2;                    // f32x2 pairs per thread
+    static constexpr int NR = NQ >= K ? NQ / K : 1;      // m values read per k
+    static constexpr int Q = 1 << (L - R);
+    static constexpr int Rn = Q >> R;
+    static constexpr int TPS = Q / NQ;                   // threads per sequence
+    static constexpr int NSET = (CL == 2 && R >= 2) ? 2 : 1;   // interleaved sets (cluster)
+    static constexpr int SPS = CL == 1 ? kThreads / TPS : 1;   // sequences per set per CTA
+    static constexpr int FLOATS = kThreads * NQ;         // floats per (set, buffer) per CTA
+    static constexpr int A = Swz<R>::A, M = Swz<R>::M;
+    // k-strides and slot strides leave the swizzle source bits untouched
+    static constexpr bool FAST = (Rn % (4 << (A + 3))) == 0;
+    static constexpr int XCH = 64;                       // staged x steps (cluster)
+    static_assert(CL == 1 ? TPS <= kThreads : TPS == CL * kThreads, "thread split");
+};
+
+// Tournament over K candidate pairs: min pair and R decision words per
+// component (bit 31 = "right child wins"; ties keep the left = first index).
+template <int R>
+__device__ __forceinline__ u64 tourney(const u64 (&c)[1 << R], unsigned (&blo)[R], unsigned (&bhi)[R]) {
+    constexpr int K = 1 << R;
+    u64 val[K];
+#pragma unroll
+    for (int k = 0; k < K; ++k) val[k] = c[k];
+    // P[j][i]: decision word of the level-(j+1) node on the chosen path of subtree i
+    unsigned Plo[R][K], Phi[R][K];
+#pragma unroll
+    for (int lev = 1; lev <= R; ++lev) {
+        const int width = K >> lev;
+#pragma unroll
+        for (int i = 0; i < width; ++i) {
+            const u64 d = sub2(val[2 * i + 1], val[2 * i]);
+            float dl, dh;
+            up2(d, dl, dh);
+            const unsigned wl = __float_as_uint(dl), wh = __float_as_uint(dh);
+#pragma unroll
+            for (int j = 0; j < lev - 1; ++j) {
+                Plo[j][i] = sel_bits(wl, Plo[j][2 * i + 1], Plo[j][2 * i]);
+                Phi[j][i] = sel_bits(wh, Phi[j][2 * i + 1], Phi[j][2 * i]);
+            }
+            Plo[lev - 1][i] = wl;
+            Phi[lev - 1][i] = wh;
+            float al, ah, bl, bh;
+            up2(val[2 * i], al, ah);
+            up2(val[2 * i + 1], bl, bh);
+            val[i] = pk2(fminf(al, bl), fminf(ah, bh));
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < R; ++j) { blo[j] = Plo[j][0]; bhi[j] = Phi[j][0]; }
+    return val[0];
+}
+
+// Per-thread view of one sequence's m buffers.
+template <class C>
+struct VitThread {
+    static constexpr int K = C::K, NQ = C::NQ, NP = C::NP, NR = C::NR, R = C::R, CL = C::CL;
+    u64 cwp[K][NP];          // codewords of the owned states s = k*Q + NQ*v + jq
+    int v, slot;
+    unsigned rank;
+    unsigned rd0, wr0;       // byte offsets of this thread's first read / write
+
+    // byte offset of float f of this thread's sequence inside a (set, buffer)
+    __device__ __forceinline__ unsigned off(int f) const {
+        unsigned c;
+        if (CL == 1) c = unsigned(slot) * unsigned(C::Q >> 2) + unsigned(f >> 2);
+        else c = unsigned((f & (C::Q / 2 - 1)) >> 2);
+        return (swz_chunk<R>(c) << 4) + unsigned((f & 3) << 2);
+    }
+    __device__ __forceinline__ int r0() const { return (NQ * v) >> R; }
+
+    __device__ __forceinline__ void setup() {
+        rd0 = off(r0());
+        wr0 = off(NQ * v);
+    }
+    // m_{t-1} reads.  own / peer: buffer base in this CTA / the peer CTA.
+    __device__ __forceinline__ void load_prev(unsigned own, unsigned peer, float (&m)[K][NR]) const {
+#pragma unroll
+        for (int k = 0; k < K; ++k) {
+            bool remote = false;
+            unsigned base = own;
+            if (CL == 2) {
+                remote = unsigned(k >> (R - 1)) != rank;
+                base = remote ? peer : own;
+            }
+            if (NR >= 4) {
+#pragma unroll
+                for (int c4 = 0; c4 < NR / 4; ++c4) {
+                    const unsigned o = C::FAST ? ((rd0 + unsigned((CL == 2 ? (k & (K / 2 - 1)) : k) * C::Rn * 4)) ^ (unsigned(c4) << 4))
+                                               : off(k * C::Rn + r0() + 4 * c4);
+                    const float4 q4 = lds4(base + o, remote);
+                    m[k][4 * c4 + 0] = q4.x; m[k][4 * c4 + 1] = q4.y;
+                    m[k][4 * c4 + 2] = q4.z; m[k][4 * c4 + 3] = q4.w;
+                }
+            } else {
+                const unsigned o = C::FAST ? (rd0 + unsigned((CL == 2 ? (k & (K / 2 - 1)) : k) * C::Rn * 4))
+                                           : off(k * C::Rn + r0());
+                m[k][0] = lds1(base + o, remote);
+            }
+        }
+    }
+
+    // One step for the owned q: writes m_t, returns the backpointer word
+    // (field of q-local index jq at bits [jq*R, jq*R + R)).
+    template <bool PREV>
+    __device__ __forceinline__ unsigned step(float x, const float (&m)[K][NR], unsigned wbase) const {
+        const u64 xx = pk2(x, x);
+        unsigned word = 0;
+        float mo[NQ];
+#pragma unroll
+        for (int p = NP - 1; p >= 0; --p) {
+            const int i = (NQ >= K) ? ((2 * p) >> R) : 0;
+            u64 c[K];
+#pragma unroll
+            for (int k = 0; k < K; ++k) {
+                u64 d = sub2(xx, cwp[k][p]);
+                d = mul2(d, d);
+                c[k] = PREV ? add2(d, pk2(m[k][i], m[k][i])) : d;
+            }
+            unsigned blo[R], bhi[R];
+            const u64 mn = tourney<R>(c, blo, bhi);
+            float lo, hi;
+            up2(mn, lo, hi);
+            mo[2 * p] = lo;
+            mo[2 * p + 1] = hi;
+#pragma unroll
+            for (int j = R - 1; j >= 0; --j) word = shift_in_sign(word, bhi[j]);
+#pragma unroll
+            for (int j = R - 1; j >= 0; --j) word = shift_in_sign(word, blo[j]);
+        }
+#pragma unroll
+        for (int c4 = 0; c4 < NQ / 4; ++c4) {
+            const unsigned o = C::FAST ? (wr0 ^ (unsigned(c4) << 4)) : off(NQ * v + 4 * c4);
+            sts4(wbase + o, mo[4 * c4], mo[4 * c4 + 1], mo[4 * c4 + 2], mo[4 * c4 + 3]);
+        }
+        return word;
+    }
+
+    // Final step: costs of all owned states, first-index argmin.
+    template <bool PREV>
+    __device__ __forceinline__ void final_argmin(float x, const float (&m)[K][NR], float &bv, int &bi) const {
+        const u64 xx = pk2(x, x);
+        bi = NQ * v;  // valid even if every cost is NaN
+#pragma unroll
+        for (int k = 0; k < K; ++k) {
+#pragma unroll
+            for (int p = 0; p < NP; ++p) {
+                const int i = (NQ >= K) ? ((2 * p) >> R) : 0;
+                u64 d = sub2(xx, cwp[k][p]);
+                d = mul2(d, d);
+                if (PREV) d = add2(d, pk2(m[k][i], m[k][i]));
+                float lo, hi;
+                up2(d, lo, hi);
+                const int s = k * C::Q + NQ * v + 2 * p;
+                if (k == 0 && p == 0) bv = lo;
+                else if (lo < bv) { bv = lo; bi = s; }
+                if (hi < bv) { bv = hi; bi = s + 1; }
+            }
+        }
+    }
+};
+
+__device__ __forceinline__ bool better(float v1, int i1, float v2, int i2) {
+    return v1 < v2 || (v1 == v2 && i1 < i2);
+}
+
+// Synchronises the threads of one sequence (CTA mode).
+template <class C>
+__device__ __forceinline__ void seq_sync(int slot) {
+    if (C::TPS <= 32) __syncwarp();
+    else if (C::TPS == kThreads) __syncthreads();
+    else asm volatile("bar.sync %0, %1;" :: "r"(1 + slot), "r"(C::TPS) : "memory");
+}
+
+template <class C>
+__global__ void __cluster_dims__(C::CL, 1, 1) __launch_bounds__(kThreads, 1)
+viterbi_fwd_kernel(VitArgs a) {
+    constexpr int K = C::K, NQ = C::NQ, NR = C::NR, NSET = C::NSET, NP = C::NP, TPS = C::TPS, CL = C::CL;
+    extern __shared__ __align__(16) float sm_v[];
+    __shared__ float red_v[NSET][kThreads / 32];
+    __shared__ int red_i[NSET][kThreads / 32];
+    __shared__ float xs[CL == 2 ? NSET : 1][2][C::XCH];
+
+    VitThread<C> th;
+    const int tid = threadIdx.x;
+    int64_t seq_base;
+    if (CL == 1) {
+        th.rank = 0;
+        th.slot = tid / TPS;
+        th.v = tid % TPS;
+        seq_base = int64_t(blockIdx.x) * C::SPS;
+    } else {
+        th.rank = cluster_rank();
+        th.slot = 0;
+        th.v = int(th.rank) * kThreads + tid;
+        seq_base = int64_t(blockIdx.x / CL) * NSET;
+    }
+    th.setup();
+#pragma unroll
+    for (int k = 0; k < K; ++k)
+#pragma unroll
+        for (int p = 0; p < NP; ++p) {
+            const int s = k * C::Q + NQ * th.v + 2 * p;
+            th.cwp[k][p] = pk2(__ldg(a.cw + s), __ldg(a.cw + s + 1));
+        }
+
+    const unsigned smem0 = unsigned(__cvta_generic_to_shared(sm_v));
+    const unsigned peer0 = CL == 2 ? mapa_shared(smem0, th.rank ^ 1u) : smem0;
+    constexpr unsigned BUF = unsigned(C::FLOATS * 4);
+
+    int64_t seq[NSET];
+    bool valid[NSET];
+    const float *xrow[NSET];
+    float xv[NSET];
+#pragma unroll
+    for (int X = 0; X < NSET; ++X) {
+        seq[X] = seq_base + (CL == 1 ? th.slot : X);
+        valid[X] = seq[X] < a.nbatch;
+        xrow[X] = a.xn + (a.seq0 + (valid[X] ? seq[X] : 0)) * int64_t(a.T);
+        if (CL == 1) {
+            xv[X] = valid[X] ? __ldg(xrow[X]) : 0.f;
+        } else if (tid < C::XCH) {
+            xs[X][0][tid] = (valid[X] && tid < a.T) ? __ldg(xrow[X] + tid) : 0.f;
+        }
+    }
+    uint32_t *bpo[NSET];
+#pragma unroll
+    for (int X = 0; X < NSET; ++X)
+        bpo[X] = a.bp + (valid[X] ? seq[X] : 0) * (int64_t(a.T - 1) * TPS) + th.v;
+
+    if (CL == 2) { cluster_arrive(); cluster_wait(); }   // peers running, staged x visible
+    else __syncthreads();
+
+    float m[K][NR];
+    bool pending = false;
+    for (int t = 0; t + 1 < a.T; ++t) {
+#pragma unroll
+        for (int X = 0; X < NSET; ++X) {
+            float x;
+            if (CL == 1) {
+                x = xv[X];
+                xv[X] = valid[X] ? __ldg(xrow[X] + t + 1) : 0.f;
+            } else {
+                const int tc = t % C::XCH;
+                x = xs[X][(t / C::XCH) & 1][tc];
+                if (tc == 0 && tid < C::XCH) {   // stage the next chunk (read a chunk later)
+                    const int tn = t + C::XCH + tid;
+                    xs[X][((t / C::XCH) + 1) & 1][tid] = (valid[X] && tn < a.T) ? __ldg(xrow[X] + tn) : 0.f;
+                }
+            }
+            const unsigned wb = smem0 + unsigned(X * 2 + (t & 1)) * BUF;
+            unsigned word;
+            if (t == 0) {
+                word = th.template step<false>(x, m, wb);
+            } else {
+                const unsigned rb = unsigned(X * 2 + ((t - 1) & 1)) * BUF;
+                th.load_prev(smem0 + rb, peer0 + rb, m);
+                word = th.template step<true>(x, m, wb);
+            }
+            if (CL == 1) {
+                seq_sync<C>(th.slot);
+            } else if (NSET == 1) {
+                cluster_arrive();
+                cluster_wait();
+            } else {
+                // the wait completes the other set's arrive (its next step reads
+                // those values); this set's arrive completes during that step
+                if (pending) cluster_wait();
+                cluster_arrive();
+                pending = true;
+            }
+            // backpointers leave after the barrier, so the release of the next
+            // arrive does not wait for a store issued just before it
+            if (valid[X]) bpo[X][int64_t(t) * TPS] = word;
+        }
+    }
+    // final step: argmin over all states of cost_{T-1}
+#pragma unroll
+    for (int X = 0; X < NSET; ++X) {
+        if (pending && X == NSET - 1) { cluster_wait(); pending = false; }
+        const int tl = a.T - 1;
+        const float x = CL == 1 ? xv[X] : xs[X][(tl / C::XCH) & 1][tl % C::XCH];
+        float bv;
+        int bi;
+        if (a.T == 1) {
+            th.template final_argmin<false>(x, m, bv, bi);
+        } else {
+            const unsigned rb = unsigned(X * 2 + ((a.T - 2) & 1)) * BUF;
+            th.load_prev(smem0 + rb, peer0 + rb, m);
+            th.template final_argmin<true>(x, m, bv, bi);
+        }
+        constexpr int segw = TPS < 32 ? TPS : 32;
+#pragma unroll
+        for (int o = 1; o < segw; o <<= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (better(ov, oi, bv, bi)) { bv = ov; bi = oi; }
+        }
+        if (TPS <= 32) {
+            if ((tid % TPS) == 0 && valid[X]) a.fin[seq[X]] = bi;
+        } else if ((tid & 31) == 0) {
+            red_v[X][tid >> 5] = bv;
+            red_i[X][tid >> 5] = bi;
+        }
+    }
+    if (TPS > 32) {
+        if (CL == 1) {
+            __syncthreads();
+            if ((tid % TPS) == 0) {
+                constexpr int wps = TPS / 32;
+                const int w0 = tid >> 5;
+                float bv = red_v[0][w0];
+                int bi = red_i[0][w0];
+                for (int w = 1; w < wps; ++w)
+                    if (better(red_v[0][w0 + w], red_i[0][w0 + w], bv, bi)) { bv = red_v[0][w0 + w]; bi = red_i[0][w0 + w]; }
+                if (valid[0]) a.fin[seq[0]] = bi;
+            }
+        } else {
+            cluster_arrive();
+            cluster_wait();
+            if (th.rank == 0 && tid == 0) {
+#pragma unroll
+                for (int X = 0; X < NSET; ++X) {
+                    float bv = red_v[X][0];
+                    int bi = red_i[X][0];
+                    for (int w = 1; w < kThreads / 32; ++w)
+                        if (better(red_v[X][w], red_i[X][w], bv, bi)) { bv = red_v[X][w]; bi = red_i[X][w]; }
+                    const unsigned rv = mapa_shared(unsigned(__cvta_generic_to_shared(&red_v[X][0])), 1u);
+                    const unsigned ri = mapa_shared(unsigned(__cvta_generic_to_shared(&red_i[X][0])), 1u);
+                    for (int w = 0; w < kThreads / 32; ++w) {
+                        float ov;
+                        int oi;
+                        asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(ov) : "r"(rv + 4u * w));
+                        asm volatile("ld.shared::cluster.s32 %0, [%1];" : "=r"(oi) : "r"(ri + 4u * w));
+                        if (better(ov, oi, bv, bi)) { bv = ov; bi = oi; }
+                    }
+                    if (valid[X]) a.fin[seq[X]] = bi;
+                }
+            }
+            cluster_arrive();   // keep shared memory alive for the peer's reads
+            cluster_wait();
+        }
+    }
+}
+
+// Traceback: one thread per sequence walks the backpointer words.
+template <int R>
+__global__ void traceback_kernel(const uint32_t *bp, const int32_t *fin, int64_t nbatch, int T, int L,
+                                 int32_t *states, int64_t seq0) {
+    constexpr int K = 1 << R, NQ = 64 / K;
+    const int64_t sq = blockIdx.x * int64_t(blockDim.x) + threadIdx.x;
+    if (sq >= nbatch) return;
+    const int Q = 1 << (L - R);
+    const int TPS = Q / NQ;
+    const uint32_t *b = bp + sq * int64_t(T - 1) * TPS;
+    int32_t *out = states + (seq0 + sq) * int64_t(T);
+    int s = fin[sq] & ((1 << L) - 1);
+    out[T - 1] = s;
+    for (int t = T - 1; t >= 1; --t) {
+        const int q = s >> R;
+        const uint32_t w = __ldg(b + int64_t(t - 1) * TPS + q / NQ);
+        const int k = (w >> ((q % NQ) * R)) & (K - 1);
+        s = k * Q + q;
+        out[t - 1] = s;
+    }
+}
+
+template <int L, int R>
+int launch_viterbi(const VitArgs &a, cudaStream_t st) {
+    constexpr int CL = L == 16 ? 2 : 1;
+    using C = VitCfg<L, R, CL>;
+    const size_t smem = size_t(C::NSET) * 2 * C::FLOATS * sizeof(float);
+    auto kern = viterbi_fwd_kernel<C>;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess)
+        return uq::check_cuda("viterbi: set smem attribute");
+    int64_t ctas;
+    if (CL == 1) ctas = (a.nbatch + C::SPS - 1) / C::SPS;
+    else ctas = (a.nbatch + C::NSET - 1) / C::NSET * CL;
+    if (ctas > 0) { uq::ProfScope _p("viterbi_fwd", st); kern<<<unsigned(ctas), kThreads, smem, st>>>(a); }
+    return uq::check_cuda("viterbi_fwd_kernel launch");
+}
+
+template <int R, int L>
+int dispatch_l(int Lrt, const VitArgs &a, cudaStream_t st) {
+    if constexpr (L > 16) {
+        return uq::fail(UQ_ERR_UNSUPPORTED, "viterbi: L=%d", Lrt);
+    } else {
+        if (Lrt == L) return launch_viterbi<L, R>(a, st);
+        return dispatch_l<R, L + 1>(Lrt, a, st);
+    }
+}
+
+template <int R>
+int run_viterbi_r(const float *xn, int64_t nseq, int T, int L, const float *cw, int32_t *states,
+                  uint32_t *bp, int32_t *fin, int64_t batch, cudaStream_t st) {
+    constexpr int LMIN = (2 * R > 6) ? 2 * R : 6;
+    for (int64_t s0 = 0; s0 < nseq; s0 += batch) {
+        VitArgs a{};
+        a.xn = xn; a.seq0 = s0; a.nbatch = std::min<int64_t>(batch, nseq - s0);
+        a.T = T; a.cw = cw; a.bp = bp; a.fin = fin;
+        int rc = dispatch_l<R, LMIN>(L, a, st);
+        if (rc) return rc;
+        const int64_t g = (a.nbatch + 127) / 128;
+        { uq::ProfScope _p("traceback", st); traceback_kernel<R><<<unsigned(g), 128, 0, st>>>(bp, fin, a.nbatch, T, L, states, s0); }
+        if ((rc = uq::check_cuda("traceback_kernel launch"))) return rc;
+    }
+    return UQ_OK;
+}
+
+__global__ void decode_kernel(const int32_t *states, const float *cw, const float *sc, int64_t group,
+                              int64_t ntot, float *out) {
+    for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < ntot; i += int64_t(gridDim.x) * blockDim.x)
+        out[i] = __fmul_rn(__ldg(cw + __ldg(states + i)), __ldg(sc + i / group));
+}
+
+__global__ void decode_rows_kernel(const int32_t *states, const float *cw, const float *sc, int64_t nrow,
+                                   int64_t T, int64_t Tp, int64_t group, float *out) {
+    const int64_t n = nrow * T;
+    for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < n; i += int64_t(gridDim.x) * blockDim.x) {
+        const int64_t r = i / T, c = i - r * T;
+        const int64_t j = r * Tp + c;
+        out[i] = __fmul_rn(__ldg(cw + __ldg(states + j)), __ldg(sc + j / group));
+    }
+}
+
+int vit_check(int64_t nseq, int T, int L, int R) {
+    if (nseq < 0 || T < 1) return uq::fail(UQ_ERR_INVALID, "viterbi: bad nseq / T");
+    if (R < 1 || R > 4 || L > 16 || L < 6 || L < 2 * R)
+        return uq::fail(UQ_ERR_UNSUPPORTED, "viterbi: (L=%d, R=%d) not built (need 1<=R<=4, max(6,2R)<=L<=16)", L, R);
+    return UQ_OK;
+}
+
+}  // namespace
+
+namespace uq {
+
+int64_t vit_seq_bytes(int T, int L) {
+    // backpointer words per sequence: (T-1) * 2^L / 64, plus the final state
+    return int64_t(T - 1) * ((int64_t(1) << L) / 64) * 4 + 4;
+}
+
+size_t trellis_ws_bytes(int64_t nseq, int T, int L) {
+    // cap the backpointer batch at ~2 GiB (whole sequences, at least one
+    // launch worth of sequences)
+    const int64_t per = vit_seq_bytes(T, L);
+    int64_t want = nseq;
+    const int64_t cap = (int64_t(2) << 30) / per;
+    const int64_t min_batch = 2 * 148;
+    if (want > cap) want = std::max<int64_t>(cap, min_batch);
+    return size_t(std::max<int64_t>(want, 1) * per) + 512;
+}
+
+int trellis_viterbi(const float *xn, int64_t nseq, int T, int L, int R, const float *cw, int32_t *states,
+                    void *ws, size_t ws_bytes, cudaStream_t st) {
+    const int64_t per = vit_seq_bytes(T, L);
+    int64_t batch = int64_t((ws_bytes > 512 ? ws_bytes - 512 : 0) / size_t(per));
+    if (batch < 1) return fail(UQ_ERR_WORKSPACE, "viterbi: workspace %zu too small (need %lld per sequence)",
+                               ws_bytes, (long long)per);
+    if (batch > nseq) batch = nseq;
+    Carver c(ws, ws_bytes);
+    int32_t *fin = c.take<int32_t>(size_t(batch));
+    uint32_t *bp = c.take<uint32_t>(size_t(batch) * size_t(T - 1) * ((size_t(1) << L) / 64));
+    switch (R) {
+        case 1: return run_viterbi_r<1>(xn, nseq, T, L, cw, states, bp, fin, batch, st);
+        case 2: return run_viterbi_r<2>(xn, nseq, T, L, cw, states, bp, fin, batch, st);
+        case 3: return run_viterbi_r<3>(xn, nseq, T, L, cw, states, bp, fin, batch, st);
+        case 4: return run_viterbi_r<4>(xn, nseq, T, L, cw, states, bp, fin, batch, st);
+    }
+    return fail(UQ_ERR_UNSUPPORTED, "viterbi: R");
+}
+
+int trellis_normalize(const void *A, int dtype, int64_t nrow, int64_t T, int64_t lda, int64_t Tp, int64_t group,
+                      float *xn, float *sc, cudaStream_t st) {
+    NormArgs a{};
+    a.A = A; a.dtype = dtype; a.nrow = nrow; a.T = T; a.lda = lda; a.Tp = Tp; a.group = int(group);
+    a.xn = xn; a.sc = sc;
+    return launch_normalize(a, st);
+}
+
+int trellis_decode(const int32_t *states, const float *cw, const float *sc, int64_t group, int64_t ntot,
+                   float *out, cudaStream_t st) {
+    const int grid = int(std::max<int64_t>(1, std::min<int64_t>((ntot + 255) / 256, int64_t(num_sms()) * 16)));
+    if (ntot > 0) { uq::ProfScope _p("decode", st); decode_kernel<<<grid, 256, 0, st>>>(states, cw, sc, group, ntot, out); }
+    return check_cuda("decode_kernel launch");
+}
+
+}  // namespace uq
+
+extern "C" {
+
+int uq_trellis_codebook(int L, float *out, void *stream) {
+    if (L < 1 || L > 16) return uq::fail(UQ_ERR_UNSUPPORTED, "uq_trellis_codebook: L=%d not in [1, 16]", L);
+    if (!out) return uq::fail(UQ_ERR_INVALID, "uq_trellis_codebook: null pointer");
+    const int S = 1 << L;
+    { uq::ProfScope _p("codebook", UQ_STREAM(stream)); codebook_kernel<<<(S + 255) / 256, 256, 0, UQ_STREAM(stream)>>>(L, out); }
+    return uq::check_cuda("codebook_kernel launch");
+}
+
+int uq_trellis_normalize(const void *A, int a_dtype, int64_t ntot, int64_t group, int64_t seg, float *xn,
+                         float *sc, void *stream) {
+    if (ntot < 0 || group < 8 || group % 8 || group > 8192 || seg < 1 || !uq::dtype_size(a_dtype))
+        return uq::fail(group % 8 || group > 8192 ? UQ_ERR_UNSUPPORTED : UQ_ERR_INVALID,
+                        "uq_trellis_normalize: bad arguments (ntot=%lld group=%lld seg=%lld)",
+                        (long long)ntot, (long long)group, (long long)seg);
+    const int64_t padded = (ntot + group - 1) / group * group;
+    if (padded % seg) return uq::fail(UQ_ERR_INVALID, "uq_trellis_normalize: padded size %lld not divisible by seg %lld",
+                                      (long long)padded, (long long)seg);
+    if (padded == 0) return UQ_OK;
+    if (!A || !xn || !sc) return uq::fail(UQ_ERR_INVALID, "uq_trellis_normalize: null pointer");
+    return uq::trellis_normalize(A, a_dtype, 1, ntot, ntot, padded, group, xn, sc, UQ_STREAM(stream));
+}
+
+int uq_trellis_normalize_rows(const void *A, int a_dtype, int64_t nrow, int64_t T, int64_t lda, int64_t group,
+                              float *xn, float *sc, void *stream) {
+    if (nrow < 0 || T < 1 || lda < T || group < 8 || group % 8 || group > 8192 || !uq::dtype_size(a_dtype))
+        return uq::fail(UQ_ERR_INVALID, "uq_trellis_normalize_rows: bad arguments");
+    if (nrow == 0) return UQ_OK;
+    if (!A || !xn || !sc) return uq::fail(UQ_ERR_INVALID, "uq_trellis_normalize_rows: null pointer");
+    const int64_t Tp = (T + group - 1) / group * group;
+    return uq::trellis_normalize(A, a_dtype, nrow, T, lda, Tp, group, xn, sc, UQ_STREAM(stream));
+}
+
+size_t uq_trellis_workspace_bytes(int64_t nseq, int T, int L, int R) {
+    if (vit_check(nseq, T, L, R) != UQ_OK) return 0;
+    return uq::trellis_ws_bytes(nseq, T, L);
+}
+
+int uq_trellis_viterbi(const float *xn, int64_t nseq, int T, int L, int R, const float *cw, int32_t *states,
+                       void *workspace, size_t workspace_bytes, void *stream) {
+    int rc = vit_check(nseq, T, L, R);
+    if (rc) return rc;
+    if (nseq == 0) return UQ_OK;
+    if (!xn || !cw || !states || !workspace) return uq::fail(UQ_ERR_INVALID, "uq_trellis_viterbi: null pointer");
+    return uq::trellis_viterbi(xn, nseq, T, L, R, cw, states, workspace, workspace_bytes, UQ_STREAM(stream));
+}
+
+int uq_trellis_decode(const int32_t *states, const float *cw, const float *sc, int64_t group, int64_t ntot,
+                      float *out, void *stream) {
+    if (ntot < 0 || group < 1) return uq::fail(UQ_ERR_INVALID, "uq_trellis_decode: bad arguments");
+    if (ntot == 0) return UQ_OK;
+    if (!states || !cw || !sc || !out) return uq::fail(UQ_ERR_INVALID, "uq_trellis_decode: null pointer");
+    return uq::trellis_decode(states, cw, sc, group, ntot, out, UQ_STREAM(stream));
+}
+
+int uq_trellis_decode_rows(const int32_t *states, const float *cw, const float *sc, int64_t nrow, int64_t T,
+                           int64_t Tp, int64_t group, float *out, void *stream) {
+    if (nrow < 0 || T < 1 || Tp < T || group < 1 || Tp % group)
+        return uq::fail(UQ_ERR_INVALID, "uq_trellis_decode_rows: bad arguments");
+    if (nrow == 0) return UQ_OK;
+    if (!states || !cw || !sc || !out) return uq::fail(UQ_ERR_INVALID, "uq_trellis_decode_rows: null pointer");
+    const int64_t n = nrow * T;
+    const int grid = int(std::max<int64_t>(1, std::min<int64_t>((n + 255) / 256, int64_t(uq::num_sms()) * 16)));
+    { uq::ProfScope _p("decode_rows", UQ_STREAM(stream)); decode_rows_kernel<<<grid, 256, 0, UQ_STREAM(stream)>>>(states, cw, sc, nrow, T, Tp, group, out); }
+    return uq::check_cuda("decode_rows_kernel launch");
+}
+
+}  // extern "C"

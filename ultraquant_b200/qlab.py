@@ -1,0 +1,134 @@
+"""Drop-in replacement for the hot-path functions of UltraQuant's ``qlab.py``.
+
+Same names, arguments, dtypes and results as the reference (qlab.py:53-183);
+the arithmetic runs in libuq_b200 on the GPU.  Functions accept host numpy
+arrays (returning numpy, like the reference) or CUDA tensors (returning CUDA
+tensors, no host round trip).
+"""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _device as D
+from . import _lib
+
+__all__ = ["wnmse", "_next_pow2", "rht_rows", "irht_rows", "_d8_decode", "e8_decode",
+           "_entropy_bpw", "q_e8_fast", "_E8_SCALE"]
+
+# qlab.py:158 -- calibrated E8 step per calib_key, reused across tensors
+_E8_SCALE: dict = {}
+
+
+def _is_dev(a) -> bool:
+    return isinstance(a, torch.Tensor) and a.is_cuda
+
+
+def _ret(t: torch.Tensor, like):
+    return t if _is_dev(like) else D.to_host(t)
+
+
+def wnmse(A, Ah) -> float:
+    """qlab.py:53-54 -- sum((A - Ah)^2) / sum(A^2) (fp64 on the device)."""
+    a = D.as_device(A, torch.float64)
+    b = D.as_device(Ah, torch.float64)
+    return float(((a - b) ** 2).sum() / (a ** 2).sum())
+
+
+def _next_pow2(n: int) -> int:
+    """qlab.py:66-69."""
+    return int(_lib.load().uq_next_pow2(int(n)))
+
+
+def rht_rows(A, seed=0):
+    """qlab.py:71-85 -- randomized Hadamard transform along rows (fp64 out)."""
+    lib = _lib.load()
+    a = D.as_device(A)
+    if a.dim() != 2:
+        raise ValueError("rht_rows expects a 2-D array (out, in)")
+    rows, n0 = a.shape
+    if n0 == 0:  # the reference pads to one zero column
+        a = torch.zeros((rows, 1), dtype=torch.float64, device=a.device)
+        n0 = 1
+    n = _next_pow2(n0)
+    out = torch.empty((rows, n), dtype=torch.float64, device=a.device)
+    if rows:
+        d = D.signs(n, seed, a.device)
+        _lib.check(lib.uq_rht_rows(a.data_ptr(), D.dtype_code(a), rows, n0, n0, d.data_ptr(),
+                                   out.data_ptr(), D.stream_handle(a.device)), "rht_rows")
+    return _ret(out, A)
+
+
+def irht_rows(X, n0, seed=0):
+    """qlab.py:87-98 -- inverse of rht_rows, cropped to n0 columns (fp64)."""
+    lib = _lib.load()
+    x = D.as_device(X)
+    rows, n = x.shape
+    if n & (n - 1):
+        raise ValueError("irht_rows: width must be a power of two")
+    n0 = int(n0)
+    out = torch.empty((rows, min(n0, n)), dtype=torch.float64, device=x.device)
+    if rows and n0:
+        d = D.signs(n, seed, x.device)
+        _lib.check(lib.uq_irht_rows(x.data_ptr(), D.dtype_code(x), rows, n, n, min(n0, n), d.data_ptr(),
+                                    out.data_ptr(), D.stream_handle(x.device)), "irht_rows")
+    return _ret(out, X)
+
+
+def _d8_decode(Y):
+    """qlab.py:133-142."""
+    lib = _lib.load()
+    y = D.as_device(Y, torch.float64).reshape(-1, 8)
+    out = torch.empty_like(y)
+    _lib.check(lib.uq_d8_decode(y.data_ptr(), y.shape[0], out.data_ptr(), D.stream_handle(y.device)), "_d8_decode")
+    return _ret(out, Y)
+
+
+def e8_decode(Y):
+    """qlab.py:144-149."""
+    lib = _lib.load()
+    y = D.as_device(Y, torch.float64).reshape(-1, 8)
+    out = torch.empty_like(y)
+    _lib.check(lib.uq_e8_decode(y.data_ptr(), y.shape[0], out.data_ptr(), D.stream_handle(y.device)), "e8_decode")
+    return _ret(out, Y)
+
+
+def _entropy_bpw(idx_pts) -> float:
+    """qlab.py:151-156 -- entropy of the distinct 8-tuples 2*pts, / 8."""
+    lib = _lib.load()
+    p = D.as_device(idx_pts, torch.float64).reshape(-1, 8)
+    nvec = p.shape[0]
+    ws = D.workspace(lib.uq_e8_entropy_workspace_bytes(nvec), p.device)
+    res = torch.empty(1, dtype=torch.float64, device=p.device)
+    _lib.check(lib.uq_e8_entropy_bpw(p.data_ptr(), nvec, res.data_ptr(), ws.data_ptr(), ws.numel(),
+                                     D.stream_handle(p.device)), "_entropy_bpw")
+    v = float(res.item())
+    if v < 0:
+        raise NotImplementedError("_entropy_bpw: a lattice index lies outside [-127, 127]")
+    return v
+
+
+def q_e8_fast(A, target_bpw=2.0, group=256, calib_key="g", fixed_step=None):
+    """qlab.py:159-183 -- per-group RMS, one global step, E8 decode (fp64)."""
+    lib = _lib.load()
+    a = D.as_device(A)
+    shape = tuple(a.shape)
+    size = a.numel()
+    st = D.stream_handle(a.device)
+    if fixed_step is not None:
+        step = float(fixed_step)
+    else:
+        if calib_key not in _E8_SCALE:
+            ws = D.workspace(lib.uq_e8_calibrate_workspace_bytes(size, group), a.device)
+            out = ctypes.c_double()
+            _lib.check(lib.uq_e8_calibrate(a.data_ptr(), D.dtype_code(a), size, int(group), float(target_bpw),
+                                           ctypes.addressof(out), ws.data_ptr(), ws.numel(), st),
+                       "q_e8_fast calibration")
+            _E8_SCALE[calib_key] = float(out.value)
+        step = _E8_SCALE[calib_key]
+    rec = torch.empty(shape, dtype=torch.float64, device=a.device)
+    if size:
+        _lib.check(lib.uq_e8_quant(a.data_ptr(), D.dtype_code(a), size, int(group), step, rec.data_ptr(), None, st),
+                   "q_e8_fast")
+    return _ret(rec, A)
