@@ -178,6 +178,20 @@ int uq_quant_e8(const void *W, int w_dtype, int64_t rows, int64_t n0, int64_t ld
                 size_t workspace_bytes, void *stream);
 
 /* ---------------------------------------------------------------------
+ * Device status (no counterpart in the reference)
+ * ------------------------------------------------------------------- */
+
+/* Synchronises `stream` and reports (and clears) a timeout of a bounded
+ * device wait in the cluster-split Viterbi kernel: UQ_ERR_TIMEOUT if one
+ * occurred since the last call, else UQ_OK. */
+int uq_device_errors(void *stream);
+
+/* Runs a one-warp kernel that waits on an mbarrier phase nothing completes;
+ * the bounded wait gives up after limit_ms (<= 2000).  Returns
+ * UQ_ERR_TIMEOUT when the bound worked (the expected outcome). */
+int uq_wait_timeout_selftest(double limit_ms, void *stream);
+
+/* ---------------------------------------------------------------------
  * Instrumentation (no counterpart in the reference; used by bench.py)
  * ------------------------------------------------------------------- */
 

@@ -142,3 +142,19 @@ def test_install_patches_reference_modules(tmp_path, monkeypatch):
     assert same_bits(mods["qlab"].rht_rows(A), O.rht_rows(A))
     for name in ("qlab", "trellis", "qat"):
         sys.modules.pop(name, None)
+
+
+def test_bounded_wait_reports_timeout():
+    """The device waits of the cluster exchange are bounded: a wait on a
+    barrier phase that nothing completes gives up and the host reads
+    UQ_ERR_TIMEOUT; the context stays usable afterwards."""
+    import torch
+    from ultraquant_b200 import _device as D
+    from ultraquant_b200 import _lib
+    lib = _lib.load()
+    st = D.stream_handle(D.device())
+    assert lib.uq_wait_timeout_selftest(50.0, st) == _lib.UQ_ERR_TIMEOUT
+    assert lib.uq_device_errors(st) == _lib.UQ_OK
+    x = torch.randn(2, 64, device="cuda")
+    import ultraquant_b200.trellis as T
+    assert T.viterbi_states(x, 12, 2).shape == (2, 64)

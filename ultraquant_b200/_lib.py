@@ -50,6 +50,8 @@ SIGNATURES = {
                                 _p, _p, _p, _sz, _p]),
     "uq_quant_e8_workspace_bytes": (_sz, [_i64, _i64, _i32]),
     "uq_quant_e8": (_i32, [_p, _i32, _i64, _i64, _i64, _p, _f64, _i32, _p, _p, _p, _p, _p, _sz, _p]),
+    "uq_device_errors": (_i32, [_p]),
+    "uq_wait_timeout_selftest": (_i32, [_f64, _p]),
     "uq_profile_enable": (None, [_i32]),
     "uq_profile_reset": (None, []),
     "uq_launch_count": (_i64, []),

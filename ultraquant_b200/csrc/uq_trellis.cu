@@ -234,6 +234,9 @@ __device__ __forceinline__ float lds1(unsigned addr, bool cluster) {
 __device__ __forceinline__ void sts4(unsigned addr, float a, float b, float c, float d) {
     asm volatile("st.shared.v4.f32 [%0], {%1,%2,%3,%4};" :: "r"(addr), "f"(a), "f"(b), "f"(c), "f"(d) : "memory");
 }
+__device__ __forceinline__ void sts4_cluster(unsigned addr, float a, float b, float c, float d) {
+    asm volatile("st.shared::cluster.v4.f32 [%0], {%1,%2,%3,%4};" :: "r"(addr), "f"(a), "f"(b), "f"(c), "f"(d) : "memory");
+}
 
 template <int R> struct Swz;
 template <> struct Swz<1> { static constexpr int A = 3, M = 7; };
@@ -264,13 +267,21 @@ template <int L_, int R_, int CL_> struct VitCfg {
     static constexpr int Rn = Q >> R;
     static constexpr int TPS = Q / NQ;                   // threads per sequence
     static constexpr int NSET = (CL == 2 && R >= 2) ? 2 : 1;   // interleaved sets (cluster)
+    static constexpr int NBUF = CL == 2 ? 3 : 2;         // m buffers per set
     static constexpr int SPS = CL == 1 ? kThreads / TPS : 1;   // sequences per set per CTA
     static constexpr int FLOATS = kThreads * NQ;         // floats per (set, buffer) per CTA
     static constexpr int A = Swz<R>::A, M = Swz<R>::M;
-    // k-strides and slot strides leave the swizzle source bits untouched
-    static constexpr bool FAST = (Rn % (4 << (A + 3))) == 0;
-    static constexpr int XCH = 64;                       // staged x steps (cluster)
+    // k-strides (Rn floats per CTA, Rn/2 in a cluster) and slot strides leave
+    // the swizzle source bits untouched: addresses are base + constants
+    static constexpr int KSTRIDE = CL == 2 ? Rn / 2 : Rn;
+    static constexpr bool FAST = (KSTRIDE % (4 << (A + 3))) == 0;
+    // cluster mode: the CTA reading a thread's outputs is bit TBIT of v, so
+    // half of each CTA's warps write locally and half into the peer
+    static constexpr int TBIT = L - R - 7;
+    static constexpr int NLOCALW = kThreads / 64;        // local writer warps per CTA
+    static constexpr unsigned TXB = unsigned(kThreads / 2) * NQ * 4;   // remote bytes per phase
     static_assert(CL == 1 ? TPS <= kThreads : TPS == CL * kThreads, "thread split");
+    static_assert(CL == 1 || (TBIT >= 5 && TBIT < 9), "writer target must be warp uniform");
 };
 
 // Tournament over K candidate pairs: min pair and R decision words per
@@ -310,6 +321,49 @@ __device__ __forceinline__ u64 tourney(const u64 (&c)[1 << R], unsigned (&blo)[R
     return val[0];
 }
 
+// ---- mbarrier helpers (cluster exchange) ------------------------------------
+__device__ __forceinline__ void mbar_init(unsigned addr, unsigned count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" :: "r"(addr), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(unsigned addr, unsigned bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" :: "r"(addr), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(unsigned addr) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" :: "r"(addr) : "memory");
+}
+__device__ __forceinline__ unsigned long long global_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+// Waits for the phase with the given parity.  Bounded: after ~2 s the thread
+// records a timeout in *err, stops waiting from then on (fail becomes true)
+// and carries on, so the kernel always runs to its end.
+__device__ __forceinline__ void mbar_wait(unsigned addr, unsigned parity, bool &fail, int *err,
+                                          unsigned long long limit_ns = 2000000000ull) {
+    if (fail) return;
+    unsigned done = 0;
+    unsigned long long t0 = 0;
+    for (unsigned it = 0;; ++it) {
+        asm volatile("{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+                     "selp.u32 %0, 1, 0, p;\n\t}" : "=r"(done) : "r"(addr), "r"(parity) : "memory");
+        if (done) return;
+        if ((it & 63) == 0) {
+            const unsigned long long now = global_ns();
+            if (it == 0) t0 = now;
+            else if (now - t0 > limit_ns) {
+                fail = true;
+                if (err) atomicExch(err, 1);
+                return;
+            }
+        }
+    }
+}
+__device__ __forceinline__ void st_async4(unsigned addr, float a, float b, float c, float d, unsigned mbar) {
+    asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1,%2,%3,%4}, [%5];"
+                 :: "r"(addr), "f"(a), "f"(b), "f"(c), "f"(d), "r"(mbar) : "memory");
+}
+
 // Per-thread view of one sequence's m buffers.
 template <class C>
 struct VitThread {
@@ -319,12 +373,19 @@ struct VitThread {
     unsigned rank;
     unsigned rd0, wr0;       // byte offsets of this thread's first read / write
 
-    // byte offset of float f of this thread's sequence inside a (set, buffer)
+    // Layout of one (set, buffer).  CTA mode: m[f] of sequence `slot` at
+    // chunk slot*Q/4 + f/4.  Cluster mode: each CTA holds the values its own
+    // threads read -- m[k*Rn + r] lives in CTA r / (Rn/2) at local float
+    // k*(Rn/2) + r % (Rn/2) -- so writers push (half of them remotely) and
+    // every read is local.  Chunks are XOR-swizzled (bank-conflict free).
+    __device__ __forceinline__ unsigned loc(int f) const {
+        if (CL == 1) return unsigned(slot) * unsigned(C::Q) + unsigned(f);
+        const int k = f / C::Rn, r = f % C::Rn;
+        return unsigned(k * (C::Rn / 2) + (r % (C::Rn / 2)));
+    }
     __device__ __forceinline__ unsigned off(int f) const {
-        unsigned c;
-        if (CL == 1) c = unsigned(slot) * unsigned(C::Q >> 2) + unsigned(f >> 2);
-        else c = unsigned((f & (C::Q / 2 - 1)) >> 2);
-        return (swz_chunk<R>(c) << 4) + unsigned((f & 3) << 2);
+        const unsigned l = loc(f);
+        return (swz_chunk<R>(l >> 2) << 4) + ((l & 3u) << 2);
     }
     __device__ __forceinline__ int r0() const { return (NQ * v) >> R; }
 
@@ -332,37 +393,35 @@ struct VitThread {
         rd0 = off(r0());
         wr0 = off(NQ * v);
     }
-    // m_{t-1} reads.  own / peer: buffer base in this CTA / the peer CTA.
-    __device__ __forceinline__ void load_prev(unsigned own, unsigned peer, float (&m)[K][NR]) const {
+
+    // m_{t-1} reads (always from this CTA's shared memory).
+    __device__ __forceinline__ void load_prev(unsigned own, float (&m)[K][NR]) const {
+        constexpr unsigned KS = unsigned(C::KSTRIDE * 4);
 #pragma unroll
         for (int k = 0; k < K; ++k) {
-            bool remote = false;
-            unsigned base = own;
-            if (CL == 2) {
-                remote = unsigned(k >> (R - 1)) != rank;
-                base = remote ? peer : own;
-            }
             if (NR >= 4) {
 #pragma unroll
                 for (int c4 = 0; c4 < NR / 4; ++c4) {
-                    const unsigned o = C::FAST ? ((rd0 + unsigned((CL == 2 ? (k & (K / 2 - 1)) : k) * C::Rn * 4)) ^ (unsigned(c4) << 4))
+                    const unsigned o = C::FAST ? ((rd0 + unsigned(k) * KS) ^ (unsigned(c4) << 4))
                                                : off(k * C::Rn + r0() + 4 * c4);
-                    const float4 q4 = lds4(base + o, remote);
+                    const float4 q4 = lds4(own + o, false);
                     m[k][4 * c4 + 0] = q4.x; m[k][4 * c4 + 1] = q4.y;
                     m[k][4 * c4 + 2] = q4.z; m[k][4 * c4 + 3] = q4.w;
                 }
             } else {
-                const unsigned o = C::FAST ? (rd0 + unsigned((CL == 2 ? (k & (K / 2 - 1)) : k) * C::Rn * 4))
-                                           : off(k * C::Rn + r0());
-                m[k][0] = lds1(base + o, remote);
+                const unsigned o = C::FAST ? (rd0 + unsigned(k) * KS) : off(k * C::Rn + r0());
+                m[k][0] = lds1(own + o, false);
             }
         }
     }
 
     // One step for the owned q: writes m_t, returns the backpointer word
-    // (field of q-local index jq at bits [jq*R, jq*R + R)).
+    // (field of q-local index jq at bits [jq*R, jq*R + R)).  wbase: target
+    // buffer in the reading CTA; remote (cluster mode): that CTA is the peer,
+    // written with st.async that completes on the peer's mbarrier rmbar.
     template <bool PREV>
-    __device__ __forceinline__ unsigned step(float x, const float (&m)[K][NR], unsigned wbase) const {
+    __device__ __forceinline__ unsigned step(float x, const float (&m)[K][NR], unsigned wbase, bool remote,
+                                             unsigned rmbar) const {
         const u64 xx = pk2(x, x);
         unsigned word = 0;
         float mo[NQ];
@@ -390,7 +449,10 @@ struct VitThread {
 #pragma unroll
         for (int c4 = 0; c4 < NQ / 4; ++c4) {
             const unsigned o = C::FAST ? (wr0 ^ (unsigned(c4) << 4)) : off(NQ * v + 4 * c4);
-            sts4(wbase + o, mo[4 * c4], mo[4 * c4 + 1], mo[4 * c4 + 2], mo[4 * c4 + 3]);
+            if (CL == 2 && remote)
+                st_async4(wbase + o, mo[4 * c4], mo[4 * c4 + 1], mo[4 * c4 + 2], mo[4 * c4 + 3], rmbar);
+            else
+                sts4(wbase + o, mo[4 * c4], mo[4 * c4 + 1], mo[4 * c4 + 2], mo[4 * c4 + 3]);
         }
         return word;
     }
@@ -431,14 +493,19 @@ __device__ __forceinline__ void seq_sync(int slot) {
     else asm volatile("bar.sync %0, %1;" :: "r"(1 + slot), "r"(C::TPS) : "memory");
 }
 
+// Timeouts of the cluster exchange (bounded mbarrier waits) are reported here.
+__device__ int g_vit_timeout;
+__device__ unsigned long long g_wait_limit_ns = 2000000000ull;
+
 template <class C>
 __global__ void __cluster_dims__(C::CL, 1, 1) __launch_bounds__(kThreads, 1)
 viterbi_fwd_kernel(VitArgs a) {
     constexpr int K = C::K, NQ = C::NQ, NR = C::NR, NSET = C::NSET, NP = C::NP, TPS = C::TPS, CL = C::CL;
+    constexpr int NBUF = C::NBUF;
     extern __shared__ __align__(16) float sm_v[];
     __shared__ float red_v[NSET][kThreads / 32];
     __shared__ int red_i[NSET][kThreads / 32];
-    __shared__ float xs[CL == 2 ? NSET : 1][2][C::XCH];
+    __shared__ __align__(8) unsigned long long full[NSET][NBUF];   // cluster mode
 
     VitThread<C> th;
     const int tid = threadIdx.x;
@@ -464,89 +531,96 @@ viterbi_fwd_kernel(VitArgs a) {
         }
 
     const unsigned smem0 = unsigned(__cvta_generic_to_shared(sm_v));
-    const unsigned peer0 = CL == 2 ? mapa_shared(smem0, th.rank ^ 1u) : smem0;
     constexpr unsigned BUF = unsigned(C::FLOATS * 4);
+    const unsigned full0 = unsigned(__cvta_generic_to_shared(&full[0][0]));
+    // cluster mode: this thread's outputs are read by CTA bit TBIT of v
+    const bool wremote = CL == 2 && (((th.v >> C::TBIT) & 1) != int(th.rank));
+    const unsigned wtarget = wremote ? mapa_shared(smem0, th.rank ^ 1u) : smem0;
+    const unsigned wfull = wremote ? mapa_shared(full0, th.rank ^ 1u) : full0;
+    bool fail = false;
 
     int64_t seq[NSET];
     bool valid[NSET];
     const float *xrow[NSET];
     float xv[NSET];
+    uint32_t *bpo[NSET];
 #pragma unroll
     for (int X = 0; X < NSET; ++X) {
         seq[X] = seq_base + (CL == 1 ? th.slot : X);
         valid[X] = seq[X] < a.nbatch;
         xrow[X] = a.xn + (a.seq0 + (valid[X] ? seq[X] : 0)) * int64_t(a.T);
-        if (CL == 1) {
-            xv[X] = valid[X] ? __ldg(xrow[X]) : 0.f;
-        } else if (tid < C::XCH) {
-            xs[X][0][tid] = (valid[X] && tid < a.T) ? __ldg(xrow[X] + tid) : 0.f;
-        }
-    }
-    uint32_t *bpo[NSET];
-#pragma unroll
-    for (int X = 0; X < NSET; ++X)
+        xv[X] = valid[X] ? __ldg(xrow[X]) : 0.f;
         bpo[X] = a.bp + (valid[X] ? seq[X] : 0) * (int64_t(a.T - 1) * TPS) + th.v;
+    }
 
-    if (CL == 2) { cluster_arrive(); cluster_wait(); }   // peers running, staged x visible
-    else __syncthreads();
+    if (CL == 2) {
+        if (tid == 0) {
+#pragma unroll
+            for (int X = 0; X < NSET; ++X)
+#pragma unroll
+                for (int j = 0; j < NBUF; ++j) {
+                    const unsigned mb = full0 + unsigned(X * NBUF + j) * 8u;
+                    mbar_init(mb, C::NLOCALW + 1);
+                    mbar_expect_tx(mb, C::TXB);        // arm phase 0
+                }
+            asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        }
+        cluster_arrive();      // peers running and barriers initialised before any st.async
+        cluster_wait();
+    }
 
     float m[K][NR];
-    bool pending = false;
     for (int t = 0; t + 1 < a.T; ++t) {
 #pragma unroll
         for (int X = 0; X < NSET; ++X) {
-            float x;
+            const float x = xv[X];
+            xv[X] = valid[X] ? __ldg(xrow[X] + t + 1) : 0.f;
+            unsigned word;
             if (CL == 1) {
-                x = xv[X];
-                xv[X] = valid[X] ? __ldg(xrow[X] + t + 1) : 0.f;
+                const unsigned wb = smem0 + unsigned(X * NBUF + (t & 1)) * BUF;
+                if (t == 0) {
+                    word = th.template step<false>(x, m, wb, false, 0u);
+                } else {
+                    th.load_prev(smem0 + unsigned(X * NBUF + ((t - 1) & 1)) * BUF, m);
+                    word = th.template step<true>(x, m, wb, false, 0u);
+                }
+                seq_sync<C>(th.slot);
             } else {
-                const int tc = t % C::XCH;
-                x = xs[X][(t / C::XCH) & 1][tc];
-                if (tc == 0 && tid < C::XCH) {   // stage the next chunk (read a chunk later)
-                    const int tn = t + C::XCH + tid;
-                    xs[X][((t / C::XCH) + 1) & 1][tid] = (valid[X] && tn < a.T) ? __ldg(xrow[X] + tn) : 0.f;
+                const int jw = t % NBUF;
+                const unsigned wb = wtarget + unsigned(X * NBUF + jw) * BUF;
+                const unsigned mbw = wfull + unsigned(X * NBUF + jw) * 8u;
+                if (t == 0) {
+                    word = th.template step<false>(x, m, wb, wremote, mbw);
+                } else {
+                    const int jr = (t - 1) % NBUF;
+                    const unsigned mbr = full0 + unsigned(X * NBUF + jr) * 8u;
+                    mbar_wait(mbr, unsigned(((t - 1) / NBUF) & 1), fail, &g_vit_timeout, g_wait_limit_ns);
+                    if (tid == 0) mbar_expect_tx(mbr, C::TXB);   // arm its next phase
+                    th.load_prev(smem0 + unsigned(X * NBUF + jr) * BUF, m);
+                    word = th.template step<true>(x, m, wb, wremote, mbw);
+                }
+                if (!wremote) {
+                    __syncwarp();
+                    if ((tid & 31) == 0) mbar_arrive(mbw);
                 }
             }
-            const unsigned wb = smem0 + unsigned(X * 2 + (t & 1)) * BUF;
-            unsigned word;
-            if (t == 0) {
-                word = th.template step<false>(x, m, wb);
-            } else {
-                const unsigned rb = unsigned(X * 2 + ((t - 1) & 1)) * BUF;
-                th.load_prev(smem0 + rb, peer0 + rb, m);
-                word = th.template step<true>(x, m, wb);
-            }
-            if (CL == 1) {
-                seq_sync<C>(th.slot);
-            } else if (NSET == 1) {
-                cluster_arrive();
-                cluster_wait();
-            } else {
-                // the wait completes the other set's arrive (its next step reads
-                // those values); this set's arrive completes during that step
-                if (pending) cluster_wait();
-                cluster_arrive();
-                pending = true;
-            }
-            // backpointers leave after the barrier, so the release of the next
-            // arrive does not wait for a store issued just before it
             if (valid[X]) bpo[X][int64_t(t) * TPS] = word;
         }
     }
     // final step: argmin over all states of cost_{T-1}
 #pragma unroll
     for (int X = 0; X < NSET; ++X) {
-        if (pending && X == NSET - 1) { cluster_wait(); pending = false; }
-        const int tl = a.T - 1;
-        const float x = CL == 1 ? xv[X] : xs[X][(tl / C::XCH) & 1][tl % C::XCH];
         float bv;
         int bi;
         if (a.T == 1) {
-            th.template final_argmin<false>(x, m, bv, bi);
+            th.template final_argmin<false>(xv[X], m, bv, bi);
         } else {
-            const unsigned rb = unsigned(X * 2 + ((a.T - 2) & 1)) * BUF;
-            th.load_prev(smem0 + rb, peer0 + rb, m);
-            th.template final_argmin<true>(x, m, bv, bi);
+            const int jr = (a.T - 2) % NBUF;
+            if (CL == 2)
+                mbar_wait(full0 + unsigned(X * NBUF + jr) * 8u, unsigned(((a.T - 2) / NBUF) & 1), fail, &g_vit_timeout,
+                          g_wait_limit_ns);
+            th.load_prev(smem0 + unsigned(X * NBUF + (CL == 2 ? jr : ((a.T - 2) & 1))) * BUF, m);
+            th.template final_argmin<true>(xv[X], m, bv, bi);
         }
         constexpr int segw = TPS < 32 ? TPS : 32;
 #pragma unroll
@@ -602,6 +676,19 @@ viterbi_fwd_kernel(VitArgs a) {
     }
 }
 
+// Self-test of the bounded wait: waits on an mbarrier phase that nothing
+// completes; the wait gives up after limit_ns and reports it in *status.
+__global__ void wait_timeout_probe_kernel(unsigned long long limit_ns, int *status) {
+    __shared__ __align__(8) unsigned long long bar;
+    const unsigned addr = unsigned(__cvta_generic_to_shared(&bar));
+    if (threadIdx.x == 0) mbar_init(addr, 1);
+    __syncthreads();
+    bool fail = false;
+    mbar_wait(addr, 0u, fail, status, limit_ns);
+    __syncthreads();
+    if (threadIdx.x == 0) mbar_arrive(addr);   // complete the phase before exit
+}
+
 // Traceback: one thread per sequence walks the backpointer words.
 template <int R>
 __global__ void traceback_kernel(const uint32_t *bp, const int32_t *fin, int64_t nbatch, int T, int L,
@@ -628,7 +715,7 @@ template <int L, int R>
 int launch_viterbi(const VitArgs &a, cudaStream_t st) {
     constexpr int CL = L == 16 ? 2 : 1;
     using C = VitCfg<L, R, CL>;
-    const size_t smem = size_t(C::NSET) * 2 * C::FLOATS * sizeof(float);
+    const size_t smem = size_t(C::NSET) * C::NBUF * C::FLOATS * sizeof(float);
     auto kern = viterbi_fwd_kernel<C>;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess)
         return uq::check_cuda("viterbi: set smem attribute");
@@ -746,6 +833,33 @@ int trellis_decode(const int32_t *states, const float *cw, const float *sc, int6
 }  // namespace uq
 
 extern "C" {
+
+int uq_device_errors(void *stream) {
+    if (cudaStreamSynchronize(UQ_STREAM(stream)) != cudaSuccess) return uq::check_cuda("uq_device_errors");
+    int flag = 0, zero = 0;
+    if (cudaMemcpyFromSymbol(&flag, g_vit_timeout, sizeof(int)) != cudaSuccess) return uq::check_cuda("read timeout flag");
+    if (flag) {
+        cudaMemcpyToSymbol(g_vit_timeout, &zero, sizeof(int));
+        return uq::fail(UQ_ERR_TIMEOUT, "a bounded device wait of the Viterbi cluster exchange timed out");
+    }
+    return UQ_OK;
+}
+
+int uq_wait_timeout_selftest(double limit_ms, void *stream) {
+    if (!(limit_ms > 0.0) || limit_ms > 2000.0) return uq::fail(UQ_ERR_INVALID, "limit_ms must be in (0, 2000]");
+    cudaStream_t st = UQ_STREAM(stream);
+    int *d = nullptr;
+    if (cudaMallocAsync(&d, sizeof(int), st) != cudaSuccess) return uq::check_cuda("selftest alloc");
+    cudaMemsetAsync(d, 0, sizeof(int), st);
+    { uq::ProfScope _p("wait_probe", st); wait_timeout_probe_kernel<<<1, 32, 0, st>>>((unsigned long long)(limit_ms * 1e6), d); }
+    int rc = uq::check_cuda("wait_timeout_probe_kernel launch");
+    int flag = 0;
+    cudaMemcpyAsync(&flag, d, sizeof(int), cudaMemcpyDeviceToHost, st);
+    cudaFreeAsync(d, st);
+    if (cudaStreamSynchronize(st) != cudaSuccess) return uq::check_cuda("selftest sync");
+    if (rc) return rc;
+    return flag ? uq::fail(UQ_ERR_TIMEOUT, "bounded wait gave up as intended") : UQ_OK;
+}
 
 int uq_trellis_codebook(int L, float *out, void *stream) {
     if (L < 1 || L > 16) return uq::fail(UQ_ERR_UNSUPPORTED, "uq_trellis_codebook: L=%d not in [1, 16]", L);

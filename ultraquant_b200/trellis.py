@@ -56,6 +56,8 @@ def viterbi_states(xn: torch.Tensor, L: int, R: int, cw: torch.Tensor | None = N
         ws = D.workspace(nbytes, xn.device)
         _lib.check(lib.uq_trellis_viterbi(xn.data_ptr(), nseq, T, L, R, cw.data_ptr(), states.data_ptr(),
                                           ws.data_ptr(), ws.numel(), D.stream_handle(xn.device)), "viterbi")
+        if L == 16:  # the cluster-split kernel reports bounded-wait timeouts
+            _lib.check(lib.uq_device_errors(D.stream_handle(xn.device)), "viterbi")
     return states
 
 
