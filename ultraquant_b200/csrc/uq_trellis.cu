@@ -267,7 +267,7 @@ template <int L_, int R_, int CL_> struct VitCfg {
     static constexpr int Rn = Q >> R;
     static constexpr int TPS = Q / NQ;                   // threads per sequence
     static constexpr int NSET = (CL == 2 && R >= 2) ? 2 : 1;   // interleaved sets (cluster)
-    static constexpr int NBUF = CL == 2 ? 3 : 2;         // m buffers per set
+    static constexpr int NBUF = 2;                       // m buffers per set
     static constexpr int SPS = CL == 1 ? kThreads / TPS : 1;   // sequences per set per CTA
     static constexpr int FLOATS = kThreads * NQ;         // floats per (set, buffer) per CTA
     static constexpr int A = Swz<R>::A, M = Swz<R>::M;
@@ -278,8 +278,11 @@ template <int L_, int R_, int CL_> struct VitCfg {
     // cluster mode: the CTA reading a thread's outputs is bit TBIT of v, so
     // half of each CTA's warps write locally and half into the peer
     static constexpr int TBIT = L - R - 7;
-    static constexpr int NLOCALW = kThreads / 64;        // local writer warps per CTA
-    static constexpr unsigned TXB = unsigned(kThreads / 2) * NQ * 4;   // remote bytes per phase
+    // cluster mode: CTA r's threads produce half r (Q/4 floats, Q bytes) of
+    // both CTAs' buffers; the peer's share is staged in a local outbox and
+    // moved with one bulk copy per step
+    static constexpr unsigned OBYTES = unsigned(Q);
+    static constexpr int OFLOATS = CL == 2 ? Q / 4 : 0;
     static_assert(CL == 1 ? TPS <= kThreads : TPS == CL * kThreads, "thread split");
     static_assert(CL == 1 || (TBIT >= 5 && TBIT < 9), "writer target must be warp uniform");
 };
@@ -359,6 +362,14 @@ __device__ __forceinline__ void mbar_wait(unsigned addr, unsigned parity, bool &
         }
     }
 }
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+// shared::cta -> shared::cluster bulk copy completing on the destination's mbarrier
+__device__ __forceinline__ void bulk_copy_to_peer(unsigned dst, unsigned src, unsigned bytes, unsigned mbar) {
+    asm volatile("cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 :: "r"(dst), "r"(src), "r"(bytes), "r"(mbar) : "memory");
+}
 __device__ __forceinline__ void st_async4(unsigned addr, float a, float b, float c, float d, unsigned mbar) {
     asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1,%2,%3,%4}, [%5];"
                  :: "r"(addr), "f"(a), "f"(b), "f"(c), "f"(d), "r"(mbar) : "memory");
@@ -415,44 +426,38 @@ struct VitThread {
         }
     }
 
-    // One step for the owned q: writes m_t, returns the backpointer word
-    // (field of q-local index jq at bits [jq*R, jq*R + R)).  wbase: target
-    // buffer in the reading CTA; remote (cluster mode): that CTA is the peer,
-    // written with st.async that completes on the peer's mbarrier rmbar.
+    // One step for the owned q: writes m_t (at wbase + offset - wshift: the
+    // local buffer, or the outbox for values the peer reads), returns the
+    // backpointer word (field of q-local index jq at bits [jq*R, jq*R + R)).
     template <bool PREV>
-    __device__ __forceinline__ unsigned step(float x, const float (&m)[K][NR], unsigned wbase, bool remote,
-                                             unsigned rmbar) const {
+    __device__ __forceinline__ unsigned step(float x, const float (&m)[K][NR], unsigned wbase, unsigned wshift) const {
         const u64 xx = pk2(x, x);
         unsigned word = 0;
-        float mo[NQ];
+        // chunks of 4 new m values (2 pairs) are stored as soon as they are
+        // complete; q are visited in descending order for the word packing
 #pragma unroll
-        for (int p = NP - 1; p >= 0; --p) {
-            const int i = (NQ >= K) ? ((2 * p) >> R) : 0;
-            u64 c[K];
+        for (int c4 = NQ / 4 - 1; c4 >= 0; --c4) {
+            float mo[4];
 #pragma unroll
-            for (int k = 0; k < K; ++k) {
-                u64 d = sub2(xx, cwp[k][p]);
-                d = mul2(d, d);
-                c[k] = PREV ? add2(d, pk2(m[k][i], m[k][i])) : d;
+            for (int p = 2 * c4 + 1; p >= 2 * c4; --p) {
+                const int i = (NQ >= K) ? ((2 * p) >> R) : 0;
+                u64 c[K];
+#pragma unroll
+                for (int k = 0; k < K; ++k) {
+                    u64 d = sub2(xx, cwp[k][p]);
+                    d = mul2(d, d);
+                    c[k] = PREV ? add2(d, pk2(m[k][i], m[k][i])) : d;
+                }
+                unsigned blo[R], bhi[R];
+                const u64 mn = tourney<R>(c, blo, bhi);
+                up2(mn, mo[2 * (p - 2 * c4)], mo[2 * (p - 2 * c4) + 1]);
+#pragma unroll
+                for (int j = R - 1; j >= 0; --j) word = shift_in_sign(word, bhi[j]);
+#pragma unroll
+                for (int j = R - 1; j >= 0; --j) word = shift_in_sign(word, blo[j]);
             }
-            unsigned blo[R], bhi[R];
-            const u64 mn = tourney<R>(c, blo, bhi);
-            float lo, hi;
-            up2(mn, lo, hi);
-            mo[2 * p] = lo;
-            mo[2 * p + 1] = hi;
-#pragma unroll
-            for (int j = R - 1; j >= 0; --j) word = shift_in_sign(word, bhi[j]);
-#pragma unroll
-            for (int j = R - 1; j >= 0; --j) word = shift_in_sign(word, blo[j]);
-        }
-#pragma unroll
-        for (int c4 = 0; c4 < NQ / 4; ++c4) {
             const unsigned o = C::FAST ? (wr0 ^ (unsigned(c4) << 4)) : off(NQ * v + 4 * c4);
-            if (CL == 2 && remote)
-                st_async4(wbase + o, mo[4 * c4], mo[4 * c4 + 1], mo[4 * c4 + 2], mo[4 * c4 + 3], rmbar);
-            else
-                sts4(wbase + o, mo[4 * c4], mo[4 * c4 + 1], mo[4 * c4 + 2], mo[4 * c4 + 3]);
+            sts4(wbase + o - wshift, mo[0], mo[1], mo[2], mo[3]);
         }
         return word;
     }
@@ -505,7 +510,7 @@ viterbi_fwd_kernel(VitArgs a) {
     extern __shared__ __align__(16) float sm_v[];
     __shared__ float red_v[NSET][kThreads / 32];
     __shared__ int red_i[NSET][kThreads / 32];
-    __shared__ __align__(8) unsigned long long full[NSET][NBUF];   // cluster mode
+    __shared__ __align__(8) unsigned long long full[NSET][NBUF];   // cluster mode: peer half landed
 
     VitThread<C> th;
     const int tid = threadIdx.x;
@@ -532,11 +537,14 @@ viterbi_fwd_kernel(VitArgs a) {
 
     const unsigned smem0 = unsigned(__cvta_generic_to_shared(sm_v));
     constexpr unsigned BUF = unsigned(C::FLOATS * 4);
-    const unsigned full0 = unsigned(__cvta_generic_to_shared(&full[0][0]));
-    // cluster mode: this thread's outputs are read by CTA bit TBIT of v
+    // cluster mode: outboxes follow the buffers; the peer's share of this
+    // thread's outputs (bit TBIT of v names the reading CTA) goes there
+    const unsigned obox0 = smem0 + unsigned(NSET * NBUF) * BUF;
     const bool wremote = CL == 2 && (((th.v >> C::TBIT) & 1) != int(th.rank));
-    const unsigned wtarget = wremote ? mapa_shared(smem0, th.rank ^ 1u) : smem0;
-    const unsigned wfull = wremote ? mapa_shared(full0, th.rank ^ 1u) : full0;
+    const unsigned half_off = th.rank * C::OBYTES;     // this CTA produces half `rank` of each buffer
+    const unsigned full0 = unsigned(__cvta_generic_to_shared(&full[0][0]));
+    const unsigned peer_smem0 = CL == 2 ? mapa_shared(smem0, th.rank ^ 1u) : 0u;
+    const unsigned peer_full0 = CL == 2 ? mapa_shared(full0, th.rank ^ 1u) : 0u;
     bool fail = false;
 
     int64_t seq[NSET];
@@ -554,18 +562,12 @@ viterbi_fwd_kernel(VitArgs a) {
     }
 
     if (CL == 2) {
-        if (tid == 0) {
-#pragma unroll
-            for (int X = 0; X < NSET; ++X)
-#pragma unroll
-                for (int j = 0; j < NBUF; ++j) {
-                    const unsigned mb = full0 + unsigned(X * NBUF + j) * 8u;
-                    mbar_init(mb, C::NLOCALW + 1);
-                    mbar_expect_tx(mb, C::TXB);        // arm phase 0
-                }
+        if (tid < NSET * NBUF) {
+            mbar_init(full0 + unsigned(tid) * 8u, 1);
+            mbar_expect_tx(full0 + unsigned(tid) * 8u, C::OBYTES);   // arm phase 0
             asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         }
-        cluster_arrive();      // peers running and barriers initialised before any st.async
+        cluster_arrive();      // peers running and barriers initialised before any copy
         cluster_wait();
     }
 
@@ -579,30 +581,34 @@ viterbi_fwd_kernel(VitArgs a) {
             if (CL == 1) {
                 const unsigned wb = smem0 + unsigned(X * NBUF + (t & 1)) * BUF;
                 if (t == 0) {
-                    word = th.template step<false>(x, m, wb, false, 0u);
+                    word = th.template step<false>(x, m, wb, 0u);
                 } else {
                     th.load_prev(smem0 + unsigned(X * NBUF + ((t - 1) & 1)) * BUF, m);
-                    word = th.template step<true>(x, m, wb, false, 0u);
+                    word = th.template step<true>(x, m, wb, 0u);
                 }
                 seq_sync<C>(th.slot);
             } else {
-                const int jw = t % NBUF;
-                const unsigned wb = wtarget + unsigned(X * NBUF + jw) * BUF;
-                const unsigned mbw = wfull + unsigned(X * NBUF + jw) * 8u;
+                const int jw = t & 1;
+                // local values into buffer jw, the peer's share into outbox jw
+                const unsigned wb = wremote ? obox0 + unsigned(X * NBUF + jw) * C::OBYTES
+                                            : smem0 + unsigned(X * NBUF + jw) * BUF;
+                const unsigned wsh = wremote ? half_off : 0u;
                 if (t == 0) {
-                    word = th.template step<false>(x, m, wb, wremote, mbw);
+                    word = th.template step<false>(x, m, wb, wsh);
                 } else {
-                    const int jr = (t - 1) % NBUF;
+                    const int jr = (t - 1) & 1;
                     const unsigned mbr = full0 + unsigned(X * NBUF + jr) * 8u;
-                    mbar_wait(mbr, unsigned(((t - 1) / NBUF) & 1), fail, &g_vit_timeout, g_wait_limit_ns);
-                    if (tid == 0) mbar_expect_tx(mbr, C::TXB);   // arm its next phase
+                    mbar_wait(mbr, unsigned(((t - 1) >> 1) & 1), fail, &g_vit_timeout, g_wait_limit_ns);
                     th.load_prev(smem0 + unsigned(X * NBUF + jr) * BUF, m);
-                    word = th.template step<true>(x, m, wb, wremote, mbw);
+                    word = th.template step<true>(x, m, wb, wsh);
+                    if (tid == 0) mbar_expect_tx(mbr, C::OBYTES);   // arm that buffer's next phase
                 }
-                if (!wremote) {
-                    __syncwarp();
-                    if ((tid & 31) == 0) mbar_arrive(mbw);
-                }
+                if (wremote) fence_proxy_async_smem();   // outbox writes -> async proxy
+                __syncthreads();                         // this CTA's step complete
+                if (tid == 0)
+                    bulk_copy_to_peer(peer_smem0 + unsigned(X * NBUF + jw) * BUF + half_off,
+                                      obox0 + unsigned(X * NBUF + jw) * C::OBYTES, C::OBYTES,
+                                      peer_full0 + unsigned(X * NBUF + jw) * 8u);
             }
             if (valid[X]) bpo[X][int64_t(t) * TPS] = word;
         }
@@ -615,11 +621,11 @@ viterbi_fwd_kernel(VitArgs a) {
         if (a.T == 1) {
             th.template final_argmin<false>(xv[X], m, bv, bi);
         } else {
-            const int jr = (a.T - 2) % NBUF;
+            const int jr = (a.T - 2) & 1;
             if (CL == 2)
-                mbar_wait(full0 + unsigned(X * NBUF + jr) * 8u, unsigned(((a.T - 2) / NBUF) & 1), fail, &g_vit_timeout,
+                mbar_wait(full0 + unsigned(X * NBUF + jr) * 8u, unsigned(((a.T - 2) >> 1) & 1), fail, &g_vit_timeout,
                           g_wait_limit_ns);
-            th.load_prev(smem0 + unsigned(X * NBUF + (CL == 2 ? jr : ((a.T - 2) & 1))) * BUF, m);
+            th.load_prev(smem0 + unsigned(X * NBUF + jr) * BUF, m);
             th.template final_argmin<true>(xv[X], m, bv, bi);
         }
         constexpr int segw = TPS < 32 ? TPS : 32;
@@ -715,7 +721,7 @@ template <int L, int R>
 int launch_viterbi(const VitArgs &a, cudaStream_t st) {
     constexpr int CL = L == 16 ? 2 : 1;
     using C = VitCfg<L, R, CL>;
-    const size_t smem = size_t(C::NSET) * C::NBUF * C::FLOATS * sizeof(float);
+    const size_t smem = size_t(C::NSET) * C::NBUF * (C::FLOATS + C::OFLOATS) * sizeof(float);
     auto kern = viterbi_fwd_kernel<C>;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess)
         return uq::check_cuda("viterbi: set smem attribute");
