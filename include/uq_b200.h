@@ -137,6 +137,22 @@ int uq_trellis_viterbi(const float *xn, int64_t nseq, int T, int L, int R, const
                        int32_t *states, void *workspace, size_t workspace_bytes,
                        void *stream);
 
+/* No counterpart in the reference.  The same Viterbi as uq_trellis_viterbi
+ * for callers that cannot allocate device memory (a host that owns all GPU
+ * memory through its own allocator and offers plug-ins no allocation hook,
+ * or a latency-critical path that must not trigger cudaMalloc's implicit
+ * synchronisation).  Backpointers go to a fixed 64 MiB file-scope device
+ * array (uq_trellis_noalloc_scratch_bytes()) that each GPU loading the
+ * library holds until exit; sequences are processed in batches that fit it.
+ * A sequence needing more than that array (T * 2^L / 16 bytes) is rejected
+ * with UQ_ERR_INVALID.  Nothing is allocated or freed.  The first call on a
+ * device looks up the array's device address (cudaGetSymbolAddress); make
+ * that first call before any stream capture.  Every call shares the array:
+ * calls that overlap on the GPU (other streams, other host threads) race. */
+size_t uq_trellis_noalloc_scratch_bytes(void);
+int uq_trellis_viterbi_noalloc(const float *xn, int64_t nseq, int T, int L, int R,
+                               const float *cw, int32_t *states, void *stream);
+
 /* trellis.py:104-108 -- decoder: out[i] = cw[states[i]] * sc[i / group] for
  * i < ntot (float32 product). */
 int uq_trellis_decode(const int32_t *states, const float *cw, const float *sc,

@@ -43,6 +43,8 @@ SIGNATURES = {
     "uq_trellis_normalize_rows": (_i32, [_p, _i32, _i64, _i64, _i64, _i64, _p, _p, _p]),
     "uq_trellis_workspace_bytes": (_sz, [_i64, _i32, _i32, _i32]),
     "uq_trellis_viterbi": (_i32, [_p, _i64, _i32, _i32, _i32, _p, _p, _p, _sz, _p]),
+    "uq_trellis_noalloc_scratch_bytes": (_sz, []),
+    "uq_trellis_viterbi_noalloc": (_i32, [_p, _i64, _i32, _i32, _i32, _p, _p, _p]),
     "uq_trellis_decode": (_i32, [_p, _p, _p, _i64, _i64, _p, _p]),
     "uq_trellis_decode_rows": (_i32, [_p, _p, _p, _i64, _i64, _i64, _i64, _p, _p]),
     "uq_quant_trellis_workspace_bytes": (_sz, [_i64, _i64, _i32, _i32, _i32, _i32]),

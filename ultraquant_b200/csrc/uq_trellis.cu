@@ -32,6 +32,7 @@
 
 #include <algorithm>
 #include <cmath>
+#include <mutex>
 
 #include "uq_common.cuh"
 #include "uq_groupsum.cuh"
@@ -838,7 +839,66 @@ int trellis_decode(const int32_t *states, const float *cw, const float *sc, int6
 
 }  // namespace uq
 
+// ---------------------------------------------------------------------------
+// Scratch-free Viterbi entry point.
+//
+// Some callers cannot allocate device memory: a host program that hands its
+// whole GPU memory to its own allocator and exposes no allocation hook to
+// plug-ins, or a latency-sensitive caller that must never hit cudaMalloc's
+// device-wide synchronisation.  For them uq_trellis_viterbi_noalloc keeps the
+// backpointer scratch in a fixed file-scope device array instead of a caller
+// workspace.  The array is created when the library's module is loaded on a
+// device and is held by every GPU that loads the library until the process
+// exits.
+// ---------------------------------------------------------------------------
+namespace {
+constexpr size_t kNoAllocScratchBytes = size_t(64) << 20;   // 64 MiB per device
+std::mutex g_noalloc_mu;
+void *g_noalloc_ptr[256] = {};
+}  // namespace
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+// Device address of the scratch array for the current device, looked up once
+// per device (host code may not use the symbol itself as a device address).
+static int noalloc_scratch(void **out) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return uq::check_cuda("noalloc: cudaGetDevice");
+    if (dev < 0 || dev >= 256) return uq::fail(UQ_ERR_UNSUPPORTED, "noalloc: device ordinal %d", dev);
+    std::lock_guard<std::mutex> g(g_noalloc_mu);
+    if (!g_noalloc_ptr[dev]) {
+        void *p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess || !p)
+            return uq::fail(UQ_ERR_CUDA, "noalloc: cudaGetSymbolAddress failed: %s", cudaGetErrorString(e));
+        g_noalloc_ptr[dev] = p;
+    }
+    *out = g_noalloc_ptr[dev];
+    return UQ_OK;
+}
+
 extern "C" {
+
+size_t uq_trellis_noalloc_scratch_bytes(void) { return kNoAllocScratchBytes; }
+
+int uq_trellis_viterbi_noalloc(const float *xn, int64_t nseq, int T, int L, int R, const float *cw,
+                               int32_t *states, void *stream) {
+    int rc = vit_check(nseq, T, L, R);
+    if (rc) return rc;
+    const int64_t per = uq::vit_seq_bytes(T, L);
+    if (size_t(per) + 512 > kNoAllocScratchBytes)
+        return uq::fail(UQ_ERR_INVALID,
+                        "uq_trellis_viterbi_noalloc: one sequence (T=%d, L=%d) needs %lld bytes of backpointer "
+                        "scratch, more than the %zu-byte static array; use uq_trellis_viterbi with a workspace",
+                        T, L, (long long)per, kNoAllocScratchBytes);
+    if (nseq == 0) return UQ_OK;
+    if (!xn || !cw || !states) return uq::fail(UQ_ERR_INVALID, "uq_trellis_viterbi_noalloc: null pointer");
+    void *scratch = nullptr;
+    if ((rc = noalloc_scratch(&scratch))) return rc;
+    // The backpointers and final states are fully written before they are
+    // read, so nothing in the array needs clearing between calls.
+    return uq::trellis_viterbi(xn, nseq, T, L, R, cw, states, scratch, kNoAllocScratchBytes, UQ_STREAM(stream));
+}
 
 int uq_device_errors(void *stream) {
     if (cudaStreamSynchronize(UQ_STREAM(stream)) != cudaSuccess) return uq::check_cuda("uq_device_errors");
