@@ -140,6 +140,109 @@ __global__ void e8_quant_kernel(E8Args a) {
     }
 }
 
+// Warp-per-groups kernel for power-of-two groups <= 256 (all reference uses):
+// no shared memory, 16-byte loads and stores, numpy-order group sums via
+// shuffles.  Phase 2 re-reads the group as 8-vectors (L1 hits).
+template <typename TIn, int G>
+__global__ void __launch_bounds__(256, 3) e8_warp_kernel(E8Args a) {
+    using W = WarpGroup<G>;
+    const int lane = threadIdx.x & 31;
+    const int64_t warp = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const int64_t e_base = warp * W::GPW * int64_t(G);          // first element of the warp
+    const TIn *A = static_cast<const TIn *>(a.A);
+    auto get = [&](int i) -> double {
+        const int64_t e = e_base + i;
+        return e < a.size ? double(__ldg(A + e)) : 0.0;
+    };
+    const double ss = warp_group_sumsq<G, double>(get);
+    const double rms = d_add(sqrt(ss / double(G)), 1e-12);
+    if (a.rms_out && (lane % W::LPG) == 0) {
+        const int64_t g = e_base / G + lane / W::LPG;
+        if (g * G < a.size) a.rms_out[g] = rms;
+    }
+    if (!a.rec && !a.idx) return;
+    for (int vb = 0; vb < W::VPW; vb += 32) {
+        const int vv = vb + lane;
+        const int gg = (vv < W::VPW ? vv : W::VPW - 1) / W::VPG;
+        const double r = __shfl_sync(0xffffffffu, rms, gg * W::LPG);
+        if (vv >= W::VPW) continue;
+        const int64_t e0 = e_base + 8 * int64_t(vv);
+        if (e0 >= a.size) continue;
+        double y[8], p[8];
+        const bool full8 = e0 + 8 <= a.size;
+        if (sizeof(TIn) == 8 && full8 && ((reinterpret_cast<uintptr_t>(A + e0) & 15) == 0)) {
+            const double2 *q = reinterpret_cast<const double2 *>(A + e0);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) { const double2 t = __ldg(q + i); y[2 * i] = t.x; y[2 * i + 1] = t.y; }
+        } else if (sizeof(TIn) == 4 && full8 && ((reinterpret_cast<uintptr_t>(A + e0) & 15) == 0)) {
+            const float4 *q = reinterpret_cast<const float4 *>(A + e0);
+#pragma unroll
+            for (int i = 0; i < 2; ++i) {
+                const float4 t = __ldg(q + i);
+                y[4 * i] = t.x; y[4 * i + 1] = t.y; y[4 * i + 2] = t.z; y[4 * i + 3] = t.w;
+            }
+        } else {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) y[i] = e0 + i < a.size ? double(__ldg(A + e0 + i)) : 0.0;
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i) y[i] = (y[i] / r) / a.step;
+        e8_point(y, p);
+        if (a.rec) {
+            double o[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) o[i] = d_mul(d_mul(p[i], a.step), r);
+            if (full8 && ((reinterpret_cast<uintptr_t>(a.rec + e0) & 15) == 0)) {
+                double2 *q = reinterpret_cast<double2 *>(a.rec + e0);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) q[i] = make_double2(o[2 * i], o[2 * i + 1]);
+            } else {
+#pragma unroll
+                for (int i = 0; i < 8; ++i) if (e0 + i < a.size) a.rec[e0 + i] = o[i];
+            }
+        }
+        if (a.idx) {
+            short o[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) o[i] = (short)(long long)d_mul(p[i], 2.0);
+            if ((reinterpret_cast<uintptr_t>(a.idx + e0) & 15) == 0) {
+                int4 pk;
+                pk.x = (unsigned short)o[0] | ((unsigned)(unsigned short)o[1] << 16);
+                pk.y = (unsigned short)o[2] | ((unsigned)(unsigned short)o[3] << 16);
+                pk.z = (unsigned short)o[4] | ((unsigned)(unsigned short)o[5] << 16);
+                pk.w = (unsigned short)o[6] | ((unsigned)(unsigned short)o[7] << 16);
+                *reinterpret_cast<int4 *>(a.idx + e0) = pk;
+            } else {
+#pragma unroll
+                for (int i = 0; i < 8; ++i) a.idx[e0 + i] = o[i];
+            }
+        }
+    }
+}
+
+template <typename TIn, int G>
+int launch_e8_warp(const E8Args &a, cudaStream_t st) {
+    using W = WarpGroup<G>;
+    const int64_t groups = (a.size + G - 1) / G;
+    const int64_t warps = (groups + W::GPW - 1) / W::GPW;
+    const int64_t blocks = (warps + 7) / 8;
+    if (blocks > 0) { uq::ProfScope _p("e8_quant", st); e8_warp_kernel<TIn, G><<<unsigned(blocks), 256, 0, st>>>(a); }
+    return uq::check_cuda("e8_warp_kernel launch");
+}
+
+template <typename TIn>
+int dispatch_e8_warp(const E8Args &a, cudaStream_t st) {
+    switch (a.group) {
+        case 8: return launch_e8_warp<TIn, 8>(a, st);
+        case 16: return launch_e8_warp<TIn, 16>(a, st);
+        case 32: return launch_e8_warp<TIn, 32>(a, st);
+        case 64: return launch_e8_warp<TIn, 64>(a, st);
+        case 128: return launch_e8_warp<TIn, 128>(a, st);
+        case 256: return launch_e8_warp<TIn, 256>(a, st);
+    }
+    return -1;
+}
+
 int e8_tile_elems(int group) {
     if (group >= 2048) return group;
     int t = group;
@@ -150,6 +253,10 @@ int e8_tile_elems(int group) {
 
 template <typename TIn>
 int launch_e8_quant(const E8Args &a0, cudaStream_t st) {
+    {
+        const int rc = dispatch_e8_warp<TIn>(a0, st);
+        if (rc >= 0) return rc;
+    }
     E8Args a = a0;
     a.tile = e8_tile_elems(a.group);
     const int ng = a.tile / a.group;

@@ -61,3 +61,43 @@ __device__ void tile_group_sumsq(const T *tile, int ngroups, int group, T *out, 
     }
     __syncthreads();
 }
+
+// ---------------------------------------------------------------------------
+// Warp-level form for power-of-two groups G in [8, 256].
+//
+// Phase 1 ("chain layout"): a group occupies LPG = 8 * NLEAF lanes, lane
+// (leaf lf, chain j) loads the leaf's elements j, j+8, j+16, ... and adds their
+// squares sequentially (numpy's 8 accumulators), then xor-shuffles 1, 2, 4
+// combine the 8 chains as ((r0+r1)+(r2+r3))+((r4+r5)+(r6+r7)) and xor 8 adds
+// the two 128-leaves.  Every lane of the group ends with the group sum.
+// ---------------------------------------------------------------------------
+template <int G> struct WarpGroup {
+    static_assert(G >= 8 && G <= 256 && (G & (G - 1)) == 0, "power-of-two group in [8, 256]");
+    static constexpr int LEAF = G < 128 ? G : 128;
+    static constexpr int NLEAF = G / LEAF;       // 1 or 2
+    static constexpr int LPG = 8 * NLEAF;        // lanes per group in the chain layout
+    static constexpr int GPW = 32 / LPG;         // groups per warp
+    static constexpr int CH = LEAF / 8;          // chain length
+    static constexpr int VPG = G / 8;            // 8-vectors per group
+    static constexpr int VPW = GPW * VPG;        // 8-vectors per warp
+};
+
+// Sum of squares of group (g0 + lane / LPG), elements read by get(i) with
+// i relative to the warp's first element (g0 * G); identical in all lanes of
+// the group.  Must be called by the full warp.
+template <int G, typename T, typename Get>
+__device__ __forceinline__ T warp_group_sumsq(Get get) {
+    using W = WarpGroup<G>;
+    const int lane = threadIdx.x & 31;
+    const int gl = lane / W::LPG, lf = (lane % W::LPG) / 8, j = lane & 7;
+    const int base = gl * G + lf * W::LEAF + j;
+    T v0 = get(base);
+    T r = sq_rn<T>(v0);
+#pragma unroll
+    for (int i = 1; i < W::CH; ++i) r = r + sq_rn<T>(get(base + 8 * i));
+    r = r + __shfl_xor_sync(0xffffffffu, r, 1);
+    r = r + __shfl_xor_sync(0xffffffffu, r, 2);
+    r = r + __shfl_xor_sync(0xffffffffu, r, 4);
+    if (W::NLEAF == 2) r = r + __shfl_xor_sync(0xffffffffu, r, 8);
+    return r;
+}

@@ -20,10 +20,12 @@
 
 namespace uq {
 int rht_forward(const void *in, int in_dtype, int64_t rows, int64_t n0, int64_t ld_in, const double *colscale,
-                const double *signs, void *out, int out_dtype, int64_t ld_out, cudaStream_t st);
+                const double *pre, const double *signs, void *out, int out_dtype, int64_t ld_out, cudaStream_t st);
 int rht_inverse(const void *in, int in_dtype, int64_t rows, int64_t n, int64_t ld_in, int64_t n0,
-                const double *signs, const double *colscale, void *out, int out_dtype, int64_t ld_out,
-                const void *ref_w, int ref_dtype, int64_t ld_w, double *err_partial, double *err, cudaStream_t st);
+                const double *signs, const double *colscale, const double *pre, void *out, int out_dtype,
+                int64_t ld_out, const void *ref_w, int ref_dtype, int64_t ld_w, double *err_partial, double *err,
+                cudaStream_t st);
+int rht_prescale(const double *colscale, const double *signs, int64_t n0, int64_t n, double *pre, cudaStream_t st);
 int64_t rht_tiles(int64_t rows, int64_t n);
 int e8_quant(const void *A, int a_dtype, int64_t size, int64_t group, double step, double *rec, int16_t *idx,
              double *rms_out, cudaStream_t st);
@@ -74,9 +76,10 @@ TrellisPlan plan_trellis(int64_t rows, int64_t n0, int L, int seg, int group) {
 }
 
 size_t carve_trellis(const TrellisPlan &p, int64_t n0, bool need_states, bool need_sc, void *base, double **sH,
-                     float **X, int32_t **states, float **sc, double **part, void **vit) {
+                     double **pre, float **X, int32_t **states, float **sc, double **part, void **vit) {
     uq::Carver c(base, ~size_t(0));
     *sH = c.take<double>(size_t(n0));
+    *pre = c.take<double>(size_t(p.n));
     *X = c.take<float>(size_t(p.padded));
     *states = need_states ? c.take<int32_t>(size_t(p.padded)) : nullptr;
     *sc = need_sc ? c.take<float>(size_t(p.ngroups)) : nullptr;
@@ -103,8 +106,8 @@ size_t uq_quant_trellis_workspace_bytes(int64_t rows, int64_t n0, int L, int R, 
     (void)R;
     if (rows < 0 || n0 < 1 || seg < 1 || group < 8) return 0;
     const TrellisPlan p = plan_trellis(rows, n0, L, seg, group);
-    double *a; float *b; int32_t *c; float *d; double *e; void *f;
-    return carve_trellis(p, n0, true, true, nullptr, &a, &b, &c, &d, &e, &f);
+    double *a, *a2; float *b; int32_t *c; float *d; double *e; void *f;
+    return carve_trellis(p, n0, true, true, nullptr, &a, &a2, &b, &c, &d, &e, &f);
 }
 
 int uq_quant_trellis(const void *W, int w_dtype, int64_t rows, int64_t n0, int64_t ldw, const double *H, int L,
@@ -119,24 +122,27 @@ int uq_quant_trellis(const void *W, int w_dtype, int64_t rows, int64_t n0, int64
     const TrellisPlan p = plan_trellis(rows, n0, L, seg, group);
     if (p.padded % seg) return uq::fail(UQ_ERR_INVALID, "uq_quant_trellis: padded size %lld not divisible by seg %d",
                                         (long long)p.padded, seg);
-    double *sH, *part;
+    double *sH, *pre, *part;
     float *X, *scw;
     int32_t *stw;
     void *vit;
-    const size_t need = carve_trellis(p, n0, states == nullptr, sc == nullptr, workspace, &sH, &X, &stw, &scw, &part, &vit);
+    const size_t need = carve_trellis(p, n0, states == nullptr, sc == nullptr, workspace, &sH, &pre, &X, &stw, &scw,
+                                      &part, &vit);
     if (workspace_bytes < need) return uq::fail(UQ_ERR_WORKSPACE, "uq_quant_trellis: workspace %zu < %zu", workspace_bytes, need);
     if (!states) states = stw;
     if (!sc) sc = scw;
     cudaStream_t st = UQ_STREAM(stream);
     { uq::ProfScope _p("importance_scale", st); importance_scale_kernel<<<1, 1024, 0, st>>>(H, n0, sH); }
     if ((rc = uq::check_cuda("importance_scale_kernel launch"))) return rc;
+    if ((rc = uq::rht_prescale(sH, signs, n0, p.n, pre, st))) return rc;
     // A = W * sH, rotated, rounded to float32 (trellis_quant_fast: A.astype(float32))
-    if ((rc = uq::rht_forward(W, w_dtype, rows, n0, ldw, sH, signs, X, UQ_F32, p.n, st))) return rc;
+    if ((rc = uq::rht_forward(W, w_dtype, rows, n0, ldw, sH, pre, signs, X, UQ_F32, p.n, st))) return rc;
     if (p.padded > p.ntot) cudaMemsetAsync(X + p.ntot, 0, size_t(p.padded - p.ntot) * sizeof(float), st);
     if ((rc = uq::trellis_normalize(X, UQ_F32, 1, p.ntot, p.ntot, p.padded, group, X, sc, st))) return rc;
     if ((rc = uq::trellis_viterbi(X, p.nseq, seg, L, R, cw, states, vit, p.vit_ws, st))) return rc;
     if ((rc = uq::trellis_decode(states, cw, sc, group, p.ntot, X, st))) return rc;
-    return uq::rht_inverse(X, UQ_F32, rows, p.n, p.n, n0, signs, sH, What, UQ_F32, n0, W, w_dtype, ldw, part, err, st);
+    return uq::rht_inverse(X, UQ_F32, rows, p.n, p.n, n0, signs, sH, pre, What, UQ_F32, n0, W, w_dtype, ldw, part,
+                           err, st);
 }
 
 size_t uq_quant_e8_workspace_bytes(int64_t rows, int64_t n0, int group) {
@@ -144,6 +150,7 @@ size_t uq_quant_e8_workspace_bytes(int64_t rows, int64_t n0, int group) {
     const int64_t n = uq_next_pow2(n0);
     uq::Carver c(nullptr, ~size_t(0));
     c.take<double>(size_t(n0));
+    c.take<double>(size_t(n));
     c.take<double>(size_t(rows * n));
     c.take<double>(size_t(2 * uq::rht_tiles(rows, n)));
     return c.off;
@@ -159,15 +166,18 @@ int uq_quant_e8(const void *W, int w_dtype, int64_t rows, int64_t n0, int64_t ld
     const int64_t n = uq_next_pow2(n0);
     uq::Carver c(workspace, workspace_bytes);
     double *sH = c.take<double>(size_t(n0));
+    double *pre = c.take<double>(size_t(n));
     double *X = c.take<double>(size_t(rows * n));
     double *part = c.take<double>(size_t(2 * uq::rht_tiles(rows, n)));
     if (!c.ok()) return uq::fail(UQ_ERR_WORKSPACE, "uq_quant_e8: workspace %zu < %zu", workspace_bytes, c.off);
     cudaStream_t st = UQ_STREAM(stream);
     { uq::ProfScope _p("importance_scale", st); importance_scale_kernel<<<1, 1024, 0, st>>>(H, n0, sH); }
     if ((rc = uq::check_cuda("importance_scale_kernel launch"))) return rc;
-    if ((rc = uq::rht_forward(W, w_dtype, rows, n0, ldw, sH, signs, X, UQ_F64, n, st))) return rc;
+    if ((rc = uq::rht_prescale(sH, signs, n0, n, pre, st))) return rc;
+    if ((rc = uq::rht_forward(W, w_dtype, rows, n0, ldw, sH, pre, signs, X, UQ_F64, n, st))) return rc;
     if ((rc = uq::e8_quant(X, UQ_F64, rows * n, group, step, X, idx, nullptr, st))) return rc;
-    return uq::rht_inverse(X, UQ_F64, rows, n, n, n0, signs, sH, What, UQ_F32, n0, W, w_dtype, ldw, part, err, st);
+    return uq::rht_inverse(X, UQ_F64, rows, n, n, n0, signs, sH, pre, What, UQ_F32, n0, W, w_dtype, ldw, part, err,
+                           st);
 }
 
 }  // extern "C"

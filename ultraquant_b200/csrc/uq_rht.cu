@@ -16,6 +16,9 @@
 // the global store is coalesced; the load is coalesced the same way.
 #include <cuda_runtime.h>
 
+#include <algorithm>
+#include <stdint.h>
+
 #include "uq_common.cuh"
 
 namespace {
@@ -35,6 +38,8 @@ struct RhtArgs {
     int b;                       // log2(n)
     const double *signs;         // n
     const double *colscale;      // optional: fwd multiplies A = in * colscale (n0); inv divides
+    const double *pre;           // fwd: colscale * signs (n; signs alone when no colscale)
+                                 // inv: colscale * signs (n0), used when colscale is set
     void *out;
     int64_t ld_out, ncols_out;   // output row stride, columns written (< n crops)
     double sqrt_n, n_d;
@@ -46,117 +51,212 @@ struct RhtArgs {
     double *err_partial;         // [gridDim.x * 2]
 };
 
-template <typename TIn, typename TOut, int MODE, int MAXT>
-__global__ void __launch_bounds__(MAXT)
-rht_tile_kernel(RhtArgs a) {
-    extern __shared__ double tile[];
+// Applies the butterfly stages of index bits [lo, hi) that lie in [p, p+4)
+// to the 16 register values x[j] = element(base + (j << p)).
+__device__ __forceinline__ void stages16(double (&x)[16], int p, int lo, int hi) {
+#pragma unroll
+    for (int lq = 0; lq < 4; ++lq) {      // stage of index bit p + lq, in order
+        if (p + lq < lo || p + lq >= hi) continue;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            if (!(j & (1 << lq))) {
+                const int k = j | (1 << lq);
+                const double u = x[j], v = x[k];
+                x[j] = d_add(u, v);
+                x[k] = d_sub(u, v);
+            }
+        }
+    }
+}
+
+// Issues the coalesced 16-byte cp.async copies of tile `t` into the chunk-
+// swizzled staging layout at `dst` (zero fill past n0 / the last row): chunk c
+// (tile order) of thread u = c / CPT lives at (u * CPT) | ((c % CPT) ^ mix(u)).
+template <typename TIn, int MODE>
+__device__ __forceinline__ void rht_stage(const RhtArgs &a, const TIn *in, int64_t t, int b, int NB, int nthr,
+                                          double *dst_tile) {
+    constexpr int EPC = 16 / int(sizeof(TIn));
+    constexpr int CPT = 16 / EPC;
+    const unsigned sbase = unsigned(__cvta_generic_to_shared(dst_tile));
+    const int nmask = (1 << b) - 1;
+    const int64_t row0 = t << (NB - b);
+    const int64_t lim = (MODE == MODE_FWD) ? a.n0 : (int64_t(1) << b);
+    for (int c = threadIdx.x; c < nthr * CPT; c += nthr) {
+        const int E = c * EPC;
+        const int64_t r = row0 + (E >> b);
+        const int e = E & nmask;
+        const int u = c / CPT, w = c % CPT;
+        const int mix = CPT == 8 ? (u & 7) : ((u >> 1) & 3);
+        const unsigned dst = sbase + unsigned(((u * CPT) | (w ^ mix)) * 16);
+        int valid = 0;
+        if (r < a.rows && e < lim) valid = int((lim - e) < EPC ? (lim - e) : EPC);
+        const TIn *src = in + (valid ? r * a.ld_in + e : 0);
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;"
+                     :: "r"(dst), "l"(src), "r"(valid * int(sizeof(TIn))) : "memory");
+    }
+}
+
+// Persistent CTAs walk the tiles (gridDim.x apart).  Pass 0 keeps index bits
+// [0, 4) in registers (16 consecutive elements per thread), intermediate
+// passes go through the swizzled shared tile, the last pass (bits
+// [NB-4, NB), consecutive threads on consecutive elements) writes straight to
+// global memory.  Fast path (rows of >= 16 elements, 16-byte aligned rows):
+// the next tile is prefetched with cp.async into the second buffer while the
+// current one is transformed.  Forward: x = rn(a * pre[e]) with
+// pre = colscale * signs (a sign flip commutes with rounding, so this equals
+// (a * colscale) * signs); padding gives 0 * pre[e] = +-0 as numpy.
+template <typename TIn, typename TOut, int MODE, int MAXT, int MINB>
+__global__ void __launch_bounds__(MAXT, MINB)
+rht_tile_kernel(RhtArgs a, int dbuf) {
+    extern __shared__ double smem_d[];
     const int b = a.b;
     const int NB = b > 12 ? b : 12;
     const int nthr = 1 << (NB - 4);
     const int tid = threadIdx.x;
-    const int64_t n = int64_t(1) << b;
-    const int rows_per_tile = 1 << (NB - b);
-    const int64_t row0 = int64_t(blockIdx.x) * rows_per_tile;
+    const int nmask = (1 << b) - 1;
+    const int64_t ntiles = (a.rows + (int64_t(1) << (NB - b)) - 1) >> (NB - b);
     const TIn *in = static_cast<const TIn *>(a.in);
+    // exact power-of-two scalings replace the divisions when possible
+    const bool fwd_pow2 = (b & 1) == 0;
+    const double fwd_mul = ldexp(1.0, -(b >> 1));
+    const double inv_mul = ldexp(1.0, -b);
+    const bool staged = b >= 4 && ((a.ld_in * int64_t(sizeof(TIn))) % 16 == 0) &&
+                        ((reinterpret_cast<uintptr_t>(in) & 15) == 0);
+    constexpr int EPC = 16 / int(sizeof(TIn));
+    constexpr int CPT = 16 / EPC;
+    const int TILE = 1 << NB;
 
-    // ---- coalesced load: combined index E = tid + nthr * j ------------------
-#pragma unroll
-    for (int j = 0; j < 16; ++j) {
-        const int E = tid + nthr * j;
-        const int64_t r = row0 + (E >> b);
-        const int e = E & int(n - 1);
-        double x;
-        if (MODE == MODE_FWD) {
-            double av = 0.0;
-            if (r < a.rows && e < a.n0) {
-                av = ld_as_f64(in + r * a.ld_in + e);
-                if (a.colscale) av = d_mul(av, __ldg(a.colscale + e));
-            }
-            x = d_mul(av, __ldg(a.signs + e));
-        } else {
-            x = 0.0;
-            if (r < a.rows) x = d_mul(ld_as_f64(in + r * a.ld_in + e), a.sqrt_n);
-        }
-        tile[swz(E)] = x;
-    }
-    __syncthreads();
-
-    // ---- passes: bits [p, p+4) in registers --------------------------------
-    int done = 0;  // stages (index bits) already applied
-    const int last_p = NB - 4;
-    for (int p = 0;; p += 4) {
-        if (p > last_p) p = last_p;
-        const int base = (tid & ((1 << p) - 1)) | ((tid >> p) << (p + 4));
+    int64_t t = blockIdx.x;
+    if (staged && t < ntiles) rht_stage<TIn, MODE>(a, in, t, b, NB, nthr, smem_d);
+    asm volatile("cp.async.commit_group;" ::: "memory");
+    for (int k = 0; t < ntiles; t += gridDim.x, ++k) {
+        double *tile = smem_d + ((dbuf && (k & 1)) ? TILE : 0);
+        const int64_t row0 = t << (NB - b);
         double x[16];
+        // ---- pass 0: load (bits [0, 4) in registers) ------------------------
+        {
+            const int E0 = tid << 4;
+            double raw[16];
+            if (staged) {
+                if (dbuf) {
+                    // prefetch the CTA's next tile into the other buffer
+                    const int64_t tn = t + gridDim.x;
+                    if (tn < ntiles) rht_stage<TIn, MODE>(a, in, tn, b, NB, nthr, smem_d + ((k & 1) ? 0 : TILE));
+                } else if (k > 0) {
+                    // single buffer: stage this tile now (the buffer was released
+                    // by the barrier that ended the previous tile)
+                    rht_stage<TIn, MODE>(a, in, t, b, NB, nthr, smem_d);
+                }
+                asm volatile("cp.async.commit_group;" ::: "memory");
+                if (dbuf) asm volatile("cp.async.wait_group 1;" ::: "memory");
+                else asm volatile("cp.async.wait_group 0;" ::: "memory");
+                __syncthreads();
+                const int mix = CPT == 8 ? (tid & 7) : ((tid >> 1) & 3);
+                const TIn *stile = reinterpret_cast<const TIn *>(tile);
 #pragma unroll
-        for (int j = 0; j < 16; ++j) x[j] = tile[swz(base + (j << p))];
-        const int hi = (p + 4 < b) ? p + 4 : b;
-        const int lo = done > p ? done : p;
+                for (int w = 0; w < CPT; ++w) {
+                    const TIn *q = stile + ((tid * CPT) | (w ^ mix)) * EPC;
 #pragma unroll
-        for (int lq = 0; lq < 4; ++lq) {      // stage of index bit p + lq, in order
-            if (p + lq < lo || p + lq >= hi) continue;
+                    for (int i = 0; i < EPC; ++i) raw[w * EPC + i] = double(q[i]);
+                }
+                __syncthreads();   // the tile is rewritten by the next pass
+            } else {
 #pragma unroll
-            for (int j = 0; j < 16; ++j) {
-                if (!(j & (1 << lq))) {
-                    const int k = j | (1 << lq);
-                    const double u = x[j], v = x[k];
-                    x[j] = d_add(u, v);
-                    x[k] = d_sub(u, v);
+                for (int j = 0; j < 16; ++j) {
+                    const int E = E0 + j;
+                    int64_t r = row0 + (E >> b);
+                    int e = E & nmask;
+                    r = r < a.rows ? r : a.rows - 1;
+                    if (MODE == MODE_FWD) e = e < a.n0 ? e : int(a.n0 - 1);
+                    raw[j] = ld_as_f64(in + r * a.ld_in + e);
                 }
             }
-        }
-        if (hi > done) done = hi;
-        if (p == last_p) {
-            // ---- epilogue: scale and store (coalesced: base == tid) --------
-            double se = 0.0, sa = 0.0;
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
-                const int E = base + (j << p);
+                const int E = E0 + j;
                 const int64_t r = row0 + (E >> b);
-                const int e = E & int(n - 1);
-                if (r >= a.rows || e >= a.ncols_out) continue;
-                double y;
-                if (MODE == MODE_FWD) {
-                    y = x[j] / a.sqrt_n;
-                } else {
-                    y = d_mul(x[j] / a.n_d, __ldg(a.signs + e));
-                    if (a.err_partial) {
-                        double w = a.ref_dtype == UQ_F32
-                            ? double(__ldg(static_cast<const float *>(a.ref_w) + r * a.ld_w + e))
-                            : __ldg(static_cast<const double *>(a.ref_w) + r * a.ld_w + e);
-                        const double A = d_mul(w, __ldg(a.colscale + e));
-                        const double dd = d_sub(A, y);
-                        se = d_add(se, d_mul(dd, dd));
-                        sa = d_add(sa, d_mul(A, A));
-                    }
-                    if (a.colscale) y = y / __ldg(a.colscale + e);
-                }
-                static_cast<TOut *>(a.out)[r * a.ld_out + e] = TOut(y);
+                const int e = E & nmask;
+                const bool ok = r < a.rows && (MODE != MODE_FWD || e < a.n0);
+                const double v = ok ? raw[j] : 0.0;
+                x[j] = MODE == MODE_FWD ? d_mul(v, __ldg(a.pre + e)) : d_mul(v, a.sqrt_n);
             }
-            if (MODE == MODE_INV && a.err_partial) {
-                // deterministic CTA reduction: warp tree, then warp 0
-                __syncthreads();
-                double *red = tile;
-                for (int o = 16; o > 0; o >>= 1) {
-                    se = d_add(se, __shfl_xor_sync(0xffffffffu, se, o));
-                    sa = d_add(sa, __shfl_xor_sync(0xffffffffu, sa, o));
-                }
-                const int w = tid >> 5, nw = nthr >> 5;
-                if ((tid & 31) == 0) { red[2 * w] = se; red[2 * w + 1] = sa; }
-                __syncthreads();
-                if (tid == 0) {
-                    double s0 = 0.0, s1 = 0.0;
-                    for (int i = 0; i < nw; ++i) { s0 = d_add(s0, red[2 * i]); s1 = d_add(s1, red[2 * i + 1]); }
-                    a.err_partial[2 * blockIdx.x] = s0;
-                    a.err_partial[2 * blockIdx.x + 1] = s1;
-                }
-            }
-            break;
+            stages16(x, 0, 0, b < 4 ? b : 4);
         }
+        int done = b < 4 ? b : 4;
+        const int last_p = NB - 4;
+        // passes p = 4, 8, ..., last_p (the last one may overlap bits already
+        // done): registers of the previous layout -> tile -> layout p
+        int prev_p = 0;
+        for (int p = 4;; p += 4) {
+            if (p > last_p) p = last_p;
+            {
+                const int pb = (tid & ((1 << prev_p) - 1)) | ((tid >> prev_p) << (prev_p + 4));
 #pragma unroll
-        for (int j = 0; j < 16; ++j) tile[swz(base + (j << p))] = x[j];
-        __syncthreads();
+                for (int j = 0; j < 16; ++j) tile[swz(pb + (j << prev_p))] = x[j];
+            }
+            __syncthreads();
+            const int base = (tid & ((1 << p) - 1)) | ((tid >> p) << (p + 4));
+#pragma unroll
+            for (int j = 0; j < 16; ++j) x[j] = tile[swz(base + (j << p))];
+            const int hi = (p + 4 < b) ? p + 4 : b;
+            stages16(x, p, done > p ? done : p, hi);
+            if (hi > done) done = hi;
+            if (p == last_p) {
+                // ---- epilogue: scale and store (coalesced: base == tid) ----
+                double se = 0.0, sa = 0.0;
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    const int E = base + (j << p);
+                    const int64_t r = row0 + (E >> b);
+                    const int e = E & nmask;
+                    if (r >= a.rows || e >= a.ncols_out) continue;
+                    double y;
+                    if (MODE == MODE_FWD) {
+                        y = fwd_pow2 ? d_mul(x[j], fwd_mul) : x[j] / a.sqrt_n;
+                    } else {
+                        // irht: (x / n) * d, x / n exact; optional / colscale
+                        const double xs = d_mul(x[j], inv_mul);
+                        y = d_mul(xs, __ldg(a.signs + e));
+                        if (a.err_partial) {
+                            double w = a.ref_dtype == UQ_F32
+                                ? double(__ldg(static_cast<const float *>(a.ref_w) + r * a.ld_w + e))
+                                : __ldg(static_cast<const double *>(a.ref_w) + r * a.ld_w + e);
+                            const double A = d_mul(w, __ldg(a.colscale + e));
+                            const double dd = d_sub(A, y);
+                            se = d_add(se, d_mul(dd, dd));
+                            sa = d_add(sa, d_mul(A, A));
+                        }
+                        // (xs * d) / cs == xs / (cs * d): a sign flip commutes with rounding
+                        if (a.colscale) y = xs / __ldg(a.pre + e);
+                    }
+                    static_cast<TOut *>(a.out)[r * a.ld_out + e] = TOut(y);
+                }
+                if (MODE == MODE_INV && a.err_partial) {
+                    // deterministic per-tile reduction: warp tree, then one thread
+                    __syncthreads();
+                    double *red = tile;
+                    for (int o = 16; o > 0; o >>= 1) {
+                        se = d_add(se, __shfl_xor_sync(0xffffffffu, se, o));
+                        sa = d_add(sa, __shfl_xor_sync(0xffffffffu, sa, o));
+                    }
+                    const int w = tid >> 5, nw = nthr >> 5;
+                    if ((tid & 31) == 0) { red[2 * w] = se; red[2 * w + 1] = sa; }
+                    __syncthreads();
+                    if (tid == 0) {
+                        double s0 = 0.0, s1 = 0.0;
+                        for (int i = 0; i < nw; ++i) { s0 = d_add(s0, red[2 * i]); s1 = d_add(s1, red[2 * i + 1]); }
+                        a.err_partial[2 * t] = s0;
+                        a.err_partial[2 * t + 1] = s1;
+                    }
+                }
+                break;
+            }
+            __syncthreads();
+            prev_p = p;
+        }
+        __syncthreads();   // this tile buffer is refilled two tiles later
     }
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
 }
 
 // Fixed-order sum of per-CTA partial pairs -> err[0..1].
@@ -180,19 +280,30 @@ __global__ void sum_pairs_kernel(const double *part, int64_t count, double *err)
     if (threadIdx.x == 0) { err[0] = s0[0]; err[1] = s1[0]; }
 }
 
+// pre[e] = colscale[e] * signs[e] for e < n0, signs[e] beyond (exact products)
+__global__ void prescale_kernel(const double *colscale, const double *signs, int64_t n0, int64_t n, double *pre) {
+    for (int64_t e = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; e < n; e += int64_t(gridDim.x) * blockDim.x)
+        pre[e] = (colscale && e < n0) ? d_mul(colscale[e], signs[e]) : signs[e];
+}
+
 template <typename TIn, typename TOut, int MODE>
 int launch_rht(const RhtArgs &a, cudaStream_t st) {
     const int NB = a.b > 12 ? a.b : 12;
     const int nthr = 1 << (NB - 4);
     const int rows_per_tile = 1 << (NB - a.b);
-    const int64_t grid = (a.rows + rows_per_tile - 1) / rows_per_tile;
-    const size_t smem = sizeof(double) << NB;
-    // 16 fp64 values per thread: keep the 128-register budget for tiles up to
-    // 2^13 elements; 2^14-element tiles need 1024 threads (64 registers).
-    auto kern = nthr <= 512 ? rht_tile_kernel<TIn, TOut, MODE, 512> : rht_tile_kernel<TIn, TOut, MODE, 1024>;
+    const int64_t ntiles = (a.rows + rows_per_tile - 1) / rows_per_tile;
+    const size_t tile_bytes = sizeof(double) << NB;
+    // double-buffer the staged tile when two fit next to each other
+    const int dbuf = 2 * tile_bytes <= 160 * 1024 ? 1 : 0;
+    const size_t smem = tile_bytes * (dbuf ? 2 : 1);
+    // 16 fp64 values per thread; 256-thread tiles (n <= 4096) run 3 CTAs per SM
+    auto kern = nthr <= 256 ? rht_tile_kernel<TIn, TOut, MODE, 256, 3>
+              : (nthr <= 512 ? rht_tile_kernel<TIn, TOut, MODE, 512, 1> : rht_tile_kernel<TIn, TOut, MODE, 1024, 1>);
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess)
         return uq::check_cuda("rht: set smem attribute");
-    if (grid > 0) { uq::ProfScope _p("rht", st); kern<<<unsigned(grid), nthr, smem, st>>>(a); }
+    const int per_sm = nthr <= 256 ? 3 : 1;
+    const int64_t grid = std::min<int64_t>(ntiles, int64_t(uq::num_sms()) * per_sm);
+    if (grid > 0) { uq::ProfScope _p("rht", st); kern<<<unsigned(grid), nthr, smem, st>>>(a, dbuf); }
     return uq::check_cuda("rht_tile_kernel launch");
 }
 
@@ -201,14 +312,16 @@ int launch_rht(const RhtArgs &a, cudaStream_t st) {
 namespace uq {
 
 // Forward RHT with optional column pre-scale; output fp64 or fp32.
+// pre: colscale * signs (n values) when colscale is given, else nullptr.
 int rht_forward(const void *in, int in_dtype, int64_t rows, int64_t n0, int64_t ld_in,
-                const double *colscale, const double *signs, void *out, int out_dtype,
+                const double *colscale, const double *pre, const double *signs, void *out, int out_dtype,
                 int64_t ld_out, cudaStream_t st) {
     RhtArgs a{};
     a.in = in; a.rows = rows; a.n0 = n0; a.ld_in = ld_in;
     const int64_t n = uq_next_pow2(n0);
     a.b = ilog2(n);
-    a.signs = signs; a.colscale = colscale; a.out = out;
+    if (colscale && !pre) return fail(UQ_ERR_INVALID, "rht: colscale needs its prescale vector");
+    a.signs = signs; a.colscale = colscale; a.pre = colscale ? pre : signs; a.out = out;
     a.ld_out = ld_out; a.ncols_out = n;
     a.sqrt_n = sqrt(double(n)); a.n_d = double(n);
     if (a.b > kMaxBits) return fail(UQ_ERR_UNSUPPORTED, "rht: n = %lld > 16384 not built", (long long)n);
@@ -221,13 +334,14 @@ int rht_forward(const void *in, int in_dtype, int64_t rows, int64_t n0, int64_t 
 
 // Inverse RHT with optional column post-division and error statistics.
 int rht_inverse(const void *in, int in_dtype, int64_t rows, int64_t n, int64_t ld_in,
-                int64_t n0, const double *signs, const double *colscale, void *out,
+                int64_t n0, const double *signs, const double *colscale, const double *pre, void *out,
                 int out_dtype, int64_t ld_out, const void *ref_w, int ref_dtype,
                 int64_t ld_w, double *err_partial, double *err, cudaStream_t st) {
     RhtArgs a{};
     a.in = in; a.rows = rows; a.n0 = n; a.ld_in = ld_in;
     a.b = ilog2(n);
-    a.signs = signs; a.colscale = colscale; a.out = out;
+    if (colscale && !pre) return fail(UQ_ERR_INVALID, "irht: colscale needs its prescale vector");
+    a.signs = signs; a.colscale = colscale; a.pre = pre; a.out = out;
     a.ld_out = ld_out; a.ncols_out = n0;
     a.sqrt_n = sqrt(double(n)); a.n_d = double(n);
     a.ref_w = ref_w; a.ref_dtype = ref_dtype; a.ld_w = ld_w; a.err_partial = err ? err_partial : nullptr;
@@ -243,6 +357,12 @@ int rht_inverse(const void *in, int in_dtype, int64_t rows, int64_t n, int64_t l
     const int64_t tiles = (rows + (1 << (NB - a.b)) - 1) >> (NB - a.b);
     { uq::ProfScope _p("sum_pairs", st); sum_pairs_kernel<<<1, 256, 0, st>>>(err_partial, tiles, err); }
     return check_cuda("sum_pairs_kernel launch");
+}
+
+int rht_prescale(const double *colscale, const double *signs, int64_t n0, int64_t n, double *pre, cudaStream_t st) {
+    const int grid = int(std::max<int64_t>(1, std::min<int64_t>((n + 255) / 256, 1024)));
+    { ProfScope _p("prescale", st); prescale_kernel<<<grid, 256, 0, st>>>(colscale, signs, n0, n, pre); }
+    return check_cuda("prescale_kernel launch");
 }
 
 int64_t rht_tiles(int64_t rows, int64_t n) {
@@ -263,7 +383,7 @@ int uq_rht_rows(const void *A, int a_dtype, int64_t rows, int64_t n0, int64_t ld
     if (rows == 0) return UQ_OK;
     if (!A || !signs || !out) return uq::fail(UQ_ERR_INVALID, "uq_rht_rows: null pointer");
     const int64_t n = uq_next_pow2(n0);
-    return uq::rht_forward(A, a_dtype, rows, n0, lda, nullptr, signs, out, UQ_F64, n, UQ_STREAM(stream));
+    return uq::rht_forward(A, a_dtype, rows, n0, lda, nullptr, nullptr, signs, out, UQ_F64, n, UQ_STREAM(stream));
 }
 
 int uq_irht_rows(const void *X, int x_dtype, int64_t rows, int64_t n, int64_t ldx, int64_t n0,
@@ -273,7 +393,7 @@ int uq_irht_rows(const void *X, int x_dtype, int64_t rows, int64_t n, int64_t ld
                         (long long)rows, (long long)n, (long long)n0);
     if (rows == 0 || n0 == 0) return UQ_OK;
     if (!X || !signs || !out) return uq::fail(UQ_ERR_INVALID, "uq_irht_rows: null pointer");
-    return uq::rht_inverse(X, x_dtype, rows, n, ldx, n0, signs, nullptr, out, UQ_F64, n0,
+    return uq::rht_inverse(X, x_dtype, rows, n, ldx, n0, signs, nullptr, nullptr, out, UQ_F64, n0,
                            nullptr, 0, 0, nullptr, nullptr, UQ_STREAM(stream));
 }
 

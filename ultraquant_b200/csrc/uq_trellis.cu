@@ -149,7 +149,82 @@ __global__ void normalize_kernel(NormArgs a) {
     }
 }
 
+// Flat mode, power-of-two groups <= 256: warp per groups, registers only.
+template <typename TIn, int G>
+__global__ void __launch_bounds__(256) normalize_warp_kernel(NormArgs a) {
+    using W = WarpGroup<G>;
+    const int lane = threadIdx.x & 31;
+    const int64_t warp = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const int64_t e_base = warp * W::GPW * int64_t(G);
+    const TIn *A = static_cast<const TIn *>(a.A);
+    const int64_t ntot = a.T;       // valid elements; a.Tp = padded total
+    auto get = [&](int i) -> float {
+        const int64_t e = e_base + i;
+        return e < ntot ? float(__ldg(A + e)) : 0.f;
+    };
+    const float ss = warp_group_sumsq<G, float>(get);
+    const float sc = __fadd_rn(sqrtf(ss / float(G)), 1e-12f);
+    if ((lane % W::LPG) == 0) {
+        const int64_t g = e_base / G + lane / W::LPG;
+        if (g * G < a.Tp) a.sc[g] = sc;
+    }
+    for (int vb = 0; vb < W::VPW; vb += 32) {
+        const int vv = vb + lane;
+        const int gg = (vv < W::VPW ? vv : W::VPW - 1) / W::VPG;
+        const float s = __shfl_sync(0xffffffffu, sc, gg * W::LPG);
+        if (vv >= W::VPW) continue;
+        const int64_t e0 = e_base + 8 * int64_t(vv);
+        if (e0 >= a.Tp) continue;
+        float x[8];
+        if (sizeof(TIn) == 4 && e0 + 8 <= ntot && ((reinterpret_cast<uintptr_t>(A + e0) & 15) == 0)) {
+            const float4 *q = reinterpret_cast<const float4 *>(A + e0);
+            const float4 t0 = __ldg(q), t1 = __ldg(q + 1);
+            x[0] = t0.x; x[1] = t0.y; x[2] = t0.z; x[3] = t0.w; x[4] = t1.x; x[5] = t1.y; x[6] = t1.z; x[7] = t1.w;
+        } else {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) x[i] = e0 + i < ntot ? float(__ldg(A + e0 + i)) : 0.f;
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i) x[i] = x[i] / s;
+        if (e0 + 8 <= a.Tp && ((reinterpret_cast<uintptr_t>(a.xn + e0) & 15) == 0)) {
+            float4 *q = reinterpret_cast<float4 *>(a.xn + e0);
+            q[0] = make_float4(x[0], x[1], x[2], x[3]);
+            q[1] = make_float4(x[4], x[5], x[6], x[7]);
+        } else {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) if (e0 + i < a.Tp) a.xn[e0 + i] = x[i];
+        }
+    }
+}
+
+template <typename TIn, int G>
+int launch_normalize_warp(const NormArgs &a, cudaStream_t st) {
+    using W = WarpGroup<G>;
+    const int64_t groups = a.Tp / G;
+    const int64_t warps = (groups + W::GPW - 1) / W::GPW;
+    const int64_t blocks = (warps + 7) / 8;
+    if (blocks > 0) { uq::ProfScope _p("normalize", st); normalize_warp_kernel<TIn, G><<<unsigned(blocks), 256, 0, st>>>(a); }
+    return uq::check_cuda("normalize_warp_kernel launch");
+}
+
+template <typename TIn>
+int dispatch_normalize_warp(const NormArgs &a, cudaStream_t st) {
+    switch (a.group) {
+        case 8: return launch_normalize_warp<TIn, 8>(a, st);
+        case 16: return launch_normalize_warp<TIn, 16>(a, st);
+        case 32: return launch_normalize_warp<TIn, 32>(a, st);
+        case 64: return launch_normalize_warp<TIn, 64>(a, st);
+        case 128: return launch_normalize_warp<TIn, 128>(a, st);
+        case 256: return launch_normalize_warp<TIn, 256>(a, st);
+    }
+    return -1;
+}
+
 int launch_normalize(NormArgs a, cudaStream_t st) {
+    if (a.nrow == 1) {   // flat mode (trellis.py:69-80)
+        const int rc = a.dtype == UQ_F32 ? dispatch_normalize_warp<float>(a, st) : dispatch_normalize_warp<double>(a, st);
+        if (rc >= 0) return rc;
+    }
     int t = a.group;
     while (t < 2048) t += a.group;
     a.tile = t;
