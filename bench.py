@@ -160,6 +160,64 @@ def run_reference(args, rank: int, world: int):
     print(json.dumps(line), flush=True)
 
 
+def run_llama8b(args, rank: int, world: int, local: int):
+    """Whole Llama-3.1-8B-shaped weight set (32 x {q, k, v, o 4096/1024 x 4096,
+    gate/up 14336 x 4096, down 4096 x 14336}), Student-t(4) weights with std
+    0.02 and log-normal imatrix, trellis L=16 T=256 with k=3 on ffn_down /
+    attn_q / attn_output and k=2 elsewhere, sharded by tensor and row block
+    (strong scaling: the set is fixed).  Weights are generated on the device
+    before the timed region."""
+    import torch
+    import torch.distributed as dist
+    from ultraquant_b200 import pipeline, shard
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=1800), device_id=dev)
+    specs = shard.llama_shapes(layers=args.layers)
+    plan = [s for s in shard.plan(specs, world) if s.rank == rank]
+    data = []
+    for sh in plan:
+        g = torch.Generator(device=dev)
+        g.manual_seed(sum(map(ord, sh.tensor.name)) * 1000 + sh.row0)
+        z = torch.randn((sh.rows, sh.tensor.cols), generator=g, device=dev)
+        chi = torch.randn((4, sh.rows, sh.tensor.cols), generator=g, device=dev).pow_(2).sum(0)
+        W = (z / torch.sqrt(chi / 4.0) / (2.0 ** 0.5) * 0.02).float()
+        gh = torch.Generator(device=dev)
+        gh.manual_seed(sum(map(ord, sh.tensor.name)))
+        H = torch.exp(torch.randn(sh.tensor.cols, generator=gh, device=dev, dtype=torch.float64))
+        data.append((sh, W, H))
+        del z, chi
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    results = []
+    for sh, W, H in data:
+        r = pipeline.quant_trellis_device(W, H, L=16, R=sh.tensor.R, seg=SEG, scale_group=GROUP, keep_codes=False)
+        results.append(shard.ShardResult(sh, r.What, r.err))
+    e1.record()
+    torch.cuda.synchronize()
+    ms = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+    wn = shard.gather_errors(results, specs)
+    weights = sum(s.rows * s.cols for s in specs)
+    if rank == 0:
+        line = {"metric": "Llama-3.1-8B-shaped weight set trellis-quantized, wall time on device",
+                "value": float(ms.item()) / 1e3, "unit": "s", "n_gpus": world, "steps": 1, "warmup": 0,
+                "higher_is_better": False, "scaling": "strong", "weights": weights,
+                "weights_per_s": weights / (float(ms.item()) / 1e3), "layers": args.layers,
+                "wnmse_mean": {k: sum(v for n, v in wn.items() if f".{k}." in n) / max(1, sum(1 for n in wn if f".{k}." in n))
+                               for k in ("attn_q", "attn_k", "attn_v", "attn_output", "ffn_gate", "ffn_up", "ffn_down")},
+                "dtype": "f32", "data": "synthetic"}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
 def workload_config(world: int):
     return {
         "workload": ("4096x4096 f32 N(0,0.02^2)+0.1% 8-sigma outliers (seed=rank), lognormal(0,1) imatrix; "
@@ -181,6 +239,10 @@ def main():
     ap.add_argument("--cpu-rows", type=int, default=8, help="rows of the CPU baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--workload", default="tensor", choices=["tensor", "llama8b"],
+                    help="tensor: the 4096x4096 L=16 k=2+3 step (default); llama8b: the whole "
+                         "Llama-3.1-8B-shaped weight set sharded over the ranks (one step)")
+    ap.add_argument("--layers", type=int, default=32, help="layers of the llama8b workload")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -189,6 +251,8 @@ def main():
 
     if args.impl == "reference":
         return run_reference(args, rank, world)
+    if args.workload == "llama8b":
+        return run_llama8b(args, rank, world, local)
 
     import numpy as np
     import torch

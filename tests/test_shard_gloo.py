@@ -1,0 +1,133 @@
+"""Host-side multi-GPU logic on CPU: the sharding plan, and the exchange steps
+(per-tensor error all-gather, row-block assembly) on world_size-2 gloo ranks.
+The per-shard quantizer here is the CPU oracle (the device pipelines are
+covered by the GPU tests); failures are injected on the host."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+import oracle as O
+from ultraquant_b200 import shard as S
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+@pytest.mark.parametrize("world", [1, 2, 4, 8])
+def test_plan_covers_every_row_once_and_balances(world):
+    specs = S.llama_shapes(layers=32)
+    shards = S.plan(specs, world)
+    cover = {}
+    for sh in shards:
+        cover.setdefault(sh.tensor.name, []).append((sh.row0, sh.row1))
+    for spec in specs:
+        spans = sorted(cover[spec.name])
+        assert spans[0][0] == 0 and spans[-1][1] == spec.rows
+        assert all(a[1] == b[0] for a, b in zip(spans, spans[1:]))
+    load = [0.0] * world
+    for sh in shards:
+        load[sh.rank] += sh.tensor.cost(sh.rows)
+    assert max(load) / min(load) < 1.01
+    # deterministic
+    assert [(s.tensor.name, s.row0, s.rank) for s in S.plan(specs, world)] == \
+           [(s.tensor.name, s.row0, s.rank) for s in shards]
+
+
+def test_llama_shapes_match_the_model():
+    specs = S.llama_shapes(layers=32)
+    assert len(specs) == 224
+    total = sum(s.rows * s.cols for s in specs)
+    assert total == 32 * (2 * 4096 * 4096 + 2 * 1024 * 4096 + 3 * 14336 * 4096)   # 6.98e9 weights
+    padded = sum(s.rows * s.padded_cols for s in specs)
+    assert padded > total and padded == total + 32 * 4096 * (16384 - 14336)
+
+
+SPECS = [S.TensorSpec("t0", 40, 300, L=8, R=2), S.TensorSpec("t1", 24, 256, L=8, R=2),
+         S.TensorSpec("t2", 16, 100, L=8, R=2)]
+
+
+def _weights(spec, r0, r1):
+    rng = np.random.RandomState(sum(map(ord, spec.name)))
+    W = rng.standard_t(4, size=(spec.rows, spec.cols)) * 0.02
+    H = np.exp(rng.normal(0, 1, size=spec.cols))
+    return W[r0:r1], H
+
+
+def _quantize(spec, W, H):
+    """E8 recipe on the CPU oracle: returns What and the error sums."""
+    Hc = np.maximum(H, H.max() * 1e-3)
+    sH = np.sqrt(Hc)[None, :]
+    A = W * sH
+    Ah = O.irht_rows(O.q_e8_fast(O.rht_rows(A), fixed_step=0.48), W.shape[1])
+    err = torch.tensor([np.sum((A - Ah) ** 2), np.sum(A ** 2)], dtype=torch.float64)
+    return torch.from_numpy((Ah / sH).astype(np.float32)), err
+
+
+def _single_process_reference():
+    shards = S.plan(SPECS, 1, block_rows=8)
+    res = S.run_shards(shards, 0, _weights, _quantize)
+    return S.gather_errors(res, SPECS), {s.name: S.assemble_rows(res, s) for s in SPECS}
+
+
+def _worker(rank, world, port, out_dir, mode):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    import datetime
+    import torch.distributed as dist
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=10))
+    try:
+        shards = S.plan(SPECS, world, block_rows=8)
+        if mode == "rank1_dies" and rank == 1:
+            os._exit(3)               # leaves between steps, nothing in flight
+        res = S.run_shards(shards, rank, _weights, _quantize)
+        errs = S.gather_errors(res, SPECS)
+        full = {s.name: S.assemble_rows(res, s, dst_rank=0) for s in SPECS}
+        if rank == 0:
+            torch.save({"errs": errs, "full": full}, os.path.join(out_dir, "r0.pt"))
+    except Exception as e:  # recorded for the failure-detection test
+        with open(os.path.join(out_dir, f"err{rank}.txt"), "w") as f:
+            f.write(type(e).__name__ + ": " + str(e))
+    finally:
+        try:
+            dist.destroy_process_group()
+        except Exception:
+            pass
+
+
+def test_gloo_two_ranks_match_single_process(tmp_path):
+    ref_errs, ref_full = _single_process_reference()
+    mp.start_processes(_worker, args=(2, _free_port(), str(tmp_path), "ok"), nprocs=2, join=True,
+                       start_method="spawn")
+    got = torch.load(tmp_path / "r0.pt")
+    for name, v in ref_errs.items():
+        assert abs(got["errs"][name] - v) <= 1e-12 * v
+    for name, t in ref_full.items():
+        assert torch.equal(got["full"][name], t)
+
+
+def test_gloo_rank_failure_is_reported(tmp_path):
+    """A rank that exits between steps: the survivor's next collective ends
+    with an error within the process-group timeout instead of hanging."""
+    import multiprocessing
+    ctx = multiprocessing.get_context("spawn")
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, str(tmp_path), "rank1_dies")) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=90)
+    alive = [p for p in procs if p.is_alive()]
+    for p in alive:
+        p.kill()
+    assert not alive, "survivor did not notice the failed rank"
+    assert procs[1].exitcode == 3
+    err = (tmp_path / "err0.txt").read_text() if (tmp_path / "err0.txt").exists() else ""
+    assert err, "rank 0 should have seen a collective failure"

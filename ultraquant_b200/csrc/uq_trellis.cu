@@ -274,6 +274,12 @@ __device__ __forceinline__ unsigned sel_bits(unsigned m, unsigned a, unsigned b)
     asm("lop3.b32 %0, %1, %2, %3, 0xCA;" : "=r"(r) : "r"(m), "r"(a), "r"(b));
     return r;
 }
+// insert the low `len` bits of a into b at bit `pos`
+__device__ __forceinline__ unsigned bfi(unsigned a, unsigned b, int pos, int len) {
+    unsigned r;
+    asm("bfi.b32 %0, %1, %2, %3, %4;" : "=r"(r) : "r"(a), "r"(b), "r"(pos), "r"(len));
+    return r;
+}
 // (word << 1) | (src >> 31)
 __device__ __forceinline__ unsigned shift_in_sign(unsigned word, unsigned src) {
     unsigned r;
@@ -510,10 +516,12 @@ struct VitThread {
         const u64 xx = pk2(x, x);
         unsigned word = 0;
         // chunks of 4 new m values (2 pairs) are stored as soon as they are
-        // complete; q are visited in descending order for the word packing
+        // complete; each chunk packs its 4*R decision bits in its own word
+        // (independent shift chains), merged with bit-field inserts
 #pragma unroll
         for (int c4 = NQ / 4 - 1; c4 >= 0; --c4) {
             float mo[4];
+            unsigned cw_bits = 0;
 #pragma unroll
             for (int p = 2 * c4 + 1; p >= 2 * c4; --p) {
                 const int i = (NQ >= K) ? ((2 * p) >> R) : 0;
@@ -528,10 +536,12 @@ struct VitThread {
                 const u64 mn = tourney<R>(c, blo, bhi);
                 up2(mn, mo[2 * (p - 2 * c4)], mo[2 * (p - 2 * c4) + 1]);
 #pragma unroll
-                for (int j = R - 1; j >= 0; --j) word = shift_in_sign(word, bhi[j]);
+                for (int j = R - 1; j >= 0; --j) cw_bits = shift_in_sign(cw_bits, bhi[j]);
 #pragma unroll
-                for (int j = R - 1; j >= 0; --j) word = shift_in_sign(word, blo[j]);
+                for (int j = R - 1; j >= 0; --j) cw_bits = shift_in_sign(cw_bits, blo[j]);
             }
+            if (c4 == NQ / 4 - 1) word = cw_bits << (4 * R * c4);
+            else word = bfi(cw_bits, word, 4 * R * c4, 4 * R);
             const unsigned o = C::FAST ? (wr0 ^ (unsigned(c4) << 4)) : off(NQ * v + 4 * c4);
             sts4(wbase + o - wshift, mo[0], mo[1], mo[2], mo[3]);
         }
