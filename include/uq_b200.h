@@ -165,6 +165,42 @@ int uq_trellis_decode_rows(const int32_t *states, const float *cw, const float *
                            float *out, void *stream);
 
 /* ---------------------------------------------------------------------
+ * Differentiable decoder of the QAT step (qat.py:35-59)
+ * ------------------------------------------------------------------- */
+
+/* qat.py:35-41 fwht_torch / qat.py:43-49 irht_torch, forward (direction 0)
+ * and the gradient torch's autograd forms (direction 1).  x: (rows, ncols_in)
+ * with row stride ldx, dtype UQ_F32 or UQ_F64 (arithmetic in that dtype),
+ * zero-padded to n = 2^k columns (n <= 32768 for f32, <= 16384 for f64).
+ * Forward: out = (FWHT(x) / sqrt(n)) [* signs] [/ colscale], first ncols_out
+ * columns.  Backward: x is the incoming gradient; out = FWHT^T(((x
+ * [/ colscale]) [* signs]) / sqrt(n)) with the stages in reverse order.
+ * signs (n) and colscale (ncols) are optional, in the same dtype. */
+int uq_fwht(const void *x, int dtype, int64_t rows, int64_t n, int64_t ldx, int64_t ncols_in,
+            const void *signs, const void *colscale, int direction, void *out, int64_t ld_out,
+            int64_t ncols_out, void *stream);
+
+/* qat.py:51-59 recon_torch: What = irht_torch(cw[states] * sc_g) / sH.
+ * states: nrow * n values (int32, or int64 when states64), the flattened
+ * rotated matrix (nrow, n); sc: one float per scale_group consecutive
+ * values; signs: n floats (+-1); sH: in0 floats (nullable = 1); out (nrow,
+ * in0) with row stride ld_out, float32.  A state outside [0, ncw) yields NaN
+ * and is reported by uq_device_errors. */
+int uq_qat_recon(const void *states, int states64, int64_t nrow, int64_t n, const float *cw,
+                 int64_t ncw, const float *sc, int64_t scale_group, const float *signs,
+                 const float *sH, int64_t in0, float *out, int64_t ld_out, void *stream);
+
+/* Gradient of recon_torch with respect to cw (ncw floats) and sc_g (ngroups
+ * floats) for the incoming gradient grad (nrow, in0), stride ld_grad. */
+size_t uq_qat_recon_backward_workspace_bytes(int64_t ncw, int64_t ngroups);
+int uq_qat_recon_backward(const float *grad, int64_t ld_grad, const void *states, int states64,
+                          int64_t nrow, int64_t n, const float *cw, int64_t ncw,
+                          const float *sc, int64_t ngroups, int64_t scale_group,
+                          const float *signs, const float *sH, int64_t in0, float *grad_cw,
+                          float *grad_sc, void *workspace, size_t workspace_bytes,
+                          void *stream);
+
+/* ---------------------------------------------------------------------
  * Importance-weighted pipelines (builder recipes around the path)
  * ------------------------------------------------------------------- */
 
@@ -198,8 +234,9 @@ int uq_quant_e8(const void *W, int w_dtype, int64_t rows, int64_t n0, int64_t ld
  * ------------------------------------------------------------------- */
 
 /* Synchronises `stream` and reports (and clears) a timeout of a bounded
- * device wait in the cluster-split Viterbi kernel: UQ_ERR_TIMEOUT if one
- * occurred since the last call, else UQ_OK. */
+ * device wait in the cluster-split Viterbi kernel (UQ_ERR_TIMEOUT) or a
+ * state outside the codebook given to the QAT decoder (UQ_ERR_INVALID)
+ * since the last call; else UQ_OK. */
 int uq_device_errors(void *stream);
 
 /* Runs a one-warp kernel that waits on an mbarrier phase nothing completes;

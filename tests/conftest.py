@@ -40,6 +40,28 @@ def g_pipeline():
     return load_golden("golden_pipeline.npz")
 
 
+@pytest.fixture(scope="session")
+def g_qat():
+    return load_golden("golden_qat.npz")
+
+
+def qat_meta(g, key):
+    vals = [int(v) for v in g[key + "_meta"]]
+    meta = dict(zip(("nrow", "ncol", "Ntot", "seg", "scale_group", "pad", "Nseg"), vals[:7]))
+    return meta, vals[7], vals[8]          # meta, L, in0
+
+
+def grad_close(got, ref, exact, rtol=2e-6):
+    """Gradient sums: |got - exact| within one fp32 rounding of the fp64 sum
+    (plus rtol of the norm), and the reference's fp32-accumulated sums within
+    rtol * ||exact|| as well."""
+    got, ref, exact = (np.asarray(v, np.float64) for v in (got, ref, exact))
+    scale = np.abs(exact).max() + 1e-30
+    ok_got = np.all(np.abs(got - exact) <= np.abs(exact) * 2 ** -23 + rtol * scale)
+    ok_ref = np.all(np.abs(ref - exact) <= 1e-4 * scale)
+    return bool(ok_got and ok_ref)
+
+
 def same_bits(a, b):
     """Bit-for-bit equality of two float arrays (signed zeros included)."""
     a = np.ascontiguousarray(a)

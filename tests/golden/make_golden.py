@@ -7,7 +7,7 @@ and outputs in ``tests/golden/*.npz``.  The reference has no test suite and no
 committed golden vectors; these fixtures pin the oracle and the CUDA path.
 
 Usage (in a container that has the reference checkout):
-    python tests/golden/make_golden.py [/path/to/reference]
+    python tests/golden/make_golden.py [/path/to/reference [rht e8 trellis pipeline qat]]
 
 The reference directory defaults to /root/reference.  Nothing at test or bench
 time reads the reference; only this generator does.
@@ -195,12 +195,71 @@ def make_pipeline(qlab, trellis, qat):
     np.savez_compressed(os.path.join(HERE, "golden_pipeline.npz"), **out)
 
 
+def make_qat(qlab, qat):
+    """qat.py:35-59: fwht_torch / irht_torch / recon_torch values and the
+    gradients torch's autograd gives for loss = sum(out * U)."""
+    import torch
+    rng = np.random.RandomState(15)
+    out = {"versions": _versions()}
+
+    def grads(fn, x, shape_out):
+        x = x.clone().requires_grad_(True)
+        y = fn(x)
+        U = torch.from_numpy(rng.normal(size=shape_out).astype(np.float32)).to(x.dtype)
+        (y * U).sum().backward()
+        return y.detach().numpy(), U.numpy(), x.grad.numpy()
+
+    for dt in ("f32", "f64"):
+        tdt = torch.float32 if dt == "f32" else torch.float64
+        for n in (1, 2, 8, 32, 256, 512, 4096, 8192):
+            rows = 3 if n <= 512 else 1
+            x = torch.from_numpy(rng.normal(size=(rows, n))).to(tdt)
+            y, U, g = grads(qat.fwht_torch, x, (rows, n))
+            out[f"fwht_{dt}_{n}_x"], out[f"fwht_{dt}_{n}_y"] = x.numpy(), y
+            out[f"fwht_{dt}_{n}_U"], out[f"fwht_{dt}_{n}_gx"] = U, g
+        for n, in0 in ((512, 300), (4096, 4096), (4096, 2999), (16384, 14336)):
+            if n == 16384 and dt == "f64":
+                continue
+            rows = 1 if n >= 4096 else 4
+            x = torch.from_numpy(rng.normal(size=(rows, n))).to(tdt)
+            y, U, g = grads(lambda t: qat.irht_torch(t, in0), x, (rows, in0))
+            key = f"irht_{dt}_{n}_{in0}"
+            out[key + "_x"], out[key + "_y"], out[key + "_U"], out[key + "_gx"] = x.numpy(), y, U, g
+    # recon_torch from the reference encoder (fixed states), forward and
+    # gradients with respect to cw and sc_g
+    cases = [("a", 8, 300, 8, 2, 64), ("b", 3, 128, 6, 2, 64), ("c", 16, 1000, 10, 3, 256)]
+    for tag, rows, n0, L, R, seg in cases:
+        W = student_t(rng, (rows, n0), std=0.02)
+        H = np.exp(rng.normal(0.0, 1.0, size=n0))
+        Hc = np.maximum(H, H.max() * 1e-3)
+        sH = np.sqrt(Hc)[None, :]
+        A = qlab.rht_rows(W * sH).astype(np.float32)
+        st, sc_g, cwn, meta = qat.trellis_encode(A, L=L, R=R, seg=seg, scale_group=256)
+        cw = torch.tensor(cwn, requires_grad=True)
+        scg = torch.tensor(sc_g, requires_grad=True)
+        sH_t = torch.tensor(sH, dtype=torch.float32)
+        Wh = qat.recon_torch(st, cw, scg, meta, sH_t, n0)
+        U = torch.from_numpy(rng.normal(size=Wh.shape).astype(np.float32))
+        (Wh * U).sum().backward()
+        key = f"recon_{tag}"
+        out[key + "_states"], out[key + "_scg"], out[key + "_sH"] = st, sc_g, sH.astype(np.float32)
+        out[key + "_meta"] = np.array([meta[k] for k in ("nrow", "ncol", "Ntot", "seg", "scale_group",
+                                                         "pad", "Nseg")] + [L, n0])
+        out[key + "_What"], out[key + "_U"] = Wh.detach().numpy(), U.numpy()
+        out[key + "_gcw"], out[key + "_gsc"] = cw.grad.numpy(), scg.grad.numpy()
+    np.savez_compressed(os.path.join(HERE, "golden_qat.npz"), **out)
+
+
+MAKERS = {"rht": lambda m: make_rht(m[0]), "e8": lambda m: make_e8(m[0]),
+          "trellis": lambda m: make_trellis(m[1], m[2]), "pipeline": lambda m: make_pipeline(*m),
+          "qat": lambda m: make_qat(m[0], m[2])}
+
+
 def main():
-    qlab, trellis, qat = _import_reference()
-    make_rht(qlab)
-    make_e8(qlab)
-    make_trellis(trellis, qat)
-    make_pipeline(qlab, trellis, qat)
+    mods = _import_reference()
+    which = sys.argv[2:] or list(MAKERS)
+    for name in which:
+        MAKERS[name](mods)
     for f in sorted(os.listdir(HERE)):
         if f.endswith(".npz"):
             print(f, os.path.getsize(os.path.join(HERE, f)))

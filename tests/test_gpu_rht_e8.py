@@ -28,7 +28,7 @@ def test_rht_golden(uq, g_rht, tag):
 
 
 @pytest.mark.parametrize("rows,n0", [(1, 2), (3, 17), (7, 255), (5, 256), (9, 4095), (2, 8191), (3, 8192),
-                                     (4, 12000), (2, 16384), (33, 64)])
+                                     (4, 12000), (2, 16384), (33, 64), (3, 16385), (2, 28672), (5, 32768)])
 def test_rht_random_vs_oracle(uq, rows, n0):
     rng = np.random.RandomState(rows * 1000 + n0)
     A = rng.standard_t(4, size=(rows, n0)) * 0.02
@@ -37,6 +37,41 @@ def test_rht_random_vs_oracle(uq, rows, n0):
     assert same_bits(uq.irht_rows(X, n0), O.irht_rows(X, n0))
     X32 = X.astype(np.float32)
     assert same_bits(uq.irht_rows(X32, n0), O.irht_rows(X32, n0))
+
+
+def test_rht_70b_width(uq):
+    """Llama-70B ffn_down width 28672 -> 32768 (row split over a 2-CTA
+    cluster): f32 and f64 inputs, forward and inverse, many rows so that every
+    cluster walks several rows; bit-exact against the oracle."""
+    rng = np.random.RandomState(70)
+    A = rng.standard_t(4, size=(300, 28672)) * 0.02
+    X = uq.rht_rows(A)
+    pick = [0, 1, 149, 298, 299]
+    assert same_bits(X[pick], O.rht_rows(A[pick]))
+    A32 = A.astype(np.float32)
+    assert same_bits(uq.rht_rows(A32)[pick], O.rht_rows(A32[pick]))
+    assert same_bits(uq.irht_rows(X, 28672)[pick], O.irht_rows(X[pick], 28672))
+    X32 = X.astype(np.float32)
+    assert same_bits(uq.irht_rows(X32, 28672)[pick], O.irht_rows(X32[pick], 28672))
+
+
+def test_pipelines_70b_width():
+    """The importance-weighted recipes at the 28672 width (E8 at 0.48 and the
+    trellis at L = 12): What bit-exact, weighted NMSE within 1e-5 relative."""
+    import torch
+    from ultraquant_b200 import pipeline as P
+    rng = np.random.RandomState(71)
+    W = (rng.standard_t(4, size=(3, 28672)) * 0.015).astype(np.float32)
+    H = np.exp(rng.normal(0.0, 1.0, size=28672))
+    assert same_bits(P.quant_step(W, H, 0.48), O.quant_step(W.astype(np.float64), H, 0.48))
+    res = P.quant_trellis_device(torch.from_numpy(W).cuda(), torch.from_numpy(H).cuda(), 12, 2, 256, 256)
+    ref = O.quant_trellis(W.astype(np.float64), H, L=12, R=2, seg=256)
+    assert same_bits(res.What.cpu().numpy(), ref)
+    Hc = np.maximum(H, H.max() * 1e-3)
+    A = W.astype(np.float64) * np.sqrt(Hc)[None, :]
+    Ah = O.irht_rows(O.trellis_quant_fast(O.rht_rows(A), L=12, R=2, seg=256), 28672)
+    w = O.wnmse(A, Ah)
+    assert abs(res.wnmse - w) <= 1e-5 * w
 
 
 def test_rht_full_size_roundtrip(uq):

@@ -140,6 +140,8 @@ def test_install_patches_reference_modules(tmp_path, monkeypatch):
     assert rht_rows is Q.rht_rows and load_WH("x") == "x"
     A = np.random.RandomState(0).randn(3, 100)
     assert same_bits(mods["qlab"].rht_rows(A), O.rht_rows(A))
+    import ultraquant_b200.qat as Qat
+    assert mods["qat"].recon_torch is Qat.recon_torch and mods["qat"].fwht_torch is Qat.fwht_torch
     for name in ("qlab", "trellis", "qat"):
         sys.modules.pop(name, None)
 

@@ -109,3 +109,74 @@ def test_pipelines(g_pipeline):
     Wh = O.recon_torch(st, torch.tensor(cwn), torch.tensor(sc_g), meta,
                        torch.tensor(sH, dtype=torch.float32), 300)
     assert same_bits(Wh.numpy(), g_pipeline["qat_recon"])
+
+
+# ---------------------------------------------------------------------------
+# qat.py:35-59 decoder: forward values and autograd gradients
+# ---------------------------------------------------------------------------
+def _fwd_bwd(fn, x, U):
+    import torch
+    x = torch.from_numpy(x).clone().requires_grad_(True)
+    y = fn(x)
+    (y * torch.from_numpy(U)).sum().backward()
+    return y.detach().numpy(), x.grad.numpy()
+
+
+@pytest.mark.parametrize("dt", ["f32", "f64"])
+def test_fwht_irht_torch(g_qat, dt):
+    for n in (1, 2, 8, 32, 256, 512, 4096, 8192):
+        k = f"fwht_{dt}_{n}"
+        y, gx = _fwd_bwd(O.fwht_torch, g_qat[k + "_x"], g_qat[k + "_U"])
+        assert same_bits(y, g_qat[k + "_y"]) and same_bits(gx, g_qat[k + "_gx"]), k
+    for n, in0 in ((512, 300), (4096, 4096), (4096, 2999), (16384, 14336)):
+        k = f"irht_{dt}_{n}_{in0}"
+        if k + "_x" not in g_qat:
+            continue
+        y, gx = _fwd_bwd(lambda t: O.irht_torch(t, in0), g_qat[k + "_x"], g_qat[k + "_U"])
+        assert same_bits(y, g_qat[k + "_y"]) and same_bits(gx, g_qat[k + "_gx"]), k
+
+
+def recon_exact_grads(states, cw, scg, U, meta, sH, in0):
+    """fp64 restatement of the recon_torch gradients: the per-element chain
+    in the tensor dtype (as torch's autograd), the two sums exact in fp64."""
+    import torch
+    n = meta["ncol"]
+    g = torch.from_numpy(U) / torch.from_numpy(sH.reshape(1, -1))
+    g = torch.nn.functional.pad(g, (0, n - in0))
+    g = g * torch.tensor(O.rht_signs(n), dtype=torch.float32)
+    g = g / float(np.float32(np.sqrt(n)))
+    h = n // 2
+    while h >= 1:     # adjoint butterflies, reverse stage order
+        v = g.reshape(-1, n // (2 * h), 2, h)
+        g = torch.cat([v[:, :, 0, :] + v[:, :, 1, :], v[:, :, 0, :] - v[:, :, 1, :]], dim=2).reshape(-1, n)
+        h //= 2
+    grec = g.reshape(-1).numpy()
+    st = np.asarray(states).reshape(-1)[: grec.size].astype(np.int64)
+    grp = np.arange(grec.size) // meta["scale_group"]
+    sc = np.asarray(scg, np.float32).reshape(-1)
+    t_cw = (grec * sc[grp]).astype(np.float32).astype(np.float64)
+    t_sc = (grec * cw[st]).astype(np.float32).astype(np.float64)
+    gcw = np.zeros(cw.size)
+    np.add.at(gcw, st, t_cw)
+    gsc = np.zeros(sc.size)
+    np.add.at(gsc, grp, t_sc)
+    return gcw, gsc
+
+
+@pytest.mark.parametrize("tag", ["a", "b", "c"])
+def test_recon_torch(g_qat, tag):
+    import torch
+    from conftest import grad_close, qat_meta
+    k = f"recon_{tag}"
+    meta, L, in0 = qat_meta(g_qat, k)
+    cw = torch.tensor(O.codebook(L), requires_grad=True)
+    scg = torch.tensor(g_qat[k + "_scg"], requires_grad=True)
+    Wh = O.recon_torch(g_qat[k + "_states"], cw, scg, meta, torch.from_numpy(g_qat[k + "_sH"]), in0)
+    assert same_bits(Wh.detach().numpy(), g_qat[k + "_What"])
+    (Wh * torch.from_numpy(g_qat[k + "_U"])).sum().backward()
+    assert same_bits(cw.grad.numpy(), g_qat[k + "_gcw"]) and same_bits(scg.grad.numpy(), g_qat[k + "_gsc"])
+    # the adjoint chain restated in fp64 sums agrees with torch's fp32 sums
+    gcw, gsc = recon_exact_grads(g_qat[k + "_states"], O.codebook(L), g_qat[k + "_scg"], g_qat[k + "_U"],
+                                 meta, g_qat[k + "_sH"], in0)
+    assert grad_close(gcw.astype(np.float32), g_qat[k + "_gcw"], gcw)
+    assert grad_close(gsc.astype(np.float32), g_qat[k + "_gsc"].reshape(-1), gsc)

@@ -4,7 +4,7 @@ Modules mirror the reference's interfaces:
 
 * ``ultraquant_b200.qlab``     -- rht_rows, irht_rows, e8_decode, q_e8_fast, ...
 * ``ultraquant_b200.trellis``  -- codebook, trellis_quant, trellis_quant_fast
-* ``ultraquant_b200.qat``      -- trellis_encode
+* ``ultraquant_b200.qat``      -- trellis_encode, fwht_torch, irht_torch, recon_torch
 * ``ultraquant_b200.pipeline`` -- the builders' importance-weighted recipes
 * ``ultraquant_b200.shard``    -- row-block sharding over torch.distributed ranks
 
@@ -26,7 +26,7 @@ _PATCH = {
     "qlab": ("_next_pow2", "rht_rows", "irht_rows", "_d8_decode", "e8_decode", "_entropy_bpw",
              "q_e8_fast", "wnmse"),
     "trellis": ("codebook", "pred_table", "trellis_quant", "trellis_quant_fast"),
-    "qat": ("trellis_encode",),
+    "qat": ("trellis_encode", "fwht_torch", "irht_torch", "recon_torch"),
 }
 
 

@@ -47,6 +47,11 @@ SIGNATURES = {
     "uq_trellis_viterbi_noalloc": (_i32, [_p, _i64, _i32, _i32, _i32, _p, _p, _p]),
     "uq_trellis_decode": (_i32, [_p, _p, _p, _i64, _i64, _p, _p]),
     "uq_trellis_decode_rows": (_i32, [_p, _p, _p, _i64, _i64, _i64, _i64, _p, _p]),
+    "uq_fwht": (_i32, [_p, _i32, _i64, _i64, _i64, _i64, _p, _p, _i32, _p, _i64, _i64, _p]),
+    "uq_qat_recon": (_i32, [_p, _i32, _i64, _i64, _p, _i64, _p, _i64, _p, _p, _i64, _p, _i64, _p]),
+    "uq_qat_recon_backward_workspace_bytes": (_sz, [_i64, _i64]),
+    "uq_qat_recon_backward": (_i32, [_p, _i64, _p, _i32, _i64, _i64, _p, _i64, _p, _i64, _i64, _p, _p,
+                                     _i64, _p, _p, _p, _sz, _p]),
     "uq_quant_trellis_workspace_bytes": (_sz, [_i64, _i64, _i32, _i32, _i32, _i32]),
     "uq_quant_trellis": (_i32, [_p, _i32, _i64, _i64, _i64, _p, _i32, _i32, _i32, _i32, _p, _p, _p, _p,
                                 _p, _p, _p, _sz, _p]),

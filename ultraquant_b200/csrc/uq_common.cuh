@@ -19,6 +19,7 @@ inline bool is_pow2(int64_t n) { return n > 0 && (n & (n - 1)) == 0; }
 inline int ilog2(int64_t n) { int b = 0; while ((int64_t(1) << b) < n) ++b; return b; }
 inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 int num_sms();
+int qat_take_bad_state();   // uq_qat.cu
 
 // Launch accounting / optional per-launch event timing (see uq_profile_*).
 void count_launch();

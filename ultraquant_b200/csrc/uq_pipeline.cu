@@ -92,7 +92,7 @@ int check_common(int64_t rows, int64_t n0, int64_t ldw, int w_dtype, int group, 
     if (rows < 0 || n0 < 1 || ldw < n0 || !uq::dtype_size(w_dtype))
         return uq::fail(UQ_ERR_INVALID, "%s: bad shape (rows=%lld n0=%lld ldw=%lld)", who, (long long)rows,
                         (long long)n0, (long long)ldw);
-    if (uq_next_pow2(n0) > 16384) return uq::fail(UQ_ERR_UNSUPPORTED, "%s: padded width > 16384 not built", who);
+    if (uq_next_pow2(n0) > 32768) return uq::fail(UQ_ERR_UNSUPPORTED, "%s: padded width > 32768 not built", who);
     if (group < 8 || group % 8 || group > 8192)
         return uq::fail(UQ_ERR_UNSUPPORTED, "%s: group %d must be a multiple of 8 in [8, 8192]", who, group);
     return UQ_OK;

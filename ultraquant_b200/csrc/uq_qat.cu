@@ -1,0 +1,389 @@
+// Differentiable decoder of UltraQuant's QAT step (qat.py:35-59) for sm_100a.
+//
+//   fwht_torch(x)      qat.py:35-41  butterflies h = 1 .. n/2 in the tensor's
+//                                    dtype, then x / sqrt(n)
+//   irht_torch(X, n0)  qat.py:43-49  fwht_torch(X) * d, cropped to n0
+//   recon_torch(...)   qat.py:51-59  irht_torch(cw[states] * sc_g) / sH
+//
+// and their gradients as torch autograd forms them: the backward of
+// `x / s` is `g / s`, of `a + b, a - b` is `ga + gb, ga - gb` applied in the
+// reverse stage order, of `v * d` is `g * d`, of `y / sH` is `g / sH`, and of
+// `cw[st] * sc` is the scatter-add of `g * sc` into cw and the per-group sum of
+// `g * cw[st]` into sc.  Every per-element step is one correctly rounded
+// operation in the tensor's dtype, so the transforms are bit-identical to
+// torch on the CPU; the two reductions of the backward accumulate exact fp32
+// terms in fp64 (more accurate than torch's fp32 sums, within tolerance).
+//
+// torch's `x / s` with a Python scalar s = sqrt(n) divides by s rounded to
+// the tensor's dtype; for even log2(n) s is a power of two and the division is
+// a multiplication by an exact power of two.
+//
+// Layout: a CTA transforms a tile of 2^NB consecutive elements (NB =
+// max(12, b), n = 2^b, 2^(NB-b) rows per tile) held in shared memory with the
+// swizzle P(E) = E ^ ((E >> 5) & 31), which keeps every access below free of
+// bank conflicts for 4-byte words (8-byte words: two-way at most).  Each of
+// the 2^(NB-5) threads keeps 32 elements in registers per pass; pass p keeps
+// index bits [p, p+5) in registers.  The tile is filled and (backward) drained
+// with thread-consecutive coalesced accesses.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <stdint.h>
+
+#include "uq_common.cuh"
+
+namespace {
+
+constexpr int VB = 5;           // log2 of the values per thread
+constexpr int V = 1 << VB;
+
+__device__ __forceinline__ int swz5(int e) { return e ^ ((e >> 5) & 31); }
+
+template <typename T> struct Ar;
+template <> struct Ar<float> {
+    static __device__ __forceinline__ float add(float a, float b) { return __fadd_rn(a, b); }
+    static __device__ __forceinline__ float sub(float a, float b) { return __fsub_rn(a, b); }
+    static __device__ __forceinline__ float mul(float a, float b) { return __fmul_rn(a, b); }
+    static __device__ __forceinline__ float div(float a, float b) { return __fdiv_rn(a, b); }
+};
+template <> struct Ar<double> {
+    static __device__ __forceinline__ double add(double a, double b) { return __dadd_rn(a, b); }
+    static __device__ __forceinline__ double sub(double a, double b) { return __dsub_rn(a, b); }
+    static __device__ __forceinline__ double mul(double a, double b) { return __dmul_rn(a, b); }
+    static __device__ __forceinline__ double div(double a, double b) { return __ddiv_rn(a, b); }
+};
+
+enum { DIR_FWD = 0, DIR_BWD = 1 };
+enum { SRC_DENSE = 0, SRC_RECON = 1 };
+enum { DST_DENSE = 0, DST_GRADS = 1 };
+
+struct FwhtArgs {
+    int64_t rows;                // rows of the transform (each n = 2^b wide)
+    int b;
+    // dense source: forward input / backward incoming gradient, (rows, ncols_x)
+    const void *x;
+    int64_t ld_x, ncols_x;
+    // code source (forward) / gradient target (backward): the rotated matrix
+    // is rec[f] = cw[states[f]] * sc[f / group], f = row * n + col
+    const void *states;
+    int states64;
+    const float *cw;
+    int64_t ncw;
+    const float *sc;
+    int64_t group;
+    int group_shift;             // log2(group) when group is a power of two, else -1
+    const void *signs;           // optional d (n), dtype T
+    const void *colscale;        // optional sH (ncols_out forward / ncols_x backward), dtype T
+    double s;                    // sqrt(n)
+    void *out;
+    int64_t ld_out, ncols_out;
+    double *gcw, *gsc;           // fp64 gradient accumulators (backward into codes)
+};
+
+__device__ int g_qat_bad_state = 0;
+
+template <typename T> __device__ __forceinline__ void stage_pair(T &u, T &v) {
+    const T a = u, c = v;
+    u = Ar<T>::add(a, c);
+    v = Ar<T>::sub(a, c);
+}
+
+// Butterfly stages of index bits [lo, hi) (all within [p, p+5)) on the 32
+// register values x[j] = element(base + (j << p)); ascending for the forward
+// transform, descending for its adjoint.
+template <typename T, int DIR>
+__device__ __forceinline__ void stages32(T (&x)[V], int p, int lo, int hi) {
+#pragma unroll
+    for (int q = 0; q < VB; ++q) {
+        const int lq = DIR == DIR_FWD ? q : VB - 1 - q;
+        if (p + lq < lo || p + lq >= hi) continue;
+#pragma unroll
+        for (int j = 0; j < V; ++j)
+            if (!(j & (1 << lq))) stage_pair<T>(x[j], x[j | (1 << lq)]);
+    }
+}
+
+__device__ __forceinline__ int64_t load_state(const FwhtArgs &a, int64_t f) {
+    const int64_t s = a.states64 ? __ldg(static_cast<const long long *>(a.states) + f)
+                                 : int64_t(__ldg(static_cast<const int *>(a.states) + f));
+    if (s < 0 || s >= a.ncw) {
+        atomicExch(&g_qat_bad_state, 1);
+        return -1;
+    }
+    return s;
+}
+
+__device__ __forceinline__ int64_t group_of(const FwhtArgs &a, int64_t f) {
+    return a.group_shift >= 0 ? (f >> a.group_shift) : f / a.group;
+}
+
+template <typename T, int DIR, int SRC, int DST, int MAXT>
+__global__ void __launch_bounds__(MAXT)
+fwht_kernel(FwhtArgs a) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    T *tile = reinterpret_cast<T *>(smem_raw);
+    using A = Ar<T>;
+    const int b = a.b;
+    const int NB = b > 12 ? b : 12;
+    const int TILE = 1 << NB;
+    const int nthr = 1 << (NB - VB);
+    const int tid = threadIdx.x;
+    const int nmask = (1 << b) - 1;
+    const int64_t n = int64_t(1) << b;
+    const int64_t ntiles = (a.rows + (int64_t(1) << (NB - b)) - 1) >> (NB - b);
+    const T s = T(a.s);
+    const bool s_pow2 = (b & 1) == 0;
+    const T s_inv = T(ldexp(1.0, -(b >> 1)));
+    const T *signs = static_cast<const T *>(a.signs);
+    const T *cs = static_cast<const T *>(a.colscale);
+
+    for (int64_t t = blockIdx.x; t < ntiles; t += gridDim.x) {
+        const int64_t row0 = t << (NB - b);
+        // ---- fill: coalesced, thread-consecutive ---------------------------
+        for (int E = tid; E < TILE; E += nthr) {
+            const int64_t r = row0 + (E >> b);
+            const int e = E & nmask;
+            T v = T(0);
+            if (r < a.rows) {
+                if (SRC == SRC_RECON) {
+                    const int64_t f = r * n + e;
+                    const int64_t st = load_state(a, f);
+                    v = st < 0 ? T(__int_as_float(0x7fc00000))
+                               : T(A::mul(T(__ldg(a.cw + st)), T(__ldg(a.sc + group_of(a, f)))));
+                } else if (e < a.ncols_x) {
+                    v = static_cast<const T *>(a.x)[r * a.ld_x + e];
+                    if (DIR == DIR_BWD) {
+                        // adjoint of (., / sH), (., * d), (., / s) in that order
+                        if (cs) v = A::div(v, cs[e]);
+                        if (signs) v = A::mul(v, signs[e]);
+                        v = s_pow2 ? A::mul(v, s_inv) : A::div(v, s);
+                    }
+                }
+            }
+            tile[swz5(E)] = v;
+        }
+        __syncthreads();
+
+        T x[V];
+        if (DIR == DIR_FWD) {
+            int done = 0;
+            for (int p = 0;; p += VB) {
+                if (p > NB - VB) p = NB - VB;
+                const int base = (tid & ((1 << p) - 1)) | ((tid >> p) << (p + VB));
+#pragma unroll
+                for (int j = 0; j < V; ++j) x[j] = tile[swz5(base + (j << p))];
+                const int hi = (p + VB < b) ? p + VB : b;
+                stages32<T, DIR_FWD>(x, p, done > p ? done : p, hi);
+                if (hi > done) done = hi;
+                if (p == NB - VB) {
+                    // epilogue from registers: base == tid, lanes on consecutive columns
+#pragma unroll
+                    for (int j = 0; j < V; ++j) {
+                        const int E = base + (j << p);
+                        const int64_t r = row0 + (E >> b);
+                        const int e = E & nmask;
+                        if (r >= a.rows || e >= a.ncols_out) continue;
+                        T y = s_pow2 ? A::mul(x[j], s_inv) : A::div(x[j], s);
+                        if (signs) y = A::mul(y, signs[e]);
+                        if (cs) y = A::div(y, cs[e]);
+                        static_cast<T *>(a.out)[r * a.ld_out + e] = y;
+                    }
+                    break;
+                }
+#pragma unroll
+                for (int j = 0; j < V; ++j) tile[swz5(base + (j << p))] = x[j];
+                __syncthreads();
+            }
+        } else {
+            int low = b;   // stages of bits >= low are done
+            for (int p = b - VB > 0 ? b - VB : 0;; p = p - VB > 0 ? p - VB : 0) {
+                const int base = (tid & ((1 << p) - 1)) | ((tid >> p) << (p + VB));
+#pragma unroll
+                for (int j = 0; j < V; ++j) x[j] = tile[swz5(base + (j << p))];
+                stages32<T, DIR_BWD>(x, p, p, low < p + VB ? low : p + VB);
+                low = p;
+                if (p == 0) break;
+#pragma unroll
+                for (int j = 0; j < V; ++j) tile[swz5(base + (j << p))] = x[j];
+                __syncthreads();
+            }
+            // registers now hold the 32 consecutive elements (tid << 5) + j
+            if (DST == DST_GRADS) {
+                const int E0 = tid << VB;
+                double acc = 0.0;
+                int64_t g_cur = -1;
+#pragma unroll
+                for (int j = 0; j < V; ++j) {
+                    const int E = E0 + j;
+                    const int64_t r = row0 + (E >> b);
+                    if (r >= a.rows) continue;
+                    const int64_t f = r * n + (E & nmask);
+                    const int64_t st = load_state(a, f);
+                    const int64_t g = group_of(a, f);
+                    if (st < 0) continue;
+                    const float gx = float(x[j]);
+                    atomicAdd(a.gcw + st, double(__fmul_rn(gx, __ldg(a.sc + g))));
+                    if (g != g_cur) {
+                        if (g_cur >= 0) atomicAdd(a.gsc + g_cur, acc);
+                        g_cur = g;
+                        acc = 0.0;
+                    }
+                    acc += double(__fmul_rn(gx, __ldg(a.cw + st)));
+                }
+                if (g_cur >= 0) atomicAdd(a.gsc + g_cur, acc);
+            } else {
+                const int base = tid << VB;
+#pragma unroll
+                for (int j = 0; j < V; ++j) tile[swz5(base + j)] = x[j];
+                __syncthreads();
+                for (int E = tid; E < TILE; E += nthr) {
+                    const int64_t r = row0 + (E >> b);
+                    const int e = E & nmask;
+                    if (r < a.rows && e < a.ncols_out) static_cast<T *>(a.out)[r * a.ld_out + e] = tile[swz5(E)];
+                }
+            }
+        }
+        __syncthreads();   // the tile is refilled for the next tile
+    }
+}
+
+__global__ void grads_to_f32_kernel(const double *g64, int64_t count, float *out) {
+    for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < count; i += int64_t(gridDim.x) * blockDim.x)
+        out[i] = __double2float_rn(g64[i]);
+}
+
+template <typename T, int DIR, int SRC, int DST>
+int launch_fwht(const FwhtArgs &a, cudaStream_t st, const char *what) {
+    const int NB = a.b > 12 ? a.b : 12;
+    const int nthr = 1 << (NB - VB);
+    const size_t smem = sizeof(T) << NB;
+    auto kern = nthr <= 128 ? fwht_kernel<T, DIR, SRC, DST, 128>
+              : nthr <= 256 ? fwht_kernel<T, DIR, SRC, DST, 256>
+              : nthr <= 512 ? fwht_kernel<T, DIR, SRC, DST, 512> : fwht_kernel<T, DIR, SRC, DST, 1024>;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess)
+        return uq::check_cuda("fwht: set smem attribute");
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, nthr, smem) != cudaSuccess || per_sm < 1)
+        return uq::check_cuda("fwht: occupancy query");
+    const int64_t ntiles = (a.rows + (int64_t(1) << (NB - a.b)) - 1) >> (NB - a.b);
+    const int64_t grid = std::min<int64_t>(ntiles, int64_t(uq::num_sms()) * per_sm);
+    if (grid > 0) { uq::ProfScope _p(what, st); kern<<<unsigned(grid), nthr, smem, st>>>(a); }
+    return uq::check_cuda("fwht_kernel launch");
+}
+
+int max_bits(int dtype) { return dtype == UQ_F32 ? 15 : 14; }   // tile <= 128 KB
+
+int set_group(FwhtArgs &a, int64_t group) {
+    a.group = group;
+    a.group_shift = uq::is_pow2(group) ? uq::ilog2(group) : -1;
+    return UQ_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int uq_fwht(const void *x, int dtype, int64_t rows, int64_t n, int64_t ldx, int64_t ncols_in,
+            const void *signs, const void *colscale, int direction, void *out, int64_t ld_out,
+            int64_t ncols_out, void *stream) {
+    if (rows < 0 || !uq::is_pow2(n) || ncols_in < 0 || ncols_in > n || ldx < ncols_in || ncols_out < 0 ||
+        ncols_out > n || ld_out < ncols_out || !uq::dtype_size(dtype) || (direction != 0 && direction != 1))
+        return uq::fail(UQ_ERR_INVALID, "uq_fwht: bad arguments (rows=%lld n=%lld ncols_in=%lld ncols_out=%lld dir=%d)",
+                        (long long)rows, (long long)n, (long long)ncols_in, (long long)ncols_out, direction);
+    if (uq::ilog2(n) > max_bits(dtype))
+        return uq::fail(UQ_ERR_UNSUPPORTED, "uq_fwht: n = %lld > %d not built for this dtype", (long long)n,
+                        1 << max_bits(dtype));
+    if (rows == 0 || ncols_out == 0) return UQ_OK;
+    if (!out || (ncols_in > 0 && !x)) return uq::fail(UQ_ERR_INVALID, "uq_fwht: null pointer");
+    FwhtArgs a{};
+    a.rows = rows; a.b = uq::ilog2(n); a.x = x; a.ld_x = ldx; a.ncols_x = ncols_in;
+    a.signs = signs; a.colscale = colscale; a.s = sqrt(double(n));
+    a.out = out; a.ld_out = ld_out; a.ncols_out = ncols_out;
+    const cudaStream_t st = UQ_STREAM(stream);
+    if (direction == 0) {
+        if (dtype == UQ_F32) return launch_fwht<float, DIR_FWD, SRC_DENSE, DST_DENSE>(a, st, "fwht");
+        return launch_fwht<double, DIR_FWD, SRC_DENSE, DST_DENSE>(a, st, "fwht");
+    }
+    if (dtype == UQ_F32) return launch_fwht<float, DIR_BWD, SRC_DENSE, DST_DENSE>(a, st, "fwht_bwd");
+    return launch_fwht<double, DIR_BWD, SRC_DENSE, DST_DENSE>(a, st, "fwht_bwd");
+}
+
+int uq_qat_recon(const void *states, int states64, int64_t nrow, int64_t n, const float *cw, int64_t ncw,
+                 const float *sc, int64_t scale_group, const float *signs, const float *sH, int64_t in0,
+                 float *out, int64_t ld_out, void *stream) {
+    if (nrow < 0 || !uq::is_pow2(n) || ncw < 1 || scale_group < 1 || in0 < 0 || in0 > n || ld_out < in0)
+        return uq::fail(UQ_ERR_INVALID, "uq_qat_recon: bad arguments (nrow=%lld n=%lld in0=%lld group=%lld)",
+                        (long long)nrow, (long long)n, (long long)in0, (long long)scale_group);
+    if (uq::ilog2(n) > max_bits(UQ_F32))
+        return uq::fail(UQ_ERR_UNSUPPORTED, "uq_qat_recon: n = %lld > 32768 not built", (long long)n);
+    if (nrow == 0 || in0 == 0) return UQ_OK;
+    if (!states || !cw || !sc || !signs || !out) return uq::fail(UQ_ERR_INVALID, "uq_qat_recon: null pointer");
+    FwhtArgs a{};
+    a.rows = nrow; a.b = uq::ilog2(n); a.states = states; a.states64 = states64 ? 1 : 0;
+    a.cw = cw; a.ncw = ncw; a.sc = sc; set_group(a, scale_group);
+    a.signs = signs; a.colscale = sH; a.s = sqrt(double(n));
+    a.out = out; a.ld_out = ld_out; a.ncols_out = in0;
+    return launch_fwht<float, DIR_FWD, SRC_RECON, DST_DENSE>(a, UQ_STREAM(stream), "qat_recon");
+}
+
+size_t uq_qat_recon_backward_workspace_bytes(int64_t ncw, int64_t ngroups) {
+    if (ncw < 0 || ngroups < 0) return 0;
+    return uq::align_up(size_t(ncw) * 8, 256) + uq::align_up(size_t(ngroups) * 8, 256);
+}
+
+int uq_qat_recon_backward(const float *grad, int64_t ld_grad, const void *states, int states64, int64_t nrow,
+                          int64_t n, const float *cw, int64_t ncw, const float *sc, int64_t ngroups,
+                          int64_t scale_group, const float *signs, const float *sH, int64_t in0,
+                          float *grad_cw, float *grad_sc, void *workspace, size_t workspace_bytes,
+                          void *stream) {
+    if (nrow < 0 || !uq::is_pow2(n) || ncw < 1 || scale_group < 1 || in0 < 0 || in0 > n || ld_grad < in0 ||
+        ngroups < 0)
+        return uq::fail(UQ_ERR_INVALID, "uq_qat_recon_backward: bad arguments (nrow=%lld n=%lld in0=%lld)",
+                        (long long)nrow, (long long)n, (long long)in0);
+    if (uq::ilog2(n) > max_bits(UQ_F32))
+        return uq::fail(UQ_ERR_UNSUPPORTED, "uq_qat_recon_backward: n = %lld > 32768 not built", (long long)n);
+    if ((nrow * n + scale_group - 1) / scale_group > ngroups)
+        return uq::fail(UQ_ERR_INVALID, "uq_qat_recon_backward: %lld scale groups < %lld needed", (long long)ngroups,
+                        (long long)((nrow * n + scale_group - 1) / scale_group));
+    const size_t need = uq_qat_recon_backward_workspace_bytes(ncw, ngroups);
+    if (!workspace || workspace_bytes < need)
+        return uq::fail(UQ_ERR_WORKSPACE, "uq_qat_recon_backward: workspace %zu < %zu bytes", workspace_bytes, need);
+    if (!grad_cw || !grad_sc || !cw || !sc || !signs || (nrow > 0 && in0 > 0 && (!grad || !states)))
+        return uq::fail(UQ_ERR_INVALID, "uq_qat_recon_backward: null pointer");
+    const cudaStream_t st = UQ_STREAM(stream);
+    uq::Carver c(workspace, workspace_bytes);
+    double *gcw = c.take<double>(size_t(ncw));
+    double *gsc = c.take<double>(size_t(ngroups));
+    if (cudaMemsetAsync(workspace, 0, need, st) != cudaSuccess) return uq::check_cuda("qat backward: memset");
+    if (nrow > 0) {
+        FwhtArgs a{};
+        a.rows = nrow; a.b = uq::ilog2(n); a.x = grad; a.ld_x = ld_grad; a.ncols_x = in0;
+        a.states = states; a.states64 = states64 ? 1 : 0; a.cw = cw; a.ncw = ncw; a.sc = sc;
+        set_group(a, scale_group);
+        a.signs = signs; a.colscale = sH; a.s = sqrt(double(n));
+        a.gcw = gcw; a.gsc = gsc;
+        const int rc = launch_fwht<float, DIR_BWD, SRC_DENSE, DST_GRADS>(a, st, "qat_recon_bwd");
+        if (rc != UQ_OK) return rc;
+    }
+    {
+        uq::ProfScope _p("qat_grads_f32", st);
+        const int g1 = int(std::max<int64_t>(1, std::min<int64_t>((ncw + 255) / 256, 1184)));
+        grads_to_f32_kernel<<<g1, 256, 0, st>>>(gcw, ncw, grad_cw);
+        const int g2 = int(std::max<int64_t>(1, std::min<int64_t>((ngroups + 255) / 256, 1184)));
+        if (ngroups > 0) grads_to_f32_kernel<<<g2, 256, 0, st>>>(gsc, ngroups, grad_sc);
+    }
+    return uq::check_cuda("qat backward: grads_to_f32_kernel launch");
+}
+
+}  // extern "C"
+
+namespace uq {
+// Reads and clears the sticky "state outside the codebook" flag of the
+// decoder kernels (after the caller synchronised).  Returns -1 on a CUDA error.
+int qat_take_bad_state() {
+    int flag = 0, zero = 0;
+    if (cudaMemcpyFromSymbol(&flag, g_qat_bad_state, sizeof(int)) != cudaSuccess) return -1;
+    if (flag && cudaMemcpyToSymbol(g_qat_bad_state, &zero, sizeof(int)) != cudaSuccess) return -1;
+    return flag;
+}
+}  // namespace uq

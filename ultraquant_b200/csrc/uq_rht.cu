@@ -14,6 +14,12 @@
 // index bits [p, p+4) in registers and runs the stages of those bits.  The
 // final pass (p = NB-4) has consecutive threads on consecutive elements, so
 // the global store is coalesced; the load is coalesced the same way.
+//
+// n = 32768 (fp64 row = 256 KB, above one CTA's shared memory): a cluster of
+// two CTAs holds one row, a half each.  Index bits [0, 14) are local to a
+// half and run as above; the last stage (h = 16384) pairs element i of the
+// first half with element i of the second, which each CTA reads from its
+// partner's shared memory (distributed shared memory, plain loads).
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -23,7 +29,8 @@
 
 namespace {
 
-constexpr int kMaxBits = 14;  // n <= 16384 doubles = 128 KB of shared memory per CTA
+constexpr int kTileBits = 14;  // n <= 16384 doubles = 128 KB of shared memory per CTA
+constexpr int kMaxBits = 15;   // n = 32768: a row split over a 2-CTA cluster
 
 __device__ __forceinline__ int swz(int e) { return e ^ ((e >> 4) & 15); }
 
@@ -259,6 +266,154 @@ rht_tile_kernel(RhtArgs a, int dbuf) {
     asm volatile("cp.async.wait_group 0;" ::: "memory");
 }
 
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n"
+                 "barrier.cluster.wait.acquire.aligned;\n" ::: "memory");
+}
+
+__device__ __forceinline__ double ld_peer_f64(unsigned addr) {
+    double v;
+    asm volatile("ld.shared::cluster.f64 %0, [%1];" : "=d"(v) : "r"(addr) : "memory");
+    return v;
+}
+
+// One row of n = 2^15 per cluster of two CTAs (1024 threads, 16 values each,
+// one 128 KB half-row tile each); clusters walk the rows.  Stages of bits
+// [0, 14) as in rht_tile_kernel on each half; stage 14 combines the halves
+// through distributed shared memory.  Partial error sums go to
+// err_partial[2 * (2 * row + rank)].
+template <typename TIn, typename TOut, int MODE>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(1024, 1)
+rht_split_kernel(RhtArgs a) {
+    extern __shared__ double smem_d[];
+    constexpr int NB = kTileBits, HALF = 1 << NB, NTHR = 1 << (NB - 4);
+    const int tid = threadIdx.x;
+    unsigned rank;
+    asm("mov.u32 %0, %%cluster_ctarank;" : "=r"(rank));
+    const int64_t col0 = int64_t(rank) * HALF;
+    RhtArgs h = a;                         // this CTA's half as a 2^14-wide problem
+    h.b = NB;
+    h.rows = a.rows;
+    const int64_t n0_loc = a.n0 - col0;
+    h.n0 = MODE == MODE_FWD ? (n0_loc < 0 ? 0 : (n0_loc > HALF ? HALF : n0_loc)) : HALF;
+    const TIn *in = static_cast<const TIn *>(a.in) + col0;
+    constexpr int EPC = 16 / int(sizeof(TIn));
+    constexpr int CPT = 16 / EPC;
+    const bool staged = ((a.ld_in * int64_t(sizeof(TIn))) % 16 == 0) && ((reinterpret_cast<uintptr_t>(in) & 15) == 0);
+    const double inv_mul = ldexp(1.0, -(NB + 1));
+    const unsigned peer_tile = [&] {
+        unsigned r2;
+        asm("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r2)
+            : "r"(unsigned(__cvta_generic_to_shared(smem_d))), "r"(rank ^ 1u));
+        return r2;
+    }();
+    const int64_t nclusters = gridDim.x / 2;
+    for (int64_t r = blockIdx.x / 2; r < a.rows; r += nclusters) {
+        double x[16];
+        {
+            double raw[16];
+            if (staged) {
+                rht_stage<TIn, MODE>(h, in, r, NB, NB, NTHR, smem_d);
+                asm volatile("cp.async.commit_group;" ::: "memory");
+                asm volatile("cp.async.wait_group 0;" ::: "memory");
+                __syncthreads();
+                const int mix = CPT == 8 ? (tid & 7) : ((tid >> 1) & 3);
+                const TIn *stile = reinterpret_cast<const TIn *>(smem_d);
+#pragma unroll
+                for (int w = 0; w < CPT; ++w) {
+                    const TIn *q = stile + ((tid * CPT) | (w ^ mix)) * EPC;
+#pragma unroll
+                    for (int i = 0; i < EPC; ++i) raw[w * EPC + i] = double(q[i]);
+                }
+                __syncthreads();
+            } else {
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    int e = (tid << 4) + j;
+                    if (MODE == MODE_FWD && e >= h.n0) e = h.n0 > 0 ? int(h.n0 - 1) : 0;
+                    raw[j] = (MODE == MODE_FWD && h.n0 == 0) ? 0.0 : ld_as_f64(in + r * a.ld_in + e);
+                }
+            }
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+                const int e = (tid << 4) + j;
+                const double v = (MODE != MODE_FWD || e < h.n0) ? raw[j] : 0.0;
+                x[j] = MODE == MODE_FWD ? d_mul(v, __ldg(a.pre + col0 + e)) : d_mul(v, a.sqrt_n);
+            }
+            stages16(x, 0, 0, 4);
+        }
+        int done = 4, prev_p = 0, base = 0;
+        for (int p = 4;; p += 4) {
+            if (p > NB - 4) p = NB - 4;
+            const int pb = (tid & ((1 << prev_p) - 1)) | ((tid >> prev_p) << (prev_p + 4));
+#pragma unroll
+            for (int j = 0; j < 16; ++j) smem_d[swz(pb + (j << prev_p))] = x[j];
+            __syncthreads();
+            base = (tid & ((1 << p) - 1)) | ((tid >> p) << (p + 4));
+#pragma unroll
+            for (int j = 0; j < 16; ++j) x[j] = smem_d[swz(base + (j << p))];
+            stages16(x, p, done > p ? done : p, NB);
+            done = p + 4;
+            if (p == NB - 4) break;
+            __syncthreads();
+            prev_p = p;
+        }
+        // ---- stage 14 across the cluster: x_lo + x_hi / x_lo - x_hi ---------
+        __syncthreads();
+#pragma unroll
+        for (int j = 0; j < 16; ++j) smem_d[swz(base + (j << (NB - 4)))] = x[j];
+        cluster_sync_all();
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            const double v = ld_peer_f64(peer_tile + unsigned(swz(base + (j << (NB - 4)))) * 8u);
+            x[j] = rank == 0 ? d_add(x[j], v) : d_sub(v, x[j]);
+        }
+        cluster_sync_all();   // the partner has read this tile before it is restaged
+        // ---- epilogue (base == tid: coalesced) ------------------------------
+        double se = 0.0, sa = 0.0;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            const int64_t e = col0 + base + (j << (NB - 4));
+            if (e >= a.ncols_out) continue;
+            double y;
+            if (MODE == MODE_FWD) {
+                y = x[j] / a.sqrt_n;
+            } else {
+                const double xs = d_mul(x[j], inv_mul);
+                y = d_mul(xs, __ldg(a.signs + e));
+                if (a.err_partial) {
+                    double w = a.ref_dtype == UQ_F32
+                        ? double(__ldg(static_cast<const float *>(a.ref_w) + r * a.ld_w + e))
+                        : __ldg(static_cast<const double *>(a.ref_w) + r * a.ld_w + e);
+                    const double A = d_mul(w, __ldg(a.colscale + e));
+                    const double dd = d_sub(A, y);
+                    se = d_add(se, d_mul(dd, dd));
+                    sa = d_add(sa, d_mul(A, A));
+                }
+                if (a.colscale) y = xs / __ldg(a.pre + e);
+            }
+            static_cast<TOut *>(a.out)[r * a.ld_out + e] = TOut(y);
+        }
+        if (MODE == MODE_INV && a.err_partial) {
+            double *red = smem_d;   // the tile is free: the partner is done with it
+            for (int o = 16; o > 0; o >>= 1) {
+                se = d_add(se, __shfl_xor_sync(0xffffffffu, se, o));
+                sa = d_add(sa, __shfl_xor_sync(0xffffffffu, sa, o));
+            }
+            const int w = tid >> 5;
+            if ((tid & 31) == 0) { red[2 * w] = se; red[2 * w + 1] = sa; }
+            __syncthreads();
+            if (tid == 0) {
+                double s0 = 0.0, s1 = 0.0;
+                for (int i = 0; i < NTHR / 32; ++i) { s0 = d_add(s0, red[2 * i]); s1 = d_add(s1, red[2 * i + 1]); }
+                a.err_partial[2 * (2 * r + rank)] = s0;
+                a.err_partial[2 * (2 * r + rank) + 1] = s1;
+            }
+        }
+        __syncthreads();
+    }
+}
+
 // Fixed-order sum of per-CTA partial pairs -> err[0..1].
 __global__ void sum_pairs_kernel(const double *part, int64_t count, double *err) {
     __shared__ double s0[256], s1[256];
@@ -287,7 +442,28 @@ __global__ void prescale_kernel(const double *colscale, const double *signs, int
 }
 
 template <typename TIn, typename TOut, int MODE>
+int launch_rht_split(const RhtArgs &a, cudaStream_t st) {
+    auto kern = rht_split_kernel<TIn, TOut, MODE>;
+    const size_t smem = sizeof(double) << kTileBits;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess)
+        return uq::check_cuda("rht split: set smem attribute");
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2; attr[0].val.clusterDim.y = 1; attr[0].val.clusterDim.z = 1;
+    cfg.gridDim = dim3(2, 1, 1); cfg.blockDim = dim3(1024, 1, 1); cfg.dynamicSmemBytes = smem; cfg.stream = st;
+    cfg.attrs = attr; cfg.numAttrs = 1;
+    int clusters = 0;
+    if (cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg) != cudaSuccess || clusters < 1)
+        return uq::check_cuda("rht split: cluster occupancy");
+    const int64_t ncl = std::min<int64_t>(a.rows, clusters);
+    if (ncl > 0) { uq::ProfScope _p("rht", st); kern<<<unsigned(2 * ncl), 1024, smem, st>>>(a); }
+    return uq::check_cuda("rht_split_kernel launch");
+}
+
+template <typename TIn, typename TOut, int MODE>
 int launch_rht(const RhtArgs &a, cudaStream_t st) {
+    if (a.b > kTileBits) return launch_rht_split<TIn, TOut, MODE>(a, st);
     const int NB = a.b > 12 ? a.b : 12;
     const int nthr = 1 << (NB - 4);
     const int rows_per_tile = 1 << (NB - a.b);
@@ -311,6 +487,8 @@ int launch_rht(const RhtArgs &a, cudaStream_t st) {
 
 namespace uq {
 
+int64_t rht_tiles(int64_t rows, int64_t n);
+
 // Forward RHT with optional column pre-scale; output fp64 or fp32.
 // pre: colscale * signs (n values) when colscale is given, else nullptr.
 int rht_forward(const void *in, int in_dtype, int64_t rows, int64_t n0, int64_t ld_in,
@@ -324,7 +502,7 @@ int rht_forward(const void *in, int in_dtype, int64_t rows, int64_t n0, int64_t 
     a.signs = signs; a.colscale = colscale; a.pre = colscale ? pre : signs; a.out = out;
     a.ld_out = ld_out; a.ncols_out = n;
     a.sqrt_n = sqrt(double(n)); a.n_d = double(n);
-    if (a.b > kMaxBits) return fail(UQ_ERR_UNSUPPORTED, "rht: n = %lld > 16384 not built", (long long)n);
+    if (a.b > kMaxBits) return fail(UQ_ERR_UNSUPPORTED, "rht: n = %lld > 32768 not built", (long long)n);
     if (in_dtype == UQ_F64 && out_dtype == UQ_F64) return launch_rht<double, double, MODE_FWD>(a, st);
     if (in_dtype == UQ_F32 && out_dtype == UQ_F64) return launch_rht<float, double, MODE_FWD>(a, st);
     if (in_dtype == UQ_F64 && out_dtype == UQ_F32) return launch_rht<double, float, MODE_FWD>(a, st);
@@ -345,7 +523,7 @@ int rht_inverse(const void *in, int in_dtype, int64_t rows, int64_t n, int64_t l
     a.ld_out = ld_out; a.ncols_out = n0;
     a.sqrt_n = sqrt(double(n)); a.n_d = double(n);
     a.ref_w = ref_w; a.ref_dtype = ref_dtype; a.ld_w = ld_w; a.err_partial = err ? err_partial : nullptr;
-    if (a.b > kMaxBits) return fail(UQ_ERR_UNSUPPORTED, "irht: n = %lld > 16384 not built", (long long)n);
+    if (a.b > kMaxBits) return fail(UQ_ERR_UNSUPPORTED, "irht: n = %lld > 32768 not built", (long long)n);
     int rc;
     if (in_dtype == UQ_F64 && out_dtype == UQ_F64) rc = launch_rht<double, double, MODE_INV>(a, st);
     else if (in_dtype == UQ_F32 && out_dtype == UQ_F64) rc = launch_rht<float, double, MODE_INV>(a, st);
@@ -353,8 +531,7 @@ int rht_inverse(const void *in, int in_dtype, int64_t rows, int64_t n, int64_t l
     else if (in_dtype == UQ_F32 && out_dtype == UQ_F32) rc = launch_rht<float, float, MODE_INV>(a, st);
     else return fail(UQ_ERR_INVALID, "irht: bad dtype");
     if (rc != UQ_OK || !err) return rc;
-    const int NB = a.b > 12 ? a.b : 12;
-    const int64_t tiles = (rows + (1 << (NB - a.b)) - 1) >> (NB - a.b);
+    const int64_t tiles = rht_tiles(rows, n);
     { uq::ProfScope _p("sum_pairs", st); sum_pairs_kernel<<<1, 256, 0, st>>>(err_partial, tiles, err); }
     return check_cuda("sum_pairs_kernel launch");
 }
@@ -367,6 +544,7 @@ int rht_prescale(const double *colscale, const double *signs, int64_t n0, int64_
 
 int64_t rht_tiles(int64_t rows, int64_t n) {
     const int b = ilog2(n);
+    if (b > kTileBits) return 2 * rows;   // one partial per half row
     const int NB = b > 12 ? b : 12;
     return (rows + (1 << (NB - b)) - 1) >> (NB - b);
 }
