@@ -20,6 +20,7 @@ inline int ilog2(int64_t n) { int b = 0; while ((int64_t(1) << b) < n) ++b; retu
 inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 int num_sms();
 int qat_take_bad_state();   // uq_qat.cu
+int rht_take_timeout();     // uq_rht.cu
 
 // Launch accounting / optional per-launch event timing (see uq_profile_*).
 void count_launch();

@@ -72,6 +72,7 @@ struct FwhtArgs {
     const float *sc;
     int64_t group;
     int group_shift;             // log2(group) when group is a power of two, else -1
+    int64_t ntot;                // rows * n: values of the flat rotated matrix
     const void *signs;           // optional d (n), dtype T
     const void *colscale;        // optional sH (ncols_out forward / ncols_x backward), dtype T
     double s;                    // sqrt(n)
@@ -117,8 +118,31 @@ __device__ __forceinline__ int64_t group_of(const FwhtArgs &a, int64_t f) {
     return a.group_shift >= 0 ? (f >> a.group_shift) : f / a.group;
 }
 
+template <typename T> struct Vec16;
+template <> struct Vec16<float> {
+    using type = float4;
+    static constexpr int N = 4;
+    static __device__ __forceinline__ float4 zero() { return make_float4(0.f, 0.f, 0.f, 0.f); }
+};
+template <> struct Vec16<double> {
+    using type = double2;
+    static constexpr int N = 2;
+    static __device__ __forceinline__ double2 zero() { return make_double2(0.0, 0.0); }
+};
+
+// Adjoint of (. / sH), (. * d), (. / s), applied in that order to an incoming
+// gradient element of column e.
+template <typename T>
+__device__ __forceinline__ T bwd_pre(const FwhtArgs &, T v, int e, const T *cs, const T *signs, bool s_pow2,
+                                     T s_inv, T s) {
+    if (cs) v = Ar<T>::div(v, cs[e]);
+    if (signs) v = Ar<T>::mul(v, signs[e]);
+    return s_pow2 ? Ar<T>::mul(v, s_inv) : Ar<T>::div(v, s);
+}
+
+// ~768 resident threads per SM (85 registers) for the 128- and 256-thread tiles
 template <typename T, int DIR, int SRC, int DST, int MAXT>
-__global__ void __launch_bounds__(MAXT)
+__global__ void __launch_bounds__(MAXT, MAXT <= 128 ? 6 : (MAXT <= 256 ? 3 : 1))
 fwht_kernel(FwhtArgs a) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     T *tile = reinterpret_cast<T *>(smem_raw);
@@ -136,31 +160,95 @@ fwht_kernel(FwhtArgs a) {
     const T s_inv = T(ldexp(1.0, -(b >> 1)));
     const T *signs = static_cast<const T *>(a.signs);
     const T *cs = static_cast<const T *>(a.colscale);
+    const bool vec_in = SRC == SRC_RECON
+        ? (!a.states64 && b >= 2 && a.group % 4 == 0 && (reinterpret_cast<uintptr_t>(a.states) & 15) == 0)
+        : (b >= 2 && a.ncols_x % Vec16<T>::N == 0 && (a.ld_x * int64_t(sizeof(T))) % 16 == 0 &&
+           (reinterpret_cast<uintptr_t>(a.x) & 15) == 0);
+    const bool vec_st = !a.states64 && b >= 2 && (reinterpret_cast<uintptr_t>(a.states) & 15) == 0;
+    const bool vec_out = b >= 2 && a.ncols_out % Vec16<T>::N == 0 && (a.ld_out * int64_t(sizeof(T))) % 16 == 0 &&
+                         (reinterpret_cast<uintptr_t>(a.out) & 15) == 0;
 
     for (int64_t t = blockIdx.x; t < ntiles; t += gridDim.x) {
         const int64_t row0 = t << (NB - b);
-        // ---- fill: coalesced, thread-consecutive ---------------------------
-        for (int E = tid; E < TILE; E += nthr) {
-            const int64_t r = row0 + (E >> b);
-            const int e = E & nmask;
-            T v = T(0);
-            if (r < a.rows) {
-                if (SRC == SRC_RECON) {
-                    const int64_t f = r * n + e;
-                    const int64_t st = load_state(a, f);
-                    v = st < 0 ? T(__int_as_float(0x7fc00000))
-                               : T(A::mul(T(__ldg(a.cw + st)), T(__ldg(a.sc + group_of(a, f)))));
-                } else if (e < a.ncols_x) {
-                    v = static_cast<const T *>(a.x)[r * a.ld_x + e];
-                    if (DIR == DIR_BWD) {
-                        // adjoint of (., / sH), (., * d), (., / s) in that order
-                        if (cs) v = A::div(v, cs[e]);
-                        if (signs) v = A::mul(v, signs[e]);
-                        v = s_pow2 ? A::mul(v, s_inv) : A::div(v, s);
+        // ---- fill: thread-consecutive; 16-byte vectors when aligned, all of a
+        //      thread's loads issued before its shared-memory stores ----------
+        if (vec_in) {
+            if (SRC == SRC_RECON) {
+                int stv[V];
+#pragma unroll
+                for (int i = 0; i < V / 4; ++i) {
+                    const int E = (tid + i * nthr) * 4;
+                    const int64_t f = (t << NB) + E;   // rows of a tile are consecutive in the flat index
+                    int4 q = make_int4(0, 0, 0, 0);
+                    if (f < a.ntot) q = __ldg(reinterpret_cast<const int4 *>(static_cast<const int *>(a.states) + f));
+                    stv[4 * i] = q.x; stv[4 * i + 1] = q.y; stv[4 * i + 2] = q.z; stv[4 * i + 3] = q.w;
+                }
+#pragma unroll
+                for (int i = 0; i < V / 4; ++i) {
+                    const int E = (tid + i * nthr) * 4;
+                    const int64_t f = (t << NB) + E;
+                    const bool in = f < a.ntot;
+                    const float scv = in ? __ldg(a.sc + group_of(a, f)) : 0.f;   // group % 4 == 0
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const int st = stv[4 * i + j];
+                        T v = T(0);
+                        if (in) {
+                            if (st < 0 || st >= a.ncw) {
+                                atomicExch(&g_qat_bad_state, 1);
+                                v = T(__int_as_float(0x7fc00000));
+                            } else {
+                                v = T(__fmul_rn(__ldg(a.cw + st), scv));
+                            }
+                        }
+                        tile[swz5(E + j)] = v;
+                    }
+                }
+            } else {
+                using VT = typename Vec16<T>::type;
+                constexpr int VE = Vec16<T>::N;
+                VT q[V / VE];
+#pragma unroll
+                for (int i = 0; i < V / VE; ++i) {
+                    const int E = (tid + i * nthr) * VE;
+                    const int64_t r = row0 + (E >> b);
+                    const int e = E & nmask;
+                    q[i] = Vec16<T>::zero();
+                    if (r < a.rows && e < a.ncols_x)
+                        q[i] = __ldg(reinterpret_cast<const VT *>(static_cast<const T *>(a.x) + r * a.ld_x + e));
+                }
+#pragma unroll
+                for (int i = 0; i < V / VE; ++i) {
+                    const int E = (tid + i * nthr) * VE;
+                    const int64_t r = row0 + (E >> b);
+                    const int e = E & nmask;
+                    const bool in = r < a.rows && e < a.ncols_x;
+#pragma unroll
+                    for (int j = 0; j < VE; ++j) {
+                        T v = reinterpret_cast<const T *>(&q[i])[j];
+                        if (DIR == DIR_BWD && in) v = bwd_pre<T>(a, v, e + j, cs, signs, s_pow2, s_inv, s);
+                        tile[swz5(E + j)] = v;
                     }
                 }
             }
-            tile[swz5(E)] = v;
+        } else {
+            for (int E = tid; E < TILE; E += nthr) {
+                const int64_t r = row0 + (E >> b);
+                const int e = E & nmask;
+                T v = T(0);
+                if (r < a.rows) {
+                    if (SRC == SRC_RECON) {
+                        const int64_t f = r * n + e;
+                        const int64_t st = load_state(a, f);
+                        v = st < 0 ? T(__int_as_float(0x7fc00000))
+                                   : T(A::mul(T(__ldg(a.cw + st)), T(__ldg(a.sc + group_of(a, f)))));
+                    } else if (e < a.ncols_x) {
+                        v = static_cast<const T *>(a.x)[r * a.ld_x + e];
+                        if (DIR == DIR_BWD) v = bwd_pre<T>(a, v, e, cs, signs, s_pow2, s_inv, s);
+                    }
+                }
+                tile[swz5(E)] = v;
+            }
         }
         __syncthreads();
 
@@ -210,15 +298,30 @@ fwht_kernel(FwhtArgs a) {
             // registers now hold the 32 consecutive elements (tid << 5) + j
             if (DST == DST_GRADS) {
                 const int E0 = tid << VB;
+                const int64_t f0 = (t << NB) + E0;   // the 32 elements are consecutive in the flat index
+                int stv[V];
+                if (vec_st) {
+#pragma unroll
+                    for (int i = 0; i < V / 4; ++i) {
+                        int4 q = make_int4(0, 0, 0, 0);
+                        if (f0 + 4 * i < a.ntot)
+                            q = __ldg(reinterpret_cast<const int4 *>(static_cast<const int *>(a.states) + f0 + 4 * i));
+                        stv[4 * i] = q.x; stv[4 * i + 1] = q.y; stv[4 * i + 2] = q.z; stv[4 * i + 3] = q.w;
+                    }
+                }
                 double acc = 0.0;
                 int64_t g_cur = -1;
 #pragma unroll
                 for (int j = 0; j < V; ++j) {
-                    const int E = E0 + j;
-                    const int64_t r = row0 + (E >> b);
-                    if (r >= a.rows) continue;
-                    const int64_t f = r * n + (E & nmask);
-                    const int64_t st = load_state(a, f);
+                    const int64_t f = f0 + j;
+                    if (f >= a.ntot) continue;
+                    int64_t st;
+                    if (vec_st) {
+                        st = stv[j];
+                        if (st < 0 || st >= a.ncw) { atomicExch(&g_qat_bad_state, 1); st = -1; }
+                    } else {
+                        st = load_state(a, f);
+                    }
                     const int64_t g = group_of(a, f);
                     if (st < 0) continue;
                     const float gx = float(x[j]);
@@ -236,10 +339,26 @@ fwht_kernel(FwhtArgs a) {
 #pragma unroll
                 for (int j = 0; j < V; ++j) tile[swz5(base + j)] = x[j];
                 __syncthreads();
-                for (int E = tid; E < TILE; E += nthr) {
-                    const int64_t r = row0 + (E >> b);
-                    const int e = E & nmask;
-                    if (r < a.rows && e < a.ncols_out) static_cast<T *>(a.out)[r * a.ld_out + e] = tile[swz5(E)];
+                if (vec_out) {
+                    using VT = typename Vec16<T>::type;
+                    constexpr int VE = Vec16<T>::N;
+#pragma unroll
+                    for (int i = 0; i < V / VE; ++i) {
+                        const int E = (tid + i * nthr) * VE;
+                        const int64_t r = row0 + (E >> b);
+                        const int e = E & nmask;
+                        if (r >= a.rows || e >= a.ncols_out) continue;
+                        VT q;
+#pragma unroll
+                        for (int j = 0; j < VE; ++j) reinterpret_cast<T *>(&q)[j] = tile[swz5(E + j)];
+                        *reinterpret_cast<VT *>(static_cast<T *>(a.out) + r * a.ld_out + e) = q;
+                    }
+                } else {
+                    for (int E = tid; E < TILE; E += nthr) {
+                        const int64_t r = row0 + (E >> b);
+                        const int e = E & nmask;
+                        if (r < a.rows && e < a.ncols_out) static_cast<T *>(a.out)[r * a.ld_out + e] = tile[swz5(E)];
+                    }
                 }
             }
         }
@@ -257,9 +376,11 @@ int launch_fwht(const FwhtArgs &a, cudaStream_t st, const char *what) {
     const int NB = a.b > 12 ? a.b : 12;
     const int nthr = 1 << (NB - VB);
     const size_t smem = sizeof(T) << NB;
+    // fp64 tiles stop at n = 16384 (512 threads)
+    constexpr int TOP = sizeof(T) == 8 ? 512 : 1024;
     auto kern = nthr <= 128 ? fwht_kernel<T, DIR, SRC, DST, 128>
               : nthr <= 256 ? fwht_kernel<T, DIR, SRC, DST, 256>
-              : nthr <= 512 ? fwht_kernel<T, DIR, SRC, DST, 512> : fwht_kernel<T, DIR, SRC, DST, 1024>;
+              : nthr <= 512 ? fwht_kernel<T, DIR, SRC, DST, 512> : fwht_kernel<T, DIR, SRC, DST, TOP>;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess)
         return uq::check_cuda("fwht: set smem attribute");
     int per_sm = 0;
@@ -321,6 +442,7 @@ int uq_qat_recon(const void *states, int states64, int64_t nrow, int64_t n, cons
     FwhtArgs a{};
     a.rows = nrow; a.b = uq::ilog2(n); a.states = states; a.states64 = states64 ? 1 : 0;
     a.cw = cw; a.ncw = ncw; a.sc = sc; set_group(a, scale_group);
+    a.ntot = nrow * n;
     a.signs = signs; a.colscale = sH; a.s = sqrt(double(n));
     a.out = out; a.ld_out = ld_out; a.ncols_out = in0;
     return launch_fwht<float, DIR_FWD, SRC_RECON, DST_DENSE>(a, UQ_STREAM(stream), "qat_recon");
@@ -360,6 +482,7 @@ int uq_qat_recon_backward(const float *grad, int64_t ld_grad, const void *states
         a.rows = nrow; a.b = uq::ilog2(n); a.x = grad; a.ld_x = ld_grad; a.ncols_x = in0;
         a.states = states; a.states64 = states64 ? 1 : 0; a.cw = cw; a.ncw = ncw; a.sc = sc;
         set_group(a, scale_group);
+        a.ntot = nrow * n;
         a.signs = signs; a.colscale = sH; a.s = sqrt(double(n));
         a.gcw = gcw; a.gsc = gsc;
         const int rc = launch_fwht<float, DIR_BWD, SRC_DENSE, DST_GRADS>(a, st, "qat_recon_bwd");

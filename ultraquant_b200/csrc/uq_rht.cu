@@ -20,9 +20,11 @@
 // half and run as above; the last stage (h = 16384) pairs element i of the
 // first half with element i of the second, which each CTA reads from its
 // partner's shared memory (distributed shared memory, plain loads).
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <mutex>
 #include <stdint.h>
 
 #include "uq_common.cuh"
@@ -414,6 +416,268 @@ rht_split_kernel(RhtArgs a) {
     }
 }
 
+// ---------------------------------------------------------------------------
+// TMA form for n = 4096 and 8192 (one CTA per row) and n = 16384 (a row split
+// over a 2-CTA cluster).  The row (half row) arrives by tensor-map loads into
+// a shared buffer with the 128-byte swizzle (16-byte chunk c of 128-byte line
+// r at c ^ (r & 7)), so that pass 0 -- thread t owns the 16 consecutive
+// elements 16t .. 16t+15 -- reads it with conflict-free 16-byte loads; the
+// next row is loaded into the second buffer meanwhile.  The result is
+// written back to the buffer in the same swizzled line layout and leaves by
+// a tensor-map store.  Columns past n0 (padding) and rows past the end are
+// zero-filled by the load and clipped by the store.  Every pass layout is a
+// compile-time constant.
+// ---------------------------------------------------------------------------
+__device__ int g_rht_timeout = 0;
+
+__device__ __forceinline__ void rmb_init(unsigned addr, unsigned count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" :: "r"(addr), "r"(count) : "memory");
+}
+__device__ __forceinline__ void rmb_expect_tx(unsigned addr, unsigned bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" :: "r"(addr), "r"(bytes) : "memory");
+}
+// Bounded wait (2 s) on a phase parity; gives up with a sticky flag.
+__device__ __forceinline__ void rmb_wait(unsigned addr, unsigned parity, bool &fail) {
+    if (fail) return;
+    unsigned long long t0 = 0;
+    for (unsigned it = 0;; ++it) {
+        unsigned done;
+        asm volatile("{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+                     "selp.u32 %0, 1, 0, p;\n\t}" : "=r"(done) : "r"(addr), "r"(parity) : "memory");
+        if (done) return;
+        if ((it & 63) == 0) {
+            unsigned long long now;
+            asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(now));
+            if (it == 0) t0 = now;
+            else if (now - t0 > 2000000000ull) {
+                fail = true;
+                atomicExch(&g_rht_timeout, 1);
+                return;
+            }
+        }
+    }
+}
+__device__ __forceinline__ void tma_load3(unsigned dst, const CUtensorMap *map, int c0, int c1, int c2, unsigned mbar) {
+    asm volatile("cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];"
+                 :: "r"(dst), "l"(map), "r"(c0), "r"(c1), "r"(c2), "r"(mbar) : "memory");
+}
+__device__ __forceinline__ void tma_store3(const CUtensorMap *map, int c0, int c1, int c2, unsigned src) {
+    asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%1, %2, %3}], [%4];"
+                 :: "l"(map), "r"(c0), "r"(c1), "r"(c2), "r"(src) : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+__device__ __forceinline__ double flip_if(double v, unsigned neg) {
+    return __longlong_as_double(__double_as_longlong(v) ^ (static_cast<long long>(neg) << 63));
+}
+__device__ __forceinline__ float4 lds128f(unsigned addr) {
+    float4 v;
+    asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr));
+    return v;
+}
+__device__ __forceinline__ double2 lds128d(unsigned addr) {
+    double2 v;
+    asm volatile("ld.shared.v2.f64 {%0,%1}, [%2];" : "=d"(v.x), "=d"(v.y) : "r"(addr));
+    return v;
+}
+
+// Byte offset of local element E in the 128-byte-line swizzled layout of a
+// T buffer (16-byte chunk c of line r stored at chunk c ^ (r & 7)).
+template <typename T> __device__ __forceinline__ unsigned line_off(int E) {
+    constexpr int EPL = 128 / int(sizeof(T));      // elements per line
+    constexpr int EPC = 16 / int(sizeof(T));       // elements per chunk
+    const int r = E / EPL, c = (E % EPL) / EPC;
+    return unsigned(r * 128 + ((c ^ (r & 7)) << 4) + (E % EPC) * int(sizeof(T)));
+}
+
+template <typename TIn, typename TOut, int MODE, int LB, int CL, bool COLS>
+__global__ void __launch_bounds__(1 << (LB - 4), LB == 12 ? 3 : 1)
+rht_tma_kernel(const __grid_constant__ CUtensorMap tin, const __grid_constant__ CUtensorMap tout, RhtArgs a) {
+    constexpr int NT = 1 << (LB - 4);
+    constexpr int HALF = 1 << LB;                  // elements per CTA and row
+    constexpr int BUFB = HALF * 8;                 // one buffer: the fp64 tile
+    constexpr int NBOX = HALF / 4096;              // tensor-map boxes of 4096 elements
+    constexpr int B = LB + (CL == 2 ? 1 : 0);      // log2(n)
+    constexpr int INB = 4096 * int(sizeof(TIn)), OUTB = 4096 * int(sizeof(TOut));
+    extern __shared__ __align__(1024) unsigned char smem_raw_r[];
+    __shared__ __align__(8) unsigned long long full[2];
+    __shared__ double red[2 * (NT / 32)];
+    const int tid = threadIdx.x;
+    unsigned rank = 0;
+    if (CL == 2) asm("mov.u32 %0, %%cluster_ctarank;" : "=r"(rank));
+    const int64_t col0 = int64_t(rank) * HALF;
+    // the swizzled tensor-map buffers start on a 1024-byte boundary
+    unsigned char *smem_r = smem_raw_r + ((1024u - (unsigned(__cvta_generic_to_shared(smem_raw_r)) & 1023u)) & 1023u);
+    const unsigned sbase = unsigned(__cvta_generic_to_shared(smem_r));
+    const unsigned bar0 = unsigned(__cvta_generic_to_shared(&full[0]));
+    const int64_t nclusters = gridDim.x / CL;
+    const int64_t first = blockIdx.x / CL;
+    constexpr int CH_IN = 4096 / (128 / int(sizeof(TIn)));     // 128-byte lines per input box
+    constexpr int CH_OUT = 4096 / (128 / int(sizeof(TOut)));
+    const int lin0 = int(col0 / (128 / int(sizeof(TIn))));
+    const int lout0 = int(col0 / (128 / int(sizeof(TOut))));
+
+    if (tid == 0) {
+        rmb_init(bar0, 1);
+        rmb_init(bar0 + 8, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+    if (tid == 0 && first < a.rows) {
+        rmb_expect_tx(bar0, NBOX * INB);
+#pragma unroll
+        for (int bx = 0; bx < NBOX; ++bx)
+            tma_load3(sbase + bx * INB, &tin, 0, lin0 + bx * CH_IN, int(first), bar0);
+    }
+    // per-thread constants: pass-0 columns 16 tid + j, last-pass columns tid + (j << (LB - 4))
+    double pre_r[COLS && MODE == MODE_FWD ? 16 : 1];
+    unsigned mask0 = 0, maskL = 0;
+    if (MODE == MODE_FWD) {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            const int64_t e = col0 + 16 * tid + j;
+            if (COLS) pre_r[j] = __ldg(a.pre + e);
+            else mask0 |= (__ldg(a.signs + e) < 0.0 ? 1u : 0u) << j;
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            const int64_t e = col0 + tid + (j << (LB - 4));
+            maskL |= (__ldg(a.signs + e) < 0.0 ? 1u : 0u) << j;
+        }
+    }
+    const double inv_mul = ldexp(1.0, -B);
+    const double fwd_mul = ldexp(1.0, -(B >> 1));
+    bool fail = false;
+    unsigned peer_base = 0;
+    if (CL == 2) asm("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(peer_base) : "r"(sbase), "r"(rank ^ 1u));
+
+    int k = 0;
+    for (int64_t r = first; r < a.rows; r += nclusters, ++k) {
+        const unsigned buf = sbase + unsigned((k & 1) * BUFB);
+        double *tile = reinterpret_cast<double *>(smem_r + (k & 1) * BUFB);
+        rmb_wait(bar0 + 8u * unsigned(k & 1), unsigned((k >> 1) & 1), fail);
+        double x[16];
+        // ---- pass 0: 16 consecutive elements from the swizzled lines ----------
+        if (sizeof(TIn) == 8) {
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+                const double2 v = lds128d(buf + unsigned(tid * 128 + ((c ^ (tid & 7)) << 4)));
+                x[2 * c] = v.x;
+                x[2 * c + 1] = v.y;
+            }
+        } else {
+            const int ln = tid >> 1, h = tid & 1;
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                const float4 v = lds128f(buf + unsigned(ln * 128 + (((4 * h + c) ^ (ln & 7)) << 4)));
+                x[4 * c] = v.x; x[4 * c + 1] = v.y; x[4 * c + 2] = v.z; x[4 * c + 3] = v.w;
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            if (MODE == MODE_FWD) x[j] = COLS ? d_mul(x[j], pre_r[j]) : flip_if(x[j], (mask0 >> j) & 1u);
+            else x[j] = d_mul(x[j], a.sqrt_n);
+        }
+        stages16(x, 0, 0, 4);
+        __syncthreads();   // everyone has its raw values: the buffer becomes the work tile
+        // prefetch the CTA's next row into the other buffer (its previous store
+        // must have finished reading it)
+        if (tid == 0 && r + nclusters < a.rows) {
+            bulk_wait_read0();
+            const unsigned nb = bar0 + 8u * unsigned((k + 1) & 1);
+            rmb_expect_tx(nb, NBOX * INB);
+#pragma unroll
+            for (int bx = 0; bx < NBOX; ++bx)
+                tma_load3(sbase + unsigned(((k + 1) & 1) * BUFB) + bx * INB, &tin, 0, lin0 + bx * CH_IN,
+                          int(r + nclusters), nb);
+        }
+        // ---- passes 4, 8, ...: transposes through the element-swizzled tile ----
+#pragma unroll
+        for (int p = 4, prev = 0, done = 4; p - 4 < LB - 4; p += 4) {
+            const int pp = p > LB - 4 ? LB - 4 : p;
+            const int pb = (tid & ((1 << prev) - 1)) | ((tid >> prev) << (prev + 4));
+#pragma unroll
+            for (int j = 0; j < 16; ++j) tile[swz(pb + (j << prev))] = x[j];
+            __syncthreads();
+            const int base = (tid & ((1 << pp) - 1)) | ((tid >> pp) << (pp + 4));
+#pragma unroll
+            for (int j = 0; j < 16; ++j) x[j] = tile[swz(base + (j << pp))];
+            stages16(x, pp, done > pp ? done : pp, LB);
+            done = pp + 4;
+            prev = pp;
+            __syncthreads();
+        }
+        // registers: elements tid + (j << (LB - 4)) of this CTA's part
+        if (CL == 2) {
+            // ---- last stage across the cluster (h = n / 2) --------------------
+#pragma unroll
+            for (int j = 0; j < 16; ++j) tile[swz(tid + (j << (LB - 4)))] = x[j];
+            cluster_sync_all();
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+                const double v = ld_peer_f64(peer_base + unsigned((k & 1) * BUFB) +
+                                             unsigned(swz(tid + (j << (LB - 4)))) * 8u);
+                x[j] = rank == 0 ? d_add(x[j], v) : d_sub(v, x[j]);
+            }
+            cluster_sync_all();
+        }
+        // ---- epilogue: scale, write the swizzled output lines, store ---------
+        double se = 0.0, sa = 0.0;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            const int E = tid + (j << (LB - 4));
+            const int64_t e = col0 + E;
+            double y;
+            if (MODE == MODE_FWD) {
+                y = (B & 1) ? x[j] / a.sqrt_n : d_mul(x[j], fwd_mul);
+            } else {
+                const double xs = d_mul(x[j], inv_mul);
+                y = flip_if(xs, (maskL >> j) & 1u);
+                if (COLS && e < a.ncols_out) {
+                    if (a.err_partial) {
+                        const double w = a.ref_dtype == UQ_F32
+                            ? double(__ldg(static_cast<const float *>(a.ref_w) + r * a.ld_w + e))
+                            : __ldg(static_cast<const double *>(a.ref_w) + r * a.ld_w + e);
+                        const double A = d_mul(w, __ldg(a.colscale + e));
+                        const double dd = d_sub(A, y);
+                        se = d_add(se, d_mul(dd, dd));
+                        sa = d_add(sa, d_mul(A, A));
+                    }
+                    y = xs / __ldg(a.pre + e);
+                }
+            }
+            const unsigned o = buf + line_off<TOut>(E);
+            if (sizeof(TOut) == 8) asm volatile("st.shared.f64 [%0], %1;" :: "r"(o), "d"(y) : "memory");
+            else asm volatile("st.shared.f32 [%0], %1;" :: "r"(o), "f"(float(y)) : "memory");
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        if (MODE == MODE_INV && COLS && a.err_partial) {
+            for (int o = 16; o > 0; o >>= 1) {
+                se = d_add(se, __shfl_xor_sync(0xffffffffu, se, o));
+                sa = d_add(sa, __shfl_xor_sync(0xffffffffu, sa, o));
+            }
+            if ((tid & 31) == 0) { red[2 * (tid >> 5)] = se; red[2 * (tid >> 5) + 1] = sa; }
+        }
+        __syncthreads();
+        if (tid == 0) {
+#pragma unroll
+            for (int bx = 0; bx < NBOX; ++bx)
+                tma_store3(&tout, 0, lout0 + bx * CH_OUT, int(r), buf + unsigned(bx * OUTB));
+            bulk_commit();
+            if (MODE == MODE_INV && COLS && a.err_partial) {
+                double s0 = 0.0, s1 = 0.0;
+                for (int i = 0; i < NT / 32; ++i) { s0 = d_add(s0, red[2 * i]); s1 = d_add(s1, red[2 * i + 1]); }
+                a.err_partial[2 * (CL * r + rank)] = s0;
+                a.err_partial[2 * (CL * r + rank) + 1] = s1;
+            }
+        }
+    }
+    if (tid == 0) bulk_wait0();
+    if (CL == 2) cluster_sync_all();   // no CTA leaves while its partner may read its tile
+}
+
 // Fixed-order sum of per-CTA partial pairs -> err[0..1].
 __global__ void sum_pairs_kernel(const double *part, int64_t count, double *err) {
     __shared__ double s0[256], s1[256];
@@ -441,6 +705,101 @@ __global__ void prescale_kernel(const double *colscale, const double *signs, int
         pre[e] = (colscale && e < n0) ? d_mul(colscale[e], signs[e]) : signs[e];
 }
 
+// ---- tensor maps -------------------------------------------------------------
+using EncodeTiled = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                 const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiled encode_fn() {
+    static EncodeTiled fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiled>(p);
+    });
+    return fn;
+}
+
+// (rows, ncols) matrix of T with row stride ld, viewed as 128-byte lines:
+// dims {elements per line, lines per row, rows}, box = 4096 elements of one row.
+template <typename T>
+bool make_line_map(CUtensorMap *m, const void *base, int64_t rows, int64_t ncols, int64_t ld) {
+    EncodeTiled fn = encode_fn();
+    if (!fn) return false;
+    constexpr int EPL = 128 / int(sizeof(T));
+    const cuuint64_t dims[3] = {cuuint64_t(EPL), cuuint64_t(ncols / EPL), cuuint64_t(rows)};
+    const cuuint64_t strides[2] = {128, cuuint64_t(ld) * sizeof(T)};
+    const cuuint32_t box[3] = {cuuint32_t(EPL), cuuint32_t(4096 / EPL), 1};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    return fn(m, sizeof(T) == 8 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT64 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3,
+              const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+              CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// The TMA form applies to n in {4096, 8192, 16384} with 16-byte aligned
+// bases, 16-byte multiple row strides and whole 128-byte lines of valid
+// columns (n0 for the input of the forward transform, n0 for the output of
+// the inverse).
+template <typename TIn, typename TOut>
+bool tma_ok(const RhtArgs &a, int64_t ncols_in) {
+    if (a.b < 12 || a.b > 14 || a.rows > (int64_t(1) << 31) - 1) return false;
+    auto al = [](const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+    return al(a.in) && al(a.out) && (a.ld_in * int64_t(sizeof(TIn))) % 16 == 0 &&
+           (a.ld_out * int64_t(sizeof(TOut))) % 16 == 0 && ncols_in % (128 / int(sizeof(TIn))) == 0 &&
+           a.ncols_out % (128 / int(sizeof(TOut))) == 0 && encode_fn() != nullptr;
+}
+
+template <typename TIn, typename TOut, int MODE, int LB, int CL, bool COLS>
+int launch_tma_v(const CUtensorMap &mi, const CUtensorMap &mo, const RhtArgs &a, cudaStream_t st, int64_t *nparts) {
+    auto kern = rht_tma_kernel<TIn, TOut, MODE, LB, CL, COLS>;
+    const int nt = 1 << (LB - 4);
+    const size_t smem = size_t(2) * (size_t(8) << LB) + 1024;   // two fp64 tiles + alignment slack
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess)
+        return uq::check_cuda("rht tma: set smem attribute");
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = CL; attr[0].val.clusterDim.y = 1; attr[0].val.clusterDim.z = 1;
+    cfg.blockDim = dim3(nt, 1, 1); cfg.dynamicSmemBytes = smem; cfg.stream = st;
+    cfg.attrs = attr; cfg.numAttrs = CL == 2 ? 1 : 0;
+    int64_t slots = 0;
+    if (CL == 2) {
+        cfg.gridDim = dim3(2, 1, 1);
+        int clusters = 0;
+        if (cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg) != cudaSuccess || clusters < 1)
+            return uq::check_cuda("rht tma: cluster occupancy");
+        slots = clusters;
+    } else {
+        int per_sm = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, nt, smem) != cudaSuccess || per_sm < 1)
+            return uq::check_cuda("rht tma: occupancy");
+        slots = int64_t(per_sm) * uq::num_sms();
+    }
+    const int64_t groups = std::min<int64_t>(a.rows, slots);
+    cfg.gridDim = dim3(unsigned(groups * CL), 1, 1);
+    *nparts = a.rows * CL;
+    if (groups > 0) {
+        uq::ProfScope _p("rht", st);
+        if (cudaLaunchKernelEx(&cfg, kern, mi, mo, a) != cudaSuccess) return uq::check_cuda("rht_tma_kernel launch");
+    }
+    return uq::check_cuda("rht_tma_kernel launch");
+}
+
+template <typename TIn, typename TOut, int MODE, bool COLS>
+int launch_tma(const RhtArgs &a, int64_t ncols_in, cudaStream_t st, int64_t *nparts) {
+    CUtensorMap mi, mo;
+    if (!make_line_map<TIn>(&mi, a.in, a.rows, ncols_in, a.ld_in) ||
+        !make_line_map<TOut>(&mo, a.out, a.rows, a.ncols_out, a.ld_out))
+        return uq::fail(UQ_ERR_CUDA, "rht: tensor map encoding failed");
+    if (a.b == 12) return launch_tma_v<TIn, TOut, MODE, 12, 1, COLS>(mi, mo, a, st, nparts);
+    if (a.b == 13) return launch_tma_v<TIn, TOut, MODE, 13, 1, COLS>(mi, mo, a, st, nparts);
+    return launch_tma_v<TIn, TOut, MODE, 13, 2, COLS>(mi, mo, a, st, nparts);
+}
+
 template <typename TIn, typename TOut, int MODE>
 int launch_rht_split(const RhtArgs &a, cudaStream_t st) {
     auto kern = rht_split_kernel<TIn, TOut, MODE>;
@@ -462,7 +821,17 @@ int launch_rht_split(const RhtArgs &a, cudaStream_t st) {
 }
 
 template <typename TIn, typename TOut, int MODE>
-int launch_rht(const RhtArgs &a, cudaStream_t st) {
+int launch_rht(const RhtArgs &a, cudaStream_t st, int64_t *nparts) {
+    const int64_t ncols_in = MODE == MODE_FWD ? a.n0 : (int64_t(1) << a.b);
+    if (tma_ok<TIn, TOut>(a, ncols_in)) {
+        // the colscale form is only used with the pipeline's error statistics or prescale
+        if (a.colscale) return launch_tma<TIn, TOut, MODE, true>(a, ncols_in, st, nparts);
+        return launch_tma<TIn, TOut, MODE, false>(a, ncols_in, st, nparts);
+    }
+    {
+        const int NB = a.b > 12 ? a.b : 12;
+        *nparts = a.b > kTileBits ? 2 * a.rows : (a.rows + (int64_t(1) << (NB - a.b)) - 1) >> (NB - a.b);
+    }
     if (a.b > kTileBits) return launch_rht_split<TIn, TOut, MODE>(a, st);
     const int NB = a.b > 12 ? a.b : 12;
     const int nthr = 1 << (NB - 4);
@@ -503,10 +872,11 @@ int rht_forward(const void *in, int in_dtype, int64_t rows, int64_t n0, int64_t 
     a.ld_out = ld_out; a.ncols_out = n;
     a.sqrt_n = sqrt(double(n)); a.n_d = double(n);
     if (a.b > kMaxBits) return fail(UQ_ERR_UNSUPPORTED, "rht: n = %lld > 32768 not built", (long long)n);
-    if (in_dtype == UQ_F64 && out_dtype == UQ_F64) return launch_rht<double, double, MODE_FWD>(a, st);
-    if (in_dtype == UQ_F32 && out_dtype == UQ_F64) return launch_rht<float, double, MODE_FWD>(a, st);
-    if (in_dtype == UQ_F64 && out_dtype == UQ_F32) return launch_rht<double, float, MODE_FWD>(a, st);
-    if (in_dtype == UQ_F32 && out_dtype == UQ_F32) return launch_rht<float, float, MODE_FWD>(a, st);
+    int64_t nparts = 0;
+    if (in_dtype == UQ_F64 && out_dtype == UQ_F64) return launch_rht<double, double, MODE_FWD>(a, st, &nparts);
+    if (in_dtype == UQ_F32 && out_dtype == UQ_F64) return launch_rht<float, double, MODE_FWD>(a, st, &nparts);
+    if (in_dtype == UQ_F64 && out_dtype == UQ_F32) return launch_rht<double, float, MODE_FWD>(a, st, &nparts);
+    if (in_dtype == UQ_F32 && out_dtype == UQ_F32) return launch_rht<float, float, MODE_FWD>(a, st, &nparts);
     return fail(UQ_ERR_INVALID, "rht: bad dtype");
 }
 
@@ -525,14 +895,14 @@ int rht_inverse(const void *in, int in_dtype, int64_t rows, int64_t n, int64_t l
     a.ref_w = ref_w; a.ref_dtype = ref_dtype; a.ld_w = ld_w; a.err_partial = err ? err_partial : nullptr;
     if (a.b > kMaxBits) return fail(UQ_ERR_UNSUPPORTED, "irht: n = %lld > 32768 not built", (long long)n);
     int rc;
-    if (in_dtype == UQ_F64 && out_dtype == UQ_F64) rc = launch_rht<double, double, MODE_INV>(a, st);
-    else if (in_dtype == UQ_F32 && out_dtype == UQ_F64) rc = launch_rht<float, double, MODE_INV>(a, st);
-    else if (in_dtype == UQ_F64 && out_dtype == UQ_F32) rc = launch_rht<double, float, MODE_INV>(a, st);
-    else if (in_dtype == UQ_F32 && out_dtype == UQ_F32) rc = launch_rht<float, float, MODE_INV>(a, st);
+    int64_t nparts = 0;
+    if (in_dtype == UQ_F64 && out_dtype == UQ_F64) rc = launch_rht<double, double, MODE_INV>(a, st, &nparts);
+    else if (in_dtype == UQ_F32 && out_dtype == UQ_F64) rc = launch_rht<float, double, MODE_INV>(a, st, &nparts);
+    else if (in_dtype == UQ_F64 && out_dtype == UQ_F32) rc = launch_rht<double, float, MODE_INV>(a, st, &nparts);
+    else if (in_dtype == UQ_F32 && out_dtype == UQ_F32) rc = launch_rht<float, float, MODE_INV>(a, st, &nparts);
     else return fail(UQ_ERR_INVALID, "irht: bad dtype");
     if (rc != UQ_OK || !err) return rc;
-    const int64_t tiles = rht_tiles(rows, n);
-    { uq::ProfScope _p("sum_pairs", st); sum_pairs_kernel<<<1, 256, 0, st>>>(err_partial, tiles, err); }
+    { uq::ProfScope _p("sum_pairs", st); sum_pairs_kernel<<<1, 256, 0, st>>>(err_partial, nparts, err); }
     return check_cuda("sum_pairs_kernel launch");
 }
 
@@ -542,9 +912,18 @@ int rht_prescale(const double *colscale, const double *signs, int64_t n0, int64_
     return check_cuda("prescale_kernel launch");
 }
 
+// Reads and clears the timeout flag of the TMA transform's bounded waits
+// (after the caller synchronised); -1 on a CUDA error.
+int rht_take_timeout() {
+    int flag = 0, zero = 0;
+    if (cudaMemcpyFromSymbol(&flag, g_rht_timeout, sizeof(int)) != cudaSuccess) return -1;
+    if (flag && cudaMemcpyToSymbol(g_rht_timeout, &zero, sizeof(int)) != cudaSuccess) return -1;
+    return flag;
+}
+
 int64_t rht_tiles(int64_t rows, int64_t n) {
     const int b = ilog2(n);
-    if (b > kTileBits) return 2 * rows;   // one partial per half row
+    if (b >= kTileBits) return 2 * rows;   // at most one partial per half row
     const int NB = b > 12 ? b : 12;
     return (rows + (1 << (NB - b)) - 1) >> (NB - b);
 }
