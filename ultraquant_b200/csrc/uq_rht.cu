@@ -417,12 +417,14 @@ rht_split_kernel(RhtArgs a) {
 }
 
 // ---------------------------------------------------------------------------
-// TMA form for n = 4096 and 8192 (one CTA per row) and n = 16384 (a row split
-// over a 2-CTA cluster).  The row (half row) arrives by tensor-map loads into
-// a shared buffer with the 128-byte swizzle (16-byte chunk c of 128-byte line
-// r at c ^ (r & 7)), so that pass 0 -- thread t owns the 16 consecutive
-// elements 16t .. 16t+15 -- reads it with conflict-free 16-byte loads; the
-// next row is loaded into the second buffer meanwhile.  The result is
+// TMA form for n = 2^12 .. 2^15.  A row is split into 2^LB-element parts, one
+// per CTA of a cluster of n / 2^LB CTAs (a single CTA for n = 2^LB).  Each
+// part arrives by tensor-map loads into a shared buffer with the 128-byte
+// swizzle (16-byte chunk c of 128-byte line r at c ^ (r & 7)), so that pass
+// 0 -- thread t owns the 16 consecutive elements 16t .. 16t+15 -- reads it
+// with conflict-free 16-byte loads; the CTA's next row is loaded into the
+// second buffer meanwhile.  Index bits above LB are the cluster stages: each
+// CTA reads its partner's part from distributed shared memory.  The result is
 // written back to the buffer in the same swizzled line layout and leaves by
 // a tensor-map store.  Columns past n0 (padding) and rows past the end are
 // zero-filled by the load and clipped by the store.  Every pass layout is a
@@ -498,14 +500,16 @@ rht_tma_kernel(const __grid_constant__ CUtensorMap tin, const __grid_constant__ 
     constexpr int HALF = 1 << LB;                  // elements per CTA and row
     constexpr int BUFB = HALF * 8;                 // one buffer: the fp64 tile
     constexpr int NBOX = HALF / 4096;              // tensor-map boxes of 4096 elements
-    constexpr int B = LB + (CL == 2 ? 1 : 0);      // log2(n)
+    constexpr int LCL = CL == 1 ? 0 : (CL == 2 ? 1 : (CL == 4 ? 2 : 3));
+    static_assert((1 << LCL) == CL, "cluster of 1, 2, 4 or 8 CTAs");
+    constexpr int B = LB + LCL;                    // log2(n)
     constexpr int INB = 4096 * int(sizeof(TIn)), OUTB = 4096 * int(sizeof(TOut));
     extern __shared__ __align__(1024) unsigned char smem_raw_r[];
     __shared__ __align__(8) unsigned long long full[2];
     __shared__ double red[2 * (NT / 32)];
     const int tid = threadIdx.x;
     unsigned rank = 0;
-    if (CL == 2) asm("mov.u32 %0, %%cluster_ctarank;" : "=r"(rank));
+    if (CL > 1) asm("mov.u32 %0, %%cluster_ctarank;" : "=r"(rank));
     const int64_t col0 = int64_t(rank) * HALF;
     // the swizzled tensor-map buffers start on a 1024-byte boundary
     unsigned char *smem_r = smem_raw_r + ((1024u - (unsigned(__cvta_generic_to_shared(smem_raw_r)) & 1023u)) & 1023u);
@@ -550,8 +554,10 @@ rht_tma_kernel(const __grid_constant__ CUtensorMap tin, const __grid_constant__ 
     const double inv_mul = ldexp(1.0, -B);
     const double fwd_mul = ldexp(1.0, -(B >> 1));
     bool fail = false;
-    unsigned peer_base = 0;
-    if (CL == 2) asm("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(peer_base) : "r"(sbase), "r"(rank ^ 1u));
+    unsigned peer_base[LCL > 0 ? LCL : 1];
+#pragma unroll
+    for (int i = 0; i < LCL; ++i)
+        asm("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(peer_base[i]) : "r"(sbase), "r"(rank ^ (1u << i)));
 
     int k = 0;
     for (int64_t r = first; r < a.rows; r += nclusters, ++k) {
@@ -610,18 +616,21 @@ rht_tma_kernel(const __grid_constant__ CUtensorMap tin, const __grid_constant__ 
             __syncthreads();
         }
         // registers: elements tid + (j << (LB - 4)) of this CTA's part
-        if (CL == 2) {
-            // ---- last stage across the cluster (h = n / 2) --------------------
+        // ---- stages of index bits LB .. B-1 across the cluster: bit LB + i pairs
+        //      CTA rank with rank ^ 2^i (lower: own + peer, upper: peer - own) --
+#pragma unroll
+        for (int i = 0; i < LCL; ++i) {
 #pragma unroll
             for (int j = 0; j < 16; ++j) tile[swz(tid + (j << (LB - 4)))] = x[j];
             cluster_sync_all();
+            const unsigned pb = peer_base[i] + unsigned((k & 1) * BUFB);
+            const bool upper = (rank >> i) & 1u;
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
-                const double v = ld_peer_f64(peer_base + unsigned((k & 1) * BUFB) +
-                                             unsigned(swz(tid + (j << (LB - 4)))) * 8u);
-                x[j] = rank == 0 ? d_add(x[j], v) : d_sub(v, x[j]);
+                const double v = ld_peer_f64(pb + unsigned(swz(tid + (j << (LB - 4)))) * 8u);
+                x[j] = upper ? d_sub(v, x[j]) : d_add(x[j], v);
             }
-            cluster_sync_all();
+            cluster_sync_all();   // the partner has read this tile before it changes
         }
         // ---- epilogue: scale, write the swizzled output lines, store ---------
         double se = 0.0, sa = 0.0;
@@ -675,7 +684,7 @@ rht_tma_kernel(const __grid_constant__ CUtensorMap tin, const __grid_constant__ 
         }
     }
     if (tid == 0) bulk_wait0();
-    if (CL == 2) cluster_sync_all();   // no CTA leaves while its partner may read its tile
+    if (CL > 1) cluster_sync_all();   // no CTA leaves while a partner may read its tile
 }
 
 // Fixed-order sum of per-CTA partial pairs -> err[0..1].
@@ -746,7 +755,7 @@ bool make_line_map(CUtensorMap *m, const void *base, int64_t rows, int64_t ncols
 // the inverse).
 template <typename TIn, typename TOut>
 bool tma_ok(const RhtArgs &a, int64_t ncols_in) {
-    if (a.b < 12 || a.b > 14 || a.rows > (int64_t(1) << 31) - 1) return false;
+    if (a.b < 12 || a.b > 15 || a.rows > (int64_t(1) << 31) - 1) return false;
     auto al = [](const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
     return al(a.in) && al(a.out) && (a.ld_in * int64_t(sizeof(TIn))) % 16 == 0 &&
            (a.ld_out * int64_t(sizeof(TOut))) % 16 == 0 && ncols_in % (128 / int(sizeof(TIn))) == 0 &&
@@ -765,10 +774,10 @@ int launch_tma_v(const CUtensorMap &mi, const CUtensorMap &mo, const RhtArgs &a,
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = CL; attr[0].val.clusterDim.y = 1; attr[0].val.clusterDim.z = 1;
     cfg.blockDim = dim3(nt, 1, 1); cfg.dynamicSmemBytes = smem; cfg.stream = st;
-    cfg.attrs = attr; cfg.numAttrs = CL == 2 ? 1 : 0;
+    cfg.attrs = attr; cfg.numAttrs = CL > 1 ? 1 : 0;
     int64_t slots = 0;
-    if (CL == 2) {
-        cfg.gridDim = dim3(2, 1, 1);
+    if (CL > 1) {
+        cfg.gridDim = dim3(CL, 1, 1);
         int clusters = 0;
         if (cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg) != cudaSuccess || clusters < 1)
             return uq::check_cuda("rht tma: cluster occupancy");
@@ -795,9 +804,16 @@ int launch_tma(const RhtArgs &a, int64_t ncols_in, cudaStream_t st, int64_t *npa
     if (!make_line_map<TIn>(&mi, a.in, a.rows, ncols_in, a.ld_in) ||
         !make_line_map<TOut>(&mo, a.out, a.rows, a.ncols_out, a.ld_out))
         return uq::fail(UQ_ERR_CUDA, "rht: tensor map encoding failed");
-    if (a.b == 12) return launch_tma_v<TIn, TOut, MODE, 12, 1, COLS>(mi, mo, a, st, nparts);
-    if (a.b == 13) return launch_tma_v<TIn, TOut, MODE, 13, 1, COLS>(mi, mo, a, st, nparts);
-    return launch_tma_v<TIn, TOut, MODE, 13, 2, COLS>(mi, mo, a, st, nparts);
+    // n = 2^b as 2^LB-element parts on a cluster of 2^(b - LB) CTAs.  Measured
+    // on B200: 8192-element parts beat 4096-element parts with one more
+    // cluster stage for n >= 8192 (the distributed-shared-memory stage costs
+    // more than the lower occupancy of the 512-thread tile).
+    switch (a.b) {
+    case 12: return launch_tma_v<TIn, TOut, MODE, 12, 1, COLS>(mi, mo, a, st, nparts);
+    case 13: return launch_tma_v<TIn, TOut, MODE, 13, 1, COLS>(mi, mo, a, st, nparts);
+    case 14: return launch_tma_v<TIn, TOut, MODE, 13, 2, COLS>(mi, mo, a, st, nparts);
+    default: return launch_tma_v<TIn, TOut, MODE, 13, 4, COLS>(mi, mo, a, st, nparts);
+    }
 }
 
 template <typename TIn, typename TOut, int MODE>
@@ -923,7 +939,7 @@ int rht_take_timeout() {
 
 int64_t rht_tiles(int64_t rows, int64_t n) {
     const int b = ilog2(n);
-    if (b >= kTileBits) return 2 * rows;   // at most one partial per half row
+    if (b >= 13) return 4 * rows;   // at most one partial per CTA of a row's cluster
     const int NB = b > 12 ? b : 12;
     return (rows + (1 << (NB - b)) - 1) >> (NB - b);
 }
