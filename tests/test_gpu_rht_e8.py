@@ -149,3 +149,46 @@ def test_q_e8_full_size(uq):
     assert same_bits(rec[pick].cpu().numpy(), O.q_e8_fast(Xs, fixed_step=0.48))
     err = float(((rec - X) ** 2).sum() / (X ** 2).sum())
     assert 0.0 < err < 0.05
+
+
+@pytest.mark.parametrize("step", [0.48, 0.4, 0.25, 0.11, 1.0 / 3.0])
+def test_q_e8_decision_boundaries(uq, step):
+    """Inputs whose scaled coordinates sit on or within 1e-12 of rounding
+    boundaries (constant-magnitude groups: y = +-c / (|c| + 1e-12) / step),
+    exact ties, signed zeros and mixed groups: bit-exact against the oracle
+    (the fp32 screen must hand every undecidable vector to the fp64 path)."""
+    rng = np.random.RandomState(int(step * 1000))
+    groups = []
+    for c in (1.0, 1e8, 3.0, 0.5, 1e-3, 7.25):
+        for pattern in range(6):
+            g = np.full(256, c)
+            if pattern == 1:
+                g *= rng.choice([-1.0, 1.0], 256)
+            elif pattern == 2:
+                g[::3] = -c / 2
+            elif pattern == 3:
+                g[rng.rand(256) < 0.5] = 0.0
+            elif pattern == 4:
+                g = g * (1 + rng.randint(-3, 4, 256) * 2.0 ** -40)
+            elif pattern == 5:
+                g = np.round(rng.normal(size=256) * 4) / 2 * c
+            groups.append(g)
+    groups.append(np.zeros(256))
+    groups.append(-np.zeros(256))
+    z = np.zeros(256)
+    z[::2] = -0.0
+    z[1::2] = 1e-300
+    groups.append(z)
+    A = np.concatenate(groups).reshape(-1, 256)
+    got = uq.q_e8_fast(A, fixed_step=step)
+    ref = O.q_e8_fast(A, fixed_step=step)
+    assert same_bits(got, ref)
+
+
+def test_q_e8_many_rows_vs_oracle(uq):
+    """1 M elements of Student-t data (131 K vectors, a few hundred of them
+    decided by the exact fp64 path): bit-exact."""
+    rng = np.random.RandomState(21)
+    A = rng.standard_t(4, size=(64, 16384)) * 0.02
+    for step in (0.48, 0.3):
+        assert same_bits(uq.q_e8_fast(A, fixed_step=step), O.q_e8_fast(A, fixed_step=step))

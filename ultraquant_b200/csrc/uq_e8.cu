@@ -70,6 +70,75 @@ __device__ __forceinline__ void e8_point(const double y[8], double p[8]) {
     for (int i = 0; i < 8; ++i) p[i] = use_b ? b[i] : a[i];
 }
 
+// ---- screened decode ----------------------------------------------------------
+// The lattice point p depends on y only through 16 roundings, two first-index
+// argmax choices, two signs and one distance comparison.  The screen decodes
+// an fp32 approximation y32 of y (|y32 - y| <= M) and accepts the point only
+// if every one of those decisions holds with a margin larger than the
+// approximation error; the point itself (integers / half-integers) is then
+// exactly the fp64 decode's.  Anything closer than the margins goes to the
+// exact fp64 path.  Margins, with |e| <= 1 for coordinate errors:
+//   roundings: distance to the half-integer boundary > 2M + 2^-22
+//   argmax:    largest |e| exceeds the second largest by > 2M + 2^-22
+//   sign:      |e_k| > M + 2^-22
+//   distances: |da - db| > 48 M + 2^-14 (8 terms, each off by <= 3M, plus
+//              fp32 rounding of sums <= 18)
+__device__ __forceinline__ bool d8_screen(const float y[8], float f[8], float M) {
+    const float tr = 2.f * M + 0x1p-22f;
+    float best = -1.f, second = -1.f;
+    int k = 0;
+    bool ok = true;
+    float sum = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        f[i] = rintf(y[i]);
+        const float ae = fabsf(__fsub_rn(y[i], f[i]));
+        ok &= __fsub_rn(0.5f, ae) > tr;
+        if (ae > best) { second = best; best = ae; k = i; }
+        else if (ae > second) second = ae;
+        sum = __fadd_rn(sum, f[i]);
+    }
+    if (int(sum) & 1) {
+        ok &= __fsub_rn(best, second) > tr;
+        float ek = 0.f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) if (i == k) ek = __fsub_rn(y[i], f[i]);
+        ok &= fabsf(ek) > M + 0x1p-22f;
+        const float sg = ek > 0.f ? 1.f : -1.f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) if (i == k) f[i] = __fadd_rn(f[i], sg);
+    }
+    return ok;
+}
+
+__device__ __forceinline__ float sum8f(const float v[8]) {
+    return __fadd_rn(__fadd_rn(__fadd_rn(v[0], v[1]), __fadd_rn(v[2], v[3])),
+                     __fadd_rn(__fadd_rn(v[4], v[5]), __fadd_rn(v[6], v[7])));
+}
+
+// Returns true and the E8 point of y (given as y32, |y32 - y| <= M) when the
+// screen decides every step; false otherwise.
+__device__ __forceinline__ bool e8_screen(const float y[8], float M, double p[8]) {
+    float a[8], b[8], ym[8], da[8], db[8];
+    bool ok = d8_screen(y, a, M);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) ym[i] = __fsub_rn(y[i], 0.5f);
+    ok &= d8_screen(ym, b, M + 0x1p-24f);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        b[i] = __fadd_rn(b[i], 0.5f);
+        const float ea = __fsub_rn(y[i], a[i]), eb = __fsub_rn(y[i], b[i]);
+        da[i] = __fmul_rn(ea, ea);
+        db[i] = __fmul_rn(eb, eb);
+    }
+    const float sa = sum8f(da), sb = sum8f(db);
+    ok &= fabsf(__fsub_rn(sa, sb)) > __fadd_rn(__fmul_rn(48.f, M), 0x1p-14f);
+    const bool use_b = sb < sa;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) p[i] = double(use_b ? b[i] : a[i]);
+    return ok;
+}
+
 __global__ void d8_kernel(const double *Y, int64_t nvec, double *out, int e8) {
     for (int64_t v = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; v < nvec;
          v += int64_t(gridDim.x) * blockDim.x) {
@@ -161,10 +230,15 @@ __global__ void __launch_bounds__(256, 3) e8_warp_kernel(E8Args a) {
         if (g * G < a.size) a.rms_out[g] = rms;
     }
     if (!a.rec && !a.idx) return;
+    // approximation only (screen); a scale below 2^-100 disables the screen
+    // (fp32 subnormal inputs would no longer meet the error bound)
+    const double rs = d_mul(rms, a.step);
+    const float inv_g = rs >= 0x1p-100 ? float(1.0 / rs) : __int_as_float(0x7fc00000);
     for (int vb = 0; vb < W::VPW; vb += 32) {
         const int vv = vb + lane;
         const int gg = (vv < W::VPW ? vv : W::VPW - 1) / W::VPG;
         const double r = __shfl_sync(0xffffffffu, rms, gg * W::LPG);
+        const float inv = __shfl_sync(0xffffffffu, inv_g, gg * W::LPG);
         if (vv >= W::VPW) continue;
         const int64_t e0 = e_base + 8 * int64_t(vv);
         if (e0 >= a.size) continue;
@@ -185,9 +259,30 @@ __global__ void __launch_bounds__(256, 3) e8_warp_kernel(E8Args a) {
 #pragma unroll
             for (int i = 0; i < 8; ++i) y[i] = e0 + i < a.size ? double(__ldg(A + e0 + i)) : 0.0;
         }
+        // fp32 screen: y32 = RN32(g) * RN32(1 / (rms * step)), |y32 - y| <= |y32| 2^-22.3
+        float y32[8];
+        float ymax = 0.f;
+        bool fin = true;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) y[i] = (y[i] / r) / a.step;
-        e8_point(y, p);
+        for (int i = 0; i < 8; ++i) {
+            y32[i] = __fmul_rn(float(y[i]), inv);
+            ymax = fmaxf(ymax, fabsf(y32[i]));
+            fin &= isfinite(y32[i]);
+        }
+        const float M = __fadd_rn(__fmul_rn(ymax, 0x1p-21f), 0x1p-40f);
+        bool zero = true;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) zero &= y[i] == 0.0;
+        if (zero) {
+            // y = (+-0 / rms) / step = +-0 exactly: the decode keeps each zero
+            // (D8 point 0, coset point at distance 2 > 0)
+#pragma unroll
+            for (int i = 0; i < 8; ++i) p[i] = y[i];
+        } else if (!(fin && ymax < 0x1p20f && e8_screen(y32, M, p))) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) y[i] = (y[i] / r) / a.step;
+            e8_point(y, p);
+        }
         if (a.rec) {
             double o[8];
 #pragma unroll
