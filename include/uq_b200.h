@@ -164,6 +164,21 @@ int uq_trellis_decode_rows(const int32_t *states, const float *cw, const float *
                            int64_t nrow, int64_t T, int64_t Tp, int64_t group,
                            float *out, void *stream);
 
+/* Packed codes of qat.trellis_encode (qat.py:11-33) state paths -- the
+ * L + R (T-1) bits per sequence behind the reference's bits-per-weight
+ * accounting; no counterpart function in the reference.  A path satisfies
+ * s_t = ((s_{t-1} << R) | b_t) mod 2^L, so it is the bit string
+ * S = s_0 2^(R(T-1)) + sum_{t>=1} (s_t mod 2^R) 2^(R(T-1-t)), stored least
+ * significant 32-bit word first, uq_trellis_packed_words(T, L, R) words per
+ * sequence; s_t = (S >> R(T-1-t)) mod 2^L.  Packing keeps only s_0 and the
+ * low R bits of later states: states that are not a trellis path (such as
+ * the Viterbi kernel's output always is) do not survive a round trip. */
+int64_t uq_trellis_packed_words(int T, int L, int R);
+int uq_trellis_pack(const int32_t *states, int64_t nseq, int T, int L, int R, uint32_t *packed,
+                    void *stream);
+int uq_trellis_unpack(const uint32_t *packed, int64_t nseq, int T, int L, int R, int32_t *states,
+                      void *stream);
+
 /* ---------------------------------------------------------------------
  * Differentiable decoder of the QAT step (qat.py:35-59)
  * ------------------------------------------------------------------- */

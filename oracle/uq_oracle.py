@@ -28,7 +28,7 @@ __all__ = [
     "entropy_bpw", "q_e8_fast", "E8_SCALE", "wnmse", "codebook", "pred_table",
     "trellis_quant", "trellis_quant_fast", "trellis_encode", "trellis_decode",
     "fwht_torch", "irht_torch", "recon_torch", "quant_trellis", "quant_step",
-    "group_rms_f32", "viterbi_segments",
+    "group_rms_f32", "viterbi_segments", "pack_states", "unpack_states",
 ]
 
 
@@ -339,3 +339,36 @@ def quant_step(W, H, step):
     sH = np.sqrt(H)[None, :]
     Ah = irht_rows(q_e8_fast(rht_rows(W * sH), fixed_step=step), W.shape[1])
     return (Ah / sH).astype(np.float32)
+
+
+# ---------------------------------------------------------------------------
+# Packed state paths (qat.py:11-33 states; the L + R (T-1) bits per sequence
+# behind the reference's bits-per-weight accounting)
+# ---------------------------------------------------------------------------
+def pack_states(states, L, R):
+    """S = s_0 2^(R(T-1)) + sum_t (s_t mod 2^R) 2^(R(T-1-t)) per sequence, as
+    little-endian 32-bit words (Python integers; small cases only)."""
+    st = np.asarray(states, dtype=np.int64)
+    nseq, T = st.shape
+    words = (L + R * (T - 1) + 31) // 32
+    out = np.zeros((nseq, words), dtype=np.uint32)
+    for i in range(nseq):
+        S = int(st[i, 0]) & ((1 << L) - 1)
+        for t in range(1, T):
+            S = (S << R) | (int(st[i, t]) & ((1 << R) - 1))
+        for w in range(words):
+            out[i, w] = (S >> (32 * w)) & 0xFFFFFFFF
+    return out
+
+
+def unpack_states(packed, T, L, R):
+    """Inverse of pack_states: s_t = (S >> R(T-1-t)) mod 2^L."""
+    pk = np.asarray(packed, dtype=np.uint32)
+    out = np.zeros((pk.shape[0], T), dtype=np.int32)
+    for i in range(pk.shape[0]):
+        S = 0
+        for w in range(pk.shape[1]):
+            S |= int(pk[i, w]) << (32 * w)
+        for t in range(T):
+            out[i, t] = (S >> (R * (T - 1 - t))) & ((1 << L) - 1)
+    return out

@@ -160,3 +160,33 @@ def test_bounded_wait_reports_timeout():
     x = torch.randn(2, 64, device="cuda")
     import ultraquant_b200.trellis as T
     assert T.viterbi_states(x, 12, 2).shape == (2, 64)
+
+
+@pytest.mark.parametrize("T,L,R", [(256, 16, 2), (256, 16, 3), (64, 12, 2), (256, 10, 3), (33, 8, 1),
+                                   (1, 16, 4), (2, 6, 3), (256, 16, 4)])
+def test_pack_states_vs_oracle(T, L, R):
+    """Packed codes: device words equal the oracle's bit strings for random
+    shift-register paths (R = 3 fields straddle words), unpack inverts."""
+    import ultraquant_b200.trellis as T_
+    rng = np.random.RandomState(T * 100 + L * 10 + R)
+    nseq = 37
+    st = np.zeros((nseq, T), dtype=np.int32)
+    st[:, 0] = rng.randint(0, 1 << L, nseq)
+    for t in range(1, T):
+        st[:, t] = ((st[:, t - 1].astype(np.int64) << R) | rng.randint(0, 1 << R, nseq)) & ((1 << L) - 1)
+    pk = T_.pack_states(st, L, R)
+    assert pk.dtype == np.uint32 and np.array_equal(pk, O.pack_states(st, L, R))
+    assert np.array_equal(T_.unpack_states(pk, T, L, R), st)
+
+
+def test_pack_viterbi_paths_roundtrip():
+    """Viterbi output (L = 16, R = 2 and 3) survives pack -> unpack on the device;
+    (L + R (T-1)) / T bits per weight."""
+    import torch
+    import ultraquant_b200.trellis as T_
+    x = torch.randn(300, 256, device="cuda")
+    for R in (2, 3):
+        st = T_.viterbi_states(x, 16, R)
+        pk = T_.pack_states(st, 16, R)
+        assert pk.shape == (300, (16 + R * 255 + 31) // 32)
+        assert torch.equal(T_.unpack_states(pk, 256, 16, R), st)

@@ -180,3 +180,15 @@ def test_recon_torch(g_qat, tag):
                                  meta, g_qat[k + "_sH"], in0)
     assert grad_close(gcw.astype(np.float32), g_qat[k + "_gcw"], gcw)
     assert grad_close(gsc.astype(np.float32), g_qat[k + "_gsc"].reshape(-1), gsc)
+
+
+@pytest.mark.parametrize("L,R,seg", [(8, 2, 64), (12, 2, 64), (10, 3, 256), (16, 4, 256)])
+def test_packed_states_roundtrip(g_trellis, L, R, seg):
+    """Reference encoder paths are shift-register paths: packing keeps them
+    whole in L + R (T-1) bits per sequence."""
+    rng = np.random.RandomState(L * 10 + R)
+    A = rng.normal(size=(4, 256)).astype(np.float32)
+    st, _, _, _ = O.trellis_encode(A, L=L, R=R, seg=seg, scale_group=256)
+    pk = O.pack_states(st, L, R)
+    assert pk.shape[1] == (L + R * (seg - 1) + 31) // 32
+    assert np.array_equal(O.unpack_states(pk, seg, L, R), st)

@@ -596,7 +596,8 @@ viterbi_fwd_kernel(VitArgs a) {
     extern __shared__ __align__(16) float sm_v[];
     __shared__ float red_v[NSET][kThreads / 32];
     __shared__ int red_i[NSET][kThreads / 32];
-    __shared__ __align__(8) unsigned long long full[NSET][NBUF];   // cluster mode: peer half landed
+    __shared__ __align__(8) unsigned long long full[NSET][NBUF];   // cluster mode: step's inputs complete
+    __shared__ unsigned done_cnt[NSET][NBUF];                       // cluster mode: warps done with a step
 
     VitThread<C> th;
     const int tid = threadIdx.x;
@@ -649,8 +650,12 @@ viterbi_fwd_kernel(VitArgs a) {
 
     if (CL == 2) {
         if (tid < NSET * NBUF) {
-            mbar_init(full0 + unsigned(tid) * 8u, 1);
+            // phase completes on: thread 0's arm (arrive + expect_tx), the last
+            // local warp's arrival (all local writes of the step done) and the
+            // peer's bulk copy (OBYTES of transaction)
+            mbar_init(full0 + unsigned(tid) * 8u, 2);
             mbar_expect_tx(full0 + unsigned(tid) * 8u, C::OBYTES);   // arm phase 0
+            done_cnt[tid / NBUF][tid % NBUF] = 0u;
             asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         }
         cluster_arrive();      // peers running and barriers initialised before any copy
@@ -690,11 +695,22 @@ viterbi_fwd_kernel(VitArgs a) {
                     if (tid == 0) mbar_expect_tx(mbr, C::OBYTES);   // arm that buffer's next phase
                 }
                 if (wremote) fence_proxy_async_smem();   // outbox writes -> async proxy
-                __syncthreads();                         // this CTA's step complete
-                if (tid == 0)
-                    bulk_copy_to_peer(peer_smem0 + unsigned(X * NBUF + jw) * BUF + half_off,
-                                      obox0 + unsigned(X * NBUF + jw) * C::OBYTES, C::OBYTES,
-                                      peer_full0 + unsigned(X * NBUF + jw) * 8u);
+                // no CTA barrier: the last warp to finish the step ships the
+                // outbox and releases the local half; warps can run up to one
+                // step apart (a warp at step t+1 has waited for every warp's
+                // step t, which orders all reuse of buffers and outboxes)
+                __syncwarp();
+                if ((tid & 31) == 0) {
+                    __threadfence_block();
+                    const unsigned old = atomicAdd(&done_cnt[X][jw], 1u);
+                    if ((old % (kThreads / 32)) == kThreads / 32 - 1) {
+                        __threadfence_block();
+                        bulk_copy_to_peer(peer_smem0 + unsigned(X * NBUF + jw) * BUF + half_off,
+                                          obox0 + unsigned(X * NBUF + jw) * C::OBYTES, C::OBYTES,
+                                          peer_full0 + unsigned(X * NBUF + jw) * 8u);
+                        mbar_arrive(full0 + unsigned(X * NBUF + jw) * 8u);
+                    }
+                }
             }
             if (valid[X]) bpo[X][int64_t(t) * TPS] = word;
         }
@@ -765,6 +781,55 @@ viterbi_fwd_kernel(VitArgs a) {
             cluster_arrive();   // keep shared memory alive for the peer's reads
             cluster_wait();
         }
+    }
+}
+
+// ---- packed codes --------------------------------------------------------------
+// A state path is a shift register, s_t = ((s_{t-1} << R) | b_t) mod 2^L, so the
+// bit string S = s_0 2^(R(T-1)) + sum_{t>=1} b_t 2^(R(T-1-t)), b_t = s_t mod 2^R,
+// holds it in L + R (T-1) bits, and s_t = (S >> R(T-1-t)) mod 2^L.  S is stored
+// least significant word first, words_per_seq 32-bit words per sequence.
+__global__ void pack_kernel(const int32_t *states, int64_t nseq, int T, int L, int R, int words,
+                            uint32_t *packed) {
+    const int64_t total = nseq * words;
+    for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
+        const int64_t sq = i / words;
+        const int w = int(i % words);
+        const int32_t *st = states + sq * T;
+        const int lo = 32 * w, hi = lo + 32;      // bit range of this word
+        uint64_t acc = 0;
+        // s_0 at offset R (T-1), width L
+        {
+            const int off = R * (T - 1);
+            if (off < hi && off + L > lo) {
+                const uint64_t v = uint64_t(uint32_t(st[0]) & ((1u << L) - 1u));
+                acc |= off >= lo ? (v << (off - lo)) : (v >> (lo - off));
+            }
+        }
+        // b_t at offset R (T-1-t), width R: t with the field overlapping [lo, hi)
+        const int t_first = max(1, T - 1 - (hi - 1) / R);
+        const int t_last = min(T - 1, T - 1 - (lo - R + 1 > 0 ? (lo - R + 1 + R - 1) / R : 0));
+        for (int t = t_first; t <= t_last; ++t) {
+            const int off = R * (T - 1 - t);
+            if (off >= hi || off + R <= lo) continue;
+            const uint64_t v = uint64_t(uint32_t(st[t]) & ((1u << R) - 1u));
+            acc |= off >= lo ? (v << (off - lo)) : (v >> (lo - off));
+        }
+        packed[i] = uint32_t(acc);
+    }
+}
+
+__global__ void unpack_kernel(const uint32_t *packed, int64_t nseq, int T, int L, int R, int words, int32_t *states) {
+    const int64_t total = nseq * T;
+    for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
+        const int64_t sq = i / T;
+        const int t = int(i % T);
+        const int off = R * (T - 1 - t);
+        const uint32_t *p = packed + sq * words;
+        const int w = off >> 5;
+        uint64_t v = __ldg(p + w);
+        if (w + 1 < words) v |= uint64_t(__ldg(p + w + 1)) << 32;
+        states[i] = int32_t((v >> (off & 31)) & ((1ull << L) - 1ull));
     }
 }
 
@@ -1082,6 +1147,33 @@ int uq_trellis_decode_rows(const int32_t *states, const float *cw, const float *
     const int grid = int(std::max<int64_t>(1, std::min<int64_t>((n + 255) / 256, int64_t(uq::num_sms()) * 16)));
     { uq::ProfScope _p("decode_rows", UQ_STREAM(stream)); decode_rows_kernel<<<grid, 256, 0, UQ_STREAM(stream)>>>(states, cw, sc, nrow, T, Tp, group, out); }
     return uq::check_cuda("decode_rows_kernel launch");
+}
+
+int64_t uq_trellis_packed_words(int T, int L, int R) {
+    if (T < 1 || L < 1 || L > 16 || R < 1 || R > 4 || R > L) return 0;
+    return (int64_t(L) + int64_t(R) * (T - 1) + 31) / 32;
+}
+
+int uq_trellis_pack(const int32_t *states, int64_t nseq, int T, int L, int R, uint32_t *packed, void *stream) {
+    const int64_t words = uq_trellis_packed_words(T, L, R);
+    if (nseq < 0 || words == 0) return uq::fail(UQ_ERR_INVALID, "uq_trellis_pack: bad arguments (T=%d L=%d R=%d)", T, L, R);
+    if (nseq == 0) return UQ_OK;
+    if (!states || !packed) return uq::fail(UQ_ERR_INVALID, "uq_trellis_pack: null pointer");
+    const int64_t n = nseq * words;
+    const int grid = int(std::max<int64_t>(1, std::min<int64_t>((n + 255) / 256, int64_t(uq::num_sms()) * 16)));
+    { uq::ProfScope _p("pack", UQ_STREAM(stream)); pack_kernel<<<grid, 256, 0, UQ_STREAM(stream)>>>(states, nseq, T, L, R, int(words), packed); }
+    return uq::check_cuda("pack_kernel launch");
+}
+
+int uq_trellis_unpack(const uint32_t *packed, int64_t nseq, int T, int L, int R, int32_t *states, void *stream) {
+    const int64_t words = uq_trellis_packed_words(T, L, R);
+    if (nseq < 0 || words == 0) return uq::fail(UQ_ERR_INVALID, "uq_trellis_unpack: bad arguments (T=%d L=%d R=%d)", T, L, R);
+    if (nseq == 0) return UQ_OK;
+    if (!states || !packed) return uq::fail(UQ_ERR_INVALID, "uq_trellis_unpack: null pointer");
+    const int64_t n = nseq * T;
+    const int grid = int(std::max<int64_t>(1, std::min<int64_t>((n + 255) / 256, int64_t(uq::num_sms()) * 16)));
+    { uq::ProfScope _p("unpack", UQ_STREAM(stream)); unpack_kernel<<<grid, 256, 0, UQ_STREAM(stream)>>>(packed, nseq, T, L, R, int(words), states); }
+    return uq::check_cuda("unpack_kernel launch");
 }
 
 }  // extern "C"

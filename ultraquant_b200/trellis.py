@@ -15,7 +15,7 @@ from . import _device as D
 from . import _lib
 
 __all__ = ["codebook", "pred_table", "trellis_quant", "trellis_quant_fast", "encode_segments",
-           "viterbi_states"]
+           "viterbi_states", "packed_words", "pack_states", "unpack_states"]
 
 
 def _dev(device) -> torch.device:
@@ -116,3 +116,45 @@ def trellis_quant(A, L=10, R=2, group=256, chunk_rows=512, device="cuda"):
         _lib.check(lib.uq_trellis_decode_rows(states.data_ptr(), cw.data_ptr(), sc.data_ptr(), nrow, T, Tp,
                                               group, out.data_ptr(), st), "decode_rows")
     return out if isinstance(A, torch.Tensor) and A.is_cuda else D.to_host(out)
+
+
+# ---------------------------------------------------------------------------
+# Packed codes (the L + R (T-1) bits per sequence behind the reference's
+# bits-per-weight accounting of qat.trellis_encode's state paths)
+# ---------------------------------------------------------------------------
+def packed_words(T: int, L: int, R: int) -> int:
+    """32-bit words per packed sequence of T states."""
+    return int(_lib.load().uq_trellis_packed_words(int(T), int(L), int(R)))
+
+
+def pack_states(states, L: int, R: int):
+    """(nseq, T) int32 state paths -> (nseq, packed_words) uint32 bit strings
+    S = s_0 2^(R(T-1)) + sum_t (s_t mod 2^R) 2^(R(T-1-t)), low word first.
+    numpy in -> numpy out; CUDA tensors in -> CUDA tensors out."""
+    lib = _lib.load()
+    on_dev = isinstance(states, torch.Tensor) and states.is_cuda
+    st = states if on_dev else torch.from_numpy(np.ascontiguousarray(np.asarray(states, dtype=np.int32)))
+    st = st.to(D.device() if not on_dev else st.device).to(torch.int32).contiguous()
+    nseq, T = st.shape
+    words = packed_words(T, L, R)
+    if words == 0:
+        raise ValueError(f"pack_states: unsupported T={T} L={L} R={R}")
+    out = torch.empty((nseq, words), dtype=torch.int32, device=st.device)
+    _lib.check(lib.uq_trellis_pack(st.data_ptr(), nseq, T, L, R, out.data_ptr(), D.stream_handle(st.device)),
+               "pack_states")
+    return out if on_dev else D.to_host(out).view(np.uint32)
+
+
+def unpack_states(packed, T: int, L: int, R: int):
+    """Inverse of pack_states: (nseq, packed_words) -> (nseq, T) int32."""
+    lib = _lib.load()
+    on_dev = isinstance(packed, torch.Tensor) and packed.is_cuda
+    pk = packed if on_dev else torch.from_numpy(np.ascontiguousarray(np.asarray(packed).view(np.int32)))
+    pk = pk.to(D.device() if not on_dev else pk.device).contiguous()
+    nseq = pk.shape[0]
+    if pk.shape[1] != packed_words(T, L, R):
+        raise ValueError(f"unpack_states: {pk.shape[1]} words per sequence, expected {packed_words(T, L, R)}")
+    out = torch.empty((nseq, T), dtype=torch.int32, device=pk.device)
+    _lib.check(lib.uq_trellis_unpack(pk.data_ptr(), nseq, T, L, R, out.data_ptr(), D.stream_handle(pk.device)),
+               "unpack_states")
+    return out if on_dev else D.to_host(out)
