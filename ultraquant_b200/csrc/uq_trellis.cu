@@ -424,8 +424,17 @@ __device__ __forceinline__ unsigned long long global_ns() {
 // Waits for the phase with the given parity.  Bounded: after ~2 s the thread
 // records a timeout in *err, stops waiting from then on (fail becomes true)
 // and carries on, so the kernel always runs to its end.
+__device__ __noinline__ void mbar_wait_slow(unsigned addr, unsigned parity, bool &fail, int *err,
+                                            unsigned long long limit_ns);
 __device__ __forceinline__ void mbar_wait(unsigned addr, unsigned parity, bool &fail, int *err,
                                           unsigned long long limit_ns = 2000000000ull) {
+    unsigned ready;
+    asm volatile("{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+                 "selp.u32 %0, 1, 0, p;\n\t}" : "=r"(ready) : "r"(addr), "r"(parity) : "memory");
+    if (!ready) mbar_wait_slow(addr, parity, fail, err, limit_ns);
+}
+__device__ __noinline__ void mbar_wait_slow(unsigned addr, unsigned parity, bool &fail, int *err,
+                                            unsigned long long limit_ns) {
     if (fail) return;
     unsigned done = 0;
     unsigned long long t0 = 0;
@@ -626,27 +635,30 @@ viterbi_fwd_kernel(VitArgs a) {
     constexpr unsigned BUF = unsigned(C::FLOATS * 4);
     // cluster mode: outboxes follow the buffers; the peer's share of this
     // thread's outputs (bit TBIT of v names the reading CTA) goes there
-    const unsigned obox0 = smem0 + unsigned(NSET * NBUF) * BUF;
+    const unsigned obox0 = smem0 + unsigned(NSET * NBUF) * BUF;   // (cluster mode; derived where used)
     const bool wremote = CL == 2 && (((th.v >> C::TBIT) & 1) != int(th.rank));
     const unsigned half_off = th.rank * C::OBYTES;     // this CTA produces half `rank` of each buffer
     const unsigned full0 = unsigned(__cvta_generic_to_shared(&full[0][0]));
-    const unsigned peer_smem0 = CL == 2 ? mapa_shared(smem0, th.rank ^ 1u) : 0u;
-    const unsigned peer_full0 = CL == 2 ? mapa_shared(full0, th.rank ^ 1u) : 0u;
+    // where this thread's step outputs go: the local buffer, or (values the
+    // peer reads) the outbox, whose offset 0 is the peer's half `rank`
+    const unsigned wbase0 = wremote ? obox0 - half_off : smem0;
+    const unsigned wstep = wremote ? unsigned(C::OBYTES) : BUF;
     bool fail = false;
 
-    int64_t seq[NSET];
-    bool valid[NSET];
-    const float *xrow[NSET];
-    float xv[NSET];
-    uint32_t *bpo[NSET];
+    // set X is sequence first + X (cluster mode) or first (CTA mode, one set);
+    // the sets' inputs and backpointers are at fixed offsets from set 0's, so
+    // one input pointer, one backpointer pointer and a validity mask carry
+    // them (registers are at the 128 limit)
+    const int64_t first = seq_base + (CL == 1 ? th.slot : 0);
+    const int64_t bstride = int64_t(a.T - 1) * TPS;
+    unsigned vmask = 0;
 #pragma unroll
-    for (int X = 0; X < NSET; ++X) {
-        seq[X] = seq_base + (CL == 1 ? th.slot : X);
-        valid[X] = seq[X] < a.nbatch;
-        xrow[X] = a.xn + (a.seq0 + (valid[X] ? seq[X] : 0)) * int64_t(a.T);
-        xv[X] = valid[X] ? __ldg(xrow[X]) : 0.f;
-        bpo[X] = a.bp + (valid[X] ? seq[X] : 0) * (int64_t(a.T - 1) * TPS) + th.v;
-    }
+    for (int X = 0; X < NSET; ++X) vmask |= (first + X < a.nbatch ? 1u : 0u) << X;
+    const float *xcur = a.xn + (a.seq0 + (vmask & 1u ? first : 0)) * int64_t(a.T);
+    uint32_t *bcur = a.bp + (vmask & 1u ? first : 0) * bstride + th.v;
+    float xv[NSET];
+#pragma unroll
+    for (int X = 0; X < NSET; ++X) xv[X] = (vmask >> X) & 1u ? __ldg(xcur + X * int64_t(a.T)) : 0.f;
 
     if (CL == 2) {
         if (tid < NSET * NBUF) {
@@ -667,7 +679,7 @@ viterbi_fwd_kernel(VitArgs a) {
 #pragma unroll
         for (int X = 0; X < NSET; ++X) {
             const float x = xv[X];
-            xv[X] = valid[X] ? __ldg(xrow[X] + t + 1) : 0.f;
+            xv[X] = (vmask >> X) & 1u ? __ldg(xcur + X * int64_t(a.T) + t + 1) : 0.f;
             unsigned word;
             if (CL == 1) {
                 const unsigned wb = smem0 + unsigned(X * NBUF + (t & 1)) * BUF;
@@ -681,9 +693,8 @@ viterbi_fwd_kernel(VitArgs a) {
             } else {
                 const int jw = t & 1;
                 // local values into buffer jw, the peer's share into outbox jw
-                const unsigned wb = wremote ? obox0 + unsigned(X * NBUF + jw) * C::OBYTES
-                                            : smem0 + unsigned(X * NBUF + jw) * BUF;
-                const unsigned wsh = wremote ? half_off : 0u;
+                const unsigned wb = wbase0 + unsigned(X * NBUF + jw) * wstep;
+                const unsigned wsh = 0u;
                 if (t == 0) {
                     word = th.template step<false>(x, m, wb, wsh);
                 } else {
@@ -701,19 +712,21 @@ viterbi_fwd_kernel(VitArgs a) {
                 // step t, which orders all reuse of buffers and outboxes)
                 __syncwarp();
                 if ((tid & 31) == 0) {
-                    __threadfence_block();
-                    const unsigned old = atomicAdd(&done_cnt[X][jw], 1u);
+                    // acq_rel: releases this warp's step, acquires all earlier warps'
+                    unsigned old;
+                    asm volatile("atom.acq_rel.cta.shared::cta.add.u32 %0, [%1], 1;"
+                                 : "=r"(old) : "r"(unsigned(__cvta_generic_to_shared(&done_cnt[X][jw]))) : "memory");
                     if ((old % (kThreads / 32)) == kThreads / 32 - 1) {
-                        __threadfence_block();
-                        bulk_copy_to_peer(peer_smem0 + unsigned(X * NBUF + jw) * BUF + half_off,
+                        bulk_copy_to_peer(mapa_shared(smem0 + unsigned(X * NBUF + jw) * BUF + half_off, th.rank ^ 1u),
                                           obox0 + unsigned(X * NBUF + jw) * C::OBYTES, C::OBYTES,
-                                          peer_full0 + unsigned(X * NBUF + jw) * 8u);
+                                          mapa_shared(full0 + unsigned(X * NBUF + jw) * 8u, th.rank ^ 1u));
                         mbar_arrive(full0 + unsigned(X * NBUF + jw) * 8u);
                     }
                 }
             }
-            if (valid[X]) bpo[X][int64_t(t) * TPS] = word;
+            if ((vmask >> X) & 1u) bcur[X * bstride] = word;
         }
+        bcur += TPS;
     }
     // final step: argmin over all states of cost_{T-1}
 #pragma unroll
@@ -738,7 +751,7 @@ viterbi_fwd_kernel(VitArgs a) {
             if (better(ov, oi, bv, bi)) { bv = ov; bi = oi; }
         }
         if (TPS <= 32) {
-            if ((tid % TPS) == 0 && valid[X]) a.fin[seq[X]] = bi;
+            if ((tid % TPS) == 0 && ((vmask >> X) & 1u)) a.fin[first + X] = bi;
         } else if ((tid & 31) == 0) {
             red_v[X][tid >> 5] = bv;
             red_i[X][tid >> 5] = bi;
@@ -754,7 +767,7 @@ viterbi_fwd_kernel(VitArgs a) {
                 int bi = red_i[0][w0];
                 for (int w = 1; w < wps; ++w)
                     if (better(red_v[0][w0 + w], red_i[0][w0 + w], bv, bi)) { bv = red_v[0][w0 + w]; bi = red_i[0][w0 + w]; }
-                if (valid[0]) a.fin[seq[0]] = bi;
+                if (vmask & 1u) a.fin[first] = bi;
             }
         } else {
             cluster_arrive();
@@ -775,7 +788,7 @@ viterbi_fwd_kernel(VitArgs a) {
                         asm volatile("ld.shared::cluster.s32 %0, [%1];" : "=r"(oi) : "r"(ri + 4u * w));
                         if (better(ov, oi, bv, bi)) { bv = ov; bi = oi; }
                     }
-                    if (valid[X]) a.fin[seq[X]] = bi;
+                    if ((vmask >> X) & 1u) a.fin[first + X] = bi;
                 }
             }
             cluster_arrive();   // keep shared memory alive for the peer's reads
