@@ -21,6 +21,7 @@ inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 int num_sms();
 int qat_take_bad_state();   // uq_qat.cu
 int rht_take_timeout();     // uq_rht.cu
+int e8_take_timeout();      // uq_e8.cu
 
 // Launch accounting / optional per-launch event timing (see uq_profile_*).
 void count_launch();

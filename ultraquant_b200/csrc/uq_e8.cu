@@ -19,6 +19,7 @@
 
 #include "uq_common.cuh"
 #include "uq_groupsum.cuh"
+#include "uq_tma.cuh"
 #include "uq_mt19937.h"
 
 namespace {
@@ -315,6 +316,149 @@ __global__ void __launch_bounds__(256, 3) e8_warp_kernel(E8Args a) {
     }
 }
 
+// ---- tensor-map form (fp64 input and output, groups of 256) ------------------
+// Persistent warps walk 512-element chunks (two groups).  A warp's next chunk
+// is loaded by a tensor-map copy (4 KB, 128-byte swizzled lines) into the
+// second of its two shared buffers while it quantizes the current one; group
+// sums read the chunk in numpy's chain order, 8-vectors are read and their
+// reconstructions written back with conflict-free 16-byte accesses, and the
+// chunk leaves by a tensor-map store.  Same arithmetic as e8_warp_kernel.
+__device__ int g_e8_timeout = 0;
+
+constexpr int kE8ChunkBytes = 4096;
+
+__global__ void __launch_bounds__(256, 2)
+e8_tma_kernel(const __grid_constant__ CUtensorMap tin, const __grid_constant__ CUtensorMap tout, E8Args a,
+              int64_t nchunks) {
+    using W = WarpGroup<256>;
+    extern __shared__ __align__(1024) unsigned char e8_smem_raw[];
+    __shared__ __align__(8) unsigned long long bars[8][2];
+    unsigned char *sm = e8_smem_raw + ((1024u - (unsigned(__cvta_generic_to_shared(e8_smem_raw)) & 1023u)) & 1023u);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const unsigned buf0 = unsigned(__cvta_generic_to_shared(sm)) + unsigned(warp * 2 * kE8ChunkBytes);
+    const unsigned bar0 = unsigned(__cvta_generic_to_shared(&bars[warp][0]));
+    const int64_t nwarps = int64_t(gridDim.x) * 8;
+    int64_t c = int64_t(blockIdx.x) * 8 + warp;
+    if (lane == 0) {
+        uq::tma::mbar_init(bar0, 1);
+        uq::tma::mbar_init(bar0 + 8, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        if (c < nchunks) {
+            uq::tma::mbar_arrive_expect_tx(bar0, kE8ChunkBytes);
+            uq::tma::load2d(buf0, &tin, 0, int(32 * c), bar0);
+        }
+    }
+    __syncwarp();
+    bool fail = false;
+    for (int k = 0; c < nchunks; c += nwarps, ++k) {
+        const unsigned buf = buf0 + unsigned((k & 1) * kE8ChunkBytes);
+        if (lane == 0 && c + nwarps < nchunks) {
+            uq::tma::bulk_wait_read0();   // the store that last used the other buffer has read it
+            const unsigned nb = bar0 + 8u * unsigned((k + 1) & 1);
+            uq::tma::mbar_arrive_expect_tx(nb, kE8ChunkBytes);
+            uq::tma::load2d(buf0 + unsigned(((k + 1) & 1) * kE8ChunkBytes), &tin, 0, int(32 * (c + nwarps)), nb);
+        }
+        uq::tma::mbar_wait_bounded(bar0 + 8u * unsigned(k & 1), unsigned((k >> 1) & 1), fail, &g_e8_timeout);
+        auto get = [&](int i) -> double { return uq::tma::lds64d(buf + uq::tma::swz128<double>(i)); };
+        const double ss = warp_group_sumsq<256, double>(get);
+        const double rms = d_add(sqrt(ss / 256.0), 1e-12);
+        const int64_t e_base = c * 512;
+        if (a.rms_out && (lane % W::LPG) == 0) a.rms_out[e_base / 256 + lane / W::LPG] = rms;
+        const double rs = d_mul(rms, a.step);
+        const float inv_g = rs >= 0x1p-100 ? float(1.0 / rs) : __int_as_float(0x7fc00000);
+#pragma unroll
+        for (int vb = 0; vb < 64; vb += 32) {
+            const int vv = vb + lane;                 // vector of the chunk
+            const int gg = vv / W::VPG;
+            const double r = __shfl_sync(0xffffffffu, rms, gg * W::LPG);
+            const float inv = __shfl_sync(0xffffffffu, inv_g, gg * W::LPG);
+            const int ln = vv >> 1, h = vv & 1;
+            unsigned addr[4];
+            double y[8], p[8];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                addr[q] = buf + unsigned(ln * 128 + (((4 * h + q) ^ (ln & 7)) << 4));
+                const double2 t = uq::tma::lds128d(addr[q]);
+                y[2 * q] = t.x;
+                y[2 * q + 1] = t.y;
+            }
+            float y32[8];
+            float ymax = 0.f;
+            bool fin = true, zero = true;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                y32[i] = __fmul_rn(float(y[i]), inv);
+                ymax = fmaxf(ymax, fabsf(y32[i]));
+                fin &= isfinite(y32[i]);
+                zero &= y[i] == 0.0;
+            }
+            const float M = __fadd_rn(__fmul_rn(ymax, 0x1p-21f), 0x1p-40f);
+            if (zero) {
+#pragma unroll
+                for (int i = 0; i < 8; ++i) p[i] = y[i];
+            } else if (!(fin && ymax < 0x1p20f && e8_screen(y32, M, p))) {
+#pragma unroll
+                for (int i = 0; i < 8; ++i) y[i] = (y[i] / r) / a.step;
+                e8_point(y, p);
+            }
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+                uq::tma::sts128d(addr[q], d_mul(d_mul(p[2 * q], a.step), r), d_mul(d_mul(p[2 * q + 1], a.step), r));
+            if (a.idx) {
+                short o[8];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) o[i] = (short)(long long)d_mul(p[i], 2.0);
+                int4 pk;
+                pk.x = (unsigned short)o[0] | ((unsigned)(unsigned short)o[1] << 16);
+                pk.y = (unsigned short)o[2] | ((unsigned)(unsigned short)o[3] << 16);
+                pk.z = (unsigned short)o[4] | ((unsigned)(unsigned short)o[5] << 16);
+                pk.w = (unsigned short)o[6] | ((unsigned)(unsigned short)o[7] << 16);
+                *reinterpret_cast<int4 *>(a.idx + e_base + 8 * vv) = pk;
+            }
+        }
+        uq::tma::fence_proxy_async();
+        __syncwarp();
+        if (lane == 0) {
+            uq::tma::store2d(&tout, 0, int(32 * c), buf);
+            uq::tma::bulk_commit();
+        }
+        __syncwarp();
+    }
+    if (lane == 0) uq::tma::bulk_wait0();
+}
+
+// Uses the tensor-map form for the whole 512-element chunks when it applies
+// (fp64 in / out, group 256, 16-byte aligned rec and idx); returns the number
+// of elements it covered (the rest goes to e8_warp_kernel), or -1 on error.
+int64_t launch_e8_tma(const E8Args &a, cudaStream_t st) {
+    if (a.group != 256 || !a.rec || (reinterpret_cast<uintptr_t>(a.A) & 15) || (reinterpret_cast<uintptr_t>(a.rec) & 15) ||
+        (a.idx && (reinterpret_cast<uintptr_t>(a.idx) & 15)) || !uq::tma::encode_fn())
+        return 0;
+    const int64_t nchunks = a.size / 512;
+    if (nchunks < 1 || nchunks * 32 > (int64_t(1) << 31)) return 0;
+    CUtensorMap mi, mo;
+    const cuuint64_t dims[2] = {16, cuuint64_t(nchunks * 32)};
+    const cuuint64_t strides[1] = {128};
+    const cuuint32_t box[2] = {16, 32};
+    if (!uq::tma::encode_lines(&mi, true, 2, a.A, dims, strides, box) ||
+        !uq::tma::encode_lines(&mo, true, 2, a.rec, dims, strides, box))
+        return 0;
+    const size_t smem = size_t(8) * 2 * kE8ChunkBytes + 1024;
+    if (cudaFuncSetAttribute(e8_tma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess) {
+        uq::check_cuda("e8 tma: set smem attribute");
+        return -1;
+    }
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, e8_tma_kernel, 256, smem) != cudaSuccess || per_sm < 1) {
+        uq::check_cuda("e8 tma: occupancy");
+        return -1;
+    }
+    const int64_t blocks = std::min<int64_t>((nchunks + 7) / 8, int64_t(per_sm) * uq::num_sms());
+    { uq::ProfScope _p("e8_quant", st); e8_tma_kernel<<<unsigned(blocks), 256, smem, st>>>(mi, mo, a, nchunks); }
+    if (uq::check_cuda("e8_tma_kernel launch") != UQ_OK) return -1;
+    return nchunks * 512;
+}
+
 template <typename TIn, int G>
 int launch_e8_warp(const E8Args &a, cudaStream_t st) {
     using W = WarpGroup<G>;
@@ -348,6 +492,21 @@ int e8_tile_elems(int group) {
 
 template <typename TIn>
 int launch_e8_quant(const E8Args &a0, cudaStream_t st) {
+    if (sizeof(TIn) == 8) {
+        const int64_t done = launch_e8_tma(a0, st);
+        if (done < 0) return UQ_ERR_CUDA;
+        if (done == a0.size) return UQ_OK;
+        if (done > 0) {
+            // the tail (less than one chunk; whole groups) through the warp kernel
+            E8Args t = a0;
+            t.A = static_cast<const double *>(a0.A) + done;
+            t.size = a0.size - done;
+            t.rec = a0.rec + done;
+            if (a0.idx) t.idx = a0.idx + done;
+            if (a0.rms_out) t.rms_out = a0.rms_out + done / 256;
+            return dispatch_e8_warp<TIn>(t, st);
+        }
+    }
     {
         const int rc = dispatch_e8_warp<TIn>(a0, st);
         if (rc >= 0) return rc;
@@ -529,6 +688,15 @@ size_t calib_ws_bytes(int64_t size, int64_t group, CalWs *w, void *base) {
 }  // namespace
 
 namespace uq {
+// Reads and clears the timeout flag of the tensor-map quantizer's bounded waits
+// (after the caller synchronised); -1 on a CUDA error.
+int e8_take_timeout() {
+    int flag = 0, zero = 0;
+    if (cudaMemcpyFromSymbol(&flag, g_e8_timeout, sizeof(int)) != cudaSuccess) return -1;
+    if (flag && cudaMemcpyToSymbol(g_e8_timeout, &zero, sizeof(int)) != cudaSuccess) return -1;
+    return flag;
+}
+
 int e8_quant(const void *A, int a_dtype, int64_t size, int64_t group, double step, double *rec,
              int16_t *idx, double *rms_out, cudaStream_t st) {
     E8Args a{};

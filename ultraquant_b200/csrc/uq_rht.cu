@@ -20,14 +20,13 @@
 // half and run as above; the last stage (h = 16384) pairs element i of the
 // first half with element i of the second, which each CTA reads from its
 // partner's shared memory (distributed shared memory, plain loads).
-#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
-#include <mutex>
 #include <stdint.h>
 
 #include "uq_common.cuh"
+#include "uq_tma.cuh"
 
 namespace {
 
@@ -432,65 +431,13 @@ rht_split_kernel(RhtArgs a) {
 // ---------------------------------------------------------------------------
 __device__ int g_rht_timeout = 0;
 
-__device__ __forceinline__ void rmb_init(unsigned addr, unsigned count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" :: "r"(addr), "r"(count) : "memory");
-}
-__device__ __forceinline__ void rmb_expect_tx(unsigned addr, unsigned bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" :: "r"(addr), "r"(bytes) : "memory");
-}
-// Bounded wait (2 s) on a phase parity; gives up with a sticky flag.
+using namespace uq::tma;
+
 __device__ __forceinline__ void rmb_wait(unsigned addr, unsigned parity, bool &fail) {
-    if (fail) return;
-    unsigned long long t0 = 0;
-    for (unsigned it = 0;; ++it) {
-        unsigned done;
-        asm volatile("{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-                     "selp.u32 %0, 1, 0, p;\n\t}" : "=r"(done) : "r"(addr), "r"(parity) : "memory");
-        if (done) return;
-        if ((it & 63) == 0) {
-            unsigned long long now;
-            asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(now));
-            if (it == 0) t0 = now;
-            else if (now - t0 > 2000000000ull) {
-                fail = true;
-                atomicExch(&g_rht_timeout, 1);
-                return;
-            }
-        }
-    }
+    mbar_wait_bounded(addr, parity, fail, &g_rht_timeout);
 }
-__device__ __forceinline__ void tma_load3(unsigned dst, const CUtensorMap *map, int c0, int c1, int c2, unsigned mbar) {
-    asm volatile("cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];"
-                 :: "r"(dst), "l"(map), "r"(c0), "r"(c1), "r"(c2), "r"(mbar) : "memory");
-}
-__device__ __forceinline__ void tma_store3(const CUtensorMap *map, int c0, int c1, int c2, unsigned src) {
-    asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%1, %2, %3}], [%4];"
-                 :: "l"(map), "r"(c0), "r"(c1), "r"(c2), "r"(src) : "memory");
-}
-__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
-__device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
-__device__ __forceinline__ void bulk_wait0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 __device__ __forceinline__ double flip_if(double v, unsigned neg) {
     return __longlong_as_double(__double_as_longlong(v) ^ (static_cast<long long>(neg) << 63));
-}
-__device__ __forceinline__ float4 lds128f(unsigned addr) {
-    float4 v;
-    asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr));
-    return v;
-}
-__device__ __forceinline__ double2 lds128d(unsigned addr) {
-    double2 v;
-    asm volatile("ld.shared.v2.f64 {%0,%1}, [%2];" : "=d"(v.x), "=d"(v.y) : "r"(addr));
-    return v;
-}
-
-// Byte offset of local element E in the 128-byte-line swizzled layout of a
-// T buffer (16-byte chunk c of line r stored at chunk c ^ (r & 7)).
-template <typename T> __device__ __forceinline__ unsigned line_off(int E) {
-    constexpr int EPL = 128 / int(sizeof(T));      // elements per line
-    constexpr int EPC = 16 / int(sizeof(T));       // elements per chunk
-    const int r = E / EPL, c = (E % EPL) / EPC;
-    return unsigned(r * 128 + ((c ^ (r & 7)) << 4) + (E % EPC) * int(sizeof(T)));
 }
 
 template <typename TIn, typename TOut, int MODE, int LB, int CL, bool COLS>
@@ -523,16 +470,16 @@ rht_tma_kernel(const __grid_constant__ CUtensorMap tin, const __grid_constant__ 
     const int lout0 = int(col0 / (128 / int(sizeof(TOut))));
 
     if (tid == 0) {
-        rmb_init(bar0, 1);
-        rmb_init(bar0 + 8, 1);
+        mbar_init(bar0, 1);
+        mbar_init(bar0 + 8, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     __syncthreads();
     if (tid == 0 && first < a.rows) {
-        rmb_expect_tx(bar0, NBOX * INB);
+        mbar_arrive_expect_tx(bar0, NBOX * INB);
 #pragma unroll
         for (int bx = 0; bx < NBOX; ++bx)
-            tma_load3(sbase + bx * INB, &tin, 0, lin0 + bx * CH_IN, int(first), bar0);
+            load3d(sbase + bx * INB, &tin, 0, lin0 + bx * CH_IN, int(first), bar0);
     }
     // per-thread constants: pass-0 columns 16 tid + j, last-pass columns tid + (j << (LB - 4))
     double pre_r[COLS && MODE == MODE_FWD ? 16 : 1];
@@ -593,10 +540,10 @@ rht_tma_kernel(const __grid_constant__ CUtensorMap tin, const __grid_constant__ 
         if (tid == 0 && r + nclusters < a.rows) {
             bulk_wait_read0();
             const unsigned nb = bar0 + 8u * unsigned((k + 1) & 1);
-            rmb_expect_tx(nb, NBOX * INB);
+            mbar_arrive_expect_tx(nb, NBOX * INB);
 #pragma unroll
             for (int bx = 0; bx < NBOX; ++bx)
-                tma_load3(sbase + unsigned(((k + 1) & 1) * BUFB) + bx * INB, &tin, 0, lin0 + bx * CH_IN,
+                load3d(sbase + unsigned(((k + 1) & 1) * BUFB) + bx * INB, &tin, 0, lin0 + bx * CH_IN,
                           int(r + nclusters), nb);
         }
         // ---- passes 4, 8, ...: transposes through the element-swizzled tile ----
@@ -657,11 +604,11 @@ rht_tma_kernel(const __grid_constant__ CUtensorMap tin, const __grid_constant__ 
                     y = xs / __ldg(a.pre + e);
                 }
             }
-            const unsigned o = buf + line_off<TOut>(E);
+            const unsigned o = buf + swz128<TOut>(E);
             if (sizeof(TOut) == 8) asm volatile("st.shared.f64 [%0], %1;" :: "r"(o), "d"(y) : "memory");
             else asm volatile("st.shared.f32 [%0], %1;" :: "r"(o), "f"(float(y)) : "memory");
         }
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        fence_proxy_async();
         if (MODE == MODE_INV && COLS && a.err_partial) {
             for (int o = 16; o > 0; o >>= 1) {
                 se = d_add(se, __shfl_xor_sync(0xffffffffu, se, o));
@@ -673,7 +620,7 @@ rht_tma_kernel(const __grid_constant__ CUtensorMap tin, const __grid_constant__ 
         if (tid == 0) {
 #pragma unroll
             for (int bx = 0; bx < NBOX; ++bx)
-                tma_store3(&tout, 0, lout0 + bx * CH_OUT, int(r), buf + unsigned(bx * OUTB));
+                store3d(&tout, 0, lout0 + bx * CH_OUT, int(r), buf + unsigned(bx * OUTB));
             bulk_commit();
             if (MODE == MODE_INV && COLS && a.err_partial) {
                 double s0 = 0.0, s1 = 0.0;
@@ -715,38 +662,15 @@ __global__ void prescale_kernel(const double *colscale, const double *signs, int
 }
 
 // ---- tensor maps -------------------------------------------------------------
-using EncodeTiled = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
-                                 const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
-                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-EncodeTiled encode_fn() {
-    static EncodeTiled fn = nullptr;
-    static std::once_flag once;
-    std::call_once(once, [] {
-        void *p = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<EncodeTiled>(p);
-    });
-    return fn;
-}
-
 // (rows, ncols) matrix of T with row stride ld, viewed as 128-byte lines:
 // dims {elements per line, lines per row, rows}, box = 4096 elements of one row.
 template <typename T>
 bool make_line_map(CUtensorMap *m, const void *base, int64_t rows, int64_t ncols, int64_t ld) {
-    EncodeTiled fn = encode_fn();
-    if (!fn) return false;
     constexpr int EPL = 128 / int(sizeof(T));
     const cuuint64_t dims[3] = {cuuint64_t(EPL), cuuint64_t(ncols / EPL), cuuint64_t(rows)};
     const cuuint64_t strides[2] = {128, cuuint64_t(ld) * sizeof(T)};
     const cuuint32_t box[3] = {cuuint32_t(EPL), cuuint32_t(4096 / EPL), 1};
-    const cuuint32_t estr[3] = {1, 1, 1};
-    return fn(m, sizeof(T) == 8 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT64 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3,
-              const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-              CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+    return encode_lines(m, sizeof(T) == 8, 3, base, dims, strides, box);
 }
 
 // The TMA form applies to n in {4096, 8192, 16384} with 16-byte aligned

@@ -1071,9 +1071,9 @@ int uq_device_errors(void *stream) {
         cudaMemcpyToSymbol(g_vit_timeout, &zero, sizeof(int));
         return uq::fail(UQ_ERR_TIMEOUT, "a bounded device wait of the Viterbi cluster exchange timed out");
     }
-    const int rto = uq::rht_take_timeout();
-    if (rto < 0) return uq::check_cuda("read transform timeout flag");
-    if (rto) return uq::fail(UQ_ERR_TIMEOUT, "a bounded device wait of the tensor-map transform timed out");
+    const int rto = uq::rht_take_timeout(), eto = uq::e8_take_timeout();
+    if (rto < 0 || eto < 0) return uq::check_cuda("read tensor-map timeout flags");
+    if (rto || eto) return uq::fail(UQ_ERR_TIMEOUT, "a bounded device wait of a tensor-map kernel timed out");
     const int bad = uq::qat_take_bad_state();
     if (bad < 0) return uq::check_cuda("read decoder state flag");
     if (bad) return uq::fail(UQ_ERR_INVALID, "a trellis state given to the decoder lies outside the codebook");
