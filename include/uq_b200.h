@@ -180,6 +180,22 @@ int uq_trellis_unpack(const uint32_t *packed, int64_t nseq, int T, int L, int R,
                       void *stream);
 
 /* ---------------------------------------------------------------------
+ * Q8_0 blocks at either side of the path (GGUF container of the builders)
+ * ------------------------------------------------------------------- */
+
+/* buildq.py:21-30 enc_q8(W): W (rows, cols) float32 or float64 (converted to
+ * float32 first), row stride ldw, cols a multiple of 32; out (rows, cols/32*34)
+ * bytes: per block of 32, float16(max|x| / 127, 0 -> 1e-9) little endian,
+ * then 32 int8 round-half-even(x / scale) clipped to [-127, 127]. */
+int uq_q8_encode(const void *W, int w_dtype, int64_t rows, int64_t cols, int64_t ldw,
+                 uint8_t *out, void *stream);
+
+/* qlab.py:27-32 deq_q8(t): blocks as above (rows, cols/32*34 bytes) ->
+ * out (rows, cols) float32 = float32(scale) * q, row stride ld_out. */
+int uq_q8_decode(const uint8_t *q8, int64_t rows, int64_t cols, float *out, int64_t ld_out,
+                 void *stream);
+
+/* ---------------------------------------------------------------------
  * Differentiable decoder of the QAT step (qat.py:35-59)
  * ------------------------------------------------------------------- */
 

@@ -28,7 +28,7 @@ __all__ = [
     "entropy_bpw", "q_e8_fast", "E8_SCALE", "wnmse", "codebook", "pred_table",
     "trellis_quant", "trellis_quant_fast", "trellis_encode", "trellis_decode",
     "fwht_torch", "irht_torch", "recon_torch", "quant_trellis", "quant_step",
-    "group_rms_f32", "viterbi_segments", "pack_states", "unpack_states",
+    "group_rms_f32", "viterbi_segments", "pack_states", "unpack_states", "enc_q8", "deq_q8",
 ]
 
 
@@ -372,3 +372,30 @@ def unpack_states(packed, T, L, R):
         for t in range(T):
             out[i, t] = (S >> (R * (T - 1 - t))) & ((1 << L) - 1)
     return out
+
+
+# ---------------------------------------------------------------------------
+# Q8_0 blocks (buildq.py:21-30 enc_q8, qlab.py:27-32 deq_q8)
+# ---------------------------------------------------------------------------
+def enc_q8(W):
+    """buildq.py:21-30: per 32-block float16(max|x|/127) + int8 round-half-even."""
+    rows, cols = W.shape
+    nb = cols // 32
+    x = W.reshape(rows, nb, 32).astype(np.float32)
+    sc = np.max(np.abs(x), 2, keepdims=True) / 127.0
+    sc = np.where(sc == 0, 1e-9, sc)
+    q = np.round(x / sc).clip(-127, 127).astype(np.int8)
+    out = np.zeros((rows, nb, 34), np.uint8)
+    out[:, :, :2] = sc.squeeze(-1).astype(np.float16).view(np.uint8).reshape(rows, nb, 2)
+    out[:, :, 2:] = q.view(np.uint8)
+    return out.reshape(rows, nb * 34)
+
+
+def deq_q8(data):
+    """qlab.py:27-32 on the raw (rows, nb*34) block bytes."""
+    rows, brow = data.shape
+    nb = brow // 34
+    d = data.reshape(rows, nb, 34)
+    sc = d[:, :, :2].copy().view(np.float16).astype(np.float32)
+    qs = d[:, :, 2:].view(np.int8).astype(np.float32)
+    return (sc * qs).reshape(rows, nb * 32)

@@ -41,6 +41,11 @@ def g_pipeline():
 
 
 @pytest.fixture(scope="session")
+def g_q8():
+    return load_golden("golden_q8.npz")
+
+
+@pytest.fixture(scope="session")
 def g_qat():
     return load_golden("golden_qat.npz")
 

@@ -250,9 +250,36 @@ def make_qat(qlab, qat):
     np.savez_compressed(os.path.join(HERE, "golden_qat.npz"), **out)
 
 
+def make_q8(qlab):
+    """buildq.py:21-30 enc_q8 and qlab.py:27-32 deq_q8 on seeded matrices with
+    zero blocks, exact halves, huge and tiny magnitudes; the encoder is
+    imported from the reference builder module."""
+    import importlib
+    buildq = importlib.import_module("buildq")
+    rng = np.random.RandomState(16)
+    out = {"versions": _versions()}
+    W = rng.normal(0, 0.02, size=(24, 1024)).astype(np.float32)
+    W[3, :32] = 0.0                                    # zero block -> scale 1e-9
+    W[4, :64] = np.arange(64) - 31.5                  # many x / sc near .5
+    W[5, 32:64] = 127.0 * np.array([k / 127.0 for k in range(32)], np.float32)
+    W[6] *= 1e4
+    W[7] *= 1e-6
+    W[8, ::2] = -W[8, 1::2]
+    W64 = rng.standard_t(4, size=(8, 256)) * 0.02
+    for tag, M in (("f32", W), ("f64", W64)):
+        q = buildq.enc_q8(M)
+
+        class _T:
+            data = q
+        out[f"q8_{tag}_W"] = M
+        out[f"q8_{tag}_enc"] = q
+        out[f"q8_{tag}_dec"] = qlab.deq_q8(_T())
+    np.savez_compressed(os.path.join(HERE, "golden_q8.npz"), **out)
+
+
 MAKERS = {"rht": lambda m: make_rht(m[0]), "e8": lambda m: make_e8(m[0]),
           "trellis": lambda m: make_trellis(m[1], m[2]), "pipeline": lambda m: make_pipeline(*m),
-          "qat": lambda m: make_qat(m[0], m[2])}
+          "qat": lambda m: make_qat(m[0], m[2]), "q8": lambda m: make_q8(m[0])}
 
 
 def main():

@@ -192,3 +192,11 @@ def test_packed_states_roundtrip(g_trellis, L, R, seg):
     pk = O.pack_states(st, L, R)
     assert pk.shape[1] == (L + R * (seg - 1) + 31) // 32
     assert np.array_equal(O.unpack_states(pk, seg, L, R), st)
+
+
+@pytest.mark.parametrize("tag", ["f32", "f64"])
+def test_q8_codec(g_q8, tag):
+    """buildq.enc_q8 / qlab.deq_q8 restated: bytes and values bit-exact."""
+    q = O.enc_q8(g_q8[f"q8_{tag}_W"])
+    assert np.array_equal(q, g_q8[f"q8_{tag}_enc"])
+    assert same_bits(O.deq_q8(q), g_q8[f"q8_{tag}_dec"])

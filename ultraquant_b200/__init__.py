@@ -5,6 +5,7 @@ Modules mirror the reference's interfaces:
 * ``ultraquant_b200.qlab``     -- rht_rows, irht_rows, e8_decode, q_e8_fast, ...
 * ``ultraquant_b200.trellis``  -- codebook, trellis_quant, trellis_quant_fast
 * ``ultraquant_b200.qat``      -- trellis_encode, fwht_torch, irht_torch, recon_torch
+* ``ultraquant_b200.q8``       -- enc_q8 / deq_q8 (Q8_0 blocks of the GGUF container)
 * ``ultraquant_b200.pipeline`` -- the builders' importance-weighted recipes
 * ``ultraquant_b200.shard``    -- row-block sharding over torch.distributed ranks
 
@@ -24,21 +25,24 @@ __version__ = "0.1.0"
 
 _PATCH = {
     "qlab": ("_next_pow2", "rht_rows", "irht_rows", "_d8_decode", "e8_decode", "_entropy_bpw",
-             "q_e8_fast", "wnmse"),
+             "q_e8_fast", "wnmse", "deq_q8"),
     "trellis": ("codebook", "pred_table", "trellis_quant", "trellis_quant_fast"),
     "qat": ("trellis_encode", "fwht_torch", "irht_torch", "recon_torch"),
+    "buildq": ("enc_q8",),
 }
+_SOURCE = {"buildq": "q8"}   # reference module -> module of this package
 
 
 def install(modules=("qlab", "trellis", "qat")):
     """Replace the hot-path functions of the reference modules ``qlab``,
-    ``trellis`` and ``qat`` (imported from ``sys.path``) by this package's.
+    ``trellis`` and ``qat`` (imported from ``sys.path``) by this package's;
+    add ``"buildq"`` to also replace its ``enc_q8``.
     Call it before the builders run ``from qlab import rht_rows``.  Returns
     the patched module objects."""
     patched = {}
     for name in modules:
         ref = importlib.import_module(name)
-        mine = importlib.import_module(f"{__name__}.{name}")
+        mine = importlib.import_module(f"{__name__}.{_SOURCE.get(name, name)}")
         for attr in _PATCH[name]:
             setattr(ref, attr, getattr(mine, attr))
         if name == "qlab":

@@ -99,16 +99,16 @@ __device__ __forceinline__ bool d8_screen(const float y[8], float f[8], float M)
         else if (ae > second) second = ae;
         sum = __fadd_rn(sum, f[i]);
     }
-    if (int(sum) & 1) {
-        ok &= __fsub_rn(best, second) > tr;
-        float ek = 0.f;
+    // odd coordinate sum: move coordinate k by sign(e_k).  Branch-free (the
+    // parity differs between the lanes of a warp); even sums keep f as is.
+    const bool odd = int(sum) & 1;
+    float ek = 0.f;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) if (i == k) ek = __fsub_rn(y[i], f[i]);
-        ok &= fabsf(ek) > M + 0x1p-22f;
-        const float sg = ek > 0.f ? 1.f : -1.f;
+    for (int i = 0; i < 8; ++i) ek = i == k ? __fsub_rn(y[i], f[i]) : ek;
+    ok &= !odd || (__fsub_rn(best, second) > tr && fabsf(ek) > M + 0x1p-22f);
+    const float sg = ek > 0.f ? 1.f : -1.f;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) if (i == k) f[i] = __fadd_rn(f[i], sg);
-    }
+    for (int i = 0; i < 8; ++i) f[i] = (odd && i == k) ? __fadd_rn(f[i], sg) : f[i];
     return ok;
 }
 

@@ -10,7 +10,8 @@ operations (the Viterbi forward).  With ``--iters 0`` it only runs the
 kernel once, which is the form to put under ``ncu -k <kernel> -c 1``.
 
 Kernels: viterbi (segments of 256, L / R), rht and irht (fp64), e8,
-normalize, fwht (fp32), recon and recon_bwd (the QAT decoder, fp32).
+normalize, fwht (fp32), recon and recon_bwd (the QAT decoder, fp32), q8enc and
+q8dec (Q8_0 blocks, fp32 side).
 """
 from __future__ import annotations
 
@@ -24,7 +25,8 @@ from . import _lib
 
 # profiler scope name of each case's kernel
 SCOPE = {"viterbi": "viterbi_fwd", "rht": "rht", "irht": "rht", "e8": "e8_quant",
-         "normalize": "normalize", "fwht": "fwht", "recon": "qat_recon", "recon_bwd": "qat_recon_bwd"}
+         "normalize": "normalize", "fwht": "fwht", "recon": "qat_recon", "recon_bwd": "qat_recon_bwd",
+         "q8enc": "q8_encode", "q8dec": "q8_decode"}
 
 
 def _peaks():
@@ -121,6 +123,17 @@ def build_case(args, lib, st):
                                                  sH.data_ptr(), n, gcw.data_ptr(), gsc.data_ptr(), ws.data_ptr(),
                                                  ws.numel(), st), "recon_bwd")
         return run, rows * n * 8, "bytes"
+    if k in ("q8enc", "q8dec"):
+        W = torch.randn(rows, n, device=dev, generator=g) * 0.02
+        q = torch.empty((rows, n // 32 * 34), dtype=torch.uint8, device=dev)
+        _lib.check(lib.uq_q8_encode(W.data_ptr(), 0, rows, n, n, q.data_ptr(), st), "q8enc")
+        if k == "q8enc":
+            def run():
+                _lib.check(lib.uq_q8_encode(W.data_ptr(), 0, rows, n, n, q.data_ptr(), st), "q8enc")
+        else:
+            def run():
+                _lib.check(lib.uq_q8_decode(q.data_ptr(), rows, n, W.data_ptr(), n, st), "q8dec")
+        return run, rows * n * 4 + rows * n // 32 * 34, "bytes"
     raise SystemExit(f"unknown kernel {k}")
 
 

@@ -13,9 +13,10 @@ import torch
 
 from . import _device as D
 from . import _lib
+from .q8 import deq_q8  # noqa: F401  (qlab.py:27-32, used by load_WH)
 
 __all__ = ["wnmse", "_next_pow2", "rht_rows", "irht_rows", "_d8_decode", "e8_decode",
-           "_entropy_bpw", "q_e8_fast", "_E8_SCALE"]
+           "_entropy_bpw", "q_e8_fast", "_E8_SCALE", "deq_q8"]
 
 # qlab.py:158 -- calibrated E8 step per calib_key, reused across tensors
 _E8_SCALE: dict = {}
