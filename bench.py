@@ -174,7 +174,7 @@ def run_llama8b(args, rank: int, world: int, local: int):
     dev = torch.device("cuda", local)
     if world > 1:
         from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=1800), device_id=dev)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
     specs = shard.llama_shapes(layers=args.layers)
     plan = [s for s in shard.plan(specs, world) if s.rank == rank]
     data = []
@@ -262,7 +262,7 @@ def main():
     dev = torch.device("cuda", local)
     if world > 1:
         from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=dev)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
 
     from ultraquant_b200 import _lib, pipeline
     lib = _lib.load()

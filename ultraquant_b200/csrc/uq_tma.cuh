@@ -1,6 +1,6 @@
 // Tensor-memory-accelerator (TMA) and mbarrier helpers shared by the
 // transform and quantizer kernels: bounded mbarrier waits, tensor-map
-// loads / stores (never with cluster multicast), bulk-group bookkeeping and
+// loads / stores into the issuing CTA's own shared memory, bulk-group bookkeeping and
 // the host-side tensor-map encoder (cuTensorMapEncodeTiled through the
 // runtime's driver entry point, so the library needs no libcuda link).
 #pragma once
