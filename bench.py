@@ -59,6 +59,10 @@ def make_inputs(seed: int):
     return W.astype(np.float32), H
 
 
+# ncu (L=16, T=256, one launch of 296 sequences): DRAM read + write bytes
+NCU_DRAM_BYTES_PER_SEQ = {2: (1.252352e6 + 251.667968e6) / 296, 3: (1.233152e6 + 251.116544e6) / 296}
+
+
 def ops_per_weight(L: int, R: int) -> int:
     """Algorithmic lane ops of one Viterbi step per weight: sub, mul, add per
     state plus (2^R - 1) compares per predecessor group."""
@@ -335,7 +339,14 @@ def main():
         "peak_source": f"nominal FP32 lanes: {n_sm} SMs x 128 x {sm_max:.0f} MHz (no measured FP32 peak on file)",
         "ops_per_weight": {f"k{R}": ops_per_weight(L_BITS, R) for R in KS},
         "launches": int(vn.value), "kernel_ms_total": vt.value, "share_of_step": vt.value / ms if ms else None,
-        "traffic": None,
+        # DRAM bytes per launch: one ncu capture of 296 sequences per k
+        # (dram__bytes_read.sum + dram__bytes_write.sum), scaled by the
+        # sequences of the bench's launches (the traffic is the backpointers,
+        # proportional to the sequences)
+        "traffic": (sum(NCU_DRAM_BYTES_PER_SEQ[R] for R in KS) / len(KS)
+                    * (ROWS * COLS // SEG) * len(KS) * args.steps / max(1, int(vn.value))),
+        "traffic_unit": "bytes per launch",
+        "traffic_source": "ncu capture, 296 sequences per k, scaled by sequences per launch",
     }
     if clocks and clocks.get("sm_mhz"):
         roofline["frac_at_measured_clock"] = achieved / (n_sm * 128 * clocks["sm_mhz"] * 1e6 / 1e12)
