@@ -260,6 +260,13 @@ int uq_quant_e8(const void *W, int w_dtype, int64_t rows, int64_t n0, int64_t ld
                 float *What, int16_t *idx, double *err, void *workspace,
                 size_t workspace_bytes, void *stream);
 
+/* qlab.py:53-54 wnmse(A, Ah) = sum((A - Ah)^2) / sum(A^2): out2 = { sum((A -
+ * Ah)^2), sum(A^2) } in fp64 over n elements of A and Ah (float32 or fp64,
+ * widened exactly); a fixed-order reduction (deterministic for a given n). */
+size_t uq_wnmse_workspace_bytes(void);
+int uq_wnmse_sums(const void *A, int a_dtype, const void *Ah, int ah_dtype, int64_t n, double *out2,
+                  void *workspace, size_t workspace_bytes, void *stream);
+
 /* ---------------------------------------------------------------------
  * Device status (no counterpart in the reference)
  * ------------------------------------------------------------------- */

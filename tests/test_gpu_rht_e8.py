@@ -192,3 +192,14 @@ def test_q_e8_many_rows_vs_oracle(uq):
     A = rng.standard_t(4, size=(64, 16384)) * 0.02
     for step in (0.48, 0.3):
         assert same_bits(uq.q_e8_fast(A, fixed_step=step), O.q_e8_fast(A, fixed_step=step))
+
+
+def test_wnmse_vs_oracle(uq):
+    """qlab.wnmse on the device: fp64 sums, within 1e-12 relative of numpy's."""
+    rng = np.random.RandomState(5)
+    A = rng.normal(size=(300, 1000))
+    Ah = A + 0.01 * rng.normal(size=A.shape)
+    for a, b in ((A, Ah), (A.astype(np.float32), Ah), (A, Ah.astype(np.float32))):
+        ref = O.wnmse(np.asarray(a, np.float64), np.asarray(b, np.float64))
+        assert abs(uq.wnmse(a, b) - ref) <= 1e-12 * ref
+    assert uq.wnmse(A, A) == 0.0

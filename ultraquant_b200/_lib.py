@@ -50,6 +50,8 @@ SIGNATURES = {
     "uq_trellis_packed_words": (_i64, [_i32, _i32, _i32]),
     "uq_trellis_pack": (_i32, [_p, _i64, _i32, _i32, _i32, _p, _p]),
     "uq_trellis_unpack": (_i32, [_p, _i64, _i32, _i32, _i32, _p, _p]),
+    "uq_wnmse_workspace_bytes": (_sz, []),
+    "uq_wnmse_sums": (_i32, [_p, _i32, _p, _i32, _i64, _p, _p, _sz, _p]),
     "uq_q8_encode": (_i32, [_p, _i32, _i64, _i64, _i64, _p, _p]),
     "uq_q8_decode": (_i32, [_p, _i64, _i64, _p, _i64, _p]),
     "uq_fwht": (_i32, [_p, _i32, _i64, _i64, _i64, _i64, _p, _p, _i32, _p, _i64, _i64, _p]),

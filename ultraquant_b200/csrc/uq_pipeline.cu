@@ -100,6 +100,43 @@ int check_common(int64_t rows, int64_t n0, int64_t ldw, int w_dtype, int group, 
 
 }  // namespace
 
+// ---- weighted NMSE (qlab.py:53-54) --------------------------------------------
+// sum((A - Ah)^2) and sum(A^2) in fp64: fixed grid of CTAs, per-thread
+// grid-stride sums, warp trees and a CTA tree into per-CTA partials, then one
+// CTA sums the partials in index order -- deterministic for a given size.
+constexpr int kNmseBlocks = 592;
+
+template <typename TA, typename TB>
+__global__ void wnmse_partial_kernel(const TA *A, const TB *Ah, int64_t n, double *part) {
+    __shared__ double s0[32], s1[32];
+    double e = 0.0, a2 = 0.0;
+    for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < n; i += int64_t(gridDim.x) * blockDim.x) {
+        const double a = double(__ldg(A + i)), d = d_sub(a, double(__ldg(Ah + i)));
+        e = d_add(e, d_mul(d, d));
+        a2 = d_add(a2, d_mul(a, a));
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+        e = d_add(e, __shfl_xor_sync(0xffffffffu, e, o));
+        a2 = d_add(a2, __shfl_xor_sync(0xffffffffu, a2, o));
+    }
+    if ((threadIdx.x & 31) == 0) { s0[threadIdx.x >> 5] = e; s1[threadIdx.x >> 5] = a2; }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        double t0 = 0.0, t1 = 0.0;
+        for (int w = 0; w < int(blockDim.x >> 5); ++w) { t0 = d_add(t0, s0[w]); t1 = d_add(t1, s1[w]); }
+        part[2 * blockIdx.x] = t0;
+        part[2 * blockIdx.x + 1] = t1;
+    }
+}
+
+__global__ void wnmse_final_kernel(const double *part, int count, double *out) {
+    if (threadIdx.x != 0) return;
+    double t0 = 0.0, t1 = 0.0;
+    for (int i = 0; i < count; ++i) { t0 = d_add(t0, part[2 * i]); t1 = d_add(t1, part[2 * i + 1]); }
+    out[0] = t0;
+    out[1] = t1;
+}
+
 extern "C" {
 
 size_t uq_quant_trellis_workspace_bytes(int64_t rows, int64_t n0, int L, int R, int seg, int group) {
@@ -178,6 +215,35 @@ int uq_quant_e8(const void *W, int w_dtype, int64_t rows, int64_t n0, int64_t ld
     if ((rc = uq::e8_quant(X, UQ_F64, rows * n, group, step, X, idx, nullptr, st))) return rc;
     return uq::rht_inverse(X, UQ_F64, rows, n, n, n0, signs, sH, pre, What, UQ_F32, n0, W, w_dtype, ldw, part, err,
                            st);
+}
+
+size_t uq_wnmse_workspace_bytes(void) { return size_t(2) * kNmseBlocks * sizeof(double); }
+
+int uq_wnmse_sums(const void *A, int a_dtype, const void *Ah, int ah_dtype, int64_t n, double *out2,
+                  void *workspace, size_t workspace_bytes, void *stream) {
+    if (n < 0 || !uq::dtype_size(a_dtype) || !uq::dtype_size(ah_dtype))
+        return uq::fail(UQ_ERR_INVALID, "uq_wnmse_sums: bad arguments (n=%lld)", (long long)n);
+    if (!out2) return uq::fail(UQ_ERR_INVALID, "uq_wnmse_sums: null output");
+    if (!workspace || workspace_bytes < uq_wnmse_workspace_bytes())
+        return uq::fail(UQ_ERR_WORKSPACE, "uq_wnmse_sums: workspace %zu < %zu bytes", workspace_bytes,
+                        uq_wnmse_workspace_bytes());
+    if (n > 0 && (!A || !Ah)) return uq::fail(UQ_ERR_INVALID, "uq_wnmse_sums: null input");
+    const cudaStream_t st = UQ_STREAM(stream);
+    double *part = static_cast<double *>(workspace);
+    {
+        uq::ProfScope _p("wnmse", st);
+        const bool a64 = a_dtype == UQ_F64, b64 = ah_dtype == UQ_F64;
+        if (a64 && b64) wnmse_partial_kernel<double, double><<<kNmseBlocks, 256, 0, st>>>(
+            static_cast<const double *>(A), static_cast<const double *>(Ah), n, part);
+        else if (a64) wnmse_partial_kernel<double, float><<<kNmseBlocks, 256, 0, st>>>(
+            static_cast<const double *>(A), static_cast<const float *>(Ah), n, part);
+        else if (b64) wnmse_partial_kernel<float, double><<<kNmseBlocks, 256, 0, st>>>(
+            static_cast<const float *>(A), static_cast<const double *>(Ah), n, part);
+        else wnmse_partial_kernel<float, float><<<kNmseBlocks, 256, 0, st>>>(
+            static_cast<const float *>(A), static_cast<const float *>(Ah), n, part);
+        wnmse_final_kernel<<<1, 32, 0, st>>>(part, kNmseBlocks, out2);
+    }
+    return uq::check_cuda("wnmse kernels launch");
 }
 
 }  // extern "C"

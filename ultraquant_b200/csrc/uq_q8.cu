@@ -7,10 +7,11 @@
 //   deq_q8  qlab.py:27-32    W = float32(float16 scale) * float32(q)
 //
 // Every step is one correctly rounded float32 (or float16 conversion)
-// operation, so the bytes and values are the reference's.  One warp per
-// 32-block span of a row: lane l holds element l of each block (coalesced
-// loads), the block maximum is a shuffle reduction (max is exact), the 32
-// quantized bytes of a block are one coalesced 32-byte store.
+// operation, so the bytes and values are the reference's.  Both kernels move
+// spans of 256 blocks (8704 bytes, a multiple of 16) through shared memory so
+// that the byte-granular block format meets global memory as 16-byte
+// vectors; the block maximum is a shuffle reduction over the 8 threads of a
+// block (max is exact).
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
@@ -21,59 +22,135 @@
 
 namespace {
 
-constexpr int kBlk = 32, kBlkBytes = 34, kSpan = 32;   // blocks per warp task
+constexpr int kBlk = 32, kBlkBytes = 34;
+constexpr int kSpan = 256;                          // blocks per CTA task
+constexpr int kSpanBytes = kSpan * kBlkBytes;       // 8704 = 544 x 16 bytes
 
+// Element i (< 32) of block gb of a (rows, nb * 32) matrix with row stride ld.
+__device__ __forceinline__ int64_t blk_base(int64_t gb, int64_t nb, int64_t ld) {
+    return (gb / nb) * ld + (gb % nb) * kBlk;
+}
+
+// 256 threads, 8 per block: lane group (tid >> 3) quantizes one block per pass,
+// each thread 4 elements; the span's 34-byte blocks are staged in shared
+// memory and leave as 16-byte stores.
 template <typename T>
-__global__ void q8_encode_kernel(const T *W, int64_t rows, int64_t nb, int64_t ld, uint8_t *out) {
-    const int lane = threadIdx.x & 31;
-    const int64_t spans = (nb + kSpan - 1) / kSpan;
-    const int64_t tasks = rows * spans;
-    const int64_t warp0 = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
-    const int64_t nwarps = (int64_t(gridDim.x) * blockDim.x) >> 5;
-    for (int64_t task = warp0; task < tasks; task += nwarps) {
-        const int64_t r = task / spans, b0 = (task % spans) * kSpan;
-        const int nblk = int(std::min<int64_t>(kSpan, nb - b0));
-        const T *src = W + r * ld + b0 * kBlk;
-        uint8_t *dst = out + (r * nb + b0) * kBlkBytes;
-        float x[kSpan];
+__global__ void __launch_bounds__(256) q8_encode_kernel(const T *W, int64_t nblocks, int64_t nb, int64_t ld,
+                                                        bool vec_in, uint8_t *out, bool vec_out) {
+    __shared__ __align__(16) uint8_t stage[kSpanBytes];
+    const int tid = threadIdx.x, sub = tid & 7;
+    for (int64_t b0 = int64_t(blockIdx.x) * kSpan; b0 < nblocks; b0 += int64_t(gridDim.x) * kSpan) {
+        const int nblk = int(nblocks - b0 < kSpan ? nblocks - b0 : int64_t(kSpan));
+        // all of the thread's loads of the span first (8 passes x 4 values)
+        float xs[kSpan / 32][4];
 #pragma unroll
-        for (int j = 0; j < kSpan; ++j) x[j] = j < nblk ? float(__ldg(src + j * kBlk + lane)) : 0.f;
+        for (int pass = 0; pass < kSpan / 32; ++pass) {
+            const int j = pass * 32 + (tid >> 3);
+            xs[pass][0] = xs[pass][1] = xs[pass][2] = xs[pass][3] = 0.f;
+            if (j < nblk) {
+                const T *src = W + blk_base(b0 + j, nb, ld) + 4 * sub;
+                if (sizeof(T) == 4 && vec_in) {
+                    const float4 v = __ldg(reinterpret_cast<const float4 *>(src));
+                    xs[pass][0] = v.x; xs[pass][1] = v.y; xs[pass][2] = v.z; xs[pass][3] = v.w;
+                } else {
 #pragma unroll
-        for (int j = 0; j < kSpan; ++j) {
-            if (j >= nblk) break;
-            float m = fabsf(x[j]);
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-            float sc = __fdiv_rn(m, 127.0f);
-            if (sc == 0.0f) sc = 1e-9f;
-            float q = rintf(__fdiv_rn(x[j], sc));
-            q = fminf(fmaxf(q, -127.0f), 127.0f);
-            dst[j * kBlkBytes + 2 + lane] = uint8_t(int8_t(int(q)));
-            if (lane == 0) {
-                // float16 scale, little endian; blocks start on even bytes
-                *reinterpret_cast<unsigned short *>(dst + j * kBlkBytes) = __half_as_ushort(__float2half_rn(sc));
+                    for (int i = 0; i < 4; ++i) xs[pass][i] = float(__ldg(src + i));
+                }
             }
         }
+#pragma unroll
+        for (int pass = 0; pass < kSpan / 32; ++pass) {
+            const int j = pass * 32 + (tid >> 3);
+            const bool ok = j < nblk;
+            const float *x = xs[pass];
+            float m = fmaxf(fmaxf(fabsf(x[0]), fabsf(x[1])), fmaxf(fabsf(x[2]), fabsf(x[3])));
+#pragma unroll
+            for (int o = 4; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+            float sc = __fdiv_rn(m, 127.0f);
+            if (sc == 0.0f) sc = 1e-9f;
+            // rint(x / sc) from t = x * RN(1/sc): |t - RN(x/sc)| < |x/sc| 2^-23 + 2^-24 |x/sc|
+            // < 2^-15 for |x/sc| <= 128, so rint(t) is the answer unless t lies
+            // within 2^-15 of a rounding boundary (then: the IEEE division)
+            const float rc = __fdiv_rn(1.0f, sc);
+            if (ok) {
+                unsigned short qb[2];
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    int qq[2];
+#pragma unroll
+                    for (int e = 0; e < 2; ++e) {
+                        const float xv = x[2 * h + e];
+                        const float t = __fmul_rn(xv, rc);
+                        float f = rintf(t);
+                        if (!(__fsub_rn(0.5f, fabsf(__fsub_rn(t, f))) > 0x1p-15f) || !(fabsf(t) <= 128.f))
+                            f = rintf(__fdiv_rn(xv, sc));
+                        qq[e] = int(fminf(fmaxf(f, -127.f), 127.f));
+                    }
+                    qb[h] = static_cast<unsigned short>((qq[0] & 0xff) | ((qq[1] & 0xff) << 8));
+                }
+                // block j starts on an even byte: 16-bit stores
+                unsigned short *bq = reinterpret_cast<unsigned short *>(stage + j * kBlkBytes + 2 + 4 * sub);
+                bq[0] = qb[0];
+                bq[1] = qb[1];
+                if (sub == 0) *reinterpret_cast<unsigned short *>(stage + j * kBlkBytes) = __half_as_ushort(__float2half_rn(sc));
+            }
+        }
+        __syncthreads();
+        const int nbytes = nblk * kBlkBytes;
+        uint8_t *dst = out + b0 * kBlkBytes;
+        if (vec_out) {
+            for (int v = tid; v < nbytes / 16; v += blockDim.x)
+                reinterpret_cast<uint4 *>(dst)[v] = reinterpret_cast<const uint4 *>(stage)[v];
+            for (int i = (nbytes / 16) * 16 + tid; i < nbytes; i += blockDim.x) dst[i] = stage[i];
+        } else {
+            for (int i = tid; i < nbytes; i += blockDim.x) dst[i] = stage[i];
+        }
+        __syncthreads();
     }
 }
 
-__global__ void q8_decode_kernel(const uint8_t *q8, int64_t rows, int64_t nb, float *out, int64_t ld_out) {
-    const int64_t total = rows * nb * kBlk;
-    for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
-        const int64_t blk = i / kBlk;                 // row-major block index
-        const int e = int(i % kBlk);
-        const uint8_t *bp = q8 + blk * kBlkBytes;
-        const unsigned short h = static_cast<unsigned short>(__ldg(bp) | (__ldg(bp + 1) << 8));
-        const float sc = __half2float(__ushort_as_half(h));
-        const float q = float(int8_t(__ldg(bp + 2 + e)));
-        const int64_t r = blk / nb, c = (blk % nb) * kBlk + e;
-        out[r * ld_out + c] = __fmul_rn(sc, q);
+// The span's bytes come in by 16-byte loads into shared memory; each thread
+// then emits float4s of one block (fp32 product of the float16 scale and q).
+__global__ void __launch_bounds__(256) q8_decode_kernel(const uint8_t *q8, int64_t nblocks, int64_t nb, bool vec_in,
+                                                        float *out, int64_t ld_out, bool vec_out) {
+    __shared__ __align__(16) uint8_t stage[kSpanBytes];
+    const int tid = threadIdx.x;
+    for (int64_t b0 = int64_t(blockIdx.x) * kSpan; b0 < nblocks; b0 += int64_t(gridDim.x) * kSpan) {
+        const int nblk = int(nblocks - b0 < kSpan ? nblocks - b0 : int64_t(kSpan));
+        const int nbytes = nblk * kBlkBytes;
+        const uint8_t *src = q8 + b0 * kBlkBytes;
+        if (vec_in) {
+            for (int v = tid; v < nbytes / 16; v += blockDim.x)
+                reinterpret_cast<uint4 *>(stage)[v] = __ldg(reinterpret_cast<const uint4 *>(src) + v);
+            for (int i = (nbytes / 16) * 16 + tid; i < nbytes; i += blockDim.x) stage[i] = __ldg(src + i);
+        } else {
+            for (int i = tid; i < nbytes; i += blockDim.x) stage[i] = __ldg(src + i);
+        }
+        __syncthreads();
+        for (int f = tid; f < nblk * 8; f += blockDim.x) {
+            const int j = f >> 3, sub = f & 7;
+            const uint8_t *bp = stage + j * kBlkBytes;
+            const float sc = __half2float(__ushort_as_half(*reinterpret_cast<const unsigned short *>(bp)));
+            const unsigned short *bq = reinterpret_cast<const unsigned short *>(bp + 2 + 4 * sub);
+            const unsigned short q01 = bq[0], q23 = bq[1];
+            const float4 o = make_float4(__fmul_rn(sc, float(int8_t(q01 & 0xff))), __fmul_rn(sc, float(int8_t(q01 >> 8))),
+                                         __fmul_rn(sc, float(int8_t(q23 & 0xff))), __fmul_rn(sc, float(int8_t(q23 >> 8))));
+            float *dst = out + blk_base(b0 + j, nb, ld_out) + 4 * sub;
+            if (vec_out) {
+                *reinterpret_cast<float4 *>(dst) = o;
+            } else {
+                dst[0] = o.x; dst[1] = o.y; dst[2] = o.z; dst[3] = o.w;
+            }
+        }
+        __syncthreads();
     }
 }
 
 int grid_for(int64_t work, int per_block) {
-    return int(std::max<int64_t>(1, std::min<int64_t>((work + per_block - 1) / per_block, int64_t(uq::num_sms()) * 16)));
+    return int(std::max<int64_t>(1, std::min<int64_t>((work + per_block - 1) / per_block, int64_t(uq::num_sms()) * 8)));
 }
+
+bool al16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
 }  // namespace
 
@@ -85,14 +162,18 @@ int uq_q8_encode(const void *W, int w_dtype, int64_t rows, int64_t cols, int64_t
                         (long long)rows, (long long)cols, (long long)ldw);
     if (rows == 0 || cols == 0) return UQ_OK;
     if (!W || !out) return uq::fail(UQ_ERR_INVALID, "uq_q8_encode: null pointer");
-    const int64_t nb = cols / kBlk;
-    const int64_t tasks = rows * ((nb + kSpan - 1) / kSpan);
-    const int grid = grid_for(tasks, 8);
+    const int64_t nb = cols / kBlk, nblocks = rows * nb;
+    const int grid = grid_for(nblocks, kSpan);
     const cudaStream_t st = UQ_STREAM(stream);
+    const bool vec_out = al16(out);
     {
         uq::ProfScope _p("q8_encode", st);
-        if (w_dtype == UQ_F32) q8_encode_kernel<float><<<grid, 256, 0, st>>>(static_cast<const float *>(W), rows, nb, ldw, out);
-        else q8_encode_kernel<double><<<grid, 256, 0, st>>>(static_cast<const double *>(W), rows, nb, ldw, out);
+        if (w_dtype == UQ_F32) {
+            const bool vec_in = al16(W) && ldw % 4 == 0;
+            q8_encode_kernel<float><<<grid, 256, 0, st>>>(static_cast<const float *>(W), nblocks, nb, ldw, vec_in, out, vec_out);
+        } else {
+            q8_encode_kernel<double><<<grid, 256, 0, st>>>(static_cast<const double *>(W), nblocks, nb, ldw, false, out, vec_out);
+        }
     }
     return uq::check_cuda("q8_encode_kernel launch");
 }
@@ -103,8 +184,10 @@ int uq_q8_decode(const uint8_t *q8, int64_t rows, int64_t cols, float *out, int6
                         (long long)rows, (long long)cols, (long long)ld_out);
     if (rows == 0 || cols == 0) return UQ_OK;
     if (!q8 || !out) return uq::fail(UQ_ERR_INVALID, "uq_q8_decode: null pointer");
-    const int grid = grid_for(rows * cols, 256);
-    { uq::ProfScope _p("q8_decode", UQ_STREAM(stream)); q8_decode_kernel<<<grid, 256, 0, UQ_STREAM(stream)>>>(q8, rows, cols / kBlk, out, ld_out); }
+    const int64_t nb = cols / kBlk, nblocks = rows * nb;
+    const int grid = grid_for(nblocks, kSpan);
+    const bool vec_out = al16(out) && ld_out % 4 == 0;
+    { uq::ProfScope _p("q8_decode", UQ_STREAM(stream)); q8_decode_kernel<<<grid, 256, 0, UQ_STREAM(stream)>>>(q8, nblocks, nb, al16(q8), out, ld_out, vec_out); }
     return uq::check_cuda("q8_decode_kernel launch");
 }
 

@@ -79,6 +79,7 @@ struct FwhtArgs {
     void *out;
     int64_t ld_out, ncols_out;
     double *gcw, *gsc;           // fp64 gradient accumulators (backward into codes)
+    int cw_smem;                 // codebook (and its gradient) staged in shared memory
 };
 
 __device__ int g_qat_bad_state = 0;
@@ -160,6 +161,19 @@ fwht_kernel(FwhtArgs a) {
     const T s_inv = T(ldexp(1.0, -(b >> 1)));
     const T *signs = static_cast<const T *>(a.signs);
     const T *cs = static_cast<const T *>(a.colscale);
+    // small codebooks (L <= 12, the QAT default) live in shared memory after
+    // the tile: the gathers and the gradient scatter-add stay on chip
+    float *cw_s = reinterpret_cast<float *>(smem_raw + (size_t(sizeof(T)) << NB));
+    double *gcw_s = reinterpret_cast<double *>(smem_raw + (size_t(sizeof(T)) << NB) + ((size_t(a.ncw) * 4 + 15) & ~size_t(15)));
+    if ((SRC == SRC_RECON || DST == DST_GRADS) && a.cw_smem) {
+        for (int i = tid; i < a.ncw; i += nthr) {
+            cw_s[i] = __ldg(a.cw + i);
+            if (DST == DST_GRADS) gcw_s[i] = 0.0;
+        }
+        __syncthreads();
+    }
+    const float *cwp = a.cw_smem ? cw_s : a.cw;
+    double *gcwp = a.cw_smem ? gcw_s : a.gcw;
     const bool vec_in = SRC == SRC_RECON
         ? (!a.states64 && b >= 2 && a.group % 4 == 0 && (reinterpret_cast<uintptr_t>(a.states) & 15) == 0)
         : (b >= 2 && a.ncols_x % Vec16<T>::N == 0 && (a.ld_x * int64_t(sizeof(T))) % 16 == 0 &&
@@ -198,7 +212,7 @@ fwht_kernel(FwhtArgs a) {
                                 atomicExch(&g_qat_bad_state, 1);
                                 v = T(__int_as_float(0x7fc00000));
                             } else {
-                                v = T(__fmul_rn(__ldg(a.cw + st), scv));
+                                v = T(__fmul_rn(cwp[st], scv));
                             }
                         }
                         tile[swz5(E + j)] = v;
@@ -241,7 +255,7 @@ fwht_kernel(FwhtArgs a) {
                         const int64_t f = r * n + e;
                         const int64_t st = load_state(a, f);
                         v = st < 0 ? T(__int_as_float(0x7fc00000))
-                                   : T(A::mul(T(__ldg(a.cw + st)), T(__ldg(a.sc + group_of(a, f)))));
+                                   : T(A::mul(T(cwp[st]), T(__ldg(a.sc + group_of(a, f)))));
                     } else if (e < a.ncols_x) {
                         v = static_cast<const T *>(a.x)[r * a.ld_x + e];
                         if (DIR == DIR_BWD) v = bwd_pre<T>(a, v, e, cs, signs, s_pow2, s_inv, s);
@@ -325,13 +339,13 @@ fwht_kernel(FwhtArgs a) {
                     const int64_t g = group_of(a, f);
                     if (st < 0) continue;
                     const float gx = float(x[j]);
-                    atomicAdd(a.gcw + st, double(__fmul_rn(gx, __ldg(a.sc + g))));
+                    atomicAdd(gcwp + st, double(__fmul_rn(gx, __ldg(a.sc + g))));
                     if (g != g_cur) {
                         if (g_cur >= 0) atomicAdd(a.gsc + g_cur, acc);
                         g_cur = g;
                         acc = 0.0;
                     }
-                    acc += double(__fmul_rn(gx, __ldg(a.cw + st)));
+                    acc += double(__fmul_rn(gx, cwp[st]));
                 }
                 if (g_cur >= 0) atomicAdd(a.gsc + g_cur, acc);
             } else {
@@ -364,6 +378,11 @@ fwht_kernel(FwhtArgs a) {
         }
         __syncthreads();   // the tile is refilled for the next tile
     }
+    if (DST == DST_GRADS && a.cw_smem) {
+        // one global add per codeword and CTA
+        for (int i = tid; i < a.ncw; i += nthr)
+            if (gcw_s[i] != 0.0) atomicAdd(a.gcw + i, gcw_s[i]);
+    }
 }
 
 __global__ void grads_to_f32_kernel(const double *g64, int64_t count, float *out) {
@@ -375,7 +394,9 @@ template <typename T, int DIR, int SRC, int DST>
 int launch_fwht(const FwhtArgs &a, cudaStream_t st, const char *what) {
     const int NB = a.b > 12 ? a.b : 12;
     const int nthr = 1 << (NB - VB);
-    const size_t smem = sizeof(T) << NB;
+    const bool codes = SRC == SRC_RECON || DST == DST_GRADS;
+    const size_t smem = (sizeof(T) << NB) +
+        (codes && a.cw_smem ? ((size_t(a.ncw) * 4 + 15) & ~size_t(15)) + (DST == DST_GRADS ? size_t(a.ncw) * 8 : 0) : 0);
     // fp64 tiles stop at n = 16384 (512 threads)
     constexpr int TOP = sizeof(T) == 8 ? 512 : 1024;
     auto kern = nthr <= 128 ? fwht_kernel<T, DIR, SRC, DST, 128>
@@ -442,6 +463,7 @@ int uq_qat_recon(const void *states, int states64, int64_t nrow, int64_t n, cons
     FwhtArgs a{};
     a.rows = nrow; a.b = uq::ilog2(n); a.states = states; a.states64 = states64 ? 1 : 0;
     a.cw = cw; a.ncw = ncw; a.sc = sc; set_group(a, scale_group);
+    a.cw_smem = ncw <= 4096 ? 1 : 0;
     a.ntot = nrow * n;
     a.signs = signs; a.colscale = sH; a.s = sqrt(double(n));
     a.out = out; a.ld_out = ld_out; a.ncols_out = in0;
@@ -485,6 +507,7 @@ int uq_qat_recon_backward(const float *grad, int64_t ld_grad, const void *states
         a.ntot = nrow * n;
         a.signs = signs; a.colscale = sH; a.s = sqrt(double(n));
         a.gcw = gcw; a.gsc = gsc;
+        a.cw_smem = ncw <= 4096 ? 1 : 0;
         const int rc = launch_fwht<float, DIR_BWD, SRC_DENSE, DST_GRADS>(a, st, "qat_recon_bwd");
         if (rc != UQ_OK) return rc;
     }

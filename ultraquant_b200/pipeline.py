@@ -43,7 +43,8 @@ def quant_trellis_device(W: torch.Tensor, H: torch.Tensor, L=12, R=2, seg=64, sc
     cw = D.codebook(L, dev)
     d = D.signs(n, seed, dev)
     What = torch.empty((rows, n0), dtype=torch.float32, device=dev)
-    err = torch.zeros(2, dtype=torch.float64, device=dev)
+    # the pipeline writes both sums; only an empty matrix leaves them to us
+    err = torch.empty(2, dtype=torch.float64, device=dev) if rows * n0 else torch.zeros(2, dtype=torch.float64, device=dev)
     padded = -(-rows * n // scale_group) * scale_group
     states = torch.empty((padded // seg, seg), dtype=torch.int32, device=dev) if keep_codes else None
     sc = torch.empty(padded // scale_group, dtype=torch.float32, device=dev) if keep_codes else None
@@ -66,7 +67,8 @@ def quant_step_device(W: torch.Tensor, H: torch.Tensor, step: float, group=256, 
     W = W.contiguous()
     d = D.signs(n, seed, dev)
     What = torch.empty((rows, n0), dtype=torch.float32, device=dev)
-    err = torch.zeros(2, dtype=torch.float64, device=dev)
+    # the pipeline writes both sums; only an empty matrix leaves them to us
+    err = torch.empty(2, dtype=torch.float64, device=dev) if rows * n0 else torch.zeros(2, dtype=torch.float64, device=dev)
     idx = torch.empty(-(-rows * n // 8) * 8, dtype=torch.int16, device=dev) if keep_codes else None
     ws = D.workspace(lib.uq_quant_e8_workspace_bytes(rows, n0, group), dev)
     _lib.check(lib.uq_quant_e8(W.data_ptr(), D.dtype_code(W), rows, n0, n0, H.data_ptr(), float(step), group,

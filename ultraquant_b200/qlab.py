@@ -9,6 +9,8 @@ from __future__ import annotations
 
 import ctypes
 
+import numpy as np
+
 import torch
 
 from . import _device as D
@@ -31,10 +33,25 @@ def _ret(t: torch.Tensor, like):
 
 
 def wnmse(A, Ah) -> float:
-    """qlab.py:53-54 -- sum((A - Ah)^2) / sum(A^2) (fp64 on the device)."""
-    a = D.as_device(A, torch.float64)
-    b = D.as_device(Ah, torch.float64)
-    return float(((a - b) ** 2).sum() / (a ** 2).sum())
+    """qlab.py:53-54 -- sum((A - Ah)^2) / sum(A^2), both sums in fp64 on the
+    device (fixed-order reduction; numpy's pairwise order differs, ~1e-15)."""
+    lib = _lib.load()
+    a = D.as_device(A)
+    b = D.as_device(Ah, dev=a.device)
+    if a.shape != b.shape:
+        raise ValueError(f"operands could not be broadcast together with shapes {tuple(a.shape)} {tuple(b.shape)}")
+    if a.dtype not in (torch.float32, torch.float64):
+        a = a.to(torch.float64)
+    if b.dtype not in (torch.float32, torch.float64):
+        b = b.to(torch.float64)
+    out = torch.empty(2, dtype=torch.float64, device=a.device)
+    ws = D.workspace(lib.uq_wnmse_workspace_bytes(), a.device)
+    _lib.check(lib.uq_wnmse_sums(a.data_ptr() if a.numel() else None, D.dtype_code(a),
+                                 b.data_ptr() if b.numel() else None, D.dtype_code(b), a.numel(),
+                                 out.data_ptr(), ws.data_ptr(), ws.numel(), D.stream_handle(a.device)), "wnmse")
+    e = D.to_host(out)
+    with np.errstate(divide="ignore", invalid="ignore"):
+        return float(e[0] / e[1])
 
 
 def _next_pow2(n: int) -> int:
