@@ -73,6 +73,20 @@ int uq_irht_rows(const void *X, int x_dtype, int64_t rows, int64_t n, int64_t ld
  * E8 lattice (qlab.py:133-183)
  * ------------------------------------------------------------------- */
 
+/* Opt-in block-factorised transform for n0 = 28 x 512 or 28 x 1024 (the
+ * ffn_down widths 14336 / 28672 without padding); no counterpart in the
+ * reference, which pads to a power of two (qlab.py:75-77).  Forward:
+ * (H_28 (x) H_P) D (A * colscale) * RN(1/sqrt(n0)) with H_28 the Paley
+ * Hadamard matrix of order 28, D the RandomState(seed) signs of length n0
+ * (`signs`), colscale nullable; out (rows, n0) fp64.  Inverse: the transpose,
+ * then * d, or / (colscale * d) when colscale is given; out float32 or fp64
+ * with row stride ld_out.  Operation order: oracle rht28_rows / irht28_rows. */
+int uq_rht28_rows(const void *A, int a_dtype, int64_t rows, int64_t n0, int64_t lda,
+                  const double *colscale, const double *signs, double *out, void *stream);
+int uq_irht28_rows(const void *X, int x_dtype, int64_t rows, int64_t n0, int64_t ldx,
+                   const double *colscale, const double *signs, void *out, int out_dtype,
+                   int64_t ld_out, void *stream);
+
 /* qlab.py:133-142 _d8_decode(Y): Y, out are (nvec, 8) fp64. */
 int uq_d8_decode(const double *Y, int64_t nvec, double *out, void *stream);
 
@@ -266,6 +280,15 @@ int uq_quant_e8(const void *W, int w_dtype, int64_t rows, int64_t n0, int64_t ld
 size_t uq_wnmse_workspace_bytes(void);
 int uq_wnmse_sums(const void *A, int a_dtype, const void *Ah, int ah_dtype, int64_t n, double *out2,
                   void *workspace, size_t workspace_bytes, void *stream);
+
+/* Opt-in variant of uq_quant_e8 for n0 = 28 x 512 / 28 x 1024 with the
+ * block-factorised transform (uq_rht28_rows) in place of the padded RHT and
+ * groups of 256; err = { sum (X - Xq)^2, sum X^2 } of the rotated matrix.  No
+ * counterpart in the reference. */
+size_t uq_quant_e8_b28_workspace_bytes(int64_t rows, int64_t n0);
+int uq_quant_e8_b28(const void *W, int w_dtype, int64_t rows, int64_t n0, int64_t ldw,
+                    const double *H, double step, const double *signs, float *What, int16_t *idx,
+                    double *err, void *workspace, size_t workspace_bytes, void *stream);
 
 /* ---------------------------------------------------------------------
  * Device status (no counterpart in the reference)

@@ -29,6 +29,7 @@ __all__ = [
     "trellis_quant", "trellis_quant_fast", "trellis_encode", "trellis_decode",
     "fwht_torch", "irht_torch", "recon_torch", "quant_trellis", "quant_step",
     "group_rms_f32", "viterbi_segments", "pack_states", "unpack_states", "enc_q8", "deq_q8",
+    "hadamard28", "rht28_rows", "irht28_rows", "quant_step_b28",
 ]
 
 
@@ -399,3 +400,101 @@ def deq_q8(data):
     sc = d[:, :, :2].copy().view(np.float16).astype(np.float32)
     qs = d[:, :, 2:].view(np.int8).astype(np.float32)
     return (sc * qs).reshape(rows, nb * 32)
+
+
+# ---------------------------------------------------------------------------
+# Opt-in block-factorised RHT for n0 = 28 * 2^m (no counterpart in the
+# reference, which pads to a power of two; parity of this mode is defined by
+# this restatement alone).  H_28 is the Paley type-I Hadamard matrix over
+# GF(27) = GF(3)[x] / (x^3 - x - 1); the transform is (H_28 (x) H_P) D / sqrt(N)
+# with the normalisation applied as a multiplication by RN(1 / sqrt(N)).
+# ---------------------------------------------------------------------------
+def hadamard28() -> np.ndarray:
+    """28 x 28 +-1 matrix with H H^T = 28 I (Paley construction, q = 27)."""
+    import itertools
+
+    def mul(a, b):
+        r = [0] * 5
+        for i in range(3):
+            for j in range(3):
+                r[i + j] = (r[i + j] + a[i] * b[j]) % 3
+        for k in (4, 3):                      # x^3 = x + 1
+            c, r[k] = r[k], 0
+            r[k - 3] = (r[k - 3] + c) % 3
+            r[k - 2] = (r[k - 2] + c) % 3
+        return tuple(r[:3])
+
+    elems = list(itertools.product(range(3), repeat=3))
+    zero = (0, 0, 0)
+    squares = {mul(a, a) for a in elems if a != zero}
+
+    def chi(a):
+        return 0 if a == zero else (1 if a in squares else -1)
+
+    Q = np.array([[chi(tuple((x - y) % 3 for x, y in zip(a, b))) for b in elems] for a in elems])
+    H = np.zeros((28, 28), dtype=np.int64)
+    H[0, :] = 1
+    H[1:, 0] = -1
+    H[1:, 1:] = Q + np.eye(27, dtype=np.int64)
+    return H
+
+
+def _fwht_blocks(x, P):
+    """Sylvester butterflies h = 1 .. P/2 inside each P-block of the rows."""
+    rows, N = x.shape
+    x = x.reshape(rows, N // P, P)
+    h = 1
+    while h < P:
+        v = x.reshape(rows, N // P, P // (2 * h), 2, h)
+        a, b = v[:, :, :, 0, :], v[:, :, :, 1, :]
+        x = np.concatenate([a + b, a - b], axis=3).reshape(rows, N // P, P)
+        h *= 2
+    return x.reshape(rows, N)
+
+
+def _mix28(x, P, transpose):
+    """z[i] = sum_k H[i, k] y[k] (or H^T) over the 28 blocks, accumulated
+    k = 0 .. 27 in order from +-y[0]."""
+    H = hadamard28()
+    M = H.T if transpose else H
+    rows, N = x.shape
+    y = x.reshape(rows, 28, P)
+    z = np.empty_like(y)
+    for i in range(28):
+        acc = y[:, 0, :] if M[i, 0] > 0 else -y[:, 0, :]
+        for k in range(1, 28):
+            acc = acc + y[:, k, :] if M[i, k] > 0 else acc - y[:, k, :]
+        z[:, i, :] = acc
+    return z.reshape(rows, N)
+
+
+def rht28_rows(A, seed=0):
+    """Opt-in forward transform for n0 = 28 P (P a power of two >= 16)."""
+    A = np.asarray(A, dtype=np.float64)
+    rows, N = A.shape
+    P = N // 28
+    assert N == 28 * P and P >= 16 and P & (P - 1) == 0
+    d = rht_signs(N, seed)
+    x = _fwht_blocks(A * d, P)
+    x = _mix28(x, P, transpose=False)
+    return x * (1.0 / np.sqrt(float(N)))
+
+
+def irht28_rows(X, seed=0):
+    """Inverse of rht28_rows: H^T mix, block butterflies, * RN(1/sqrt(N)), * d."""
+    X = np.asarray(X, dtype=np.float64)
+    rows, N = X.shape
+    P = N // 28
+    x = _mix28(X, P, transpose=True)
+    x = _fwht_blocks(x, P)
+    return (x * (1.0 / np.sqrt(float(N)))) * rht_signs(N, seed)
+
+
+def quant_step_b28(W, H, step):
+    """Opt-in buildalloc recipe with the block-factorised transform:
+    What = irht28(q_e8_fast(rht28(W sH), fixed_step)) / sH (float32)."""
+    Hc = np.maximum(H, H.max() * 1e-3)
+    sH = np.sqrt(Hc)[None, :]
+    X = rht28_rows(np.asarray(W, np.float64) * sH)
+    Xq = q_e8_fast(X, fixed_step=step)
+    return (irht28_rows(Xq) / sH).astype(np.float32), X, Xq

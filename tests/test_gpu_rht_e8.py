@@ -203,3 +203,37 @@ def test_wnmse_vs_oracle(uq):
         ref = O.wnmse(np.asarray(a, np.float64), np.asarray(b, np.float64))
         assert abs(uq.wnmse(a, b) - ref) <= 1e-12 * ref
     assert uq.wnmse(A, A) == 0.0
+
+
+@pytest.mark.parametrize("rows,n0", [(1, 14336), (3, 28672), (150, 14336)])
+def test_block28_vs_oracle(uq, rows, n0):
+    """Opt-in unpadded 28 x P transform (no reference counterpart): forward
+    and inverse bit-exact against the oracle's operation order, f32 / f64 input."""
+    rng = np.random.RandomState(rows + n0)
+    A = rng.standard_t(4, size=(rows, n0)) * 0.02
+    pick = sorted({0, rows // 2, rows - 1})
+    X = uq.rht_rows(A, block28=True)
+    assert same_bits(X[pick], O.rht28_rows(A[pick]))
+    A32 = A.astype(np.float32)
+    assert same_bits(uq.rht_rows(A32, block28=True)[pick], O.rht28_rows(A32[pick]))
+    assert same_bits(uq.irht_rows(X, n0, block28=True)[pick], O.irht28_rows(X[pick]))
+
+
+def test_quant_step_block28_vs_oracle():
+    """Opt-in buildalloc recipe on an ffn_down-shaped slice with the unpadded
+    transform: What bit-exact, weighted NMSE (rotated domain) within 1e-12 of
+    the oracle's and within 1e-6 of the original-domain value."""
+    import torch
+    from ultraquant_b200 import pipeline as P
+    rng = np.random.RandomState(29)
+    W = (rng.standard_t(4, size=(8, 14336)) / np.sqrt(2) * 0.015).astype(np.float32)
+    H = np.exp(rng.normal(0.0, 1.0, size=14336))
+    res = P.quant_step_device(torch.from_numpy(W).cuda(), torch.from_numpy(H).cuda(), 0.48, block28=True)
+    ref, X, Xq = O.quant_step_b28(W.astype(np.float64), H, 0.48)
+    assert same_bits(res.What.cpu().numpy(), ref)
+    w_rot = float(np.sum((X - Xq) ** 2) / np.sum(X ** 2))
+    assert abs(res.wnmse - w_rot) <= 1e-12 * w_rot
+    Hc = np.maximum(H, H.max() * 1e-3)
+    A = W.astype(np.float64) * np.sqrt(Hc)[None, :]
+    Ah = ref.astype(np.float64) * np.sqrt(Hc)[None, :]
+    assert abs(res.wnmse - O.wnmse(A, Ah)) <= 1e-6 * res.wnmse + 1e-6

@@ -200,3 +200,16 @@ def test_q8_codec(g_q8, tag):
     q = O.enc_q8(g_q8[f"q8_{tag}_W"])
     assert np.array_equal(q, g_q8[f"q8_{tag}_enc"])
     assert same_bits(O.deq_q8(q), g_q8[f"q8_{tag}_dec"])
+
+
+def test_block28_transform_restatement():
+    """Opt-in H_28 (x) H_P transform: H_28 is a Hadamard matrix, the
+    transform is orthogonal and the inverse restores the input."""
+    H = O.hadamard28()
+    assert np.array_equal(H @ H.T, 28 * np.eye(28, dtype=np.int64))
+    rng = np.random.RandomState(28)
+    for n0 in (14336, 28672):
+        A = rng.normal(size=(2, n0))
+        X = O.rht28_rows(A)
+        assert abs(np.sum(X ** 2) / np.sum(A ** 2) - 1) < 1e-12
+        assert np.abs(O.irht28_rows(X) - A).max() < 1e-13

@@ -31,6 +31,8 @@ SIGNATURES = {
     "uq_rht_signs": (_i32, [_u32, _i64, _p]),
     "uq_rht_rows": (_i32, [_p, _i32, _i64, _i64, _i64, _p, _p, _p]),
     "uq_irht_rows": (_i32, [_p, _i32, _i64, _i64, _i64, _i64, _p, _p, _p]),
+    "uq_rht28_rows": (_i32, [_p, _i32, _i64, _i64, _i64, _p, _p, _p, _p]),
+    "uq_irht28_rows": (_i32, [_p, _i32, _i64, _i64, _i64, _p, _p, _p, _i32, _i64, _p]),
     "uq_d8_decode": (_i32, [_p, _i64, _p, _p]),
     "uq_e8_decode": (_i32, [_p, _i64, _p, _p]),
     "uq_e8_quant": (_i32, [_p, _i32, _i64, _i64, _f64, _p, _p, _p]),
@@ -64,6 +66,8 @@ SIGNATURES = {
                                 _p, _p, _p, _sz, _p]),
     "uq_quant_e8_workspace_bytes": (_sz, [_i64, _i64, _i32]),
     "uq_quant_e8": (_i32, [_p, _i32, _i64, _i64, _i64, _p, _f64, _i32, _p, _p, _p, _p, _p, _sz, _p]),
+    "uq_quant_e8_b28_workspace_bytes": (_sz, [_i64, _i64]),
+    "uq_quant_e8_b28": (_i32, [_p, _i32, _i64, _i64, _i64, _p, _f64, _p, _p, _p, _p, _p, _sz, _p]),
     "uq_device_errors": (_i32, [_p]),
     "uq_wait_timeout_selftest": (_i32, [_f64, _p]),
     "uq_profile_enable": (None, [_i32]),

@@ -138,6 +138,10 @@ __global__ void wnmse_final_kernel(const double *part, int count, double *out) {
 }
 
 extern "C" {
+int uq_rht28_rows(const void *A, int a_dtype, int64_t rows, int64_t n0, int64_t lda, const double *colscale,
+                  const double *signs, double *out, void *stream);
+int uq_irht28_rows(const void *X, int x_dtype, int64_t rows, int64_t n0, int64_t ldx, const double *colscale,
+                   const double *signs, void *out, int out_dtype, int64_t ld_out, void *stream);
 
 size_t uq_quant_trellis_workspace_bytes(int64_t rows, int64_t n0, int L, int R, int seg, int group) {
     (void)R;
@@ -244,6 +248,44 @@ int uq_wnmse_sums(const void *A, int a_dtype, const void *Ah, int ah_dtype, int6
         wnmse_final_kernel<<<1, 32, 0, st>>>(part, kNmseBlocks, out2);
     }
     return uq::check_cuda("wnmse kernels launch");
+}
+
+// Opt-in: the buildalloc recipe with the block-factorised transform for
+// n0 = 28 x 512 / 28 x 1024 (no padding).  Weighted error sums are taken in the
+// rotated domain (the transform is orthogonal: equal to the original-domain
+// sums up to rounding).
+size_t uq_quant_e8_b28_workspace_bytes(int64_t rows, int64_t n0) {
+    if (rows < 0 || n0 < 1) return 0;
+    uq::Carver c(nullptr, ~size_t(0));
+    c.take<double>(size_t(n0));
+    c.take<double>(size_t(rows * n0));
+    c.take<double>(size_t(rows * n0));
+    c.take<unsigned char>(uq_wnmse_workspace_bytes());
+    return c.off;
+}
+
+int uq_quant_e8_b28(const void *W, int w_dtype, int64_t rows, int64_t n0, int64_t ldw, const double *H, double step,
+                    const double *signs, float *What, int16_t *idx, double *err, void *workspace,
+                    size_t workspace_bytes, void *stream) {
+    int rc = check_common(rows, n0, ldw, w_dtype, 256, "uq_quant_e8_b28");
+    if (rc) return rc;
+    if (n0 != 28 * 512 && n0 != 28 * 1024)
+        return uq::fail(UQ_ERR_INVALID, "uq_quant_e8_b28: n0 = %lld is not 28 x 512 or 28 x 1024", (long long)n0);
+    if (rows == 0) return UQ_OK;
+    if (!W || !H || !signs || !What || !err || !workspace) return uq::fail(UQ_ERR_INVALID, "uq_quant_e8_b28: null pointer");
+    uq::Carver c(workspace, workspace_bytes);
+    double *sH = c.take<double>(size_t(n0));
+    double *X = c.take<double>(size_t(rows * n0));
+    double *Xq = c.take<double>(size_t(rows * n0));
+    unsigned char *part = c.take<unsigned char>(uq_wnmse_workspace_bytes());
+    if (!c.ok()) return uq::fail(UQ_ERR_WORKSPACE, "uq_quant_e8_b28: workspace %zu < %zu", workspace_bytes, c.off);
+    cudaStream_t st = UQ_STREAM(stream);
+    { uq::ProfScope _p("importance_scale", st); importance_scale_kernel<<<1, 1024, 0, st>>>(H, n0, sH); }
+    if ((rc = uq::check_cuda("importance_scale_kernel launch"))) return rc;
+    if ((rc = uq_rht28_rows(W, w_dtype, rows, n0, ldw, sH, signs, X, stream))) return rc;
+    if ((rc = uq::e8_quant(X, UQ_F64, rows * n0, 256, step, Xq, idx, nullptr, st))) return rc;
+    if ((rc = uq_wnmse_sums(X, UQ_F64, Xq, UQ_F64, rows * n0, err, part, uq_wnmse_workspace_bytes(), stream))) return rc;
+    return uq_irht28_rows(Xq, UQ_F64, rows, n0, n0, sH, signs, What, UQ_F32, n0, stream);
 }
 
 }  // extern "C"

@@ -23,6 +23,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <type_traits>
 #include <stdint.h>
 
 #include "uq_common.cuh"
@@ -634,6 +635,152 @@ rht_tma_kernel(const __grid_constant__ CUtensorMap tin, const __grid_constant__ 
     if (CL > 1) cluster_sync_all();   // no CTA leaves while a partner may read its tile
 }
 
+// ---------------------------------------------------------------------------
+// Opt-in block-factorised transform for n0 = 28 * P (P = 512 or 1024: the
+// ffn_down widths 14336 and 28672 without padding).  No counterpart in the
+// reference (it pads to a power of two); the operation order is the one of
+// the oracle's rht28_rows / irht28_rows:
+//   forward  x = rn(A * colscale) * d; 512/1024-point butterflies in each of
+//            the 28 blocks; z_i = sum_k H[i][k] y_k (sequential from +-y_0);
+//            out = z * RN(1 / sqrt(N))
+//   inverse  w_k = sum_i H[i][k] x_i; block butterflies; y = rn(w * RN(1/sqrt N));
+//            out = y * d, or y / (colscale * d)
+// H is the Paley type-I Hadamard matrix of order 28 (q = 27); the masks below
+// hold its -1 entries (bit k of row i, and bit i of column k).
+// One CTA of 512 threads per row, the row in shared memory (the per-block
+// swizzle E ^ ((E >> 4) & 15) keeps the butterfly passes and the column reads
+// conflict-free).
+// ---------------------------------------------------------------------------
+__host__ __device__ constexpr unsigned h28_row(int i) {
+    constexpr unsigned t[28] = {
+    0x0000000u, 0x076e535u, 0x0adea69u, 0x11bf0d3u, 0x38739a5u, 0x5475749u, 0x8c78e93u, 0xc09dd27u, 0xa12be4du, 0x6247c9bu,
+    0xdca681du, 0xbd4d02bu, 0x7e1a447u, 0xe7348e1u, 0xeae9151u, 0xf1d2631u, 0x3ba4f03u, 0x57c9a85u, 0x8f93589u, 0x4d03b73u,
+    0x9a056f5u, 0x3488df9u, 0x691c39du, 0xd22a3abu, 0xa4c63c7u, 0x49e04efu, 0x935095fu, 0x26b123fu};
+    return t[i];
+}
+__host__ __device__ constexpr unsigned h28_col(int i) {
+    constexpr unsigned t[28] = {
+    0xffffffeu, 0xf891ac8u, 0xf521592u, 0xee40f24u, 0xc78c64au, 0xab8a896u, 0x738712cu, 0x3f62258u, 0x5ed40b2u, 0x9db8164u,
+    0x23593e2u, 0x42b27d4u, 0x81e4bb8u, 0x18c971eu, 0x1512eaeu, 0x0e259ceu, 0xc44b0fcu, 0xa81657au, 0x702ca76u, 0xb27c48cu,
+    0x64fa90au, 0xc977206u, 0x92e3c62u, 0x25d5c54u, 0x4b39c38u, 0x961fb10u, 0x2caf6a0u, 0x594edc0u};
+    return t[i];
+}
+
+struct R28Args {
+    const void *in;
+    int64_t rows, ld_in;
+    int m;                      // P = 2^m
+    const double *signs;        // N
+    const double *colscale;     // N or null
+    void *out;
+    int64_t ld_out;
+    double c;                   // RN(1 / sqrt(N))
+};
+
+// z_i = sum_k (+-) y_k with the signs of row i (or column i when T) of H.
+template <bool T>
+__device__ __forceinline__ double mix_one(const double (&y)[28], int i) {
+    const unsigned mask = T ? h28_col(i) : h28_row(i);
+    double acc = (mask & 1u) ? -y[0] : y[0];
+#pragma unroll
+    for (int k = 1; k < 28; ++k) acc = ((mask >> k) & 1u) ? d_sub(acc, y[k]) : d_add(acc, y[k]);
+    return acc;
+}
+
+template <typename TIn, typename TOut, int MODE>
+__global__ void __launch_bounds__(512, 1) rht28_kernel(R28Args a) {
+    extern __shared__ double t28[];
+    const int tid = threadIdx.x, m = a.m, P = 1 << m;
+    const int N = 28 * P;
+    for (int64_t r = blockIdx.x; r < a.rows; r += gridDim.x) {
+        // ---- load (forward: scale and sign) ----------------------------------
+        const TIn *src = static_cast<const TIn *>(a.in) + r * a.ld_in;
+        for (int e = tid; e < N; e += 512) {
+            double v = double(__ldg(src + e));
+            if (MODE == MODE_FWD) {
+                if (a.colscale) v = d_mul(v, __ldg(a.colscale + e));
+                v = d_mul(v, __ldg(a.signs + e));
+            }
+            t28[((e >> m) << m) + swz(e & (P - 1))] = v;
+        }
+        __syncthreads();
+        // ---- column mix (the inverse does it first) ----------------------------
+        auto mix_columns = [&](auto Tc, bool to_global) {
+            constexpr bool T = decltype(Tc)::value;
+            for (int j = tid; j < P; j += 512) {
+                const int sj = swz(j);
+                double y[28];
+#pragma unroll
+                for (int k = 0; k < 28; ++k) y[k] = t28[(k << m) + sj];
+#pragma unroll
+                for (int i = 0; i < 28; ++i) {
+                    const double z = mix_one<T>(y, i);
+                    if (to_global)
+                        static_cast<TOut *>(a.out)[r * a.ld_out + (i << m) + j] = TOut(d_mul(z, a.c));
+                    else
+                        t28[(i << m) + sj] = z;
+                }
+            }
+        };
+        if (MODE == MODE_INV) {
+            mix_columns(std::integral_constant<bool, true>{}, false);
+            __syncthreads();
+        }
+        // ---- butterflies inside each of the 28 blocks ---------------------------
+        const int tasks = 28 << (m - 4);             // 16 values per task
+        int done = 0;
+        for (int p = 0;; p += 4) {
+            if (p > m - 4) p = m - 4;
+            const bool last = p == m - 4;
+            for (int u = tid; u < tasks; u += 512) {
+                const int k = u >> (m - 4), l = u & ((1 << (m - 4)) - 1);
+                const int base = (l & ((1 << p) - 1)) | ((l >> p) << (p + 4));
+                double x[16];
+#pragma unroll
+                for (int j = 0; j < 16; ++j) x[j] = t28[(k << m) + swz(base + (j << p))];
+                stages16(x, p, done > p ? done : p, m);
+                if (MODE == MODE_INV && last) {
+                    // base == l: consecutive tasks write consecutive columns
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        const int e = (k << m) + base + (j << p);
+                        const double xs = d_mul(x[j], a.c);
+                        double y;
+                        if (a.colscale) y = xs / d_mul(__ldg(a.colscale + e), __ldg(a.signs + e));
+                        else y = d_mul(xs, __ldg(a.signs + e));
+                        static_cast<TOut *>(a.out)[r * a.ld_out + e] = TOut(y);
+                    }
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) t28[(k << m) + swz(base + (j << p))] = x[j];
+                }
+            }
+            done = p + 4;
+            __syncthreads();
+            if (last) break;
+        }
+        if (MODE == MODE_FWD) mix_columns(std::integral_constant<bool, false>{}, true);
+        __syncthreads();   // the row buffer is reloaded for the next row
+    }
+}
+
+template <typename TIn, typename TOut, int MODE>
+int launch_rht28(const R28Args &a, cudaStream_t st) {
+    auto kern = rht28_kernel<TIn, TOut, MODE>;
+    const size_t smem = size_t(28) * (size_t(8) << a.m);
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess)
+        return uq::check_cuda("rht28: set smem attribute");
+    const int64_t grid = std::min<int64_t>(a.rows, uq::num_sms());
+    if (grid > 0) { uq::ProfScope _p("rht", st); kern<<<unsigned(grid), 512, smem, st>>>(a); }
+    return uq::check_cuda("rht28_kernel launch");
+}
+
+int rht28_m(int64_t n0) {
+    for (int m = 9; m <= 10; ++m)
+        if (n0 == 28 * (int64_t(1) << m)) return m;
+    return -1;
+}
+
 // Fixed-order sum of per-CTA partial pairs -> err[0..1].
 __global__ void sum_pairs_kernel(const double *part, int64_t count, double *err) {
     __shared__ double s0[256], s1[256];
@@ -892,6 +1039,39 @@ int uq_irht_rows(const void *X, int x_dtype, int64_t rows, int64_t n, int64_t ld
     if (!X || !signs || !out) return uq::fail(UQ_ERR_INVALID, "uq_irht_rows: null pointer");
     return uq::rht_inverse(X, x_dtype, rows, n, ldx, n0, signs, nullptr, nullptr, out, UQ_F64, n0,
                            nullptr, 0, 0, nullptr, nullptr, UQ_STREAM(stream));
+}
+
+int uq_rht28_rows(const void *A, int a_dtype, int64_t rows, int64_t n0, int64_t lda, const double *colscale,
+                  const double *signs, double *out, void *stream) {
+    const int m = rht28_m(n0);
+    if (rows < 0 || m < 0 || lda < n0 || !uq::dtype_size(a_dtype))
+        return uq::fail(UQ_ERR_INVALID, "uq_rht28_rows: n0 = %lld is not 28 x 512 or 28 x 1024 (rows=%lld lda=%lld)",
+                        (long long)n0, (long long)rows, (long long)lda);
+    if (rows == 0) return UQ_OK;
+    if (!A || !signs || !out) return uq::fail(UQ_ERR_INVALID, "uq_rht28_rows: null pointer");
+    R28Args a{};
+    a.in = A; a.rows = rows; a.ld_in = lda; a.m = m; a.signs = signs; a.colscale = colscale;
+    a.out = out; a.ld_out = n0; a.c = 1.0 / sqrt(double(n0));
+    if (a_dtype == UQ_F64) return launch_rht28<double, double, MODE_FWD>(a, UQ_STREAM(stream));
+    return launch_rht28<float, double, MODE_FWD>(a, UQ_STREAM(stream));
+}
+
+int uq_irht28_rows(const void *X, int x_dtype, int64_t rows, int64_t n0, int64_t ldx, const double *colscale,
+                   const double *signs, void *out, int out_dtype, int64_t ld_out, void *stream) {
+    const int m = rht28_m(n0);
+    if (rows < 0 || m < 0 || ldx < n0 || ld_out < n0 || !uq::dtype_size(x_dtype) || !uq::dtype_size(out_dtype))
+        return uq::fail(UQ_ERR_INVALID, "uq_irht28_rows: n0 = %lld is not 28 x 512 or 28 x 1024 (rows=%lld)",
+                        (long long)n0, (long long)rows);
+    if (rows == 0) return UQ_OK;
+    if (!X || !signs || !out) return uq::fail(UQ_ERR_INVALID, "uq_irht28_rows: null pointer");
+    R28Args a{};
+    a.in = X; a.rows = rows; a.ld_in = ldx; a.m = m; a.signs = signs; a.colscale = colscale;
+    a.out = out; a.ld_out = ld_out; a.c = 1.0 / sqrt(double(n0));
+    const cudaStream_t st = UQ_STREAM(stream);
+    if (x_dtype == UQ_F64 && out_dtype == UQ_F64) return launch_rht28<double, double, MODE_INV>(a, st);
+    if (x_dtype == UQ_F64 && out_dtype == UQ_F32) return launch_rht28<double, float, MODE_INV>(a, st);
+    if (x_dtype == UQ_F32 && out_dtype == UQ_F64) return launch_rht28<float, double, MODE_INV>(a, st);
+    return launch_rht28<float, float, MODE_INV>(a, st);
 }
 
 }  // extern "C"

@@ -57,11 +57,27 @@ def quant_trellis_device(W: torch.Tensor, H: torch.Tensor, L=12, R=2, seg=64, sc
 
 
 def quant_step_device(W: torch.Tensor, H: torch.Tensor, step: float, group=256, seed=0,
-                      keep_codes=False) -> QuantResult:
-    """Device-resident buildalloc recipe (E8 at a fixed step)."""
+                      keep_codes=False, block28=False) -> QuantResult:
+    """Device-resident buildalloc recipe (E8 at a fixed step).  ``block28``
+    (opt-in, widths 28 x 512 / 28 x 1024, groups of 256): the unpadded
+    block-factorised transform, error sums in the rotated domain."""
     lib = _lib.load()
     dev = W.device
     rows, n0 = W.shape
+    if block28:
+        if group != 256:
+            raise ValueError("block28 quantizes groups of 256")
+        H = H.to(device=dev, dtype=torch.float64).contiguous()
+        W = W.contiguous()
+        d = D.signs(n0, seed, dev)
+        What = torch.empty((rows, n0), dtype=torch.float32, device=dev)
+        err = torch.empty(2, dtype=torch.float64, device=dev) if rows else torch.zeros(2, dtype=torch.float64, device=dev)
+        idx = torch.empty(rows * n0, dtype=torch.int16, device=dev) if keep_codes else None
+        ws = D.workspace(lib.uq_quant_e8_b28_workspace_bytes(rows, n0), dev)
+        _lib.check(lib.uq_quant_e8_b28(W.data_ptr(), D.dtype_code(W), rows, n0, n0, H.data_ptr(), float(step),
+                                       d.data_ptr(), What.data_ptr(), D.ptr(idx), err.data_ptr(), ws.data_ptr(),
+                                       ws.numel(), D.stream_handle(dev)), "uq_quant_e8_b28")
+        return QuantResult(What, err, idx=idx)
     n = int(lib.uq_next_pow2(n0))
     H = H.to(device=dev, dtype=torch.float64).contiguous()
     W = W.contiguous()
@@ -96,8 +112,9 @@ def quant_trellis(W, H, L=12, R=2, seg=64, scale_group=256):
     return _host_result(quant_trellis_device(w, h, L, R, seg, scale_group, keep_codes=False).What, W)
 
 
-def quant_step(W, H, step):
-    """buildalloc.py:21-24 on host arrays: returns What float32."""
+def quant_step(W, H, step, block28=False):
+    """buildalloc.py:21-24 on host arrays: returns What float32 (``block28``:
+    the opt-in unpadded transform for widths 28 x 512 / 28 x 1024)."""
     w = D.as_device(W)
     h = D.as_device(H, torch.float64)
-    return _host_result(quant_step_device(w, h, step).What, W)
+    return _host_result(quant_step_device(w, h, step, block28=block28).What, W)

@@ -11,7 +11,7 @@ kernel once, which is the form to put under ``ncu -k <kernel> -c 1``.
 
 Kernels: viterbi (segments of 256, L / R), rht and irht (fp64), e8,
 normalize, fwht (fp32), recon and recon_bwd (the QAT decoder, fp32), q8enc and
-q8dec (Q8_0 blocks, fp32 side).
+q8dec (Q8_0 blocks, fp32 side), rht28 (opt-in unpadded 28 x P transform, --n0).
 """
 from __future__ import annotations
 
@@ -26,7 +26,7 @@ from . import _lib
 # profiler scope name of each case's kernel
 SCOPE = {"viterbi": "viterbi_fwd", "rht": "rht", "irht": "rht", "e8": "e8_quant",
          "normalize": "normalize", "fwht": "fwht", "recon": "qat_recon", "recon_bwd": "qat_recon_bwd",
-         "q8enc": "q8_encode", "q8dec": "q8_decode"}
+         "q8enc": "q8_encode", "q8dec": "q8_decode", "rht28": "rht"}
 
 
 def _peaks():
@@ -123,6 +123,14 @@ def build_case(args, lib, st):
                                                  sH.data_ptr(), n, gcw.data_ptr(), gsc.data_ptr(), ws.data_ptr(),
                                                  ws.numel(), st), "recon_bwd")
         return run, rows * n * 8, "bytes"
+    if k == "rht28":
+        A = torch.randn(rows, n0, dtype=torch.float64, device=dev, generator=g)
+        out = torch.empty_like(A)
+        d28 = D.signs(n0, 0, dev)
+
+        def run():
+            _lib.check(lib.uq_rht28_rows(A.data_ptr(), 1, rows, n0, n0, None, d28.data_ptr(), out.data_ptr(), st), "rht28")
+        return run, rows * n0 * 16, "bytes"
     if k in ("q8enc", "q8dec"):
         W = torch.randn(rows, n, device=dev, generator=g) * 0.02
         q = torch.empty((rows, n // 32 * 34), dtype=torch.uint8, device=dev)

@@ -59,13 +59,26 @@ def _next_pow2(n: int) -> int:
     return int(_lib.load().uq_next_pow2(int(n)))
 
 
-def rht_rows(A, seed=0):
-    """qlab.py:71-85 -- randomized Hadamard transform along rows (fp64 out)."""
+def _signs_n(n: int, seed: int, dev):
+    return D.signs(n, seed, dev)
+
+
+def rht_rows(A, seed=0, block28=False):
+    """qlab.py:71-85 -- randomized Hadamard transform along rows (fp64 out).
+    ``block28=True`` (opt-in, no reference counterpart) uses the unpadded
+    H_28 (x) H_P transform for widths 28 x 512 and 28 x 1024."""
     lib = _lib.load()
     a = D.as_device(A)
     if a.dim() != 2:
         raise ValueError("rht_rows expects a 2-D array (out, in)")
     rows, n0 = a.shape
+    if block28:
+        out = torch.empty((rows, n0), dtype=torch.float64, device=a.device)
+        if rows:
+            d = _signs_n(n0, seed, a.device)
+            _lib.check(lib.uq_rht28_rows(a.data_ptr(), D.dtype_code(a), rows, n0, n0, None, d.data_ptr(),
+                                         out.data_ptr(), D.stream_handle(a.device)), "rht_rows(block28)")
+        return _ret(out, A)
     if n0 == 0:  # the reference pads to one zero column
         a = torch.zeros((rows, 1), dtype=torch.float64, device=a.device)
         n0 = 1
@@ -78,11 +91,19 @@ def rht_rows(A, seed=0):
     return _ret(out, A)
 
 
-def irht_rows(X, n0, seed=0):
-    """qlab.py:87-98 -- inverse of rht_rows, cropped to n0 columns (fp64)."""
+def irht_rows(X, n0, seed=0, block28=False):
+    """qlab.py:87-98 -- inverse of rht_rows, cropped to n0 columns (fp64).
+    ``block28=True``: inverse of the opt-in unpadded transform (n0 = width)."""
     lib = _lib.load()
     x = D.as_device(X)
     rows, n = x.shape
+    if block28:
+        out = torch.empty((rows, n), dtype=torch.float64, device=x.device)
+        if rows:
+            d = _signs_n(n, seed, x.device)
+            _lib.check(lib.uq_irht28_rows(x.data_ptr(), D.dtype_code(x), rows, n, n, None, d.data_ptr(),
+                                          out.data_ptr(), 1, n, D.stream_handle(x.device)), "irht_rows(block28)")
+        return _ret(out, X)
     if n & (n - 1):
         raise ValueError("irht_rows: width must be a power of two")
     n0 = int(n0)
