@@ -169,8 +169,9 @@ def run_llama8b(args, rank: int, world: int, local: int):
     gate/up 14336 x 4096, down 4096 x 14336}), Student-t(4) weights with std
     0.02 and log-normal imatrix, trellis L=16 T=256 with k=3 on ffn_down /
     attn_q / attn_output and k=2 elsewhere, sharded by tensor and row block
-    (strong scaling: the set is fixed).  Weights are generated on the device
-    before the timed region."""
+    (strong scaling: the set is fixed).  ``--workload llama70b``: the
+    Llama-3-70B shapes (hidden 8192, k/v 1024 x 8192, ffn 28672), std 0.015,
+    uniform k=2.  Weights are generated on the device before the timed region."""
     import torch
     import torch.distributed as dist
     from ultraquant_b200 import pipeline, shard
@@ -179,7 +180,14 @@ def run_llama8b(args, rank: int, world: int, local: int):
     if world > 1:
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
-    specs = shard.llama_shapes(layers=args.layers)
+    if args.workload == "llama70b":
+        specs = shard.llama_shapes(layers=args.layers, hidden=8192, kv=1024, ffn=28672,
+                                   k_by_type={t: 2 for t in ("attn_q", "attn_k", "attn_v", "attn_output",
+                                                             "ffn_gate", "ffn_up", "ffn_down")})
+        std = 0.015
+    else:
+        specs = shard.llama_shapes(layers=args.layers)
+        std = 0.02
     plan = [s for s in shard.plan(specs, world) if s.rank == rank]
     data = []
     for sh in plan:
@@ -187,7 +195,7 @@ def run_llama8b(args, rank: int, world: int, local: int):
         g.manual_seed(sum(map(ord, sh.tensor.name)) * 1000 + sh.row0)
         z = torch.randn((sh.rows, sh.tensor.cols), generator=g, device=dev)
         chi = torch.randn((4, sh.rows, sh.tensor.cols), generator=g, device=dev).pow_(2).sum(0)
-        W = (z / torch.sqrt(chi / 4.0) / (2.0 ** 0.5) * 0.02).float()
+        W = (z / torch.sqrt(chi / 4.0) / (2.0 ** 0.5) * std).float()
         gh = torch.Generator(device=dev)
         gh.manual_seed(sum(map(ord, sh.tensor.name)))
         H = torch.exp(torch.randn(sh.tensor.cols, generator=gh, device=dev, dtype=torch.float64))
@@ -210,7 +218,8 @@ def run_llama8b(args, rank: int, world: int, local: int):
     wn = shard.gather_errors(results, specs)
     weights = sum(s.rows * s.cols for s in specs)
     if rank == 0:
-        line = {"metric": "Llama-3.1-8B-shaped weight set trellis-quantized, wall time on device",
+        model = "Llama-3-70B" if args.workload == "llama70b" else "Llama-3.1-8B"
+        line = {"metric": f"{model}-shaped weight set trellis-quantized, wall time on device",
                 "value": float(ms.item()) / 1e3, "unit": "s", "n_gpus": world, "steps": 1, "warmup": 0,
                 "higher_is_better": False, "scaling": "strong", "weights": weights,
                 "weights_per_s": weights / (float(ms.item()) / 1e3), "layers": args.layers,
@@ -243,10 +252,11 @@ def main():
     ap.add_argument("--cpu-rows", type=int, default=8, help="rows of the CPU baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--workload", default="tensor", choices=["tensor", "llama8b"],
-                    help="tensor: the 4096x4096 L=16 k=2+3 step (default); llama8b: the whole "
-                         "Llama-3.1-8B-shaped weight set sharded over the ranks (one step)")
-    ap.add_argument("--layers", type=int, default=32, help="layers of the llama8b workload")
+    ap.add_argument("--workload", default="tensor", choices=["tensor", "llama8b", "llama70b"],
+                    help="tensor: the 4096x4096 L=16 k=2+3 step (default); llama8b / llama70b: the "
+                         "whole Llama-3.1-8B- / Llama-3-70B-shaped weight set sharded over the ranks (one step)")
+    ap.add_argument("--layers", type=int, default=None,
+                    help="layers of the llama workloads (default 32 for llama8b, 80 for llama70b)")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -255,7 +265,9 @@ def main():
 
     if args.impl == "reference":
         return run_reference(args, rank, world)
-    if args.workload == "llama8b":
+    if args.workload in ("llama8b", "llama70b"):
+        if args.layers is None:
+            args.layers = 80 if args.workload == "llama70b" else 32
         return run_llama8b(args, rank, world, local)
 
     import numpy as np

@@ -87,6 +87,13 @@ int uq_irht28_rows(const void *X, int x_dtype, int64_t rows, int64_t n0, int64_t
                    const double *colscale, const double *signs, void *out, int out_dtype,
                    int64_t ld_out, void *stream);
 
+/* qlab.py:100-106 q_uniform(A, bpw, bs): per block of bs values, amax =
+ * max|x| + 1e-12, out = rint(x / amax * lvl) / lvl * amax in the array's
+ * dtype (UQ_F32 / UQ_F64); lvl = 2^(round(bpw) - 1) - 1 computed by the
+ * caller (Python round).  size must be a multiple of bs. */
+int uq_q_uniform(const void *A, int dtype, int64_t size, int64_t bs, int64_t lvl, void *out,
+                 void *stream);
+
 /* qlab.py:133-142 _d8_decode(Y): Y, out are (nvec, 8) fp64. */
 int uq_d8_decode(const double *Y, int64_t nvec, double *out, void *stream);
 

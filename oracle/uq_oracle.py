@@ -29,7 +29,7 @@ __all__ = [
     "trellis_quant", "trellis_quant_fast", "trellis_encode", "trellis_decode",
     "fwht_torch", "irht_torch", "recon_torch", "quant_trellis", "quant_step",
     "group_rms_f32", "viterbi_segments", "pack_states", "unpack_states", "enc_q8", "deq_q8",
-    "hadamard28", "rht28_rows", "irht28_rows", "quant_step_b28",
+    "hadamard28", "rht28_rows", "irht28_rows", "quant_step_b28", "q_uniform",
 ]
 
 
@@ -498,3 +498,11 @@ def quant_step_b28(W, H, step):
     X = rht28_rows(np.asarray(W, np.float64) * sH)
     Xq = q_e8_fast(X, fixed_step=step)
     return (irht28_rows(Xq) / sH).astype(np.float32), X, Xq
+
+
+def q_uniform(A, bpw, bs=32):
+    """qlab.py:100-106: per-block absmax, rint(x / amax * lvl) / lvl * amax."""
+    x = A.reshape(-1, bs)
+    amax = np.max(np.abs(x), axis=1, keepdims=True) + 1e-12
+    lvl = (1 << (int(round(bpw)) - 1)) - 1
+    return (np.round(x / amax * lvl) / lvl * amax).reshape(A.shape)

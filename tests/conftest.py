@@ -41,6 +41,11 @@ def g_pipeline():
 
 
 @pytest.fixture(scope="session")
+def g_quniform():
+    return load_golden("golden_quniform.npz")
+
+
+@pytest.fixture(scope="session")
 def g_q8():
     return load_golden("golden_q8.npz")
 

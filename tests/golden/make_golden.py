@@ -277,9 +277,26 @@ def make_q8(qlab):
     np.savez_compressed(os.path.join(HERE, "golden_q8.npz"), **out)
 
 
+def make_quniform(qlab):
+    """qlab.py:100-106 q_uniform on fp64 and fp32 matrices at several rates."""
+    rng = np.random.RandomState(17)
+    out = {"versions": _versions()}
+    A = rng.standard_t(4, size=(16, 256)) * 0.02
+    A[2, :32] = 0.0
+    A[3, :32] = np.arange(32) / 31.0 - 0.5
+    for tag, M in (("f64", A), ("f32", A.astype(np.float32))):
+        out[f"qu_{tag}_A"] = M
+        for bpw in (2, 3, 4, 2.5):
+            with np.errstate(invalid="ignore"):
+                out[f"qu_{tag}_{bpw}"] = qlab.q_uniform(M, bpw)
+        out[f"qu_{tag}_bs64"] = qlab.q_uniform(M, 3, bs=64)
+    np.savez_compressed(os.path.join(HERE, "golden_quniform.npz"), **out)
+
+
 MAKERS = {"rht": lambda m: make_rht(m[0]), "e8": lambda m: make_e8(m[0]),
           "trellis": lambda m: make_trellis(m[1], m[2]), "pipeline": lambda m: make_pipeline(*m),
-          "qat": lambda m: make_qat(m[0], m[2]), "q8": lambda m: make_q8(m[0])}
+          "qat": lambda m: make_qat(m[0], m[2]), "q8": lambda m: make_q8(m[0]),
+          "quniform": lambda m: make_quniform(m[0])}
 
 
 def main():

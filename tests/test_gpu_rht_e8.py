@@ -237,3 +237,18 @@ def test_quant_step_block28_vs_oracle():
     A = W.astype(np.float64) * np.sqrt(Hc)[None, :]
     Ah = ref.astype(np.float64) * np.sqrt(Hc)[None, :]
     assert abs(res.wnmse - O.wnmse(A, Ah)) <= 1e-6 * res.wnmse + 1e-6
+
+
+@pytest.mark.parametrize("tag", ["f64", "f32"])
+def test_q_uniform_golden(uq, g_quniform, tag):
+    """qlab.q_uniform (lab quantizer): bit-exact against the reference in both dtypes."""
+    A = g_quniform[f"qu_{tag}_A"]
+    for bpw in (2, 3, 4, 2.5):
+        got = uq.q_uniform(A, bpw)
+        assert got.dtype == A.dtype and same_bits(got, g_quniform[f"qu_{tag}_{bpw}"])
+    assert same_bits(uq.q_uniform(A, 3, bs=64), g_quniform[f"qu_{tag}_bs64"])
+    rng = np.random.RandomState(3)
+    B = rng.normal(size=(64, 4096))
+    assert same_bits(uq.q_uniform(B, 3), O.q_uniform(B, 3))
+    with pytest.raises(ValueError):
+        uq.q_uniform(np.zeros((3, 10)), 2)

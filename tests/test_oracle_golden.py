@@ -213,3 +213,12 @@ def test_block28_transform_restatement():
         X = O.rht28_rows(A)
         assert abs(np.sum(X ** 2) / np.sum(A ** 2) - 1) < 1e-12
         assert np.abs(O.irht28_rows(X) - A).max() < 1e-13
+
+
+@pytest.mark.parametrize("tag", ["f64", "f32"])
+def test_q_uniform(g_quniform, tag):
+    A = g_quniform[f"qu_{tag}_A"]
+    for bpw in (2, 3, 4, 2.5):
+        with np.errstate(invalid="ignore"):
+            assert same_bits(O.q_uniform(A, bpw), g_quniform[f"qu_{tag}_{bpw}"])
+    assert same_bits(O.q_uniform(A, 3, bs=64), g_quniform[f"qu_{tag}_bs64"])

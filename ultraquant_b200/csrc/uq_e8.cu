@@ -525,6 +525,28 @@ int launch_e8_quant(const E8Args &a0, cudaStream_t st) {
     return uq::check_cuda("e8_quant_kernel launch");
 }
 
+// ---- q_uniform (qlab.py:100-106) ------------------------------------------------
+// Per block of bs consecutive values: amax = max|x| + 1e-12 (in the array's
+// dtype), xh = rint(x / amax * lvl) / lvl * amax, each step one IEEE operation
+// in that dtype.  One warp per block.
+template <typename T>
+__global__ void q_uniform_kernel(const T *A, int64_t nblocks, int64_t bs, T lvl, T *out) {
+    const int lane = threadIdx.x & 31;
+    const int64_t w0 = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const int64_t nw = (int64_t(gridDim.x) * blockDim.x) >> 5;
+    for (int64_t b = w0; b < nblocks; b += nw) {
+        const T *x = A + b * bs;
+        T m = T(0);
+        for (int64_t i = lane; i < bs; i += 32) m = fmax(m, fabs(__ldg(x + i)));
+        for (int o = 16; o > 0; o >>= 1) m = fmax(m, __shfl_xor_sync(0xffffffffu, m, o));
+        const T amax = m + T(1e-12);
+        for (int64_t i = lane; i < bs; i += 32) {
+            const T q = rint((__ldg(x + i) / amax) * lvl);
+            out[b * bs + i] = (q / lvl) * amax;
+        }
+    }
+}
+
 // ---- entropy of lattice indices --------------------------------------------
 // Key: byte i = (2*p_i truncated) + 128, coordinate values must lie in
 // [-127, 127]; byte 0 never occurs, so key 0 marks an empty slot.
@@ -804,6 +826,27 @@ int uq_e8_calibrate(const void *A, int a_dtype, int64_t size, int64_t group, dou
     }
     *step_host = (lo + hi) / 2;
     return UQ_OK;
+}
+
+int uq_q_uniform(const void *A, int dtype, int64_t size, int64_t bs, int64_t lvl, void *out, void *stream) {
+    if (size < 0 || bs < 1 || size % bs || !uq::dtype_size(dtype))
+        return uq::fail(UQ_ERR_INVALID, "uq_q_uniform: cannot reshape array of size %lld into shape (-1,%lld)",
+                        (long long)size, (long long)bs);
+    if (size == 0) return UQ_OK;
+    if (!A || !out) return uq::fail(UQ_ERR_INVALID, "uq_q_uniform: null pointer");
+    const int64_t nblocks = size / bs;
+    const int grid = int(std::max<int64_t>(1, std::min<int64_t>((nblocks + 7) / 8, int64_t(uq::num_sms()) * 16)));
+    const cudaStream_t st = UQ_STREAM(stream);
+    {
+        uq::ProfScope _p("q_uniform", st);
+        if (dtype == UQ_F64)
+            q_uniform_kernel<double><<<grid, 256, 0, st>>>(static_cast<const double *>(A), nblocks, bs, double(lvl),
+                                                           static_cast<double *>(out));
+        else
+            q_uniform_kernel<float><<<grid, 256, 0, st>>>(static_cast<const float *>(A), nblocks, bs, float(lvl),
+                                                          static_cast<float *>(out));
+    }
+    return uq::check_cuda("q_uniform_kernel launch");
 }
 
 }  // extern "C"

@@ -18,7 +18,7 @@ from . import _lib
 from .q8 import deq_q8  # noqa: F401  (qlab.py:27-32, used by load_WH)
 
 __all__ = ["wnmse", "_next_pow2", "rht_rows", "irht_rows", "_d8_decode", "e8_decode",
-           "_entropy_bpw", "q_e8_fast", "_E8_SCALE", "deq_q8"]
+           "_entropy_bpw", "q_e8_fast", "_E8_SCALE", "deq_q8", "q_uniform"]
 
 # qlab.py:158 -- calibrated E8 step per calib_key, reused across tensors
 _E8_SCALE: dict = {}
@@ -113,6 +113,19 @@ def irht_rows(X, n0, seed=0, block28=False):
         _lib.check(lib.uq_irht_rows(x.data_ptr(), D.dtype_code(x), rows, n, n, min(n0, n), d.data_ptr(),
                                     out.data_ptr(), D.stream_handle(x.device)), "irht_rows")
     return _ret(out, X)
+
+
+def q_uniform(A, bpw, bs=32):
+    """qlab.py:100-106 -- per-block absmax uniform quantizer (dtype of A)."""
+    lib = _lib.load()
+    a = D.as_device(A)
+    lvl = (1 << (int(round(bpw)) - 1)) - 1
+    out = torch.empty_like(a)
+    if a.numel() % bs:
+        raise ValueError(f"cannot reshape array of size {a.numel()} into shape (-1,{bs})")
+    _lib.check(lib.uq_q_uniform(a.data_ptr() if a.numel() else None, D.dtype_code(a), a.numel(), int(bs), lvl,
+                                out.data_ptr() if out.numel() else None, D.stream_handle(a.device)), "q_uniform")
+    return _ret(out, A)
 
 
 def _d8_decode(Y):
