@@ -94,6 +94,24 @@ int uq_irht28_rows(const void *X, int x_dtype, int64_t rows, int64_t n0, int64_t
 int uq_q_uniform(const void *A, int dtype, int64_t size, int64_t bs, int64_t lvl, void *out,
                  void *stream);
 
+/* qlab.py:185-198 q_e8(A, bpw, group_scale): finite-codebook E8 quantizer.
+ * A: `size` values (UQ_F32 / UQ_F64), flattened and zero-padded to whole
+ * groups of `group` (a multiple of 8, at most 8192); s = sqrt(mean(g^2)) +
+ * 1e-12 per group, gn = g / s as 8-vectors, out[e] = cb[nearest] * s (fp64,
+ * `size` values).  cb: K x 8 fp64 codewords, cb32 the same rounded to fp32
+ * (16-byte aligned).  When cb is qlab.py:111-124's e8_codebook(K) -- the K
+ * grid points of smallest norm, divided by `scale` -- pass that scale and
+ * norm_cut = the K-th smallest lattice norm (+inf when K covers the grid),
+ * which lets vectors whose nearest lattice point is a codeword skip the
+ * search; pass norm_cut = 0 for any other codebook.  Nearest = smallest
+ * Euclidean distance (cKDTree.query); on an exact fp64 tie the lowest index.
+ * Synchronises the stream; a non-finite gn returns UQ_ERR_INVALID (cKDTree's
+ * ValueError).  Workspace: uq_q_e8_workspace_bytes(size, group). */
+size_t uq_q_e8_workspace_bytes(int64_t size, int64_t group);
+int uq_q_e8(const void *A, int a_dtype, int64_t size, int64_t group, const double *cb,
+            const float *cb32, int64_t K, double scale, double norm_cut, double *out,
+            void *workspace, size_t workspace_bytes, void *stream);
+
 /* qlab.py:133-142 _d8_decode(Y): Y, out are (nvec, 8) fp64. */
 int uq_d8_decode(const double *Y, int64_t nvec, double *out, void *stream);
 

@@ -30,6 +30,7 @@ __all__ = [
     "fwht_torch", "irht_torch", "recon_torch", "quant_trellis", "quant_step",
     "group_rms_f32", "viterbi_segments", "pack_states", "unpack_states", "enc_q8", "deq_q8",
     "hadamard28", "rht28_rows", "irht28_rows", "quant_step_b28", "q_uniform",
+    "e8_codebook", "nearest_exact", "q_e8",
 ]
 
 
@@ -506,3 +507,68 @@ def q_uniform(A, bpw, bs=32):
     amax = np.max(np.abs(x), axis=1, keepdims=True) + 1e-12
     lvl = (1 << (int(round(bpw)) - 1)) - 1
     return (np.round(x / amax * lvl) / lvl * amax).reshape(A.shape)
+
+
+# ---------------------------------------------------------------------------
+# Finite-codebook E8 quantizer  (qlab.py:110-124, 185-198)
+# ---------------------------------------------------------------------------
+_E8CB: dict = {}
+_E8PTS: list = []
+
+
+def _e8_points():
+    """(D8 grid points as int8, norms of the point list, argsort of the norms)."""
+    if not _E8PTS:
+        g = (np.indices((7,) * 8, dtype=np.int8).reshape(8, -1).T - 3).astype(np.int8)
+        d8 = g[(g.astype(np.int64).sum(1) % 2) == 0]
+        n_d8 = (d8.astype(np.int64) ** 2).sum(1)
+        n_half = ((2 * d8.astype(np.int64) + 1) ** 2).sum(1) // 4    # |p + 1/2|^2, an integer
+        norms = np.concatenate([n_d8, n_half]).astype(np.float64)
+        _E8PTS.extend([d8, norms, np.argsort(norms)])
+    return _E8PTS
+
+
+def e8_codebook(K):
+    """qlab.py:111-124: the points of D8 (even coordinate sum, coordinates in
+    [-3, 3]) followed by the same points plus 1/2, both in grid order (first
+    coordinate slowest); the K of smallest norm by np.argsort (numpy's order
+    among equal norms), divided by sqrt(mean |p|^2 / 8)."""
+    if K not in _E8CB:
+        d8, _, order = _e8_points()
+        ids = order[:K]
+        pts = d8[ids % len(d8)].astype(np.float64) + np.where(ids >= len(d8), 0.5, 0.0)[:, None]
+        _E8CB[K] = pts / np.sqrt((pts ** 2).sum(1).mean() / 8)
+    return _E8CB[K]
+
+
+def nearest_exact(X, cb, chunk=2048):
+    """Exact Euclidean nearest neighbour (what cKDTree.query returns for
+    eps = 0): fp64 distances sum_i (x_i - c_i)^2 in coordinate order, the
+    smallest, lowest index on equal distances."""
+    out = np.empty(len(X), np.int64)
+    for s in range(0, len(X), chunk):
+        x = X[s:s + chunk]
+        d = np.zeros((len(x), len(cb)))
+        for i in range(X.shape[1]):
+            e = x[:, i:i + 1] - cb[None, :, i]
+            d = d + e * e
+        out[s:s + chunk] = np.argmin(d, axis=1)
+    return out
+
+
+def q_e8(A, bpw, group_scale=256):
+    """qlab.py:185-198: zero-pad the flattened A (fp64) to whole groups,
+    s = sqrt(mean(g^2)) + 1e-12 per group, gn = g / s as 8-vectors, out =
+    cb[nearest] * s."""
+    K = 1 << int(round(bpw * 8))
+    cb = e8_codebook(K)
+    flat = np.asarray(A).ravel().astype(np.float64)
+    flat = np.concatenate([flat, np.zeros((-flat.size) % group_scale)])
+    g = flat.reshape(-1, group_scale)
+    s = np.sqrt((g ** 2).mean(1, keepdims=True)) + 1e-12
+    gn = (g / s).reshape(-1, 8)
+    if not np.isfinite(gn).all():
+        raise ValueError("'x' must be finite, check for nan or inf values")
+    idx = nearest_exact(gn, cb)
+    rec = (cb[idx].reshape(-1, group_scale) * s).ravel()[:np.asarray(A).size]
+    return rec.reshape(np.shape(A))

@@ -46,6 +46,11 @@ def g_quniform():
 
 
 @pytest.fixture(scope="session")
+def g_qe8():
+    return load_golden("golden_qe8.npz")
+
+
+@pytest.fixture(scope="session")
 def g_q8():
     return load_golden("golden_q8.npz")
 
@@ -80,3 +85,42 @@ def same_bits(a, b):
         return False
     iv = {4: np.int32, 8: np.int64, 2: np.int16, 1: np.int8}[a.dtype.itemsize]
     return bool(np.array_equal(a.view(iv), b.view(iv)))
+
+
+def qe8_same_or_tie(got, ref, A, bpw, group=256, max_ties=4):
+    """q_e8 outputs (qlab.py:185-198) bit-equal except on 8-vectors whose two
+    reconstructions are codewords at exactly equal distance from gn (checked
+    in rational arithmetic) -- ties that cKDTree breaks by the order of its
+    tree search.  Returns the number of tied vectors (at most max_ties)."""
+    from fractions import Fraction
+    import oracle as O
+    got = np.ascontiguousarray(got, np.float64).ravel()
+    ref = np.ascontiguousarray(ref, np.float64).ravel()
+    if got.shape != ref.shape:
+        return -1
+    diff = np.flatnonzero(got.view(np.int64) != ref.view(np.int64))
+    if diff.size == 0:
+        return 0
+    cb = O.e8_codebook(1 << int(round(bpw * 8)))
+    flat = np.asarray(A, np.float64).ravel()
+    flat = np.concatenate([flat, np.zeros((-flat.size) % group)])
+    g = flat.reshape(-1, group)
+    s = np.repeat(np.sqrt((g ** 2).mean(1, keepdims=True)) + 1e-12, group, axis=1).reshape(-1, 8)
+    gn = (g / (np.sqrt((g ** 2).mean(1, keepdims=True)) + 1e-12)).reshape(-1, 8)
+    vecs = np.unique(diff // 8)
+    assert vecs.size <= max_ties, f"{vecs.size} vectors differ"
+    n = got.size
+    for v in vecs:
+        valid = np.arange(8 * v, min(8 * v + 8, n)) - 8 * v
+        def code(out):
+            rec = cb * s[v][None, :]
+            hit = np.all(rec[:, valid].view(np.int64) == out[8 * v + valid].view(np.int64)[None, :], axis=1)
+            j = np.flatnonzero(hit)
+            assert j.size, f"vector {v}: output is not a scaled codeword"
+            return int(j[0])
+        jg, jr = code(got), code(ref)
+        exact = [sum((Fraction(float(gn[v, i])) - Fraction(float(cb[j, i]))) ** 2 for i in range(8)) for j in (jg, jr)]
+        assert exact[0] == exact[1], f"vector {v}: codewords {jg} and {jr} are not at equal distance"
+        d = ((gn[v][None, :] - cb) ** 2).sum(1)
+        assert float(exact[0]) <= d.min() * (1 + 1e-12), f"vector {v}: not a nearest codeword"
+    return int(vecs.size)

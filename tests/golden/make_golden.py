@@ -293,10 +293,42 @@ def make_quniform(qlab):
     np.savez_compressed(os.path.join(HERE, "golden_quniform.npz"), **out)
 
 
+def make_qe8(qlab):
+    """qlab.py:185-198 q_e8 (cKDTree nearest codeword) at three rates, fp32
+    input, another group size, a ragged size and edge rows; fingerprints of
+    e8_codebook (qlab.py:111-124) for several K."""
+    import hashlib
+    rng = np.random.RandomState(21)
+    out = {"versions": _versions()}
+    Ks = np.array([16, 256, 4096, 65536, 1 << 20], np.int64)
+    out["cb_K"] = Ks
+    out["cb_sha256"] = np.array([hashlib.sha256(qlab.e8_codebook(int(K)).tobytes()).hexdigest() for K in Ks])
+    out["cb_256"] = qlab.e8_codebook(256)
+    A = student_t(rng, (16, 512), std=0.02)
+    out["qe_A"] = A
+    for bpw in (1.0, 1.5, 2.0):
+        out[f"qe_A_{bpw}"] = qlab.q_e8(A, bpw)
+    out["qe_A32_2.0"] = qlab.q_e8(A.astype(np.float32), 2.0)
+    out["qe_A_g64_2.0"] = qlab.q_e8(A[:8], 2.0, group_scale=64)
+    R = rng.standard_normal((7, 100))
+    out["qe_R"] = R
+    out["qe_R_2.0"] = qlab.q_e8(R, 2.0)
+    E = student_t(rng, (6, 256), std=0.02)
+    E[0] = 0.0                       # zero group
+    E[1, :] = 0.0
+    E[1, 7] = 5.0                    # one outlier in a group
+    E[2] = 0.013                     # constant group
+    E[3] *= 1e-200                   # tiny values
+    E[4, ::2] = 0.0                  # half zeros
+    out["qe_E"] = E
+    out["qe_E_2.0"] = qlab.q_e8(E, 2.0)
+    np.savez_compressed(os.path.join(HERE, "golden_qe8.npz"), **out)
+
+
 MAKERS = {"rht": lambda m: make_rht(m[0]), "e8": lambda m: make_e8(m[0]),
           "trellis": lambda m: make_trellis(m[1], m[2]), "pipeline": lambda m: make_pipeline(*m),
           "qat": lambda m: make_qat(m[0], m[2]), "q8": lambda m: make_q8(m[0]),
-          "quniform": lambda m: make_quniform(m[0])}
+          "quniform": lambda m: make_quniform(m[0]), "qe8": lambda m: make_qe8(m[0])}
 
 
 def main():

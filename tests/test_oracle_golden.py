@@ -3,7 +3,7 @@ import numpy as np
 import pytest
 
 import oracle as O
-from conftest import same_bits
+from conftest import qe8_same_or_tie, same_bits
 
 
 def test_signs(g_rht):
@@ -222,3 +222,44 @@ def test_q_uniform(g_quniform, tag):
         with np.errstate(invalid="ignore"):
             assert same_bits(O.q_uniform(A, bpw), g_quniform[f"qu_{tag}_{bpw}"])
     assert same_bits(O.q_uniform(A, 3, bs=64), g_quniform[f"qu_{tag}_bs64"])
+
+
+# ---- finite-codebook E8 (qlab.py:110-124, 185-198) ------------------------------
+QE8_CASES = [("qe_A", "qe_A_1.0", 1.0, 256, False), ("qe_A", "qe_A_1.5", 1.5, 256, False),
+             ("qe_A", "qe_A_2.0", 2.0, 256, False), ("qe_A", "qe_A32_2.0", 2.0, 256, True),
+             ("qe_R", "qe_R_2.0", 2.0, 256, False), ("qe_E", "qe_E_2.0", 2.0, 256, False)]
+
+
+def _qe8_input(g, key, f32):
+    A = g[key]
+    return A.astype(np.float32) if f32 else A
+
+
+def test_e8_codebook_oracle(g_qe8):
+    """The oracle's codebook construction reproduces the reference's bytes."""
+    import hashlib
+    for K, digest in zip(g_qe8["cb_K"], g_qe8["cb_sha256"]):
+        assert hashlib.sha256(O.e8_codebook(int(K)).tobytes()).hexdigest() == str(digest)
+    assert same_bits(O.e8_codebook(256), g_qe8["cb_256"])
+
+
+def test_e8_codebook_host(g_qe8):
+    """The product's host-side codebook table (numpy, no device) is the
+    reference's, bit for bit, for every golden K."""
+    import hashlib
+    from ultraquant_b200 import qlab as Q
+    for K, digest in zip(g_qe8["cb_K"], g_qe8["cb_sha256"]):
+        assert hashlib.sha256(Q.e8_codebook(int(K)).tobytes()).hexdigest() == str(digest)
+
+
+@pytest.mark.parametrize("case", QE8_CASES, ids=[c[1] for c in QE8_CASES])
+def test_q_e8_oracle(g_qe8, case):
+    key, out, bpw, group, f32 = case
+    A = _qe8_input(g_qe8, key, f32)
+    # exact distance ties (the edge rows' lone outlier) may pick another codeword
+    assert qe8_same_or_tie(O.q_e8(A, bpw, group), g_qe8[out], A, bpw, group) >= 0
+
+
+def test_q_e8_oracle_group64(g_qe8):
+    A = g_qe8["qe_A"][:8]
+    assert qe8_same_or_tie(O.q_e8(A, 2.0, group_scale=64), g_qe8["qe_A_g64_2.0"], A, 2.0, 64) == 0

@@ -25,7 +25,7 @@ __version__ = "0.1.0"
 
 _PATCH = {
     "qlab": ("_next_pow2", "rht_rows", "irht_rows", "_d8_decode", "e8_decode", "_entropy_bpw",
-             "q_e8_fast", "wnmse", "deq_q8", "q_uniform"),
+             "q_e8_fast", "wnmse", "deq_q8", "q_uniform", "e8_codebook", "q_e8"),
     "trellis": ("codebook", "pred_table", "trellis_quant", "trellis_quant_fast"),
     "qat": ("trellis_encode", "fwht_torch", "irht_torch", "recon_torch"),
     "buildq": ("enc_q8",),

@@ -34,6 +34,8 @@ SIGNATURES = {
     "uq_rht28_rows": (_i32, [_p, _i32, _i64, _i64, _i64, _p, _p, _p, _p]),
     "uq_irht28_rows": (_i32, [_p, _i32, _i64, _i64, _i64, _p, _p, _p, _i32, _i64, _p]),
     "uq_q_uniform": (_i32, [_p, _i32, _i64, _i64, _i64, _p, _p]),
+    "uq_q_e8_workspace_bytes": (_sz, [_i64, _i64]),
+    "uq_q_e8": (_i32, [_p, _i32, _i64, _i64, _p, _p, _i64, _f64, _f64, _p, _p, _sz, _p]),
     "uq_d8_decode": (_i32, [_p, _i64, _p, _p]),
     "uq_e8_decode": (_i32, [_p, _i64, _p, _p]),
     "uq_e8_quant": (_i32, [_p, _i32, _i64, _i64, _f64, _p, _p, _p]),

@@ -3,8 +3,10 @@
 // Bit-exactness: the reference runs the Sylvester butterflies in fp64 with
 // stage order h = 1, 2, 4, ..., n/2.  Every output is the same sequence of
 // correctly rounded adds / subtracts whatever the data layout, so the kernel
-// only has to keep the stage order.  Scaling uses IEEE division by sqrt(n)
-// (forward) and by n (inverse) exactly like numpy.
+// only has to keep the stage order.  Scaling divides by sqrt(n) (forward;
+// a multiplication by 2^(-b/2) for even b, else Markstein's correction of
+// x * RN(1/sqrt(n)), both correctly rounded) and by n (inverse) exactly like
+// numpy.
 //
 // Layout: a CTA owns a tile of 2^NB consecutive elements (NB = max(12, b),
 // n = 2^b; one tile holds 2^(NB-b) rows).  The tile lives in shared memory as
@@ -52,6 +54,7 @@ struct RhtArgs {
     void *out;
     int64_t ld_out, ncols_out;   // output row stride, columns written (< n crops)
     double sqrt_n, n_d;
+    double inv_sqrt_n;           // RN(1 / sqrt_n), host IEEE division
     // optional error statistics for the inverse of the importance pipeline:
     // A = rn(W * colscale) recomputed from W, partial sums per CTA.
     const void *ref_w;           // W (rows, n0) with stride ld_w, dtype = ref_dtype
@@ -59,6 +62,20 @@ struct RhtArgs {
     int ref_dtype;
     double *err_partial;         // [gridDim.x * 2]
 };
+
+// x / sqrt(n), correctly rounded, for odd log2(n) (the reference divides by
+// np.sqrt(n)).  Markstein's final correction (P. Markstein, IBM J. Res. Dev.
+// 34(1), 1990): with y = RN(1/d) and q0 = RN(x y) within one ulp of x/d, the
+// remainder r = x - q0 d is exact as an FMA and RN(q0 + r y) is the correctly
+// rounded quotient.  Magnitudes where an intermediate could leave the normal
+// range take the IEEE division.
+__device__ __forceinline__ double div_sqrt_n(double x, const RhtArgs &a) {
+    const double q0 = d_mul(x, a.inv_sqrt_n);
+    const double r = __fma_rn(-q0, a.sqrt_n, x);
+    const double q = __fma_rn(r, a.inv_sqrt_n, q0);
+    const double ax = fabs(x);
+    return (ax > 0x1p-960 && ax < 0x1p960) ? q : x / a.sqrt_n;
+}
 
 // Applies the butterfly stages of index bits [lo, hi) that lie in [p, p+4)
 // to the 16 register values x[j] = element(base + (j << p)).
@@ -221,7 +238,7 @@ rht_tile_kernel(RhtArgs a, int dbuf) {
                     if (r >= a.rows || e >= a.ncols_out) continue;
                     double y;
                     if (MODE == MODE_FWD) {
-                        y = fwd_pow2 ? d_mul(x[j], fwd_mul) : x[j] / a.sqrt_n;
+                        y = fwd_pow2 ? d_mul(x[j], fwd_mul) : div_sqrt_n(x[j], a);
                     } else {
                         // irht: (x / n) * d, x / n exact; optional / colscale
                         const double xs = d_mul(x[j], inv_mul);
@@ -271,6 +288,16 @@ rht_tile_kernel(RhtArgs a, int dbuf) {
 __device__ __forceinline__ void cluster_sync_all() {
     asm volatile("barrier.cluster.arrive.release.aligned;\n"
                  "barrier.cluster.wait.acquire.aligned;\n" ::: "memory");
+}
+
+__device__ __forceinline__ void cluster_arrive_rel() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait_acq() {
+    asm volatile("barrier.cluster.wait.acquire.aligned;\n" ::: "memory");
+}
+__device__ __forceinline__ void st_peer_f64(unsigned addr, double v) {
+    asm volatile("st.shared::cluster.f64 [%0], %1;" :: "r"(addr), "d"(v) : "memory");
 }
 
 __device__ __forceinline__ double ld_peer_f64(unsigned addr) {
@@ -379,7 +406,7 @@ rht_split_kernel(RhtArgs a) {
             if (e >= a.ncols_out) continue;
             double y;
             if (MODE == MODE_FWD) {
-                y = x[j] / a.sqrt_n;
+                y = div_sqrt_n(x[j], a);
             } else {
                 const double xs = d_mul(x[j], inv_mul);
                 y = d_mul(xs, __ldg(a.signs + e));
@@ -469,6 +496,20 @@ rht_tma_kernel(const __grid_constant__ CUtensorMap tin, const __grid_constant__ 
     constexpr int CH_OUT = 4096 / (128 / int(sizeof(TOut)));
     const int lin0 = int(col0 / (128 / int(sizeof(TIn))));
     const int lout0 = int(col0 / (128 / int(sizeof(TOut))));
+    // Two-CTA rows (n = 2^(LB+1)): CTA r finishes the pairs (i, i + 2^LB) for
+    // i in [r 2^(LB-1), (r+1) 2^(LB-1)), so its outputs are two column ranges of
+    // 2^(LB-1): the sums (register j < 8) and the differences (j >= 8).
+    // Otherwise register j holds column col0 + tid + (j << (LB - 4)).
+    auto out_col = [&](int j) -> int64_t {
+        if (CL == 2)
+            return int64_t(j < 8 ? 0 : (1 << LB)) + (int64_t(rank) << (LB - 1)) + tid + ((j & 7) << (LB - 4));
+        return col0 + tid + (j << (LB - 4));
+    };
+    // index of register j's output in the store buffer (whole boxes of 4096)
+    auto out_idx = [&](int j) -> int {
+        if (CL == 2) return (j < 8 ? 0 : (1 << (LB - 1))) + tid + ((j & 7) << (LB - 4));
+        return tid + (j << (LB - 4));
+    };
 
     if (tid == 0) {
         mbar_init(bar0, 1);
@@ -494,10 +535,7 @@ rht_tma_kernel(const __grid_constant__ CUtensorMap tin, const __grid_constant__ 
         }
     } else {
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-            const int64_t e = col0 + tid + (j << (LB - 4));
-            maskL |= (__ldg(a.signs + e) < 0.0 ? 1u : 0u) << j;
-        }
+        for (int j = 0; j < 16; ++j) maskL |= (__ldg(a.signs + out_col(j)) < 0.0 ? 1u : 0u) << j;
     }
     const double inv_mul = ldexp(1.0, -B);
     const double fwd_mul = ldexp(1.0, -(B >> 1));
@@ -506,6 +544,10 @@ rht_tma_kernel(const __grid_constant__ CUtensorMap tin, const __grid_constant__ 
 #pragma unroll
     for (int i = 0; i < LCL; ++i)
         asm("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(peer_base[i]) : "r"(sbase), "r"(rank ^ (1u << i)));
+    // two-CTA rows: the partner's values arrive in an inbox after the two tiles
+    const unsigned inbox = sbase + 2u * unsigned(BUFB);
+    const unsigned peer_inbox = peer_base[0] + 2u * unsigned(BUFB);
+    if (CL == 2) cluster_arrive_rel();   // opens the first "inbox read" phase
 
     int k = 0;
     for (int64_t r = first; r < a.rows; r += nclusters, ++k) {
@@ -566,29 +608,49 @@ rht_tma_kernel(const __grid_constant__ CUtensorMap tin, const __grid_constant__ 
         // registers: elements tid + (j << (LB - 4)) of this CTA's part
         // ---- stages of index bits LB .. B-1 across the cluster: bit LB + i pairs
         //      CTA rank with rank ^ 2^i (lower: own + peer, upper: peer - own) --
+        if (CL == 2) {
+            // push the partner's half of the pairs into its inbox (remote
+            // stores do not stall), one barrier, then finish the own half
+            cluster_wait_acq();   // the partner has read its inbox (previous row)
 #pragma unroll
-        for (int i = 0; i < LCL; ++i) {
+            for (int jj = 0; jj < 8; ++jj)
+                st_peer_f64(peer_inbox + 8u * unsigned(tid + (jj << (LB - 4))), rank == 0 ? x[8 + jj] : x[jj]);
+            cluster_arrive_rel();
+            cluster_wait_acq();   // the partner's values are in this inbox
 #pragma unroll
-            for (int j = 0; j < 16; ++j) tile[swz(tid + (j << (LB - 4)))] = x[j];
-            cluster_sync_all();
-            const unsigned pb = peer_base[i] + unsigned((k & 1) * BUFB);
-            const bool upper = (rank >> i) & 1u;
-#pragma unroll
-            for (int j = 0; j < 16; ++j) {
-                const double v = ld_peer_f64(pb + unsigned(swz(tid + (j << (LB - 4)))) * 8u);
-                x[j] = upper ? d_sub(v, x[j]) : d_add(x[j], v);
+            for (int jj = 0; jj < 8; ++jj) {
+                const double v = lds64d(inbox + 8u * unsigned(tid + (jj << (LB - 4))));
+                const double own = rank == 0 ? x[jj] : x[8 + jj];
+                const double lo = rank == 0 ? own : v, hi = rank == 0 ? v : own;
+                x[jj] = d_add(lo, hi);
+                x[8 + jj] = d_sub(lo, hi);
             }
-            cluster_sync_all();   // the partner has read this tile before it changes
+            cluster_arrive_rel();   // inbox read
+        } else {
+#pragma unroll
+            for (int i = 0; i < LCL; ++i) {
+#pragma unroll
+                for (int j = 0; j < 16; ++j) tile[swz(tid + (j << (LB - 4)))] = x[j];
+                cluster_sync_all();
+                const unsigned pb = peer_base[i] + unsigned((k & 1) * BUFB);
+                const bool upper = (rank >> i) & 1u;
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    const double v = ld_peer_f64(pb + unsigned(swz(tid + (j << (LB - 4)))) * 8u);
+                    x[j] = upper ? d_sub(v, x[j]) : d_add(x[j], v);
+                }
+                cluster_sync_all();   // the partner has read this tile before it changes
+            }
         }
         // ---- epilogue: scale, write the swizzled output lines, store ---------
         double se = 0.0, sa = 0.0;
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
-            const int E = tid + (j << (LB - 4));
-            const int64_t e = col0 + E;
+            const int E = out_idx(j);
+            const int64_t e = out_col(j);
             double y;
             if (MODE == MODE_FWD) {
-                y = (B & 1) ? x[j] / a.sqrt_n : d_mul(x[j], fwd_mul);
+                y = (B & 1) ? div_sqrt_n(x[j], a) : d_mul(x[j], fwd_mul);
             } else {
                 const double xs = d_mul(x[j], inv_mul);
                 y = flip_if(xs, (maskL >> j) & 1u);
@@ -620,8 +682,12 @@ rht_tma_kernel(const __grid_constant__ CUtensorMap tin, const __grid_constant__ 
         __syncthreads();
         if (tid == 0) {
 #pragma unroll
-            for (int bx = 0; bx < NBOX; ++bx)
-                store3d(&tout, 0, lout0 + bx * CH_OUT, int(r), buf + unsigned(bx * OUTB));
+            for (int bx = 0; bx < NBOX; ++bx) {
+                // box bx holds columns out_col of its first register range
+                const int c0 = CL == 2 ? int((bx == 0 ? 0 : (1 << LB)) + (int(rank) << (LB - 1))) / (128 / int(sizeof(TOut)))
+                                       : lout0 + bx * CH_OUT;
+                store3d(&tout, 0, c0, int(r), buf + unsigned(bx * OUTB));
+            }
             bulk_commit();
             if (MODE == MODE_INV && COLS && a.err_partial) {
                 double s0 = 0.0, s1 = 0.0;
@@ -632,7 +698,8 @@ rht_tma_kernel(const __grid_constant__ CUtensorMap tin, const __grid_constant__ 
         }
     }
     if (tid == 0) bulk_wait0();
-    if (CL > 1) cluster_sync_all();   // no CTA leaves while a partner may read its tile
+    if (CL == 2) cluster_wait_acq();  // closes the last "inbox read" phase
+    else if (CL > 1) cluster_sync_all();   // no CTA leaves while a partner may read its tile
 }
 
 // ---------------------------------------------------------------------------
@@ -837,7 +904,8 @@ template <typename TIn, typename TOut, int MODE, int LB, int CL, bool COLS>
 int launch_tma_v(const CUtensorMap &mi, const CUtensorMap &mo, const RhtArgs &a, cudaStream_t st, int64_t *nparts) {
     auto kern = rht_tma_kernel<TIn, TOut, MODE, LB, CL, COLS>;
     const int nt = 1 << (LB - 4);
-    const size_t smem = size_t(2) * (size_t(8) << LB) + 1024;   // two fp64 tiles + alignment slack
+    // two fp64 tiles (+ the two-CTA inbox of 2^(LB-1) values) + alignment slack
+    const size_t smem = size_t(2) * (size_t(8) << LB) + (CL == 2 ? (size_t(8) << (LB - 1)) : 0) + 1024;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess)
         return uq::check_cuda("rht tma: set smem attribute");
     cudaLaunchConfig_t cfg = {};
@@ -957,7 +1025,7 @@ int rht_forward(const void *in, int in_dtype, int64_t rows, int64_t n0, int64_t 
     if (colscale && !pre) return fail(UQ_ERR_INVALID, "rht: colscale needs its prescale vector");
     a.signs = signs; a.colscale = colscale; a.pre = colscale ? pre : signs; a.out = out;
     a.ld_out = ld_out; a.ncols_out = n;
-    a.sqrt_n = sqrt(double(n)); a.n_d = double(n);
+    a.sqrt_n = sqrt(double(n)); a.n_d = double(n); a.inv_sqrt_n = 1.0 / a.sqrt_n;
     if (a.b > kMaxBits) return fail(UQ_ERR_UNSUPPORTED, "rht: n = %lld > 32768 not built", (long long)n);
     int64_t nparts = 0;
     if (in_dtype == UQ_F64 && out_dtype == UQ_F64) return launch_rht<double, double, MODE_FWD>(a, st, &nparts);
@@ -978,7 +1046,7 @@ int rht_inverse(const void *in, int in_dtype, int64_t rows, int64_t n, int64_t l
     if (colscale && !pre) return fail(UQ_ERR_INVALID, "irht: colscale needs its prescale vector");
     a.signs = signs; a.colscale = colscale; a.pre = pre; a.out = out;
     a.ld_out = ld_out; a.ncols_out = n0;
-    a.sqrt_n = sqrt(double(n)); a.n_d = double(n);
+    a.sqrt_n = sqrt(double(n)); a.n_d = double(n); a.inv_sqrt_n = 1.0 / a.sqrt_n;
     a.ref_w = ref_w; a.ref_dtype = ref_dtype; a.ld_w = ld_w; a.err_partial = err ? err_partial : nullptr;
     if (a.b > kMaxBits) return fail(UQ_ERR_UNSUPPORTED, "irht: n = %lld > 32768 not built", (long long)n);
     int rc;

@@ -421,37 +421,38 @@ __device__ __forceinline__ unsigned long long global_ns() {
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
     return t;
 }
-// Waits for the phase with the given parity.  Bounded: after ~2 s the thread
-// records a timeout in *err, stops waiting from then on (fail becomes true)
-// and carries on, so the kernel always runs to its end.
-__device__ __noinline__ void mbar_wait_slow(unsigned addr, unsigned parity, bool &fail, int *err,
-                                            unsigned long long limit_ns);
-__device__ __forceinline__ void mbar_wait(unsigned addr, unsigned parity, bool &fail, int *err,
-                                          unsigned long long limit_ns = 2000000000ull) {
-    unsigned ready;
-    asm volatile("{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-                 "selp.u32 %0, 1, 0, p;\n\t}" : "=r"(ready) : "r"(addr), "r"(parity) : "memory");
-    if (!ready) mbar_wait_slow(addr, parity, fail, err, limit_ns);
-}
-__device__ __noinline__ void mbar_wait_slow(unsigned addr, unsigned parity, bool &fail, int *err,
+// Waits for the phase with the given parity.  Bounded: after limit_ns the
+// wait records a timeout in *err and returns true, and later waits given
+// fail = true return at once, so the kernel always runs to its end.  The fast
+// path is one try_wait; the polling loop is out of line.
+__device__ __noinline__ bool mbar_wait_slow(unsigned addr, unsigned parity, bool fail, int *err,
                                             unsigned long long limit_ns) {
-    if (fail) return;
+    if (fail) return true;
     unsigned done = 0;
     unsigned long long t0 = 0;
     for (unsigned it = 0;; ++it) {
         asm volatile("{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
                      "selp.u32 %0, 1, 0, p;\n\t}" : "=r"(done) : "r"(addr), "r"(parity) : "memory");
-        if (done) return;
+        if (done) return false;
         if ((it & 63) == 0) {
             const unsigned long long now = global_ns();
             if (it == 0) t0 = now;
             else if (now - t0 > limit_ns) {
-                fail = true;
                 if (err) atomicExch(err, 1);
-                return;
+                return true;
             }
         }
     }
+}
+__device__ __forceinline__ bool mbar_ready(unsigned addr, unsigned parity) {
+    unsigned ready;
+    asm volatile("{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+                 "selp.u32 %0, 1, 0, p;\n\t}" : "=r"(ready) : "r"(addr), "r"(parity) : "memory");
+    return ready != 0;
+}
+__device__ __forceinline__ void mbar_wait(unsigned addr, unsigned parity, bool &fail, int *err,
+                                          unsigned long long limit_ns) {
+    if (!mbar_ready(addr, parity)) fail = mbar_wait_slow(addr, parity, fail, err, limit_ns);
 }
 __device__ __forceinline__ void fence_proxy_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -597,6 +598,14 @@ __device__ __forceinline__ void seq_sync(int slot) {
 __device__ int g_vit_timeout;
 __device__ unsigned long long g_wait_limit_ns = 2000000000ull;
 
+__device__ __noinline__ bool vit_wait_slow(unsigned addr, unsigned parity, bool fail) {
+    return mbar_wait_slow(addr, parity, fail, &g_vit_timeout, g_wait_limit_ns);
+}
+// The Viterbi exchange's bounded wait (limit g_wait_limit_ns, flag g_vit_timeout).
+__device__ __forceinline__ void vit_wait(unsigned addr, unsigned parity, bool &fail) {
+    if (!mbar_ready(addr, parity)) fail = vit_wait_slow(addr, parity, fail);
+}
+
 template <class C>
 __global__ void __cluster_dims__(C::CL, 1, 1) __launch_bounds__(kThreads, 1)
 viterbi_fwd_kernel(VitArgs a) {
@@ -662,7 +671,8 @@ viterbi_fwd_kernel(VitArgs a) {
 
     if (CL == 2) {
         if (tid < NSET * NBUF) {
-            // phase completes on: thread 0's arm (arrive + expect_tx), the last
+            // phase completes on: the arm (arrive + expect_tx; here for phase 0,
+            // later by the last warp of the step that read the buffer), the last
             // local warp's arrival (all local writes of the step done) and the
             // peer's bulk copy (OBYTES of transaction)
             mbar_init(full0 + unsigned(tid) * 8u, 2);
@@ -700,10 +710,9 @@ viterbi_fwd_kernel(VitArgs a) {
                 } else {
                     const int jr = (t - 1) & 1;
                     const unsigned mbr = full0 + unsigned(X * NBUF + jr) * 8u;
-                    mbar_wait(mbr, unsigned(((t - 1) >> 1) & 1), fail, &g_vit_timeout, g_wait_limit_ns);
+                    vit_wait(mbr, unsigned(((t - 1) >> 1) & 1), fail);
                     th.load_prev(smem0 + unsigned(X * NBUF + jr) * BUF, m);
                     word = th.template step<true>(x, m, wb, wsh);
-                    if (tid == 0) mbar_expect_tx(mbr, C::OBYTES);   // arm that buffer's next phase
                 }
                 if (wremote) fence_proxy_async_smem();   // outbox writes -> async proxy
                 // no CTA barrier: the last warp to finish the step ships the
@@ -717,6 +726,10 @@ viterbi_fwd_kernel(VitArgs a) {
                     asm volatile("atom.acq_rel.cta.shared::cta.add.u32 %0, [%1], 1;"
                                  : "=r"(old) : "r"(unsigned(__cvta_generic_to_shared(&done_cnt[X][jw]))) : "memory");
                     if ((old % (kThreads / 32)) == kThreads / 32 - 1) {
+                        // every warp has passed its wait on the buffer read in
+                        // this step: arm that buffer's next phase (before the
+                        // copy below, which the peer's next copy into it follows)
+                        if (t > 0) mbar_expect_tx(full0 + unsigned(X * NBUF + ((t - 1) & 1)) * 8u, C::OBYTES);
                         bulk_copy_to_peer(mapa_shared(smem0 + unsigned(X * NBUF + jw) * BUF + half_off, th.rank ^ 1u),
                                           obox0 + unsigned(X * NBUF + jw) * C::OBYTES, C::OBYTES,
                                           mapa_shared(full0 + unsigned(X * NBUF + jw) * 8u, th.rank ^ 1u));
@@ -738,8 +751,7 @@ viterbi_fwd_kernel(VitArgs a) {
         } else {
             const int jr = (a.T - 2) & 1;
             if (CL == 2)
-                mbar_wait(full0 + unsigned(X * NBUF + jr) * 8u, unsigned(((a.T - 2) >> 1) & 1), fail, &g_vit_timeout,
-                          g_wait_limit_ns);
+                vit_wait(full0 + unsigned(X * NBUF + jr) * 8u, unsigned(((a.T - 2) >> 1) & 1), fail);
             th.load_prev(smem0 + unsigned(X * NBUF + jr) * BUF, m);
             th.template final_argmin<true>(xv[X], m, bv, bi);
         }

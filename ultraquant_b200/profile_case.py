@@ -11,7 +11,8 @@ kernel once, which is the form to put under ``ncu -k <kernel> -c 1``.
 
 Kernels: viterbi (segments of 256, L / R), rht and irht (fp64), e8,
 normalize, fwht (fp32), recon and recon_bwd (the QAT decoder, fp32), q8enc and
-q8dec (Q8_0 blocks, fp32 side), rht28 (opt-in unpadded 28 x P transform, --n0).
+q8dec (Q8_0 blocks, fp32 side), rht28 (opt-in unpadded 28 x P transform, --n0),
+qe8 (finite-codebook E8, fp64, --bpw; all of its kernels).
 """
 from __future__ import annotations
 
@@ -26,7 +27,7 @@ from . import _lib
 # profiler scope name of each case's kernel
 SCOPE = {"viterbi": "viterbi_fwd", "rht": "rht", "irht": "rht", "e8": "e8_quant",
          "normalize": "normalize", "fwht": "fwht", "recon": "qat_recon", "recon_bwd": "qat_recon_bwd",
-         "q8enc": "q8_encode", "q8dec": "q8_decode", "rht28": "rht"}
+         "q8enc": "q8_encode", "q8dec": "q8_decode", "rht28": "rht", "qe8": "qe8_search"}
 
 
 def _peaks():
@@ -131,6 +132,18 @@ def build_case(args, lib, st):
         def run():
             _lib.check(lib.uq_rht28_rows(A.data_ptr(), 1, rows, n0, n0, None, d28.data_ptr(), out.data_ptr(), st), "rht28")
         return run, rows * n0 * 16, "bytes"
+    if k == "qe8":
+        from . import qlab as Q
+        A = torch.randn(rows, n, dtype=torch.float64, device=dev, generator=g) * 0.02
+        K = 1 << int(round(args.bpw * 8))
+        cb, cb32, scale, cut = Q._e8_codebook_dev(K, dev)
+        out = torch.empty_like(A)
+        ws = D.workspace(lib.uq_q_e8_workspace_bytes(A.numel(), 256), dev)
+
+        def run():
+            _lib.check(lib.uq_q_e8(A.data_ptr(), 1, A.numel(), 256, cb.data_ptr(), cb32.data_ptr(), cb.shape[0],
+                                   scale, cut, out.data_ptr(), ws.data_ptr(), ws.numel(), st), "qe8")
+        return run, A.numel() * 16, "bytes"
     if k in ("q8enc", "q8dec"):
         W = torch.randn(rows, n, device=dev, generator=g) * 0.02
         q = torch.empty((rows, n // 32 * 34), dtype=torch.uint8, device=dev)
@@ -153,6 +166,7 @@ def main(argv=None):
     ap.add_argument("--n0", type=int, default=0, help="unpadded width of rht / irht (default n)")
     ap.add_argument("--L", type=int, default=16)
     ap.add_argument("--R", type=int, default=2)
+    ap.add_argument("--bpw", type=float, default=2.0, help="rate of the qe8 case")
     ap.add_argument("--iters", type=int, default=10)
     args = ap.parse_args(argv)
     lib = _lib.load()
@@ -176,10 +190,27 @@ def main(argv=None):
     cnt = _lib.ctypes.c_int64(0)
     _lib.check(lib.uq_profile_read(SCOPE[args.kernel].encode(), _lib.ctypes.byref(tot), _lib.ctypes.byref(cnt)),
                "profile")
+    rec = {"kernel": args.kernel, "rows": args.rows, "n": args.n0 or args.n, "runs": args.iters,
+           "launches": cnt.value}
+    if args.kernel == "qe8":
+        # every kernel of the call, and the call as a whole (events on the stream)
+        for scope in ("e8_quant", "qe8_cb_norm", "qe8_classify", "qe8_search", "qe8_exact"):
+            t, c = _lib.ctypes.c_double(0.0), _lib.ctypes.c_int64(0)
+            _lib.check(lib.uq_profile_read(scope.encode(), _lib.ctypes.byref(t), _lib.ctypes.byref(c)), "profile")
+            rec[f"ms_{scope}"] = t.value / args.iters
+        lib.uq_profile_enable(0)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        flush.fill_(1)
+        e0.record()
+        run()
+        e1.record()
+        torch.cuda.synchronize()
+        rec["ms_call"] = e0.elapsed_time(e1)
+        rec["bpw"] = args.bpw
+        rec["weights_per_s"] = args.rows * args.n / (rec["ms_call"] * 1e-3)
     lib.uq_profile_enable(0)
     ms = tot.value / args.iters            # device time of the kernel per run (all its launches)
-    rec = {"kernel": args.kernel, "rows": args.rows, "n": args.n0 or args.n, "runs": args.iters,
-           "launches": cnt.value, "ms_per_run": ms}
+    rec["ms_per_run"] = ms
     if unit == "bytes":
         peak, kind = _peaks()
         gbs = units / (ms * 1e-3) / 1e9

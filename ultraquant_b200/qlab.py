@@ -18,7 +18,7 @@ from . import _lib
 from .q8 import deq_q8  # noqa: F401  (qlab.py:27-32, used by load_WH)
 
 __all__ = ["wnmse", "_next_pow2", "rht_rows", "irht_rows", "_d8_decode", "e8_decode",
-           "_entropy_bpw", "q_e8_fast", "_E8_SCALE", "deq_q8", "q_uniform"]
+           "_entropy_bpw", "q_e8_fast", "_E8_SCALE", "deq_q8", "q_uniform", "e8_codebook", "q_e8"]
 
 # qlab.py:158 -- calibrated E8 step per calib_key, reused across tensors
 _E8_SCALE: dict = {}
@@ -125,6 +125,82 @@ def q_uniform(A, bpw, bs=32):
         raise ValueError(f"cannot reshape array of size {a.numel()} into shape (-1,{bs})")
     _lib.check(lib.uq_q_uniform(a.data_ptr() if a.numel() else None, D.dtype_code(a), a.numel(), int(bs), lvl,
                                 out.data_ptr() if out.numel() else None, D.stream_handle(a.device)), "q_uniform")
+    return _ret(out, A)
+
+
+# qlab.py:110 -- codebooks per K (host fp64), and their device copies
+_E8_CACHE: dict = {}
+_E8_DEV: dict = {}
+
+
+def _e8_grid_norms():
+    """Lattice norms of the reference's point list (qlab.py:113-118): the
+    grid g in [-3, 3]^8 (first coordinate slowest) with an even coordinate
+    sum, then the same points plus 1/2.  |g|^2 and |g + 1/2|^2 = |g|^2 +
+    sum(g) + 2 are integers, so the fp64 values equal the reference's
+    (pts**2).sum(1) exactly.  Returns (grid ids of the even points, norms)."""
+    v = np.arange(-3, 4, dtype=np.int64)
+    sq, tot = v * v, v.copy()
+    for _ in range(7):
+        sq = np.add.outer(sq, v * v).ravel()
+        tot = np.add.outer(tot, v).ravel()
+    even = np.flatnonzero((tot & 1) == 0)
+    n_int = sq[even]
+    return even, np.concatenate([n_int, n_int + tot[even] + 2]).astype(np.float64)
+
+
+def _e8_build(K):
+    """(codebook, scale c, boundary norm) of qlab.py:111-124 for K points: the
+    K points of smallest norm (np.argsort over the same norm list, so the
+    members of the boundary shell are the reference's), each divided by
+    c = sqrt(mean |p|^2 / 8); every grid point of lattice norm below the
+    boundary norm is a codeword (+inf when K covers the grid)."""
+    if K not in _E8_CACHE:
+        even, norms = _e8_grid_norms()
+        order = np.argsort(norms)
+        ids = order[:K]
+        ne = even.size
+        gid = even[ids % ne]
+        digits = (gid[:, None] // (7 ** np.arange(7, -1, -1, dtype=np.int64))) % 7
+        pts = (digits - 3).astype(np.float64) + np.where(ids >= ne, 0.5, 0.0)[:, None]
+        scale = np.sqrt((pts ** 2).sum(1).mean() / 8)
+        cut = float(norms[order[K - 1]]) if K < norms.size else float("inf")
+        _E8_CACHE[K] = (pts / scale, float(scale), cut)
+    return _E8_CACHE[K]
+
+
+def e8_codebook(K):
+    """qlab.py:111-124 -- the (K, 8) fp64 codebook, bit for bit."""
+    return _e8_build(K)[0]
+
+
+def _e8_codebook_dev(K, dev):
+    """Device copies (fp64, fp32) of e8_codebook(K), its scale and boundary norm."""
+    key = (int(K), dev.index)
+    if key not in _E8_DEV:
+        cb, scale, cut = _e8_build(K)
+        t64 = torch.from_numpy(np.ascontiguousarray(cb)).to(dev)
+        _E8_DEV[key] = (t64, t64.to(torch.float32), scale, cut)
+    return _E8_DEV[key]
+
+
+def q_e8(A, bpw, group_scale=256):
+    """qlab.py:185-198 -- per-group scaled 8-vectors to the nearest codeword of
+    e8_codebook(2^round(8 bpw)) (fp64, A's shape).  Nearest as cKDTree's exact
+    Euclidean query; on an exact fp64 distance tie the lowest index."""
+    lib = _lib.load()
+    K = 1 << int(round(bpw * 8))
+    a = D.as_device(A)
+    if a.dtype not in (torch.float32, torch.float64):
+        a = a.to(torch.float64)
+    out = torch.empty(tuple(a.shape), dtype=torch.float64, device=a.device)
+    n = a.numel()
+    if n:
+        cb, cb32, scale, cut = _e8_codebook_dev(K, a.device)
+        ws = D.workspace(lib.uq_q_e8_workspace_bytes(n, int(group_scale)), a.device)
+        _lib.check(lib.uq_q_e8(a.data_ptr(), D.dtype_code(a), n, int(group_scale), cb.data_ptr(), cb32.data_ptr(),
+                               cb.shape[0], scale, cut, out.data_ptr(), ws.data_ptr(), ws.numel(),
+                               D.stream_handle(a.device)), "q_e8")
     return _ret(out, A)
 
 
