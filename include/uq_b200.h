@@ -143,6 +143,23 @@ int uq_e8_calibrate(const void *A, int a_dtype, int64_t size, int64_t group,
                     double target_bpw, double *step_host, void *workspace,
                     size_t workspace_bytes, void *stream);
 
+/* The pieces of uq_e8_calibrate, for a tensor whose row blocks live on
+ * several devices (the sample spans the whole tensor):
+ *  - uq_e8_sample_indices: qlab.py:173's RandomState(0).randint(0, nvec, ns)
+ *    (host memory, no device work);
+ *  - uq_e8_sample_gn: out[i] = the normalised 8-vector gn (qlab.py:167-168:
+ *    x / (sqrt(mean(g^2)) + 1e-12) of its group) of local vector vec_ids[i]
+ *    (device array) of A, a block of whole groups of the tensor;
+ *  - uq_e8_calibrate_sample: the 18-step bisection (qlab.py:174-180) on ns
+ *    such vectors in sample order; synchronises, step in *step_host. */
+int uq_e8_sample_indices(int64_t nvec, int64_t ns, int64_t *out_host);
+size_t uq_e8_sample_gn_workspace_bytes(int64_t size, int64_t group);
+int uq_e8_sample_gn(const void *A, int a_dtype, int64_t size, int64_t group, const int64_t *vec_ids,
+                    int64_t count, double *out, void *workspace, size_t workspace_bytes, void *stream);
+size_t uq_e8_calibrate_sample_workspace_bytes(int64_t ns);
+int uq_e8_calibrate_sample(const double *sub, int64_t ns, double target_bpw, double *step_host,
+                           void *workspace, size_t workspace_bytes, void *stream);
+
 /* ---------------------------------------------------------------------
  * Bitshift trellis (trellis.py:14-108, qat.py:11-59)
  * ------------------------------------------------------------------- */

@@ -30,7 +30,7 @@ __all__ = [
     "fwht_torch", "irht_torch", "recon_torch", "quant_trellis", "quant_step",
     "group_rms_f32", "viterbi_segments", "pack_states", "unpack_states", "enc_q8", "deq_q8",
     "hadamard28", "rht28_rows", "irht28_rows", "quant_step_b28", "q_uniform",
-    "e8_codebook", "nearest_exact", "q_e8",
+    "e8_codebook", "nearest_exact", "q_e8", "e8_bisect", "group_gn",
 ]
 
 
@@ -133,6 +133,26 @@ def entropy_bpw(idx_pts: np.ndarray) -> float:
 E8_SCALE: dict = {}
 
 
+def e8_bisect(sub, target_bpw):
+    """qlab.py:174-180 -- 18 halvings of [0.3, 10] on the entropy rate of the
+    decoded sample `sub` (normalised 8-vectors in sample order)."""
+    lo, hi = 0.3, 10.0
+    for _ in range(18):
+        mid = (lo + hi) / 2
+        if entropy_bpw(e8_decode(sub / mid)) > target_bpw:
+            lo = mid
+        else:
+            hi = mid
+    return (lo + hi) / 2
+
+
+def group_gn(A, group=256):
+    """qlab.py:164-168 -- the normalised 8-vectors gn of A (fp64)."""
+    flat = np.asarray(A).ravel().astype(np.float64)
+    g = np.concatenate([flat, np.zeros((-flat.size) % group)]).reshape(-1, group)
+    return (g / (np.sqrt((g ** 2).mean(1, keepdims=True)) + 1e-12)).reshape(-1, 8)
+
+
 def q_e8_fast(A, target_bpw=2.0, group=256, calib_key="g", fixed_step=None,
               cache=None):
     """qlab.py:159-183 -- per-group RMS normalisation, one global step, E8.
@@ -150,15 +170,7 @@ def q_e8_fast(A, target_bpw=2.0, group=256, calib_key="g", fixed_step=None,
         if calib_key not in cache:
             ns = min(600_000, gn.shape[0])
             pick = np.random.RandomState(0).randint(0, gn.shape[0], ns)
-            sub = gn[pick]
-            lo, hi = 0.3, 10.0
-            for _ in range(18):
-                mid = (lo + hi) / 2
-                if entropy_bpw(e8_decode(sub / mid)) > target_bpw:
-                    lo = mid
-                else:
-                    hi = mid
-            cache[calib_key] = (lo + hi) / 2
+            cache[calib_key] = e8_bisect(gn[pick], target_bpw)
         step = cache[calib_key]
     rec = (e8_decode(gn / step) * step).reshape(-1, group) * rms
     return rec.ravel()[:A.size].reshape(A.shape)

@@ -252,3 +252,24 @@ def test_q_uniform_golden(uq, g_quniform, tag):
     assert same_bits(uq.q_uniform(B, 3), O.q_uniform(B, 3))
     with pytest.raises(ValueError):
         uq.q_uniform(np.zeros((3, 10)), 2)
+
+
+def test_sharded_e8_calibration_device(uq):
+    """The calibration pieces of a row-sharded tensor (sample ids, device gn
+    of the local vectors, device bisection) give the single-call step, with
+    the tensor held as three uneven row blocks by one process."""
+    import torch
+    from ultraquant_b200 import shard as S
+    rng = np.random.RandomState(12)
+    W = rng.standard_t(4, size=(300, 1024)) * 0.02
+    uq._E8_SCALE.pop("shard", None)
+    whole = uq.q_e8_fast(W, target_bpw=2.5, calib_key="shard")
+    step_whole = uq._E8_SCALE.pop("shard")
+    cache = {}
+    O.q_e8_fast(W, 2.5, calib_key="o", cache=cache)
+    assert step_whole == cache["o"]
+    spec = S.TensorSpec("w", 300, 1024)
+    cuts = [0, 7, 160, 300]
+    blocks = [(cuts[i], torch.from_numpy(W[cuts[i]:cuts[i + 1]]).cuda()) for i in range(3)]
+    assert S.calibrate_e8(blocks, spec, 2.5) == step_whole
+    assert whole.shape == W.shape

@@ -131,3 +131,46 @@ def test_gloo_rank_failure_is_reported(tmp_path):
     assert procs[1].exitcode == 3
     err = (tmp_path / "err0.txt").read_text() if (tmp_path / "err0.txt").exists() else ""
     assert err, "rank 0 should have seen a collective failure"
+
+
+# ---- calibrated E8 step of a row-sharded tensor (qlab.py:171-180) -------------
+CAL_SPEC = S.TensorSpec("cal", 48, 512)
+
+
+def _cal_blocks(rank, world):
+    rng = np.random.RandomState(9)
+    W = rng.standard_t(4, size=(CAL_SPEC.rows, CAL_SPEC.cols)) * 0.02
+    cut = [0, 16, 40, 48]
+    mine = [(0, 3)] if world == 1 else ([(0, 1)] if rank == 0 else [(1, 2), (2, 3)])
+    return W, [(cut[a], torch.from_numpy(W[cut[a]:cut[b]])) for a, b in mine]
+
+
+def _oracle_gn(A, ids):
+    return torch.from_numpy(O.group_gn(A.numpy())[ids.numpy()])
+
+
+def _cal_worker(rank, world, port, out_dir):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    import datetime
+    import torch.distributed as dist
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=30))
+    try:
+        _, blocks = _cal_blocks(rank, world)
+        step = S.calibrate_e8(blocks, CAL_SPEC, 1.0, sample_gn=_oracle_gn,
+                              bisect=lambda sub: O.e8_bisect(sub.numpy(), 1.0))
+        torch.save(step, os.path.join(out_dir, f"step{rank}.pt"))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_gloo_sharded_e8_calibration_matches_single_process(tmp_path):
+    """Two ranks holding uneven row blocks (rank 1 two of them) draw the same
+    sample, gather the normalised vectors and get the single-process step."""
+    W, _ = _cal_blocks(0, 1)
+    cache = {}
+    O.q_e8_fast(W, 1.0, calib_key="k", cache=cache)
+    assert 0.31 < cache["k"] < 9.9            # an interior step, not a bracket end
+    mp.start_processes(_cal_worker, args=(2, _free_port(), str(tmp_path)), nprocs=2, join=True,
+                       start_method="spawn")
+    for r in range(2):
+        assert torch.load(tmp_path / f"step{r}.pt") == cache["k"]

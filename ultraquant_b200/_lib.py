@@ -43,6 +43,11 @@ SIGNATURES = {
     "uq_e8_entropy_bpw": (_i32, [_p, _i64, _p, _p, _sz, _p]),
     "uq_e8_calibrate_workspace_bytes": (_sz, [_i64, _i64]),
     "uq_e8_calibrate": (_i32, [_p, _i32, _i64, _i64, _f64, _p, _p, _sz, _p]),
+    "uq_e8_sample_indices": (_i32, [_i64, _i64, _p]),
+    "uq_e8_sample_gn_workspace_bytes": (_sz, [_i64, _i64]),
+    "uq_e8_sample_gn": (_i32, [_p, _i32, _i64, _i64, _p, _i64, _p, _p, _sz, _p]),
+    "uq_e8_calibrate_sample_workspace_bytes": (_sz, [_i64]),
+    "uq_e8_calibrate_sample": (_i32, [_p, _i64, _f64, _p, _p, _sz, _p]),
     "uq_trellis_codebook": (_i32, [_i32, _p, _p]),
     "uq_trellis_normalize": (_i32, [_p, _i32, _i64, _i64, _i64, _p, _p, _p]),
     "uq_trellis_normalize_rows": (_i32, [_p, _i32, _i64, _i64, _i64, _i64, _p, _p, _p]),

@@ -568,30 +568,6 @@ __global__ void e8_scaled_keys_kernel(const double *sub, int64_t ns, double step
     }
 }
 
-struct CalWs {
-    double *rms, *sub, *pts, *bpw;
-    int64_t *pick;
-    void *ent;
-    size_t ent_bytes;
-};
-
-size_t calib_ws_bytes(int64_t size, int64_t group, CalWs *w, void *base) {
-    const int64_t padded = (size + group - 1) / group * group;
-    const int64_t ngroups = padded / group, nvec = padded / 8;
-    const int64_t ns = nvec < 600000 ? nvec : 600000;
-    uq::Carver c(base, ~size_t(0));
-    CalWs t;
-    t.rms = c.take<double>(ngroups);
-    t.pick = c.take<int64_t>(ns);
-    t.sub = c.take<double>(ns * 8);
-    t.pts = c.take<double>(ns * 8);
-    t.bpw = c.take<double>(1);
-    t.ent_bytes = entropy_ws_bytes(ns, nullptr, nullptr);
-    t.ent = c.take<char>(t.ent_bytes);
-    if (w) *w = t;
-    return c.off;
-}
-
 }  // namespace
 
 namespace uq {
@@ -660,9 +636,94 @@ int uq_e8_entropy_bpw(const double *pts, int64_t nvec, double *bpw, void *worksp
     return entropy_run(PtsSrc{pts}, nvec, bpw, workspace, workspace_bytes, UQ_STREAM(stream));
 }
 
+
+int uq_e8_sample_indices(int64_t nvec, int64_t ns, int64_t *out_host) {
+    if (nvec < 1 || ns < 0 || (ns > 0 && !out_host))
+        return uq::fail(UQ_ERR_INVALID, "uq_e8_sample_indices: bad arguments (nvec=%lld ns=%lld)", (long long)nvec,
+                        (long long)ns);
+    uq::MT19937 g;
+    g.seed(0);
+    g.randint(0, nvec, ns, out_host);
+    return UQ_OK;
+}
+
+size_t uq_e8_sample_gn_workspace_bytes(int64_t size, int64_t group) {
+    if (size < 0 || group < 8) return 0;
+    return uq::align_up(size_t((size + group - 1) / group) * 8, 256);
+}
+
+int uq_e8_sample_gn(const void *A, int a_dtype, int64_t size, int64_t group, const int64_t *vec_ids, int64_t count,
+                    double *out, void *workspace, size_t workspace_bytes, void *stream) {
+    int rc = e8_check(size, group, "uq_e8_sample_gn");
+    if (rc) return rc;
+    if (count < 0 || !uq::dtype_size(a_dtype)) return uq::fail(UQ_ERR_INVALID, "uq_e8_sample_gn: bad arguments");
+    if (count == 0 || size == 0) return UQ_OK;
+    if (!A || !vec_ids || !out || !workspace) return uq::fail(UQ_ERR_INVALID, "uq_e8_sample_gn: null pointer");
+    if (workspace_bytes < uq_e8_sample_gn_workspace_bytes(size, group))
+        return uq::fail(UQ_ERR_WORKSPACE, "uq_e8_sample_gn: workspace %zu too small", workspace_bytes);
+    const cudaStream_t st = UQ_STREAM(stream);
+    double *rms = static_cast<double *>(workspace);
+    if ((rc = uq::e8_quant(A, a_dtype, size, group, 1.0, nullptr, nullptr, rms, st))) return rc;
+    const int grid = std::max(1, std::min<int>(int((count * 8 + 255) / 256), uq::num_sms() * 16));
+    uq::count_launch();
+    if (a_dtype == UQ_F64)
+        gather_gn_kernel<double><<<grid, 256, 0, st>>>(static_cast<const double *>(A), size, int(group), rms, vec_ids, count, out);
+    else
+        gather_gn_kernel<float><<<grid, 256, 0, st>>>(static_cast<const float *>(A), size, int(group), rms, vec_ids, count, out);
+    return uq::check_cuda("gather_gn_kernel launch");
+}
+
+size_t uq_e8_calibrate_sample_workspace_bytes(int64_t ns) {
+    if (ns < 1) return 0;
+    uq::Carver c(nullptr, ~size_t(0));
+    c.take<double>(size_t(ns) * 8);
+    c.take<double>(1);
+    c.take<char>(entropy_ws_bytes(ns, nullptr, nullptr));
+    return c.off;
+}
+
+int uq_e8_calibrate_sample(const double *sub, int64_t ns, double target_bpw, double *step_host, void *workspace,
+                           size_t workspace_bytes, void *stream) {
+    if (ns < 1 || !sub || !step_host || !workspace)
+        return uq::fail(UQ_ERR_INVALID, "uq_e8_calibrate_sample: bad arguments");
+    if (workspace_bytes < uq_e8_calibrate_sample_workspace_bytes(ns))
+        return uq::fail(UQ_ERR_WORKSPACE, "uq_e8_calibrate_sample: workspace %zu too small", workspace_bytes);
+    uq::Carver c(workspace, workspace_bytes);
+    double *pts = c.take<double>(size_t(ns) * 8);
+    double *bpw_d = c.take<double>(1);
+    const size_t ent_bytes = entropy_ws_bytes(ns, nullptr, nullptr);
+    void *ent = c.take<char>(ent_bytes);
+    const cudaStream_t st = UQ_STREAM(stream);
+    int rc;
+    // qlab.py:174-180: 18 halvings of [0.3, 10] on the entropy of the decoded sample
+    double lo = 0.3, hi = 10.0;
+    for (int it = 0; it < 18; ++it) {
+        const double mid = (lo + hi) / 2;
+        const int g2 = std::max(1, std::min<int>(int((ns + 127) / 128), uq::num_sms() * 16));
+        { uq::ProfScope _p("e8_scaled_keys", st); e8_scaled_keys_kernel<<<g2, 128, 0, st>>>(sub, ns, mid, pts); }
+        if ((rc = uq::check_cuda("e8_scaled_keys_kernel launch"))) return rc;
+        if ((rc = entropy_run(PtsSrc{pts}, ns, bpw_d, ent, ent_bytes, st))) return rc;
+        double bpw = 0.0;
+        if (cudaMemcpyAsync(&bpw, bpw_d, sizeof(double), cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+            cudaStreamSynchronize(st) != cudaSuccess)
+            return uq::check_cuda("calibrate: read entropy");
+        if (bpw < 0) return uq::fail(UQ_ERR_UNSUPPORTED, "calibrate: lattice index outside [-127, 127] at step %g", mid);
+        if (bpw > target_bpw) lo = mid; else hi = mid;
+    }
+    *step_host = (lo + hi) / 2;
+    return UQ_OK;
+}
+
 size_t uq_e8_calibrate_workspace_bytes(int64_t size, int64_t group) {
     if (size < 0 || group < 8) return 0;
-    return calib_ws_bytes(size, group, nullptr, nullptr);
+    const int64_t padded = (size + group - 1) / group * group;
+    const int64_t nvec = padded / 8, ns = nvec < 600000 ? nvec : 600000;
+    uq::Carver c(nullptr, ~size_t(0));
+    c.take<char>(uq_e8_sample_gn_workspace_bytes(size, group));
+    c.take<int64_t>(size_t(ns));
+    c.take<double>(size_t(ns) * 8);
+    c.take<char>(uq_e8_calibrate_sample_workspace_bytes(ns));
+    return c.off;
 }
 
 int uq_e8_calibrate(const void *A, int a_dtype, int64_t size, int64_t group, double target_bpw,
@@ -671,46 +732,28 @@ int uq_e8_calibrate(const void *A, int a_dtype, int64_t size, int64_t group, dou
     if (rc) return rc;
     if (size < 1 || !A || !step_host || !workspace || !uq::dtype_size(a_dtype))
         return uq::fail(UQ_ERR_INVALID, "uq_e8_calibrate: bad arguments");
-    cudaStream_t st = UQ_STREAM(stream);
-    CalWs w;
-    const size_t need = calib_ws_bytes(size, group, &w, workspace);
-    if (workspace_bytes < need) return uq::fail(UQ_ERR_WORKSPACE, "uq_e8_calibrate: workspace %zu < %zu", workspace_bytes, need);
+    if (workspace_bytes < uq_e8_calibrate_workspace_bytes(size, group))
+        return uq::fail(UQ_ERR_WORKSPACE, "uq_e8_calibrate: workspace %zu < %zu", workspace_bytes,
+                        uq_e8_calibrate_workspace_bytes(size, group));
+    const cudaStream_t st = UQ_STREAM(stream);
     const int64_t padded = (size + group - 1) / group * group;
     const int64_t nvec = padded / 8;
     const int64_t ns = nvec < 600000 ? nvec : 600000;
-    // group RMS of the whole tensor
-    rc = uq::e8_quant(A, a_dtype, size, group, 1.0, nullptr, nullptr, w.rms, st);
-    if (rc) return rc;
-    // RandomState(0).randint(0, nvec, ns)
-    std::vector<int64_t> pick(static_cast<size_t>(ns), 0);
-    uq::MT19937 g;
-    g.seed(0);
-    g.randint(0, nvec, ns, pick.data());
-    if (cudaMemcpyAsync(w.pick, pick.data(), size_t(ns) * sizeof(int64_t), cudaMemcpyHostToDevice, st) != cudaSuccess)
+    uq::Carver c(workspace, workspace_bytes);
+    const size_t gn_ws = uq_e8_sample_gn_workspace_bytes(size, group);
+    void *gws = c.take<char>(gn_ws);
+    int64_t *pick = c.take<int64_t>(size_t(ns));
+    double *sub = c.take<double>(size_t(ns) * 8);
+    const size_t cal_ws = uq_e8_calibrate_sample_workspace_bytes(ns);
+    void *cws = c.take<char>(cal_ws);
+    // RandomState(0).randint(0, nvec, ns) over the whole (padded) tensor
+    std::vector<int64_t> h(static_cast<size_t>(ns), 0);
+    if ((rc = uq_e8_sample_indices(nvec, ns, h.data()))) return rc;
+    if (cudaMemcpyAsync(pick, h.data(), size_t(ns) * sizeof(int64_t), cudaMemcpyHostToDevice, st) != cudaSuccess ||
+        cudaStreamSynchronize(st) != cudaSuccess)
         return uq::check_cuda("calibrate: copy subsample indices");
-    const int grid = std::max(1, std::min<int>(int((ns * 8 + 255) / 256), uq::num_sms() * 16));
-    uq::count_launch();
-    if (a_dtype == UQ_F64)
-        gather_gn_kernel<double><<<grid, 256, 0, st>>>(static_cast<const double *>(A), size, int(group), w.rms, w.pick, ns, w.sub);
-    else
-        gather_gn_kernel<float><<<grid, 256, 0, st>>>(static_cast<const float *>(A), size, int(group), w.rms, w.pick, ns, w.sub);
-    if ((rc = uq::check_cuda("gather_gn_kernel launch"))) return rc;
-    double lo = 0.3, hi = 10.0;
-    for (int it = 0; it < 18; ++it) {
-        const double mid = (lo + hi) / 2;
-        const int g2 = std::max(1, std::min<int>(int((ns + 127) / 128), uq::num_sms() * 16));
-        { uq::ProfScope _p("e8_scaled_keys", st); e8_scaled_keys_kernel<<<g2, 128, 0, st>>>(w.sub, ns, mid, w.pts); }
-        if ((rc = uq::check_cuda("e8_scaled_keys_kernel launch"))) return rc;
-        if ((rc = entropy_run(PtsSrc{w.pts}, ns, w.bpw, w.ent, w.ent_bytes, st))) return rc;
-        double bpw = 0.0;
-        if (cudaMemcpyAsync(&bpw, w.bpw, sizeof(double), cudaMemcpyDeviceToHost, st) != cudaSuccess ||
-            cudaStreamSynchronize(st) != cudaSuccess)
-            return uq::check_cuda("calibrate: read entropy");
-        if (bpw < 0) return uq::fail(UQ_ERR_UNSUPPORTED, "calibrate: lattice index outside [-127, 127] at step %g", mid);
-        if (bpw > target_bpw) lo = mid; else hi = mid;
-    }
-    *step_host = (lo + hi) / 2;
-    return UQ_OK;
+    if ((rc = uq_e8_sample_gn(A, a_dtype, size, group, pick, ns, sub, gws, gn_ws, stream))) return rc;
+    return uq_e8_calibrate_sample(sub, ns, target_bpw, step_host, cws, cal_ws, stream);
 }
 
 int uq_q_uniform(const void *A, int dtype, int64_t size, int64_t bs, int64_t lvl, void *out, void *stream) {

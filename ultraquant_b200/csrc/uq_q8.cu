@@ -82,9 +82,10 @@ __global__ void __launch_bounds__(256) q8_encode_kernel(const T *W, int64_t nblo
                         const float xv = x[2 * h + e];
                         const float t = __fmul_rn(xv, rc);
                         float f = rintf(t);
-                        if (!(__fsub_rn(0.5f, fabsf(__fsub_rn(t, f))) > 0x1p-15f) || !(fabsf(t) <= 128.f))
-                            f = rintf(__fdiv_rn(xv, sc));
-                        qq[e] = int(fminf(fmaxf(f, -127.f), 127.f));
+                        // (NaN / inf t, from a huge reciprocal, also fail the test)
+                        if (!(__fsub_rn(0.5f, fabsf(__fsub_rn(t, f))) > 0x1p-15f)) f = rintf(__fdiv_rn(xv, sc));
+                        // |x / sc| <= 127 (1 + 2^-23): f is already within [-127, 127]
+                        qq[e] = __float2int_rn(f);
                     }
                     qb[h] = static_cast<unsigned short>((qq[0] & 0xff) | ((qq[1] & 0xff) << 8));
                 }
@@ -146,8 +147,14 @@ __global__ void __launch_bounds__(256) q8_decode_kernel(const uint8_t *q8, int64
     }
 }
 
-int grid_for(int64_t work, int per_block) {
-    return int(std::max<int64_t>(1, std::min<int64_t>((work + per_block - 1) / per_block, int64_t(uq::num_sms()) * 8)));
+// One wave of resident CTAs (persistent grid-stride over spans): a second,
+// partial wave would leave SMs idle at the end.
+template <typename K>
+int grid_for(K kern, int64_t work, int per_block) {
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, 256, 0) != cudaSuccess || per_sm < 1) per_sm = 1;
+    return int(std::max<int64_t>(1, std::min<int64_t>((work + per_block - 1) / per_block,
+                                                      int64_t(uq::num_sms()) * per_sm)));
 }
 
 bool al16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
@@ -163,15 +170,16 @@ int uq_q8_encode(const void *W, int w_dtype, int64_t rows, int64_t cols, int64_t
     if (rows == 0 || cols == 0) return UQ_OK;
     if (!W || !out) return uq::fail(UQ_ERR_INVALID, "uq_q8_encode: null pointer");
     const int64_t nb = cols / kBlk, nblocks = rows * nb;
-    const int grid = grid_for(nblocks, kSpan);
     const cudaStream_t st = UQ_STREAM(stream);
     const bool vec_out = al16(out);
     {
         uq::ProfScope _p("q8_encode", st);
         if (w_dtype == UQ_F32) {
             const bool vec_in = al16(W) && ldw % 4 == 0;
+            const int grid = grid_for(q8_encode_kernel<float>, nblocks, kSpan);
             q8_encode_kernel<float><<<grid, 256, 0, st>>>(static_cast<const float *>(W), nblocks, nb, ldw, vec_in, out, vec_out);
         } else {
+            const int grid = grid_for(q8_encode_kernel<double>, nblocks, kSpan);
             q8_encode_kernel<double><<<grid, 256, 0, st>>>(static_cast<const double *>(W), nblocks, nb, ldw, false, out, vec_out);
         }
     }
@@ -185,7 +193,7 @@ int uq_q8_decode(const uint8_t *q8, int64_t rows, int64_t cols, float *out, int6
     if (rows == 0 || cols == 0) return UQ_OK;
     if (!q8 || !out) return uq::fail(UQ_ERR_INVALID, "uq_q8_decode: null pointer");
     const int64_t nb = cols / kBlk, nblocks = rows * nb;
-    const int grid = grid_for(nblocks, kSpan);
+    const int grid = grid_for(q8_decode_kernel, nblocks, kSpan);
     const bool vec_out = al16(out) && ld_out % 4 == 0;
     { uq::ProfScope _p("q8_decode", UQ_STREAM(stream)); q8_decode_kernel<<<grid, 256, 0, UQ_STREAM(stream)>>>(q8, nblocks, nb, al16(q8), out, ld_out, vec_out); }
     return uq::check_cuda("q8_decode_kernel launch");

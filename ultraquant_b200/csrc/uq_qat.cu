@@ -141,14 +141,19 @@ __device__ __forceinline__ T bwd_pre(const FwhtArgs &, T v, int e, const T *cs, 
     return s_pow2 ? Ar<T>::mul(v, s_inv) : Ar<T>::div(v, s);
 }
 
-// ~768 resident threads per SM (85 registers) for the 128- and 256-thread tiles
-template <typename T, int DIR, int SRC, int DST, int MAXT>
-__global__ void __launch_bounds__(MAXT, MAXT <= 128 ? 6 : (MAXT <= 256 ? 3 : 1))
+// ~768 resident threads per SM (80 registers) for the 128- and 256-thread fp32
+// tiles, ~384 (168 registers: 32 fp64 values) for fp64.
+// BC > 0: the row width 2^BC (>= 4096, one row per tile) is a compile-time
+// constant, so every pass, index and branch below folds; BC = 0 reads it from
+// the arguments (narrow rows, several per tile).
+template <typename T, int DIR, int SRC, int DST, int MAXT, int BC>
+__global__ void __launch_bounds__(MAXT, sizeof(T) == 8 ? (MAXT <= 128 ? 3 : (MAXT <= 256 ? 2 : 1))
+                                                       : (MAXT <= 128 ? 6 : (MAXT <= 256 ? 3 : 1)))
 fwht_kernel(FwhtArgs a) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     T *tile = reinterpret_cast<T *>(smem_raw);
     using A = Ar<T>;
-    const int b = a.b;
+    const int b = BC ? BC : a.b;
     const int NB = b > 12 ? b : 12;
     const int TILE = 1 << NB;
     const int nthr = 1 << (NB - VB);
@@ -188,34 +193,38 @@ fwht_kernel(FwhtArgs a) {
         //      thread's loads issued before its shared-memory stores ----------
         if (vec_in) {
             if (SRC == SRC_RECON) {
-                int stv[V];
+                // in two halves: states (16-byte loads), then all codeword
+                // gathers and group scales of the half in flight before use
 #pragma unroll
-                for (int i = 0; i < V / 4; ++i) {
-                    const int E = (tid + i * nthr) * 4;
-                    const int64_t f = (t << NB) + E;   // rows of a tile are consecutive in the flat index
-                    int4 q = make_int4(0, 0, 0, 0);
-                    if (f < a.ntot) q = __ldg(reinterpret_cast<const int4 *>(static_cast<const int *>(a.states) + f));
-                    stv[4 * i] = q.x; stv[4 * i + 1] = q.y; stv[4 * i + 2] = q.z; stv[4 * i + 3] = q.w;
-                }
+                for (int h = 0; h < 2; ++h) {
+                    constexpr int HV = V / 2;
+                    int stv[HV];
 #pragma unroll
-                for (int i = 0; i < V / 4; ++i) {
-                    const int E = (tid + i * nthr) * 4;
-                    const int64_t f = (t << NB) + E;
-                    const bool in = f < a.ntot;
-                    const float scv = in ? __ldg(a.sc + group_of(a, f)) : 0.f;   // group % 4 == 0
+                    for (int i = 0; i < HV / 4; ++i) {
+                        const int E = (tid + (h * HV / 4 + i) * nthr) * 4;
+                        const int64_t f = (t << NB) + E;   // rows of a tile are consecutive in the flat index
+                        int4 q = make_int4(0, 0, 0, 0);
+                        if (f < a.ntot) q = __ldg(reinterpret_cast<const int4 *>(static_cast<const int *>(a.states) + f));
+                        stv[4 * i] = q.x; stv[4 * i + 1] = q.y; stv[4 * i + 2] = q.z; stv[4 * i + 3] = q.w;
+                    }
+                    float cv[HV];
+                    bool bad = false;
 #pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        const int st = stv[4 * i + j];
-                        T v = T(0);
-                        if (in) {
-                            if (st < 0 || st >= a.ncw) {
-                                atomicExch(&g_qat_bad_state, 1);
-                                v = T(__int_as_float(0x7fc00000));
-                            } else {
-                                v = T(__fmul_rn(cwp[st], scv));
-                            }
-                        }
-                        tile[swz5(E + j)] = v;
+                    for (int j = 0; j < HV; ++j) {
+                        const bool ok = stv[j] >= 0 && stv[j] < a.ncw;
+                        bad |= !ok;   // padding past ntot reads state 0, which is valid
+                        cv[j] = a.cw_smem ? cwp[ok ? stv[j] : 0] : __ldg(cwp + (ok ? stv[j] : 0));
+                        if (!ok) cv[j] = __int_as_float(0x7fc00000);
+                    }
+                    if (bad) atomicExch(&g_qat_bad_state, 1);
+#pragma unroll
+                    for (int i = 0; i < HV / 4; ++i) {
+                        const int E = (tid + (h * HV / 4 + i) * nthr) * 4;
+                        const int64_t f = (t << NB) + E;
+                        const bool in = f < a.ntot;
+                        const float scv = in ? __ldg(a.sc + group_of(a, f)) : 0.f;   // group % 4 == 0
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) tile[swz5(E + j)] = in ? T(__fmul_rn(cv[4 * i + j], scv)) : T(0);
                     }
                 }
             } else {
@@ -269,8 +278,11 @@ fwht_kernel(FwhtArgs a) {
         T x[V];
         if (DIR == DIR_FWD) {
             int done = 0;
-            for (int p = 0;; p += VB) {
-                if (p > NB - VB) p = NB - VB;
+            const int npass = (NB + VB - 1) / VB;
+#pragma unroll
+            for (int ip = 0; ip < 3; ++ip) {
+                if (ip >= npass) break;
+                const int p = ip * VB < NB - VB ? ip * VB : NB - VB;
                 const int base = (tid & ((1 << p) - 1)) | ((tid >> p) << (p + VB));
 #pragma unroll
                 for (int j = 0; j < V; ++j) x[j] = tile[swz5(base + (j << p))];
@@ -298,7 +310,9 @@ fwht_kernel(FwhtArgs a) {
             }
         } else {
             int low = b;   // stages of bits >= low are done
-            for (int p = b - VB > 0 ? b - VB : 0;; p = p - VB > 0 ? p - VB : 0) {
+            int p = b - VB > 0 ? b - VB : 0;
+#pragma unroll
+            for (int ip = 0; ip < 4; ++ip) {
                 const int base = (tid & ((1 << p) - 1)) | ((tid >> p) << (p + VB));
 #pragma unroll
                 for (int j = 0; j < V; ++j) x[j] = tile[swz5(base + (j << p))];
@@ -308,44 +322,51 @@ fwht_kernel(FwhtArgs a) {
 #pragma unroll
                 for (int j = 0; j < V; ++j) tile[swz5(base + (j << p))] = x[j];
                 __syncthreads();
+                p = p - VB > 0 ? p - VB : 0;
             }
             // registers now hold the 32 consecutive elements (tid << 5) + j
             if (DST == DST_GRADS) {
                 const int E0 = tid << VB;
                 const int64_t f0 = (t << NB) + E0;   // the 32 elements are consecutive in the flat index
-                int stv[V];
-                if (vec_st) {
-#pragma unroll
-                    for (int i = 0; i < V / 4; ++i) {
-                        int4 q = make_int4(0, 0, 0, 0);
-                        if (f0 + 4 * i < a.ntot)
-                            q = __ldg(reinterpret_cast<const int4 *>(static_cast<const int *>(a.states) + f0 + 4 * i));
-                        stv[4 * i] = q.x; stv[4 * i + 1] = q.y; stv[4 * i + 2] = q.z; stv[4 * i + 3] = q.w;
-                    }
-                }
                 double acc = 0.0;
                 int64_t g_cur = -1;
 #pragma unroll
-                for (int j = 0; j < V; ++j) {
-                    const int64_t f = f0 + j;
-                    if (f >= a.ntot) continue;
-                    int64_t st;
+                for (int h = 0; h < 2; ++h) {
+                    constexpr int HV = V / 2;
+                    int stv[HV];
                     if (vec_st) {
-                        st = stv[j];
-                        if (st < 0 || st >= a.ncw) { atomicExch(&g_qat_bad_state, 1); st = -1; }
-                    } else {
-                        st = load_state(a, f);
+#pragma unroll
+                        for (int i = 0; i < HV / 4; ++i) {
+                            const int64_t f = f0 + h * HV + 4 * i;
+                            int4 q = make_int4(0, 0, 0, 0);
+                            if (f < a.ntot)
+                                q = __ldg(reinterpret_cast<const int4 *>(static_cast<const int *>(a.states) + f));
+                            stv[4 * i] = q.x; stv[4 * i + 1] = q.y; stv[4 * i + 2] = q.z; stv[4 * i + 3] = q.w;
+                        }
                     }
-                    const int64_t g = group_of(a, f);
-                    if (st < 0) continue;
-                    const float gx = float(x[j]);
-                    atomicAdd(gcwp + st, double(__fmul_rn(gx, __ldg(a.sc + g))));
-                    if (g != g_cur) {
-                        if (g_cur >= 0) atomicAdd(a.gsc + g_cur, acc);
-                        g_cur = g;
-                        acc = 0.0;
+#pragma unroll
+                    for (int jj = 0; jj < HV; ++jj) {
+                        const int j = h * HV + jj;
+                        const int64_t f = f0 + j;
+                        if (f >= a.ntot) continue;
+                        int64_t st;
+                        if (vec_st) {
+                            st = stv[jj];
+                            if (st < 0 || st >= a.ncw) { atomicExch(&g_qat_bad_state, 1); st = -1; }
+                        } else {
+                            st = load_state(a, f);
+                        }
+                        const int64_t g = group_of(a, f);
+                        if (st < 0) continue;
+                        const float gx = float(x[j]);
+                        atomicAdd(gcwp + st, double(__fmul_rn(gx, __ldg(a.sc + g))));
+                        if (g != g_cur) {
+                            if (g_cur >= 0) atomicAdd(a.gsc + g_cur, acc);
+                            g_cur = g;
+                            acc = 0.0;
+                        }
+                        acc += double(__fmul_rn(gx, cwp[st]));
                     }
-                    acc += double(__fmul_rn(gx, cwp[st]));
                 }
                 if (g_cur >= 0) atomicAdd(a.gsc + g_cur, acc);
             } else {
@@ -399,9 +420,12 @@ int launch_fwht(const FwhtArgs &a, cudaStream_t st, const char *what) {
         (codes && a.cw_smem ? ((size_t(a.ncw) * 4 + 15) & ~size_t(15)) + (DST == DST_GRADS ? size_t(a.ncw) * 8 : 0) : 0);
     // fp64 tiles stop at n = 16384 (512 threads)
     constexpr int TOP = sizeof(T) == 8 ? 512 : 1024;
-    auto kern = nthr <= 128 ? fwht_kernel<T, DIR, SRC, DST, 128>
-              : nthr <= 256 ? fwht_kernel<T, DIR, SRC, DST, 256>
-              : nthr <= 512 ? fwht_kernel<T, DIR, SRC, DST, 512> : fwht_kernel<T, DIR, SRC, DST, TOP>;
+    // one-row tiles of 4096 .. 32768 get the width as a compile-time constant
+    auto kern = a.b == 12 ? fwht_kernel<T, DIR, SRC, DST, 128, 12>
+              : a.b == 13 ? fwht_kernel<T, DIR, SRC, DST, 256, 13>
+              : a.b == 14 ? fwht_kernel<T, DIR, SRC, DST, 512, 14>
+              : a.b == 15 ? fwht_kernel<T, DIR, SRC, DST, TOP, (sizeof(T) == 8 ? 0 : 15)>
+              : fwht_kernel<T, DIR, SRC, DST, 128, 0>;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess)
         return uq::check_cuda("fwht: set smem attribute");
     int per_sm = 0;

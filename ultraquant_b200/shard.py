@@ -10,7 +10,10 @@ only exchanges are
 * an all-gather of the per-tensor error statistics {sum (A-Ah)^2, sum A^2}
   (weighted NMSE per tensor, whichever ranks held its row blocks), and
 * optionally, assembling a tensor's outputs (What, states, scales) on one
-  rank with NCCL gathers.
+  rank with NCCL gathers, and
+* for the calibrated E8 step (qlab.py:171-180), whose 600k-vector sample
+  spans the whole tensor: a gather of the sampled normalised vectors to one
+  rank, which bisects, and a broadcast of the step.
 
 The plan is deterministic (every rank computes it locally) and balances the
 ranks by padded weights x trellis cost per weight.
@@ -21,7 +24,8 @@ from dataclasses import dataclass, field
 
 import torch
 
-__all__ = ["TensorSpec", "Shard", "plan", "llama_shapes", "run_shards", "gather_errors", "assemble_rows"]
+__all__ = ["TensorSpec", "Shard", "plan", "llama_shapes", "run_shards", "gather_errors", "assemble_rows",
+           "calibrate_e8"]
 
 
 @dataclass(frozen=True)
@@ -195,3 +199,103 @@ def plan_blocks_for(spec, results, group=None) -> dict:
         for r0, r1, owner in lst:
             out[r0] = (r1, owner)
     return out
+
+
+def _device_sample_gn(A: torch.Tensor, vec_ids: torch.Tensor, group: int) -> torch.Tensor:
+    from . import _device as D, _lib
+    lib = _lib.load()
+    out = torch.empty((vec_ids.numel(), 8), dtype=torch.float64, device=A.device)
+    if vec_ids.numel():
+        ids = vec_ids.to(A.device, torch.int64).contiguous()
+        ws = D.workspace(lib.uq_e8_sample_gn_workspace_bytes(A.numel(), group), A.device)
+        _lib.check(lib.uq_e8_sample_gn(A.data_ptr(), D.dtype_code(A), A.numel(), group, ids.data_ptr(), ids.numel(),
+                                       out.data_ptr(), ws.data_ptr(), ws.numel(), D.stream_handle(A.device)),
+                   "e8 sample gn")
+    return out
+
+
+def _device_bisect(sub: torch.Tensor, target_bpw: float) -> float:
+    import ctypes
+    from . import _device as D, _lib
+    lib = _lib.load()
+    sub = sub.to(D.device(), torch.float64).contiguous()
+    ws = D.workspace(lib.uq_e8_calibrate_sample_workspace_bytes(sub.shape[0]), sub.device)
+    step = ctypes.c_double()
+    _lib.check(lib.uq_e8_calibrate_sample(sub.data_ptr(), sub.shape[0], float(target_bpw), ctypes.addressof(step),
+                                          ws.data_ptr(), ws.numel(), D.stream_handle(sub.device)), "e8 calibration")
+    return float(step.value)
+
+
+def _sample_indices(nvec: int, ns: int):
+    import ctypes
+    import numpy as np
+    from . import _lib
+    out = np.empty(ns, dtype=np.int64)
+    _lib.check(_lib.load().uq_e8_sample_indices(nvec, ns, out.ctypes.data_as(ctypes.c_void_p)), "e8 sample indices")
+    return out
+
+
+def calibrate_e8(blocks, spec: TensorSpec, target_bpw: float = 2.0, group: int = 256, root: int = 0,
+                 sample_gn=None, bisect=None, pg=None) -> float:
+    """The calibrated step of q_e8_fast (qlab.py:171-180) for a tensor split by
+    row blocks across ranks, equal to the single-process step: every rank draws
+    the same sample of vector ids over the whole tensor (RandomState(0).randint
+    (0, nvec, ns), ns = min(600000, nvec)), computes the normalised vectors of
+    the ids it holds, `root` places them in sample order and bisects, and the
+    step is broadcast.  blocks: [(row0, A_block)] of this rank (rows x
+    spec.cols, whole groups: spec.cols % group == 0).  sample_gn(A_block, ids)
+    -> (k, 8) fp64 and bisect(sub) -> step default to the device kernels."""
+    import numpy as np
+    import torch.distributed as dist
+    if spec.cols % group or group % 8:
+        raise ValueError(f"calibrate_e8: row blocks must hold whole groups (cols={spec.cols}, group={group})")
+    sample_gn = sample_gn or (lambda A, ids: _device_sample_gn(A, ids, group))
+    bisect = bisect or (lambda sub: _device_bisect(sub, target_bpw))
+    nvec = spec.rows * spec.cols // 8
+    ns = min(600_000, nvec)
+    pick = _sample_indices(nvec, ns)
+    vpr = spec.cols // 8                         # vectors per row
+    pos_l, gn_l = [], []
+    for row0, A in blocks:
+        v0, v1 = row0 * vpr, (row0 + A.shape[0]) * vpr
+        pos = np.flatnonzero((pick >= v0) & (pick < v1))
+        if pos.size:
+            gn_l.append(sample_gn(A, torch.from_numpy(pick[pos] - v0)).to(torch.float64).cpu())
+            pos_l.append(torch.from_numpy(pos))
+    pos = torch.cat(pos_l) if pos_l else torch.zeros(0, dtype=torch.int64)
+    gn = torch.cat(gn_l) if gn_l else torch.zeros((0, 8), dtype=torch.float64)
+    if not (dist.is_available() and dist.is_initialized()):
+        sub = torch.empty((ns, 8), dtype=torch.float64)
+        sub[pos] = gn
+        return float(bisect(sub))
+    rank, world = dist.get_rank(pg), dist.get_world_size(pg)
+    dev = (torch.device("cuda", torch.cuda.current_device())
+           if dist.get_backend(pg) == "nccl" else torch.device("cpu"))
+    n = torch.tensor([pos.numel()], dtype=torch.int64, device=dev)
+    sizes = [torch.zeros_like(n) for _ in range(world)]
+    dist.all_gather(sizes, n, group=pg)
+    mx = max(int(x) for x in sizes)
+    rec = torch.full((max(mx, 1), 9), -1.0, dtype=torch.float64)
+    rec[: pos.numel(), 0] = pos.to(torch.float64)  # ids < 2^53: exact
+    rec[: pos.numel(), 1:] = gn
+    rec = rec.to(dev)
+    allr = [torch.empty_like(rec) for _ in range(world)]
+    dist.all_gather(allr, rec, group=pg)
+    # the root always broadcasts (NaN when the blocks did not cover the
+    # sample exactly once), so every rank leaves the collective together
+    step = torch.full((1,), float("nan"), dtype=torch.float64, device=dev)
+    got = -1
+    if rank == root:
+        rows = torch.cat([r.cpu() for r in allr])
+        rows = rows[rows[:, 0] >= 0]
+        got = rows.shape[0]
+        ids = rows[:, 0].to(torch.int64)
+        if got == ns and torch.unique(ids).numel() == ns:
+            sub = torch.empty((ns, 8), dtype=torch.float64)
+            sub[ids] = rows[:, 1:]
+            step[0] = bisect(sub)
+    dist.broadcast(step, src=root, group=pg)
+    if step.isnan().item():
+        raise RuntimeError(f"calibrate_e8: the ranks' row blocks do not cover the tensor once "
+                           f"({got if rank == root else '?'} of {ns} sampled vectors)")
+    return float(step.item())
