@@ -66,12 +66,23 @@ __global__ void __launch_bounds__(256) q8_encode_kernel(const T *W, int64_t nblo
             float m = fmaxf(fmaxf(fabsf(x[0]), fabsf(x[1])), fmaxf(fabsf(x[2]), fabsf(x[3])));
 #pragma unroll
             for (int o = 4; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-            float sc = __fdiv_rn(m, 127.0f);
+            // sc = RN(m / 127): Markstein's correction (P. Markstein, IBM J. Res.
+            // Dev. 34(1), 1990) of q0 = RN(m y), y = RN(1/127): the remainder
+            // m - q0 127 is exact as an FMA and RN(q0 + r y) is the correctly
+            // rounded quotient while nothing leaves the normal range; other m
+            // take the IEEE division
+            constexpr float y127 = 1.0f / 127.0f;
+            const float q0 = __fmul_rn(m, y127);
+            float sc = __fmaf_rn(__fmaf_rn(-q0, 127.0f, m), y127, q0);
+            if (!(m >= 0x1p-100f && m <= 0x1p100f)) sc = __fdiv_rn(m, 127.0f);
             if (sc == 0.0f) sc = 1e-9f;
-            // rint(x / sc) from t = x * RN(1/sc): |t - RN(x/sc)| < |x/sc| 2^-23 + 2^-24 |x/sc|
-            // < 2^-15 for |x/sc| <= 128, so rint(t) is the answer unless t lies
-            // within 2^-15 of a rounding boundary (then: the IEEE division)
-            const float rc = __fdiv_rn(1.0f, sc);
+            // rint(x / sc) from t = x * rc, rc the hardware reciprocal (rcp.approx,
+            // within 1 ulp of 1/sc): |t - x/sc| <= |x/sc| (2^-23 + 2^-24) (1 + 2^-23)
+            // < 2^-15 for |x/sc| <= 127 (1 + 2^-23), so rint(t) is the answer
+            // unless t lies within 2^-15 of a rounding boundary (then: the IEEE
+            // division).  A subnormal sc flushes to an infinite rc: no t passes.
+            float rc;
+            asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(rc) : "f"(sc));
             if (ok) {
                 unsigned short qb[2];
 #pragma unroll
@@ -87,7 +98,7 @@ __global__ void __launch_bounds__(256) q8_encode_kernel(const T *W, int64_t nblo
                         // |x / sc| <= 127 (1 + 2^-23): f is already within [-127, 127]
                         qq[e] = __float2int_rn(f);
                     }
-                    qb[h] = static_cast<unsigned short>((qq[0] & 0xff) | ((qq[1] & 0xff) << 8));
+                    qb[h] = static_cast<unsigned short>(__byte_perm(qq[0], qq[1], 0x0040));
                 }
                 // block j starts on an even byte: 16-bit stores
                 unsigned short *bq = reinterpret_cast<unsigned short *>(stage + j * kBlkBytes + 2 + 4 * sub);

@@ -496,18 +496,21 @@ rht_tma_kernel(const __grid_constant__ CUtensorMap tin, const __grid_constant__ 
     constexpr int CH_OUT = 4096 / (128 / int(sizeof(TOut)));
     const int lin0 = int(col0 / (128 / int(sizeof(TIn))));
     const int lout0 = int(col0 / (128 / int(sizeof(TOut))));
-    // Two-CTA rows (n = 2^(LB+1)): CTA r finishes the pairs (i, i + 2^LB) for
-    // i in [r 2^(LB-1), (r+1) 2^(LB-1)), so its outputs are two column ranges of
-    // 2^(LB-1): the sums (register j < 8) and the differences (j >= 8).
-    // Otherwise register j holds column col0 + tid + (j << (LB - 4)).
+    // Rows over 2 or 4 CTAs (PUSH): the cross-CTA stages are finished by
+    // halves (below), so register j ends up holding column
+    // blk(j) 2^LB + a 2^(LB-1) + tid + ((j & 7) << (LB - 4)), a = rank & 1,
+    // blk(j) = (rank >> 1) + (j < 8 ? 0 : CL / 2): two column ranges of
+    // 2^(LB-1) per CTA.  Otherwise register j holds col0 + tid + (j << (LB-4)).
+    constexpr bool PUSH = CL == 2 || CL == 4;
     auto out_col = [&](int j) -> int64_t {
-        if (CL == 2)
-            return int64_t(j < 8 ? 0 : (1 << LB)) + (int64_t(rank) << (LB - 1)) + tid + ((j & 7) << (LB - 4));
+        if (PUSH)
+            return (int64_t((rank >> 1) + (j < 8 ? 0 : CL / 2)) << LB) + (int64_t(rank & 1u) << (LB - 1)) + tid +
+                   ((j & 7) << (LB - 4));
         return col0 + tid + (j << (LB - 4));
     };
     // index of register j's output in the store buffer (whole boxes of 4096)
     auto out_idx = [&](int j) -> int {
-        if (CL == 2) return (j < 8 ? 0 : (1 << (LB - 1))) + tid + ((j & 7) << (LB - 4));
+        if (PUSH) return (j < 8 ? 0 : (1 << (LB - 1))) + tid + ((j & 7) << (LB - 4));
         return tid + (j << (LB - 4));
     };
 
@@ -544,10 +547,11 @@ rht_tma_kernel(const __grid_constant__ CUtensorMap tin, const __grid_constant__ 
 #pragma unroll
     for (int i = 0; i < LCL; ++i)
         asm("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(peer_base[i]) : "r"(sbase), "r"(rank ^ (1u << i)));
-    // two-CTA rows: the partner's values arrive in an inbox after the two tiles
+    // PUSH rows: a partner's values arrive in an inbox after the two tiles
+    // (inbox i for the stage with rank ^ 2^i)
+    constexpr unsigned INBOX = 8u << (LB - 1);
     const unsigned inbox = sbase + 2u * unsigned(BUFB);
-    const unsigned peer_inbox = peer_base[0] + 2u * unsigned(BUFB);
-    if (CL == 2) cluster_arrive_rel();   // opens the first "inbox read" phase
+    if (PUSH) cluster_arrive_rel();   // opens the first "inbox read" phase
 
     int k = 0;
     for (int64_t r = first; r < a.rows; r += nclusters, ++k) {
@@ -608,24 +612,33 @@ rht_tma_kernel(const __grid_constant__ CUtensorMap tin, const __grid_constant__ 
         // registers: elements tid + (j << (LB - 4)) of this CTA's part
         // ---- stages of index bits LB .. B-1 across the cluster: bit LB + i pairs
         //      CTA rank with rank ^ 2^i (lower: own + peer, upper: peer - own) --
-        if (CL == 2) {
-            // push the partner's half of the pairs into its inbox (remote
-            // stores do not stall), one barrier, then finish the own half
-            cluster_wait_acq();   // the partner has read its inbox (previous row)
+        if (PUSH) {
+            // Stage of bit LB + i with CTA rank ^ 2^i: of the 2^LB pairs at
+            // local index jj (registers jj, 8 + jj: the lower and upper of
+            // this CTA's two ranges), the lower CTA (bit i of rank clear)
+            // finishes those of registers < 8 and the upper those >= 8; each
+            // pushes the other half into the partner's inbox (remote stores
+            // do not stall) and one cluster barrier makes them visible.
+            cluster_wait_acq();   // every inbox of the previous row has been read
 #pragma unroll
-            for (int jj = 0; jj < 8; ++jj)
-                st_peer_f64(peer_inbox + 8u * unsigned(tid + (jj << (LB - 4))), rank == 0 ? x[8 + jj] : x[jj]);
-            cluster_arrive_rel();
-            cluster_wait_acq();   // the partner's values are in this inbox
+            for (int i = 0; i < LCL; ++i) {
+                const bool up = (rank >> i) & 1u;
 #pragma unroll
-            for (int jj = 0; jj < 8; ++jj) {
-                const double v = lds64d(inbox + 8u * unsigned(tid + (jj << (LB - 4))));
-                const double own = rank == 0 ? x[jj] : x[8 + jj];
-                const double lo = rank == 0 ? own : v, hi = rank == 0 ? v : own;
-                x[jj] = d_add(lo, hi);
-                x[8 + jj] = d_sub(lo, hi);
+                for (int jj = 0; jj < 8; ++jj)
+                    st_peer_f64(peer_base[i] + 2u * unsigned(BUFB) + unsigned(i) * INBOX +
+                                    8u * unsigned(tid + (jj << (LB - 4))), up ? x[jj] : x[8 + jj]);
+                cluster_arrive_rel();
+                cluster_wait_acq();   // the partner's values are in inbox i
+#pragma unroll
+                for (int jj = 0; jj < 8; ++jj) {
+                    const double v = lds64d(inbox + unsigned(i) * INBOX + 8u * unsigned(tid + (jj << (LB - 4))));
+                    const double own = up ? x[8 + jj] : x[jj];
+                    const double lo = up ? v : own, hi = up ? own : v;
+                    x[jj] = d_add(lo, hi);
+                    x[8 + jj] = d_sub(lo, hi);
+                }
             }
-            cluster_arrive_rel();   // inbox read
+            cluster_arrive_rel();   // inboxes read
         } else {
 #pragma unroll
             for (int i = 0; i < LCL; ++i) {
@@ -684,8 +697,7 @@ rht_tma_kernel(const __grid_constant__ CUtensorMap tin, const __grid_constant__ 
 #pragma unroll
             for (int bx = 0; bx < NBOX; ++bx) {
                 // box bx holds columns out_col of its first register range
-                const int c0 = CL == 2 ? int((bx == 0 ? 0 : (1 << LB)) + (int(rank) << (LB - 1))) / (128 / int(sizeof(TOut)))
-                                       : lout0 + bx * CH_OUT;
+                const int c0 = PUSH ? int(out_col(bx * 8) - tid) / (128 / int(sizeof(TOut))) : lout0 + bx * CH_OUT;
                 store3d(&tout, 0, c0, int(r), buf + unsigned(bx * OUTB));
             }
             bulk_commit();
@@ -698,7 +710,7 @@ rht_tma_kernel(const __grid_constant__ CUtensorMap tin, const __grid_constant__ 
         }
     }
     if (tid == 0) bulk_wait0();
-    if (CL == 2) cluster_wait_acq();  // closes the last "inbox read" phase
+    if (PUSH) cluster_wait_acq();   // closes the last "inbox read" phase
     else if (CL > 1) cluster_sync_all();   // no CTA leaves while a partner may read its tile
 }
 
@@ -904,8 +916,9 @@ template <typename TIn, typename TOut, int MODE, int LB, int CL, bool COLS>
 int launch_tma_v(const CUtensorMap &mi, const CUtensorMap &mo, const RhtArgs &a, cudaStream_t st, int64_t *nparts) {
     auto kern = rht_tma_kernel<TIn, TOut, MODE, LB, CL, COLS>;
     const int nt = 1 << (LB - 4);
-    // two fp64 tiles (+ the two-CTA inbox of 2^(LB-1) values) + alignment slack
-    const size_t smem = size_t(2) * (size_t(8) << LB) + (CL == 2 ? (size_t(8) << (LB - 1)) : 0) + 1024;
+    // two fp64 tiles (+ one inbox of 2^(LB-1) values per cross-CTA stage) + alignment slack
+    const size_t smem = size_t(2) * (size_t(8) << LB) + ((CL == 2 || CL == 4) ? size_t(CL / 2) * (size_t(8) << (LB - 1)) : 0) +
+                        1024;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess)
         return uq::check_cuda("rht tma: set smem attribute");
     cudaLaunchConfig_t cfg = {};
