@@ -173,3 +173,30 @@ def test_qat_loop_runs_through_dropin(Q, g_qat):
         ls.backward()
         opt.step()
     assert loss().item() < l0
+
+
+@pytest.mark.parametrize("nrow,n,L,in0", [(64, 4096, 12, 4096), (24, 8192, 12, 7000), (8, 16384, 10, 14336),
+                                          (16, 8192, 16, 8192)])
+def test_recon_widths_vs_oracle(Q, nrow, n, L, in0):
+    """The row-layout decoder at 4096 / 8192 / 16384 columns, codebooks in
+    shared memory (L <= 12) and in global memory (L = 16), cropped widths:
+    forward bit-exact against the oracle, gradients against the fp64
+    restatement."""
+    import torch
+    from test_oracle_golden import recon_exact_grads
+    rng = np.random.RandomState(nrow + n + L)
+    states = rng.randint(0, 1 << L, size=(nrow * n // 256, 256)).astype(np.int32)
+    scg = (np.abs(rng.normal(size=(nrow * n // 256, 1))) + 0.1).astype(np.float32)
+    sH = np.sqrt(np.maximum(np.exp(rng.normal(size=(1, in0))), 1e-3)).astype(np.float32)
+    meta = dict(nrow=nrow, ncol=n, Ntot=nrow * n, seg=256, scale_group=256, pad=0, Nseg=states.shape[0])
+    cwn = O.codebook(L)
+    cw = torch.tensor(cwn, device="cuda", requires_grad=True)
+    sc = torch.tensor(scg, device="cuda", requires_grad=True)
+    Wh = Q.recon_torch(states, cw, sc, meta, torch.tensor(sH, device="cuda"), in0)
+    ref = O.recon_torch(states, torch.tensor(cwn), torch.tensor(scg), meta, torch.tensor(sH), in0)
+    assert same_bits(Wh.detach().cpu().numpy(), ref.numpy())
+    U = rng.normal(size=(nrow, in0)).astype(np.float32)
+    (Wh * torch.from_numpy(U).cuda()).sum().backward()
+    gcw, gsc = recon_exact_grads(states, cwn, scg, U, meta, sH, in0)
+    assert grad_close(cw.grad.cpu().numpy(), gcw, gcw)
+    assert grad_close(sc.grad.cpu().numpy().reshape(-1), gsc, gsc)

@@ -141,6 +141,54 @@ __device__ __forceinline__ T bwd_pre(const FwhtArgs &, T v, int e, const T *cs, 
     return s_pow2 ? Ar<T>::mul(v, s_inv) : Ar<T>::div(v, s);
 }
 
+// Backward into the codes for the 32 consecutive flat elements f0 + j held in
+// x[j]: scatter-add x * sc into the codeword gradients (fp64) and per-group
+// sums of x * cw[state] into the scale gradients.
+template <typename T>
+__device__ __forceinline__ void scatter_grads(const FwhtArgs &a, const T (&x)[V], int64_t f0, bool vec_st,
+                                              const float *cwp, double *gcwp) {
+    double acc = 0.0;
+    int64_t g_cur = -1;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        constexpr int HV = V / 2;
+        int stv[HV];
+        if (vec_st) {
+#pragma unroll
+            for (int i = 0; i < HV / 4; ++i) {
+                const int64_t f = f0 + h * HV + 4 * i;
+                int4 q = make_int4(0, 0, 0, 0);
+                if (f < a.ntot) q = __ldg(reinterpret_cast<const int4 *>(static_cast<const int *>(a.states) + f));
+                stv[4 * i] = q.x; stv[4 * i + 1] = q.y; stv[4 * i + 2] = q.z; stv[4 * i + 3] = q.w;
+            }
+        }
+#pragma unroll
+        for (int jj = 0; jj < HV; ++jj) {
+            const int j = h * HV + jj;
+            const int64_t f = f0 + j;
+            if (f >= a.ntot) continue;
+            int64_t st;
+            if (vec_st) {
+                st = stv[jj];
+                if (st < 0 || st >= a.ncw) { atomicExch(&g_qat_bad_state, 1); st = -1; }
+            } else {
+                st = load_state(a, f);
+            }
+            const int64_t g = group_of(a, f);
+            if (st < 0) continue;
+            const float gx = float(x[j]);
+            atomicAdd(gcwp + st, double(__fmul_rn(gx, __ldg(a.sc + g))));
+            if (g != g_cur) {
+                if (g_cur >= 0) atomicAdd(a.gsc + g_cur, acc);
+                g_cur = g;
+                acc = 0.0;
+            }
+            acc += double(__fmul_rn(gx, cwp[st]));
+        }
+    }
+    if (g_cur >= 0) atomicAdd(a.gsc + g_cur, acc);
+}
+
 // ~768 resident threads per SM (80 registers) for the 128- and 256-thread fp32
 // tiles, ~384 (168 registers: 32 fp64 values) for fp64.
 // BC > 0: the row width 2^BC (>= 4096, one row per tile) is a compile-time
@@ -326,49 +374,7 @@ fwht_kernel(FwhtArgs a) {
             }
             // registers now hold the 32 consecutive elements (tid << 5) + j
             if (DST == DST_GRADS) {
-                const int E0 = tid << VB;
-                const int64_t f0 = (t << NB) + E0;   // the 32 elements are consecutive in the flat index
-                double acc = 0.0;
-                int64_t g_cur = -1;
-#pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    constexpr int HV = V / 2;
-                    int stv[HV];
-                    if (vec_st) {
-#pragma unroll
-                        for (int i = 0; i < HV / 4; ++i) {
-                            const int64_t f = f0 + h * HV + 4 * i;
-                            int4 q = make_int4(0, 0, 0, 0);
-                            if (f < a.ntot)
-                                q = __ldg(reinterpret_cast<const int4 *>(static_cast<const int *>(a.states) + f));
-                            stv[4 * i] = q.x; stv[4 * i + 1] = q.y; stv[4 * i + 2] = q.z; stv[4 * i + 3] = q.w;
-                        }
-                    }
-#pragma unroll
-                    for (int jj = 0; jj < HV; ++jj) {
-                        const int j = h * HV + jj;
-                        const int64_t f = f0 + j;
-                        if (f >= a.ntot) continue;
-                        int64_t st;
-                        if (vec_st) {
-                            st = stv[jj];
-                            if (st < 0 || st >= a.ncw) { atomicExch(&g_qat_bad_state, 1); st = -1; }
-                        } else {
-                            st = load_state(a, f);
-                        }
-                        const int64_t g = group_of(a, f);
-                        if (st < 0) continue;
-                        const float gx = float(x[j]);
-                        atomicAdd(gcwp + st, double(__fmul_rn(gx, __ldg(a.sc + g))));
-                        if (g != g_cur) {
-                            if (g_cur >= 0) atomicAdd(a.gsc + g_cur, acc);
-                            g_cur = g;
-                            acc = 0.0;
-                        }
-                        acc += double(__fmul_rn(gx, cwp[st]));
-                    }
-                }
-                if (g_cur >= 0) atomicAdd(a.gsc + g_cur, acc);
+                scatter_grads<T>(a, x, (t << NB) + (tid << VB), vec_st, cwp, gcwp);
             } else {
                 const int base = tid << VB;
 #pragma unroll
@@ -406,13 +412,163 @@ fwht_kernel(FwhtArgs a) {
     }
 }
 
+
+// fp32 rows of n = 2^NB (NB = 12..14), one row per CTA iteration, as
+// R = 2^(NB-5) tile rows of 32 columns in shared memory with a row stride of
+// 36 floats; R threads hold 32 values each:
+//   pass A  thread t: tile row t, elements 32 t + j         (index bits 0..4)
+//   pass B  thread t: column t & 31 of rows 32 (t >> 5) + k  (bits 5..9)
+//   pass C  thread t: elements t + (k << (NB - 5))           (bits NB-5 .. NB-1)
+// Every shared address is a per-thread base plus a compile-time offset, and
+// every access is conflict-free: pass A moves 16-byte row chunks (144-byte
+// stride: 8 lanes cover the 32 banks), passes B and C put a warp on 32
+// consecutive columns of one row.  Pass A is filled straight from global
+// memory (or from the codes) and the output leaves from pass C with coalesced
+// stores.  Forward only (fwht, irht and recon values); the backward's
+// gradient scatter measured faster in fwht_kernel.
+constexpr int kRowStride = 36;
+
+template <int DIR, int SRC, int DST, int NB>
+__global__ void __launch_bounds__(1 << (NB - 5), NB == 12 ? 6 : (NB == 13 ? 3 : 1))
+qat_rows_kernel(FwhtArgs a) {
+    static_assert(DIR == DIR_FWD && DST == DST_DENSE, "forward values only");
+    using T = float;
+    using A = Ar<float>;
+    constexpr int R = 1 << (NB - 5), P = NB - 5;
+    constexpr int64_t n = int64_t(1) << NB;
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    float *tq = reinterpret_cast<float *>(smem_raw);
+    const int tid = threadIdx.x;
+    const float s = float(a.s);
+    constexpr bool s_pow2 = (NB & 1) == 0;
+    const float s_inv = float(ldexp(1.0, -(NB >> 1)));
+    const float *signs = static_cast<const float *>(a.signs);
+    const float *cs = static_cast<const float *>(a.colscale);
+    // codebooks of up to 4096 entries (L <= 12) are staged after the tile
+    float *cw_s = reinterpret_cast<float *>(smem_raw + size_t(R) * kRowStride * 4);
+    if (SRC == SRC_RECON && a.cw_smem) {
+        for (int i = tid; i < a.ncw; i += R) cw_s[i] = __ldg(a.cw + i);
+        __syncthreads();
+    }
+    const float *cwp = a.cw_smem ? cw_s : a.cw;
+    const bool vec_st = !a.states64 && (reinterpret_cast<uintptr_t>(a.states) & 15) == 0;
+    const bool vec_x = (reinterpret_cast<uintptr_t>(a.x) & 15) == 0 && (a.ld_x % 4) == 0;
+    float *rowA = tq + tid * kRowStride;                                       // pass A
+    float *colB = tq + (32 * (tid >> 5)) * kRowStride + (tid & 31);            // pass B, + k * 36
+    float *colC = tq + (tid >> 5) * kRowStride + (tid & 31);                   // pass C, + (k << (P-5)) * 36
+
+    for (int64_t row = blockIdx.x; row < a.rows; row += gridDim.x) {
+        float x[V];
+        {
+            const int e0 = 32 * tid;
+            if (SRC == SRC_RECON) {
+                const int64_t f0 = row * n + e0;
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    int stv[16];
+                    if (vec_st) {
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) {
+                            const int4 q = __ldg(reinterpret_cast<const int4 *>(static_cast<const int *>(a.states) + f0 + 16 * h) + i);
+                            stv[4 * i] = q.x; stv[4 * i + 1] = q.y; stv[4 * i + 2] = q.z; stv[4 * i + 3] = q.w;
+                        }
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) stv[j] = int(load_state(a, f0 + 16 * h + j));
+                    }
+                    bool bad = false;
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        const bool ok = stv[j] >= 0 && stv[j] < a.ncw;
+                        bad |= !ok;
+                        const float c = a.cw_smem ? cwp[ok ? stv[j] : 0] : __ldg(cwp + (ok ? stv[j] : 0));
+                        x[16 * h + j] = ok ? c : __int_as_float(0x7fc00000);
+                    }
+                    if (bad) atomicExch(&g_qat_bad_state, 1);
+                    // one scale when the 16 values share a group (groups of >= 16, aligned)
+                    const int64_t g0 = group_of(a, f0 + 16 * h), g1 = group_of(a, f0 + 16 * h + 15);
+                    if (g0 == g1) {
+                        const float sc = __ldg(a.sc + g0);
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) x[16 * h + j] = __fmul_rn(x[16 * h + j], sc);
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 16; ++j)
+                            x[16 * h + j] = __fmul_rn(x[16 * h + j], __ldg(a.sc + group_of(a, f0 + 16 * h + j)));
+                    }
+                }
+            } else {
+                const float *src = static_cast<const float *>(a.x) + row * a.ld_x + e0;
+                if (vec_x && e0 + 32 <= a.ncols_x) {
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        const float4 q = __ldg(reinterpret_cast<const float4 *>(src) + i);
+                        x[4 * i] = q.x; x[4 * i + 1] = q.y; x[4 * i + 2] = q.z; x[4 * i + 3] = q.w;
+                    }
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) x[j] = e0 + j < a.ncols_x ? __ldg(src + j) : 0.f;
+                }
+            }
+            stages32<T, DIR_FWD>(x, 0, 0, 5);
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+                *reinterpret_cast<float4 *>(rowA + 4 * i) = make_float4(x[4 * i], x[4 * i + 1], x[4 * i + 2], x[4 * i + 3]);
+            __syncthreads();
+#pragma unroll
+            for (int k = 0; k < 32; ++k) x[k] = colB[k * kRowStride];
+            stages32<T, DIR_FWD>(x, 5, 5, 10);
+#pragma unroll
+            for (int k = 0; k < 32; ++k) colB[k * kRowStride] = x[k];
+            __syncthreads();
+#pragma unroll
+            for (int k = 0; k < 32; ++k) x[k] = colC[(k << (P - 5)) * kRowStride];
+            stages32<T, DIR_FWD>(x, P, 10, NB);
+            float *dst = static_cast<float *>(a.out) + row * a.ld_out;
+#pragma unroll
+            for (int k = 0; k < 32; ++k) {
+                const int e = tid + (k << P);
+                if (e >= a.ncols_out) continue;
+                float y = s_pow2 ? A::mul(x[k], s_inv) : A::div(x[k], s);
+                if (signs) y = A::mul(y, __ldg(signs + e));
+                if (cs) y = A::div(y, __ldg(cs + e));
+                dst[e] = y;
+            }
+        }
+        __syncthreads();   // the tile is rewritten for the next row
+    }
+}
+
 __global__ void grads_to_f32_kernel(const double *g64, int64_t count, float *out) {
     for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < count; i += int64_t(gridDim.x) * blockDim.x)
         out[i] = __double2float_rn(g64[i]);
 }
 
+template <int DIR, int SRC, int DST, int NB>
+int launch_rows(const FwhtArgs &a, cudaStream_t st, const char *what) {
+    const bool codes = SRC == SRC_RECON || DST == DST_GRADS;
+    const size_t smem = (size_t(kRowStride) * 4 << (NB - 5)) +
+        (codes && a.cw_smem ? ((size_t(a.ncw) * 4 + 15) & ~size_t(15)) + (DST == DST_GRADS ? size_t(a.ncw) * 8 : 0) : 0);
+    auto kern = qat_rows_kernel<DIR, SRC, DST, NB>;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess)
+        return uq::check_cuda("qat rows: set smem attribute");
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, 1 << (NB - 5), smem) != cudaSuccess || per_sm < 1)
+        return uq::check_cuda("qat rows: occupancy query");
+    const int64_t grid = std::min<int64_t>(a.rows, int64_t(uq::num_sms()) * per_sm);
+    if (grid > 0) { uq::ProfScope _p(what, st); kern<<<unsigned(grid), 1 << (NB - 5), smem, st>>>(a); }
+    return uq::check_cuda("qat_rows_kernel launch");
+}
+
 template <typename T, int DIR, int SRC, int DST>
 int launch_fwht(const FwhtArgs &a, cudaStream_t st, const char *what) {
+    // forward fp32 rows of 4096..16384: the row-layout kernel (measured faster;
+    // the backward's gradient scatter is faster in the tile kernel)
+    if constexpr (sizeof(T) == 4 && DIR == DIR_FWD) {
+        if (a.b == 12) return launch_rows<DIR, SRC, DST, 12>(a, st, what);
+        if (a.b == 13) return launch_rows<DIR, SRC, DST, 13>(a, st, what);
+        if (a.b == 14) return launch_rows<DIR, SRC, DST, 14>(a, st, what);
+    }
     const int NB = a.b > 12 ? a.b : 12;
     const int nthr = 1 << (NB - VB);
     const bool codes = SRC == SRC_RECON || DST == DST_GRADS;
