@@ -10,7 +10,7 @@
 // operation, so the bytes and values are the reference's.  Both kernels move
 // spans of 256 blocks (8704 bytes, a multiple of 16) through shared memory so
 // that the byte-granular block format meets global memory as 16-byte
-// vectors; the block maximum is a shuffle reduction over the 8 threads of a
+// vectors; the block maximum is a shuffle reduction over the 4 threads of a
 // block (max is exact).
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -31,41 +31,50 @@ __device__ __forceinline__ int64_t blk_base(int64_t gb, int64_t nb, int64_t ld) 
     return (gb / nb) * ld + (gb % nb) * kBlk;
 }
 
-// 256 threads, 8 per block: lane group (tid >> 3) quantizes one block per pass,
-// each thread 4 elements; the span's 34-byte blocks are staged in shared
-// memory and leave as 16-byte stores.
+// 256 threads, 4 per block: lane group (tid >> 2) quantizes one block per pass,
+// each thread 8 elements (two 16-byte loads), so a block's scale and
+// reciprocal are computed once per 8 values; the span's 34-byte blocks are
+// staged in shared memory and leave as 16-byte stores.
+constexpr int kTPB = 4, kVPT = kBlk / kTPB, kPasses = kSpan / (256 / kTPB);
+
 template <typename T>
 __global__ void __launch_bounds__(256) q8_encode_kernel(const T *W, int64_t nblocks, int64_t nb, int64_t ld,
                                                         bool vec_in, uint8_t *out, bool vec_out) {
     __shared__ __align__(16) uint8_t stage[kSpanBytes];
-    const int tid = threadIdx.x, sub = tid & 7;
+    const int tid = threadIdx.x, sub = tid & (kTPB - 1);
     for (int64_t b0 = int64_t(blockIdx.x) * kSpan; b0 < nblocks; b0 += int64_t(gridDim.x) * kSpan) {
         const int nblk = int(nblocks - b0 < kSpan ? nblocks - b0 : int64_t(kSpan));
-        // all of the thread's loads of the span first (8 passes x 4 values)
-        float xs[kSpan / 32][4];
+        // all of the thread's loads of the span first (4 passes x 8 values)
+        float xs[kPasses][kVPT];
 #pragma unroll
-        for (int pass = 0; pass < kSpan / 32; ++pass) {
-            const int j = pass * 32 + (tid >> 3);
-            xs[pass][0] = xs[pass][1] = xs[pass][2] = xs[pass][3] = 0.f;
+        for (int pass = 0; pass < kPasses; ++pass) {
+            const int j = pass * (256 / kTPB) + tid / kTPB;
+#pragma unroll
+            for (int i = 0; i < kVPT; ++i) xs[pass][i] = 0.f;
             if (j < nblk) {
-                const T *src = W + blk_base(b0 + j, nb, ld) + 4 * sub;
+                const T *src = W + blk_base(b0 + j, nb, ld) + kVPT * sub;
                 if (sizeof(T) == 4 && vec_in) {
-                    const float4 v = __ldg(reinterpret_cast<const float4 *>(src));
-                    xs[pass][0] = v.x; xs[pass][1] = v.y; xs[pass][2] = v.z; xs[pass][3] = v.w;
+#pragma unroll
+                    for (int h = 0; h < kVPT / 4; ++h) {
+                        const float4 v = __ldg(reinterpret_cast<const float4 *>(src) + h);
+                        xs[pass][4 * h] = v.x; xs[pass][4 * h + 1] = v.y; xs[pass][4 * h + 2] = v.z; xs[pass][4 * h + 3] = v.w;
+                    }
                 } else {
 #pragma unroll
-                    for (int i = 0; i < 4; ++i) xs[pass][i] = float(__ldg(src + i));
+                    for (int i = 0; i < kVPT; ++i) xs[pass][i] = float(__ldg(src + i));
                 }
             }
         }
 #pragma unroll
-        for (int pass = 0; pass < kSpan / 32; ++pass) {
-            const int j = pass * 32 + (tid >> 3);
+        for (int pass = 0; pass < kPasses; ++pass) {
+            const int j = pass * (256 / kTPB) + tid / kTPB;
             const bool ok = j < nblk;
             const float *x = xs[pass];
-            float m = fmaxf(fmaxf(fabsf(x[0]), fabsf(x[1])), fmaxf(fabsf(x[2]), fabsf(x[3])));
+            float m = fabsf(x[0]);
 #pragma unroll
-            for (int o = 4; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+            for (int i = 1; i < kVPT; ++i) m = fmaxf(m, fabsf(x[i]));
+#pragma unroll
+            for (int o = kTPB / 2; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
             // sc = RN(m / 127): Markstein's correction (P. Markstein, IBM J. Res.
             // Dev. 34(1), 1990) of q0 = RN(m y), y = RN(1/127): the remainder
             // m - q0 127 is exact as an FMA and RN(q0 + r y) is the correctly
@@ -84,26 +93,20 @@ __global__ void __launch_bounds__(256) q8_encode_kernel(const T *W, int64_t nblo
             float rc;
             asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(rc) : "f"(sc));
             if (ok) {
-                unsigned short qb[2];
+                int qq[kVPT];
 #pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    int qq[2];
-#pragma unroll
-                    for (int e = 0; e < 2; ++e) {
-                        const float xv = x[2 * h + e];
-                        const float t = __fmul_rn(xv, rc);
-                        float f = rintf(t);
-                        // (NaN / inf t, from a huge reciprocal, also fail the test)
-                        if (!(__fsub_rn(0.5f, fabsf(__fsub_rn(t, f))) > 0x1p-15f)) f = rintf(__fdiv_rn(xv, sc));
-                        // |x / sc| <= 127 (1 + 2^-23): f is already within [-127, 127]
-                        qq[e] = __float2int_rn(f);
-                    }
-                    qb[h] = static_cast<unsigned short>(__byte_perm(qq[0], qq[1], 0x0040));
+                for (int e = 0; e < kVPT; ++e) {
+                    const float t = __fmul_rn(x[e], rc);
+                    float f = rintf(t);
+                    // (NaN / inf t, from a huge reciprocal, also fail the test)
+                    if (!(__fsub_rn(0.5f, fabsf(__fsub_rn(t, f))) > 0x1p-15f)) f = rintf(__fdiv_rn(x[e], sc));
+                    // |x / sc| <= 127 (1 + 2^-23): f is already within [-127, 127]
+                    qq[e] = __float2int_rn(f);
                 }
                 // block j starts on an even byte: 16-bit stores
-                unsigned short *bq = reinterpret_cast<unsigned short *>(stage + j * kBlkBytes + 2 + 4 * sub);
-                bq[0] = qb[0];
-                bq[1] = qb[1];
+                unsigned short *bq = reinterpret_cast<unsigned short *>(stage + j * kBlkBytes + 2 + kVPT * sub);
+#pragma unroll
+                for (int h = 0; h < kVPT / 2; ++h) bq[h] = static_cast<unsigned short>(__byte_perm(qq[2 * h], qq[2 * h + 1], 0x0040));
                 if (sub == 0) *reinterpret_cast<unsigned short *>(stage + j * kBlkBytes) = __half_as_ushort(__float2half_rn(sc));
             }
         }

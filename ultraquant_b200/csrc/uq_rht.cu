@@ -475,8 +475,8 @@ rht_tma_kernel(const __grid_constant__ CUtensorMap tin, const __grid_constant__ 
     constexpr int HALF = 1 << LB;                  // elements per CTA and row
     constexpr int BUFB = HALF * 8;                 // one buffer: the fp64 tile
     constexpr int NBOX = HALF / 4096;              // tensor-map boxes of 4096 elements
-    constexpr int LCL = CL == 1 ? 0 : (CL == 2 ? 1 : (CL == 4 ? 2 : 3));
-    static_assert((1 << LCL) == CL, "cluster of 1, 2, 4 or 8 CTAs");
+    constexpr int LCL = CL == 1 ? 0 : (CL == 2 ? 1 : 2);
+    static_assert(CL == 1 || CL == 2 || CL == 4, "rows of 1, 2 or 4 CTAs");
     constexpr int B = LB + LCL;                    // log2(n)
     constexpr int INB = 4096 * int(sizeof(TIn)), OUTB = 4096 * int(sizeof(TOut));
     extern __shared__ __align__(1024) unsigned char smem_raw_r[];
@@ -612,7 +612,7 @@ rht_tma_kernel(const __grid_constant__ CUtensorMap tin, const __grid_constant__ 
         // registers: elements tid + (j << (LB - 4)) of this CTA's part
         // ---- stages of index bits LB .. B-1 across the cluster: bit LB + i pairs
         //      CTA rank with rank ^ 2^i (lower: own + peer, upper: peer - own) --
-        if (PUSH) {
+        if constexpr (PUSH) {
             // Stage of bit LB + i with CTA rank ^ 2^i: of the 2^LB pairs at
             // local index jj (registers jj, 8 + jj: the lower and upper of
             // this CTA's two ranges), the lower CTA (bit i of rank clear)
@@ -639,21 +639,6 @@ rht_tma_kernel(const __grid_constant__ CUtensorMap tin, const __grid_constant__ 
                 }
             }
             cluster_arrive_rel();   // inboxes read
-        } else {
-#pragma unroll
-            for (int i = 0; i < LCL; ++i) {
-#pragma unroll
-                for (int j = 0; j < 16; ++j) tile[swz(tid + (j << (LB - 4)))] = x[j];
-                cluster_sync_all();
-                const unsigned pb = peer_base[i] + unsigned((k & 1) * BUFB);
-                const bool upper = (rank >> i) & 1u;
-#pragma unroll
-                for (int j = 0; j < 16; ++j) {
-                    const double v = ld_peer_f64(pb + unsigned(swz(tid + (j << (LB - 4)))) * 8u);
-                    x[j] = upper ? d_sub(v, x[j]) : d_add(x[j], v);
-                }
-                cluster_sync_all();   // the partner has read this tile before it changes
-            }
         }
         // ---- epilogue: scale, write the swizzled output lines, store ---------
         double se = 0.0, sa = 0.0;
@@ -711,7 +696,6 @@ rht_tma_kernel(const __grid_constant__ CUtensorMap tin, const __grid_constant__ 
     }
     if (tid == 0) bulk_wait0();
     if (PUSH) cluster_wait_acq();   // closes the last "inbox read" phase
-    else if (CL > 1) cluster_sync_all();   // no CTA leaves while a partner may read its tile
 }
 
 // ---------------------------------------------------------------------------
