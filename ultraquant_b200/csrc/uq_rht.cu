@@ -478,7 +478,10 @@ rht_tma_kernel(const __grid_constant__ CUtensorMap tin, const __grid_constant__ 
     constexpr int LCL = CL == 1 ? 0 : (CL == 2 ? 1 : 2);
     static_assert(CL == 1 || CL == 2 || CL == 4, "rows of 1, 2 or 4 CTAs");
     constexpr int B = LB + LCL;                    // log2(n)
-    constexpr int INB = 4096 * int(sizeof(TIn)), OUTB = 4096 * int(sizeof(TOut));
+    // loads move 4096-element boxes, stores 2048-element boxes (so that the two
+    // output ranges of a PUSH row, 2^(LB-1) columns each, are whole boxes)
+    constexpr int OBOX = 2048, NOBOX = HALF / OBOX;
+    constexpr int INB = 4096 * int(sizeof(TIn)), OUTB = OBOX * int(sizeof(TOut));
     extern __shared__ __align__(1024) unsigned char smem_raw_r[];
     __shared__ __align__(8) unsigned long long full[2];
     __shared__ double red[2 * (NT / 32)];
@@ -493,7 +496,7 @@ rht_tma_kernel(const __grid_constant__ CUtensorMap tin, const __grid_constant__ 
     const int64_t nclusters = gridDim.x / CL;
     const int64_t first = blockIdx.x / CL;
     constexpr int CH_IN = 4096 / (128 / int(sizeof(TIn)));     // 128-byte lines per input box
-    constexpr int CH_OUT = 4096 / (128 / int(sizeof(TOut)));
+    constexpr int CH_OUT = OBOX / (128 / int(sizeof(TOut)));
     const int lin0 = int(col0 / (128 / int(sizeof(TIn))));
     const int lout0 = int(col0 / (128 / int(sizeof(TOut))));
     // Rows over 2 or 4 CTAs (PUSH): the cross-CTA stages are finished by
@@ -680,9 +683,12 @@ rht_tma_kernel(const __grid_constant__ CUtensorMap tin, const __grid_constant__ 
         __syncthreads();
         if (tid == 0) {
 #pragma unroll
-            for (int bx = 0; bx < NBOX; ++bx) {
-                // box bx holds columns out_col of its first register range
-                const int c0 = PUSH ? int(out_col(bx * 8) - tid) / (128 / int(sizeof(TOut))) : lout0 + bx * CH_OUT;
+            for (int bx = 0; bx < NOBOX; ++bx) {
+                // PUSH: boxes [0, NOBOX/2) hold the first column range
+                // (registers < 8), the rest the second
+                const int c0 = PUSH ? int(out_col((bx / (NOBOX / 2)) * 8) - tid + (bx % (NOBOX / 2)) * OBOX) /
+                                          (128 / int(sizeof(TOut)))
+                                    : lout0 + bx * CH_OUT;
                 store3d(&tout, 0, c0, int(r), buf + unsigned(bx * OUTB));
             }
             bulk_commit();
@@ -875,11 +881,11 @@ __global__ void prescale_kernel(const double *colscale, const double *signs, int
 // (rows, ncols) matrix of T with row stride ld, viewed as 128-byte lines:
 // dims {elements per line, lines per row, rows}, box = 4096 elements of one row.
 template <typename T>
-bool make_line_map(CUtensorMap *m, const void *base, int64_t rows, int64_t ncols, int64_t ld) {
+bool make_line_map(CUtensorMap *m, const void *base, int64_t rows, int64_t ncols, int64_t ld, int box_elems) {
     constexpr int EPL = 128 / int(sizeof(T));
     const cuuint64_t dims[3] = {cuuint64_t(EPL), cuuint64_t(ncols / EPL), cuuint64_t(rows)};
     const cuuint64_t strides[2] = {128, cuuint64_t(ld) * sizeof(T)};
-    const cuuint32_t box[3] = {cuuint32_t(EPL), cuuint32_t(4096 / EPL), 1};
+    const cuuint32_t box[3] = {cuuint32_t(EPL), cuuint32_t(box_elems / EPL), 1};
     return encode_lines(m, sizeof(T) == 8, 3, base, dims, strides, box);
 }
 
@@ -937,8 +943,8 @@ int launch_tma_v(const CUtensorMap &mi, const CUtensorMap &mo, const RhtArgs &a,
 template <typename TIn, typename TOut, int MODE, bool COLS>
 int launch_tma(const RhtArgs &a, int64_t ncols_in, cudaStream_t st, int64_t *nparts) {
     CUtensorMap mi, mo;
-    if (!make_line_map<TIn>(&mi, a.in, a.rows, ncols_in, a.ld_in) ||
-        !make_line_map<TOut>(&mo, a.out, a.rows, a.ncols_out, a.ld_out))
+    if (!make_line_map<TIn>(&mi, a.in, a.rows, ncols_in, a.ld_in, 4096) ||
+        !make_line_map<TOut>(&mo, a.out, a.rows, a.ncols_out, a.ld_out, 2048))
         return uq::fail(UQ_ERR_CUDA, "rht: tensor map encoding failed");
     // n = 2^b as 2^LB-element parts on a cluster of 2^(b - LB) CTAs.  Measured
     // on B200: 8192-element parts beat 4096-element parts with one more
