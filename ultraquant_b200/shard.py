@@ -1,6 +1,6 @@
 """Sharding the quantization of a weight set across GPUs (one process per GPU).
 
-Every unit of the path is independent (SURVEY's multi-GPU analysis): the RHT
+Every unit of the path is independent: the RHT
 is per row, E8 groups (256) and trellis segments (T) lie inside rows because
 the padded width is a power of two >= 256.  So a weight set is split by
 tensor and, for large tensors, by row block; each rank quantizes its share
