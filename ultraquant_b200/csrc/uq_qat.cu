@@ -451,6 +451,24 @@ qat_rows_kernel(FwhtArgs a) {
         __syncthreads();
     }
     const float *cwp = a.cw_smem ? cw_s : a.cw;
+    // recon of 4096-wide rows with a staged codebook: sH (ncols_out values) is
+    // staged after it (16 KB; measured 20.8 -> 27.1 % of HBM at L = 12).  With
+    // the codebook in global memory sH stays there too: the extra shared memory
+    // takes L1 from the codebook lookups (measured 16.5 -> 12.6 % at L = 16);
+    // wider rows would lose resident CTAs to it.
+    const bool cs_smem = SRC == SRC_RECON && NB == 12 && cs && a.cw_smem;
+    float *cs_s = reinterpret_cast<float *>(smem_raw + size_t(R) * kRowStride * 4 +
+                                            ((size_t(a.ncw) * 4 + 15) & ~size_t(15)));
+    if (cs_smem) {
+        for (int i = tid; i < a.ncols_out; i += R) cs_s[i] = __ldg(cs + i);
+        __syncthreads();
+    }
+    // bit k: the output column tid + (k << (NB - 5)) takes a negative sign (recon)
+    unsigned dneg = 0;
+    if (SRC == SRC_RECON && signs) {
+#pragma unroll
+        for (int k = 0; k < 32; ++k) dneg |= (__ldg(signs + tid + (k << P)) < 0.f ? 1u : 0u) << k;
+    }
     const bool vec_st = !a.states64 && (reinterpret_cast<uintptr_t>(a.states) & 15) == 0;
     const bool vec_x = (reinterpret_cast<uintptr_t>(a.x) & 15) == 0 && (a.ld_x % 4) == 0;
     float *rowA = tq + tid * kRowStride;                                       // pass A
@@ -530,8 +548,10 @@ qat_rows_kernel(FwhtArgs a) {
                 const int e = tid + (k << P);
                 if (e >= a.ncols_out) continue;
                 float y = s_pow2 ? A::mul(x[k], s_inv) : A::div(x[k], s);
-                if (signs) y = A::mul(y, __ldg(signs + e));
-                if (cs) y = A::div(y, __ldg(cs + e));
+                // recon's d is +-1: the product is a sign flip, read once per CTA
+                if (SRC == SRC_RECON) y = ((dneg >> k) & 1u) ? -y : y;
+                else if (signs) y = A::mul(y, __ldg(signs + e));
+                if (cs) y = A::div(y, cs_smem ? cs_s[e] : __ldg(cs + e));
                 dst[e] = y;
             }
         }
@@ -548,7 +568,8 @@ template <int DIR, int SRC, int DST, int NB>
 int launch_rows(const FwhtArgs &a, cudaStream_t st, const char *what) {
     const bool codes = SRC == SRC_RECON || DST == DST_GRADS;
     const size_t smem = (size_t(kRowStride) * 4 << (NB - 5)) +
-        (codes && a.cw_smem ? ((size_t(a.ncw) * 4 + 15) & ~size_t(15)) + (DST == DST_GRADS ? size_t(a.ncw) * 8 : 0) : 0);
+        (codes && a.cw_smem ? ((size_t(a.ncw) * 4 + 15) & ~size_t(15)) + (DST == DST_GRADS ? size_t(a.ncw) * 8 : 0) : 0) +
+        (SRC == SRC_RECON && NB == 12 && a.cw_smem && a.colscale ? size_t(a.ncols_out) * 4 : 0);
     auto kern = qat_rows_kernel<DIR, SRC, DST, NB>;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess)
         return uq::check_cuda("qat rows: set smem attribute");
