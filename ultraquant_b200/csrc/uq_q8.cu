@@ -93,15 +93,26 @@ __global__ void __launch_bounds__(256) q8_encode_kernel(const T *W, int64_t nblo
             float rc;
             asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(rc) : "f"(sc));
             if (ok) {
+                // rint(t) as (t + 1.5 2^23) - 1.5 2^23: for |t| < 2^22 the sum lies
+                // in [2^23, 2^24), where the spacing is 1, so round-to-nearest-even
+                // of the addition is rint(t), and the sum's low byte is rint(t)
+                // as a two's-complement int8 (1.5 2^23 = 0x4B400000 ends in 0x00)
+                constexpr float kMagic = 12582912.0f;
                 int qq[kVPT];
+                bool bad = false;
 #pragma unroll
                 for (int e = 0; e < kVPT; ++e) {
                     const float t = __fmul_rn(x[e], rc);
-                    float f = rintf(t);
+                    const float sm = __fadd_rn(t, kMagic);
+                    const float f = __fsub_rn(sm, kMagic);
                     // (NaN / inf t, from a huge reciprocal, also fail the test)
-                    if (!(__fsub_rn(0.5f, fabsf(__fsub_rn(t, f))) > 0x1p-15f)) f = rintf(__fdiv_rn(x[e], sc));
-                    // |x / sc| <= 127 (1 + 2^-23): f is already within [-127, 127]
-                    qq[e] = __float2int_rn(f);
+                    bad |= !(__fsub_rn(0.5f, fabsf(__fsub_rn(t, f))) > 0x1p-15f);
+                    qq[e] = int(__float_as_uint(sm));
+                }
+                if (bad) {
+                    // |x / sc| <= 127 (1 + 2^-23): the quotient rounds into [-127, 127]
+#pragma unroll
+                    for (int e = 0; e < kVPT; ++e) qq[e] = __float2int_rn(rintf(__fdiv_rn(x[e], sc)));
                 }
                 // block j starts on an even byte: 16-bit stores
                 unsigned short *bq = reinterpret_cast<unsigned short *>(stage + j * kBlkBytes + 2 + kVPT * sub);
