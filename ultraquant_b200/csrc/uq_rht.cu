@@ -296,8 +296,11 @@ __device__ __forceinline__ void cluster_arrive_rel() {
 __device__ __forceinline__ void cluster_wait_acq() {
     asm volatile("barrier.cluster.wait.acquire.aligned;\n" ::: "memory");
 }
-__device__ __forceinline__ void st_peer_f64(unsigned addr, double v) {
-    asm volatile("st.shared::cluster.f64 [%0], %1;" :: "r"(addr), "d"(v) : "memory");
+// 8-byte store into a cluster peer's shared memory that completes on the
+// peer's mbarrier (complete_tx of 8 bytes): no release fence on the writer
+__device__ __forceinline__ void st_async_f64(unsigned addr, double v, unsigned mbar) {
+    asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.b64 [%0], %1, [%2];"
+                 :: "r"(addr), "l"(__double_as_longlong(v)), "r"(mbar) : "memory");
 }
 
 __device__ __forceinline__ double ld_peer_f64(unsigned addr) {
@@ -477,6 +480,7 @@ rht_tma_kernel(const __grid_constant__ CUtensorMap tin, const __grid_constant__ 
     constexpr int NBOX = HALF / 4096;              // tensor-map boxes of 4096 elements
     constexpr int LCL = CL == 1 ? 0 : (CL == 2 ? 1 : 2);
     static_assert(CL == 1 || CL == 2 || CL == 4, "rows of 1, 2 or 4 CTAs");
+    constexpr bool PUSH_ROWS = CL == 2 || CL == 4;
     constexpr int B = LB + LCL;                    // log2(n)
     // loads move 4096-element boxes, stores 2048-element boxes (so that the two
     // output ranges of a PUSH row, 2^(LB-1) columns each, are whole boxes)
@@ -484,6 +488,7 @@ rht_tma_kernel(const __grid_constant__ CUtensorMap tin, const __grid_constant__ 
     constexpr int INB = 4096 * int(sizeof(TIn)), OUTB = OBOX * int(sizeof(TOut));
     extern __shared__ __align__(1024) unsigned char smem_raw_r[];
     __shared__ __align__(8) unsigned long long full[2];
+    __shared__ __align__(8) unsigned long long ibar[2];   // PUSH: inbox i filled
     __shared__ double red[2 * (NT / 32)];
     const int tid = threadIdx.x;
     unsigned rank = 0;
@@ -517,9 +522,14 @@ rht_tma_kernel(const __grid_constant__ CUtensorMap tin, const __grid_constant__ 
         return tid + (j << (LB - 4));
     };
 
+    const unsigned ibar0 = unsigned(__cvta_generic_to_shared(&ibar[0]));
     if (tid == 0) {
         mbar_init(bar0, 1);
         mbar_init(bar0 + 8, 1);
+        // an inbox's phase completes on this CTA's arm (arrive + expect_tx)
+        // and the partner's INBOX bytes of st.async
+        if (PUSH_ROWS)
+            for (int i = 0; i < LCL; ++i) mbar_init(ibar0 + 8u * unsigned(i), 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     __syncthreads();
@@ -546,10 +556,13 @@ rht_tma_kernel(const __grid_constant__ CUtensorMap tin, const __grid_constant__ 
     const double inv_mul = ldexp(1.0, -B);
     const double fwd_mul = ldexp(1.0, -(B >> 1));
     bool fail = false;
-    unsigned peer_base[LCL > 0 ? LCL : 1];
+    unsigned peer_base[LCL > 0 ? LCL : 1], peer_ibar[LCL > 0 ? LCL : 1];
 #pragma unroll
-    for (int i = 0; i < LCL; ++i)
+    for (int i = 0; i < LCL; ++i) {
         asm("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(peer_base[i]) : "r"(sbase), "r"(rank ^ (1u << i)));
+        asm("mapa.shared::cluster.u32 %0, %1, %2;"
+            : "=r"(peer_ibar[i]) : "r"(ibar0 + 8u * unsigned(i)), "r"(rank ^ (1u << i)));
+    }
     // PUSH rows: a partner's values arrive in an inbox after the two tiles
     // (inbox i for the stage with rank ^ 2^i)
     constexpr unsigned INBOX = 8u << (LB - 1);
@@ -620,18 +633,19 @@ rht_tma_kernel(const __grid_constant__ CUtensorMap tin, const __grid_constant__ 
             // local index jj (registers jj, 8 + jj: the lower and upper of
             // this CTA's two ranges), the lower CTA (bit i of rank clear)
             // finishes those of registers < 8 and the upper those >= 8; each
-            // pushes the other half into the partner's inbox (remote stores
-            // do not stall) and one cluster barrier makes them visible.
+            // pushes the other half into the partner's inbox by st.async,
+            // which completes on the partner's inbox mbarrier (no fence and
+            // no cluster barrier on the data path).
             cluster_wait_acq();   // every inbox of the previous row has been read
 #pragma unroll
             for (int i = 0; i < LCL; ++i) {
                 const bool up = (rank >> i) & 1u;
+                if (tid == 0) mbar_arrive_expect_tx(ibar0 + 8u * unsigned(i), INBOX);
 #pragma unroll
                 for (int jj = 0; jj < 8; ++jj)
-                    st_peer_f64(peer_base[i] + 2u * unsigned(BUFB) + unsigned(i) * INBOX +
-                                    8u * unsigned(tid + (jj << (LB - 4))), up ? x[jj] : x[8 + jj]);
-                cluster_arrive_rel();
-                cluster_wait_acq();   // the partner's values are in inbox i
+                    st_async_f64(peer_base[i] + 2u * unsigned(BUFB) + unsigned(i) * INBOX +
+                                     8u * unsigned(tid + (jj << (LB - 4))), up ? x[jj] : x[8 + jj], peer_ibar[i]);
+                rmb_wait(ibar0 + 8u * unsigned(i), unsigned(k & 1), fail);   // the partner's values are in inbox i
 #pragma unroll
                 for (int jj = 0; jj < 8; ++jj) {
                     const double v = lds64d(inbox + unsigned(i) * INBOX + 8u * unsigned(tid + (jj << (LB - 4))));
