@@ -87,6 +87,18 @@ def same_bits(a, b):
     return bool(np.array_equal(a.view(iv), b.view(iv)))
 
 
+def same_bits_or_nan(a, b):
+    """same_bits, except that a NaN matches any NaN: IEEE 754 leaves the sign
+    and payload of a generated NaN (inf * 0) to the hardware (x86 SSE gives
+    0xFFC00000, the GPU 0x7FFFFFFF)."""
+    a = np.ascontiguousarray(a)
+    b = np.ascontiguousarray(b)
+    if a.shape != b.shape or a.dtype != b.dtype:
+        return False
+    na, nb = np.isnan(a), np.isnan(b)
+    return bool(np.array_equal(na, nb)) and same_bits(a[~na], b[~nb])
+
+
 def qe8_same_or_tie(got, ref, A, bpw, group=256, max_ties=4):
     """q_e8 outputs (qlab.py:185-198) bit-equal except on 8-vectors whose two
     reconstructions are codewords at exactly equal distance from gn (checked

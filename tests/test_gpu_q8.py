@@ -5,7 +5,7 @@ import numpy as np
 import pytest
 
 import oracle as O
-from conftest import same_bits
+from conftest import same_bits, same_bits_or_nan
 
 pytestmark = pytest.mark.gpu
 
@@ -48,3 +48,28 @@ def test_q8_device_tensors_and_errors(Q8):
     assert same_bits(back.cpu().numpy(), ref)
     with pytest.raises(ValueError):
         Q8.enc_q8(np.zeros((2, 33), np.float32))
+
+
+def test_q8_rounding_ties_and_extreme_scales(Q8):
+    """Values on the rounding boundaries (x / scale = k + 1/2 exactly, where
+    the reciprocal screen must hand over to the division) and scales at the
+    ends of the fp32 range (the scale's own division fallback, subnormal
+    scales whose reciprocal overflows), against the oracle."""
+    rng = np.random.RandomState(7)
+    rows = []
+    for e in (-140, -126, -101, -100, -30, 0, 30, 99, 100, 101):
+        s = np.float32(2.0 ** e)
+        k = rng.randint(-126, 126, size=31)
+        blk = np.concatenate([[127.0], k + 0.5]) * np.float64(s)
+        rows.append(rng.permutation(blk))
+        # the same values scaled by a non-power of two (scale no longer exact)
+        rows.append(rng.permutation(blk) * 1.37)
+    W = np.asarray(rows, dtype=np.float32).reshape(len(rows), 32)
+    W = np.concatenate([W, np.zeros((1, 32), np.float32), -W[:3]], axis=0)
+    with np.errstate(over="ignore"):   # float16 scales of 2^100 and up are inf
+        ref = O.enc_q8(W)
+    q = Q8.enc_q8(W)
+    assert np.array_equal(q, ref)
+    # an inf scale times q = 0 is NaN
+    with np.errstate(invalid="ignore"):
+        assert same_bits_or_nan(Q8.deq_q8(q), O.deq_q8(q))
