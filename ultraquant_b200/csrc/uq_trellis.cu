@@ -908,6 +908,50 @@ int launch_viterbi(const VitArgs &a, cudaStream_t st) {
     return uq::check_cuda("viterbi_fwd_kernel launch");
 }
 
+// Sequences that one wave of resident CTAs (clusters for L = 16) covers, or 0
+// if the occupancy query fails.  Batches that are whole multiples of it leave
+// no partly filled last wave (2,048-sequence batches at L = 16 ran 13.84
+// waves of 74 clusters: 1.1 % of the cluster slots idle).
+template <int L, int R>
+int64_t viterbi_wave() {
+    constexpr int CL = L == 16 ? 2 : 1;
+    using C = VitCfg<L, R, CL>;
+    const size_t smem = size_t(C::NSET) * C::NBUF * (C::FLOATS + C::OFLOATS) * sizeof(float);
+    auto kern = viterbi_fwd_kernel<C>;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
+    if (CL == 1) {
+        int per_sm = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, smem) != cudaSuccess) {
+            cudaGetLastError();
+            return 0;
+        }
+        return int64_t(per_sm) * uq::num_sms() * C::SPS;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(unsigned(CL * 64), 1, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    int ncl = 0;
+    if (cudaOccupancyMaxActiveClusters(&ncl, kern, &cfg) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
+    return int64_t(ncl) * C::NSET;
+}
+
+template <int R, int L>
+int64_t wave_l(int Lrt) {
+    if constexpr (L > 16) {
+        return 0;
+    } else {
+        if (Lrt == L) return viterbi_wave<L, R>();
+        return wave_l<R, L + 1>(Lrt);
+    }
+}
+
 template <int R, int L>
 int dispatch_l(int Lrt, const VitArgs &a, cudaStream_t st) {
     if constexpr (L > 16) {
@@ -922,6 +966,10 @@ template <int R>
 int run_viterbi_r(const float *xn, int64_t nseq, int T, int L, const float *cw, int32_t *states,
                   uint32_t *bp, int32_t *fin, int64_t batch, cudaStream_t st) {
     constexpr int LMIN = (2 * R > 6) ? 2 * R : 6;
+    if (batch < nseq) {
+        const int64_t wave = wave_l<R, LMIN>(L);
+        if (wave > 0 && batch > wave) batch = batch / wave * wave;
+    }
     for (int64_t s0 = 0; s0 < nseq; s0 += batch) {
         VitArgs a{};
         a.xn = xn; a.seq0 = s0; a.nbatch = std::min<int64_t>(batch, nseq - s0);
@@ -968,11 +1016,13 @@ int64_t vit_seq_bytes(int T, int L) {
 }
 
 size_t trellis_ws_bytes(int64_t nseq, int T, int L) {
-    // cap the backpointer batch at ~2 GiB (whole sequences, at least one
-    // launch worth of sequences)
+    // cap the backpointer batch at ~8 GiB (whole sequences, at least one
+    // launch worth of sequences): each batch ends with a traceback launch
+    // that is latency bound (~0.19 ms whatever its size), so larger batches
+    // mean fewer of them (at L = 16, T = 256: 7,900 sequences per batch)
     const int64_t per = vit_seq_bytes(T, L);
     int64_t want = nseq;
-    const int64_t cap = (int64_t(2) << 30) / per;
+    const int64_t cap = (int64_t(8) << 30) / per;
     const int64_t min_batch = 2 * 148;
     if (want > cap) want = std::max<int64_t>(cap, min_batch);
     return size_t(std::max<int64_t>(want, 1) * per) + 512;
