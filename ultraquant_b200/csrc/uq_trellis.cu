@@ -685,6 +685,7 @@ viterbi_fwd_kernel(VitArgs a) {
     }
 
     float m[K][NR];
+#pragma unroll 2
     for (int t = 0; t + 1 < a.T; ++t) {
 #pragma unroll
         for (int X = 0; X < NSET; ++X) {
