@@ -350,6 +350,9 @@ template <int L_, int R_, int CL_> struct VitCfg {
     static constexpr int TPS = Q / NQ;                   // threads per sequence
     static constexpr int NSET = (CL == 2 && R >= 2) ? 2 : 1;   // interleaved sets (cluster)
     static constexpr int NBUF = 2;                       // m buffers per set
+    // step loop unrolled by two (buffer parities become constants) where that
+    // measured faster and stays free of spills at the 128-register cap
+    static constexpr int UNROLL = (R_ == 2 && CL_ == 1) || R_ == 3 ? 2 : 1;
     static constexpr int SPS = CL == 1 ? kThreads / TPS : 1;   // sequences per set per CTA
     static constexpr int FLOATS = kThreads * NQ;         // floats per (set, buffer) per CTA
     static constexpr int A = Swz<R>::A, M = Swz<R>::M;
@@ -685,7 +688,7 @@ viterbi_fwd_kernel(VitArgs a) {
     }
 
     float m[K][NR];
-#pragma unroll 2
+#pragma unroll (C::UNROLL)
     for (int t = 0; t + 1 < a.T; ++t) {
 #pragma unroll
         for (int X = 0; X < NSET; ++X) {
