@@ -194,9 +194,14 @@ __device__ __forceinline__ void scatter_grads(const FwhtArgs &a, const T (&x)[V]
 // BC > 0: the row width 2^BC (>= 4096, one row per tile) is a compile-time
 // constant, so every pass, index and branch below folds; BC = 0 reads it from
 // the arguments (narrow rows, several per tile).
-template <typename T, int DIR, int SRC, int DST, int MAXT, int BC>
-__global__ void __launch_bounds__(MAXT, sizeof(T) == 8 ? (MAXT <= 128 ? 3 : (MAXT <= 256 ? 2 : 1))
-                                                       : (MAXT <= 128 ? 6 : (MAXT <= 256 ? 3 : 1)))
+// MINB > 0 overrides the resident-CTA target: the fp32 gradient kernels with
+// the codebook and its fp64 accumulators in shared memory (48 KB) fit 3
+// (128 threads) or 2 (256 threads) CTAs per SM anyway, so they take the
+// registers that 6 / 3 would leave unused (no spills).
+template <typename T, int DIR, int SRC, int DST, int MAXT, int BC, int MINB = 0>
+__global__ void __launch_bounds__(MAXT, MINB > 0 ? MINB
+                                        : (sizeof(T) == 8 ? (MAXT <= 128 ? 3 : (MAXT <= 256 ? 2 : 1))
+                                                          : (MAXT <= 128 ? 6 : (MAXT <= 256 ? 3 : 1))))
 fwht_kernel(FwhtArgs a) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     T *tile = reinterpret_cast<T *>(smem_raw);
@@ -607,6 +612,14 @@ int launch_fwht(const FwhtArgs &a, cudaStream_t st, const char *what) {
         else if (a.b == 14) kern = fwht_kernel<T, DIR, SRC, DST, 512, 14>;
     }
     if (a.b == 15) kern = fwht_kernel<T, DIR, SRC, DST, TOP, (sizeof(T) == 8 ? 0 : 15)>;
+    if constexpr (sizeof(T) == 4 && DST == DST_GRADS) {
+        // measured at L = 12: 8.1 -> 8.6 % of HBM (4096 x 4096); with the
+        // codebook in global memory (L = 16) 6 CTAs per SM stay faster
+        if (a.cw_smem) {
+            if (a.b <= 12) kern = a.b == 12 ? fwht_kernel<T, DIR, SRC, DST, 128, 12, 3> : fwht_kernel<T, DIR, SRC, DST, 128, 0, 3>;
+            else if (a.b == 13) kern = fwht_kernel<T, DIR, SRC, DST, 256, 13, 2>;
+        }
+    }
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess)
         return uq::check_cuda("fwht: set smem attribute");
     int per_sm = 0;
