@@ -698,7 +698,12 @@ viterbi_fwd_kernel(VitArgs a) {
 #pragma unroll
         for (int X = 0; X < NSET; ++X) {
             const float x = xv[X];
-            xv[X] = (vmask >> X) & 1u ? __ldg(xcur + (Off(X) * Off(a.T) + Off(t + 1))) : 0.f;
+            // (the L = 16 R = 3 form measured 54.4 % with this association
+            // of the offset, 53.9 % with the one below)
+            if constexpr (sizeof(Off) == 8)
+                xv[X] = (vmask >> X) & 1u ? __ldg(xcur + X * int64_t(a.T) + t + 1) : 0.f;
+            else
+                xv[X] = (vmask >> X) & 1u ? __ldg(xcur + (Off(X) * Off(a.T) + Off(t + 1))) : 0.f;
             unsigned word;
             if (CL == 1) {
                 const unsigned wb = smem0 + unsigned(X * NBUF + (t & 1)) * BUF;
