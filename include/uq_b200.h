@@ -59,7 +59,7 @@ int64_t uq_next_pow2(int64_t n0);
 /* qlab.py:71-85 rht_rows(A, seed): out[rows, n] = FWHT(pad(A) * d) / sqrt(n),
  * fp64, stages h = 1..n/2 in order (bit-exact with numpy).  A is f32 or f64
  * (a_dtype), row stride lda >= n0.  signs: device, length n = next_pow2(n0).
- * n <= 16384 in this build. */
+ * n <= 32768 (larger n returns UQ_ERR_UNSUPPORTED). */
 int uq_rht_rows(const void *A, int a_dtype, int64_t rows, int64_t n0, int64_t lda,
                 const double *signs, double *out, void *stream);
 
