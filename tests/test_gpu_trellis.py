@@ -190,3 +190,33 @@ def test_pack_viterbi_paths_roundtrip():
         pk = T_.pack_states(st, 16, R)
         assert pk.shape == (300, (16 + R * 255 + 31) // 32)
         assert torch.equal(T_.unpack_states(pk, 256, 16, R), st)
+
+
+@pytest.mark.parametrize("L,R,nseq,fit", [(12, 2, 3000, 2500), (16, 2, 400, 300), (16, 3, 300, 200)])
+def test_viterbi_small_workspace_batches(L, R, nseq, fit):
+    """A workspace that holds only `fit` sequences: the entry point runs
+    several backpointer batches, each cut down to whole waves of resident
+    CTAs (clusters at L = 16), and returns the states of a single batch."""
+    import torch
+    from ultraquant_b200 import _device as D
+    from ultraquant_b200 import _lib
+    lib = _lib.load()
+    T = 256
+    torch.manual_seed(nseq + L)
+    x = torch.randn(nseq, T, device="cuda")
+    cw = D.codebook(L, x.device)
+
+    def run(ws_bytes):
+        out = torch.full((nseq, T), -1, dtype=torch.int32, device=x.device)
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=x.device)
+        rc = lib.uq_trellis_viterbi(x.data_ptr(), nseq, T, L, R, cw.data_ptr(), out.data_ptr(), ws.data_ptr(),
+                                    ws.numel(), D.stream_handle(x.device))
+        assert rc == 0, lib.uq_last_error()
+        return out
+
+    per_seq = (T - 1) * ((1 << L) // 64) * 4 + 4
+    full = run(lib.uq_trellis_workspace_bytes(nseq, T, L, R))
+    small = run(fit * per_seq + 512)
+    torch.cuda.synchronize()
+    assert torch.equal(small, full)
+    assert int(full.min()) >= 0 and int(full.max()) < (1 << L)
