@@ -510,15 +510,26 @@ rht_tma_kernel(const __grid_constant__ CUtensorMap tin, const __grid_constant__ 
     // blk(j) = (rank >> 1) + (j < 8 ? 0 : CL / 2): two column ranges of
     // 2^(LB-1) per CTA.  Otherwise register j holds col0 + tid + (j << (LB-4)).
     constexpr bool PUSH = CL == 2 || CL == 4;
+    // Single-CTA rows of 8192 (LB = 13): the last index bit (12) is done with
+    // lane shuffles instead of a third transpose through the tile.  The pass
+    // over bits 8..11 reads with lane bit 4 on element bit 12, so register j
+    // then holds element (tid & 15) | ((tid >> 5) & 15) << 4 | j << 8 |
+    // ((tid >> 4) & 1) << 12.
+    constexpr bool SHFL12 = LB == 13 && CL == 1;
+    auto elem12 = [&](int j) -> int {
+        return (tid & 15) | (((tid >> 5) & 15) << 4) | (j << 8) | (((tid >> 4) & 1) << 12);
+    };
     auto out_col = [&](int j) -> int64_t {
         if (PUSH)
             return (int64_t((rank >> 1) + (j < 8 ? 0 : CL / 2)) << LB) + (int64_t(rank & 1u) << (LB - 1)) + tid +
                    ((j & 7) << (LB - 4));
+        if (SHFL12) return col0 + elem12(j);
         return col0 + tid + (j << (LB - 4));
     };
     // index of register j's output in the store buffer (whole boxes of 4096)
     auto out_idx = [&](int j) -> int {
         if (PUSH) return (j < 8 ? 0 : (1 << (LB - 1))) + tid + ((j & 7) << (LB - 4));
+        if (SHFL12) return elem12(j);
         return tid + (j << (LB - 4));
     };
 
@@ -611,19 +622,31 @@ rht_tma_kernel(const __grid_constant__ CUtensorMap tin, const __grid_constant__ 
         }
         // ---- passes 4, 8, ...: transposes through the element-swizzled tile ----
 #pragma unroll
-        for (int p = 4, prev = 0, done = 4; p - 4 < LB - 4; p += 4) {
+        for (int p = 4, prev = 0, done = 4; p - 4 < (SHFL12 ? 8 : LB - 4); p += 4) {
             const int pp = p > LB - 4 ? LB - 4 : p;
             const int pb = (tid & ((1 << prev) - 1)) | ((tid >> prev) << (prev + 4));
 #pragma unroll
             for (int j = 0; j < 16; ++j) tile[swz(pb + (j << prev))] = x[j];
             __syncthreads();
-            const int base = (tid & ((1 << pp) - 1)) | ((tid >> pp) << (pp + 4));
+            // (SHFL12, bits 8..11: lane bit 4 reads element bit 12; each half
+            // warp still covers all banks once)
+            const int base = (SHFL12 && pp == 8) ? elem12(0)
+                                                 : ((tid & ((1 << pp) - 1)) | ((tid >> pp) << (pp + 4)));
 #pragma unroll
             for (int j = 0; j < 16; ++j) x[j] = tile[swz(base + (j << pp))];
-            stages16(x, pp, done > pp ? done : pp, LB);
+            stages16(x, pp, done > pp ? done : pp, SHFL12 ? 12 : LB);
             done = pp + 4;
             prev = pp;
             __syncthreads();
+        }
+        if constexpr (SHFL12) {
+            // stage h = 4096: lanes l and l ^ 16 hold the pair (lower: bit 4 clear)
+            const bool upper = (tid >> 4) & 1;
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+                const double o = __shfl_xor_sync(0xffffffffu, x[j], 16);
+                x[j] = upper ? d_sub(o, x[j]) : d_add(x[j], o);
+            }
         }
         // registers: elements tid + (j << (LB - 4)) of this CTA's part
         // ---- stages of index bits LB .. B-1 across the cluster: bit LB + i pairs
