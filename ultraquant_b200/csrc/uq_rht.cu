@@ -515,17 +515,19 @@ rht_tma_kernel(const __grid_constant__ CUtensorMap tin, const __grid_constant__ 
     // over bits 8..11 reads with lane bit 4 on element bit 12, so register j
     // then holds element (tid & 15) | ((tid >> 5) & 15) << 4 | j << 8 |
     // ((tid >> 4) & 1) << 12.
-    // Rows of 16384 (two CTAs) too: the push stage pairs equal register slots
-    // of the two parts whatever the layout; CTA rank r then finishes the
-    // slots r*8 .. r*8+7, i.e. the elements with bit 11 = r, and stores them
-    // as four 2048-column boxes (both parts, bit 12 = 0 and 1).
-    constexpr bool SHFL12 = LB == 13 && (CL == 1 || CL == 2);
-    constexpr bool SHFL12_PUSH = SHFL12 && CL == 2;
+    // Rows of 16384 / 32768 (2 / 4 CTAs) too: the push stages pair equal
+    // register slots of the parts whatever the layout; CTA rank r then
+    // finishes the slots (r & 1)*8 .. +7, i.e. the elements with bit 11 =
+    // r & 1, of two parts, and stores them as four 2048-column boxes (both
+    // parts, bit 12 = 0 and 1).
+    constexpr bool SHFL12 = LB == 13;
+    constexpr bool SHFL12_PUSH = SHFL12 && (CL == 2 || CL == 4);
     auto elem12 = [&](int j) -> int {
         return (tid & 15) | (((tid >> 5) & 15) << 4) | (j << 8) | (((tid >> 4) & 1) << 12);
     };
     auto out_col = [&](int j) -> int64_t {
-        if (SHFL12_PUSH) return (int64_t(j < 8 ? 0 : 1) << LB) + elem12(int(rank) * 8 + (j & 7));
+        if (SHFL12_PUSH)
+            return (int64_t((rank >> 1) + (j < 8 ? 0 : CL / 2)) << LB) + elem12(int(rank & 1u) * 8 + (j & 7));
         if (PUSH)
             return (int64_t((rank >> 1) + (j < 8 ? 0 : CL / 2)) << LB) + (int64_t(rank & 1u) << (LB - 1)) + tid +
                    ((j & 7) << (LB - 4));
@@ -535,7 +537,7 @@ rht_tma_kernel(const __grid_constant__ CUtensorMap tin, const __grid_constant__ 
     // index of register j's output in the store buffer (whole boxes of 4096)
     auto out_idx = [&](int j) -> int {
         if (SHFL12_PUSH) {
-            const int e = elem12(int(rank) * 8 + (j & 7));
+            const int e = elem12(int(rank & 1u) * 8 + (j & 7));
             return (j < 8 ? 0 : (1 << (LB - 1))) + (((e >> 12) & 1) << 11) + (e & 2047);
         }
         if (PUSH) return (j < 8 ? 0 : (1 << (LB - 1))) + tid + ((j & 7) << (LB - 4));
@@ -733,10 +735,11 @@ rht_tma_kernel(const __grid_constant__ CUtensorMap tin, const __grid_constant__ 
             for (int bx = 0; bx < NOBOX; ++bx) {
                 // PUSH: boxes [0, NOBOX/2) hold the first column range
                 // (registers < 8), the rest the second
-                // SHFL12_PUSH: box bx = (part bx >> 1, bit 12 = bx & 1) of the
-                // columns with bit 11 = rank
+                // SHFL12_PUSH: box bx = (column range bx >> 1, bit 12 = bx & 1)
+                // of the columns with bit 11 = rank & 1
                 const int c0 = SHFL12_PUSH
-                    ? ((bx >> 1) * (1 << LB) + (bx & 1) * 4096 + int(rank) * 2048) / (128 / int(sizeof(TOut)))
+                    ? ((int(rank >> 1) + (bx >> 1) * (CL / 2)) * (1 << LB) + (bx & 1) * 4096 + int(rank & 1u) * 2048) /
+                          (128 / int(sizeof(TOut)))
                     : PUSH ? int(out_col((bx / (NOBOX / 2)) * 8) - tid + (bx % (NOBOX / 2)) * OBOX) /
                                  (128 / int(sizeof(TOut)))
                            : lout0 + bx * CH_OUT;
