@@ -1,33 +1,41 @@
 #!/usr/bin/env python
 """Benchmark: trellis-quantized weights/s on B200.
 
-Workload (the configuration the metric is quoted on, single GPU): a
-4096 x 4096 float32 weight matrix, N(0, 0.02^2) from seed 0 with 0.1 % of the
-entries replaced by +-8 sigma outliers, and a log-normal(0, 1) per-column
-imatrix.  One step runs the importance-weighted trellis recipe of
-buildtrellis.py -- A = W*sqrt(H), RHT (fp64), per-256 RMS, Viterbi with
-L = 16 state bits and T = 256, decode, inverse RHT, /sqrt(H), weighted-error
-statistics -- once at k = 2 and once at k = 3 bits/weight.  Synthetic, seeded
-inputs stand in for real checkpoints.
+Workload (the configuration the metric is quoted on): one 4096 x 4096 float32
+weight matrix, N(0, 0.02^2) from seed 0 with 0.1 % of the entries replaced by
++-8 sigma outliers, and a log-normal(0, 1) per-column imatrix.  One step runs
+the importance-weighted trellis recipe of buildtrellis.py -- A = W*sqrt(H),
+RHT (fp64), per-256 RMS, Viterbi with L = 16 state bits and T = 256, decode,
+inverse RHT, /sqrt(H), weighted-error statistics -- at k = 3 and at k = 2
+bits/weight, packs every sequence's state path into its L + R(T-1) bits, and
+ends with every rank holding the whole tensor's packed codes, per-256 scales
+and per-tensor error sums.  Synthetic, seeded inputs stand in for real
+checkpoints.
 
-value     : weights quantized per second (both k), inputs resident in HBM.
-e2e       : the same through the public host API (pinned host W in, host
-            What out, copies inside the timed region).
-roofline  : the Viterbi forward kernel against the FP32 lane peak, timed
-            live with CUDA events around its launches.
+Multi-GPU (torchrun, one process per GPU): the same tensor is split by row
+blocks across the ranks ("strong" scaling: the work per step is fixed); each
+rank quantizes its rows and the step ends with ONE NCCL all-gather of the
+packed codes, scales and error sums (the path's only exchange).  Time = max
+over ranks of the CUDA-event time; value = the tensor's weights (both k) per
+second.
+
+value     : weights quantized per second, inputs resident in HBM.
+e2e       : the same through the public API (ultraquant_b200.shard) with the
+            rank's rows in pinned host memory: host->device copies, the
+            quantization, the gather, and device->host copies of What and (rank
+            0) the gathered codes are all inside the timed region.
+roofline  : the Viterbi forward kernel (the step's dominant kernel) against a
+            MEASURED FP32 lane peak (uq_fp32_lane_probe, same process);
+            roofline_kernels: the RHT and E8 kernels against measured HBM.
 cpu_baseline / --impl reference : the CPU restatement of the reference's
             torch path (oracle/) on the host cores, on a bounded row sample.
-
-Multi-GPU (torchrun): every rank quantizes its own tensor (seed = rank, as the
-tensors of a model are independent); per-tensor error statistics are
-all-gathered over NCCL.  Time = max over ranks; value = all ranks' weights /
-that time ("weak" scaling).
 """
 from __future__ import annotations
 
 import argparse
 import json
 import os
+import platform
 import statistics
 import subprocess
 import sys
@@ -41,12 +49,14 @@ METRIC = "trellis-quantized weights/sec (L=16, T=256, k=2 and k=3, importance-we
 UNIT = "weights/s"
 ROWS = COLS = 4096
 L_BITS = 16
-KS = (2, 3)
+KS = (3, 2)
 SEG = 256
 GROUP = 256
-# ncu capture of viterbi_fwd_kernel<2,2> (profiles/viterbi_l16r2_ncu.md): DRAM
-# bytes per processed weight, used to scale to one full launch.
-NCU_TRAFFIC_BYTES_PER_WEIGHT = None
+HBM_FALLBACK_GBS = 6650.0
+
+# ncu (L=16, T=256, one launch of 296 sequences per k): DRAM read + write
+# bytes of viterbi_fwd_kernel per sequence (the traffic is the backpointers)
+NCU_DRAM_BYTES_PER_SEQ = {2: (1.252352e6 + 251.667968e6) / 296, 3: (1.233152e6 + 251.116544e6) / 296}
 
 
 def make_inputs(seed: int):
@@ -59,14 +69,46 @@ def make_inputs(seed: int):
     return W.astype(np.float32), H
 
 
-# ncu (L=16, T=256, one launch of 296 sequences): DRAM read + write bytes
-NCU_DRAM_BYTES_PER_SEQ = {2: (1.252352e6 + 251.667968e6) / 296, 3: (1.233152e6 + 251.116544e6) / 296}
-
-
 def ops_per_weight(L: int, R: int) -> int:
     """Algorithmic lane ops of one Viterbi step per weight: sub, mul, add per
     state plus (2^R - 1) compares per predecessor group."""
     return 3 * (1 << L) + ((1 << R) - 1) * (1 << (L - R))
+
+
+def measured_peaks():
+    """HBM GB/s from the pool's MEASURED_PEAKS.json, else the fallback figure."""
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            pk = json.load(f)
+        return float(pk["hbm_gbs"]), "measured (MEASURED_PEAKS.json hbm_gbs)"
+    except (OSError, ValueError, KeyError, TypeError):
+        return HBM_FALLBACK_GBS, "fallback 6.65 TB/s (no MEASURED_PEAKS.json)"
+
+
+def host_info():
+    import numpy as np
+    import torch
+    model = platform.processor() or ""
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    model = line.split(":", 1)[1].strip()
+                    break
+    except OSError:
+        pass
+    try:
+        affinity = len(os.sched_getaffinity(0))
+    except AttributeError:
+        affinity = os.cpu_count()
+    info = {"host_cpus": os.cpu_count(), "cpus_usable": affinity, "cpu_model": model,
+            "numpy": np.__version__, "torch": torch.__version__}
+    try:
+        import scipy
+        info["scipy"] = scipy.__version__
+    except ImportError:
+        pass
+    return info
 
 
 class ClockSampler:
@@ -106,13 +148,14 @@ class ClockSampler:
             os.unlink(self.f.name)
         except Exception:
             return None
-        sm, mx, reasons = [], [], set()
+        sm, mx, pw, reasons = [], [], [], set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for r in rows:
             r = [x.strip() for x in r]
             try:
                 sm.append(float(r[1]))
                 mx.append(float(r[2]))
+                pw.append(float(r[3]))
             except (ValueError, IndexError):
                 continue
             for nm, v in zip(names, r[5:9]):
@@ -121,11 +164,32 @@ class ClockSampler:
         if not sm:
             return None
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
-                "samples": len(sm)}
+                "samples": len(sm), "power_w_max": max(pw) if pw else None}
+
+
+def phys_gpu_index(local: int) -> int:
+    phys = os.environ.get("CUDA_VISIBLE_DEVICES", "")
+    parts = [p.strip() for p in phys.split(",")] if phys else []
+    return int(parts[local]) if local < len(parts) and parts[local].isdigit() else local
+
+
+# ---------------------------------------------------------------------------
+# CPU legs (reference arm, cpu_baseline)
+# ---------------------------------------------------------------------------
+def use_all_host_threads() -> int:
+    """torch.distributed.run sets OMP_NUM_THREADS=1 for every rank; the CPU
+    legs run on rank 0 alone, so give torch every core this process may use."""
+    import torch
+    try:
+        n = len(os.sched_getaffinity(0))
+    except AttributeError:
+        n = os.cpu_count() or 1
+    torch.set_num_threads(max(1, n))
+    return torch.get_num_threads()
 
 
 def cpu_reference_sample(W, H, rows: int):
-    """Oracle restatement of the reference path on `rows` rows (k=2 and k=3)."""
+    """Oracle restatement of the reference path on `rows` rows (k=3 and k=2)."""
     import numpy as np
     import torch
     import oracle as O
@@ -138,109 +202,408 @@ def cpu_reference_sample(W, H, rows: int):
 
 
 def run_reference(args, rank: int, world: int):
-    """--impl reference: the reference's CPU path (restated in oracle/) on the
-    host cores of rank 0; other ranks exit without work."""
+    """--impl reference: the reference's CPU path (its torch / numpy
+    operations restated in oracle/, bit-exact with the reference on the
+    golden vectors) on the host cores of rank 0; other ranks exit without
+    work."""
     if rank != 0:
         return
+    threads = use_all_host_threads()
     W, H = make_inputs(0)
     rows = args.cpu_rows
     for _ in range(args.warmup):
         cpu_reference_sample(W, H, rows)
-    tot_w, tot_t, cores = 0, 0.0, 1
+    tot_w, tot_t = 0, 0.0
     for _ in range(args.steps):
-        w, t, cores = cpu_reference_sample(W, H, rows)
+        w, t, _ = cpu_reference_sample(W, H, rows)
         tot_w += w
         tot_t += t
     value = tot_w / tot_t
-    sample = f"first {rows} rows of the 4096x4096 tensor ({rows * COLS} weights) at k=2 and k=3 per step"
+    sample = f"first {rows} rows of the 4096x4096 tensor ({rows * COLS} weights) at k=3 and k=2 per step"
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * tot_t / args.steps,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic", "config": workload_config(world),
-        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample,
+                         **host_info()},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
 
-def run_llama8b(args, rank: int, world: int, local: int):
-    """Whole Llama-3.1-8B-shaped weight set (32 x {q, k, v, o 4096/1024 x 4096,
-    gate/up 14336 x 4096, down 4096 x 14336}), Student-t(4) weights with std
-    0.02 and log-normal imatrix, trellis L=16 T=256 with k=3 on ffn_down /
-    attn_q / attn_output and k=2 elsewhere, sharded by tensor and row block
-    (strong scaling: the set is fixed).  ``--workload llama70b``: the
-    Llama-3-70B shapes (hidden 8192, k/v 1024 x 8192, ffn 28672), std 0.015,
-    uniform k=2.  Weights are generated on the device before the timed region."""
+# ---------------------------------------------------------------------------
+# measured peaks and per-kernel rooflines
+# ---------------------------------------------------------------------------
+def fp32_lane_peak(lib, dev, iters: int = 40000):
+    """Measured FP32 lane rate (uq_fp32_lane_probe, packed f32x2 sub/mul/add
+    chains on every SM): best of three launches after one warm-up."""
+    import ctypes
+    import torch
+    from ultraquant_b200 import _device as D, _lib
+    st = D.stream_handle(dev)
+    ops = ctypes.c_double()
+    out = {}
+    for mode, name in ((0, "packed_f32x2"), (1, "scalar_f32")):
+        _lib.check(lib.uq_fp32_lane_probe(mode, iters, ctypes.addressof(ops), st), "fp32 probe")
+        best = 0.0
+        for _ in range(3):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            _lib.check(lib.uq_fp32_lane_probe(mode, iters, ctypes.addressof(ops), st), "fp32 probe")
+            e1.record()
+            torch.cuda.synchronize()
+            best = max(best, ops.value / (e0.elapsed_time(e1) * 1e-3))
+        out[name] = best / 1e12
+    return out
+
+
+def hbm_kernel_rooflines():
+    """RHT / iRHT (fp64, 4096 columns and ffn_down's 14336 padded to 16384)
+    and the E8 quantizer at config 3's rotated shape (4096 x 16384, step
+    0.48): CUDA-event time per launch, L2 flushed between launches."""
+    from ultraquant_b200 import profile_case as PC
+    peak, src = measured_peaks()
+    cases = [("rht", 4096, 4096, 0), ("irht", 4096, 4096, 0), ("rht", 4096, 16384, 14336),
+             ("irht", 4096, 16384, 14336), ("e8", 4096, 16384, 0)]
+    out = []
+    for k, rows, n, n0 in cases:
+        rec = PC.measure(k, rows=rows, n=n, n0=n0, iters=5, hbm_peak=peak)
+        kern = {"rht": "rht_tma_kernel (forward)", "irht": "rht_tma_kernel (inverse)", "e8": "e8_tma_kernel"}[k]
+        out.append({"kernel": kern, "shape": f"{rows}x{n0 or n}" + (f" (padded to {n})" if n0 else ""),
+                    "dtype": "f64", "bound": "hbm", "achieved": rec["achieved_gbs"], "peak": peak, "unit": "GB/s",
+                    "frac": rec["achieved_gbs"] / peak, "peak_source": src,
+                    "bytes_per_launch": rec["algorithmic_bytes"], "ms_per_launch": rec["ms_per_run"]})
+    return out
+
+
+# ---------------------------------------------------------------------------
+# default workload: the 4096 x 4096 tensor at k=3 and k=2, row-split
+# ---------------------------------------------------------------------------
+def workload_config(world: int):
+    return {
+        "workload": ("4096x4096 f32 N(0,0.02^2)+0.1% 8-sigma outliers (seed 0), lognormal(0,1) imatrix; "
+                     "importance-weighted RHT(fp64) + bitshift-trellis Viterbi L=16 T=256 at k=3 and k=2, "
+                     "scale group 256, decode, iRHT, packed codes; rows split across ranks, NCCL all-gather of "
+                     "packed codes + scales + error sums"),
+        "rows": ROWS, "cols": COLS, "L": L_BITS, "k": list(KS), "T": SEG, "scale_group": GROUP,
+        "weights_per_step": ROWS * COLS * len(KS),
+        "parallelism": f"row blocks of {ROWS // world} rows x{world} ranks" + (" + all-gather" if world > 1 else ""),
+        "l2": "working set > L2: 4 KiB of backpointers per weight written each step",
+    }
+
+
+def run_tensor(args, rank: int, world: int, local: int):
+    import ctypes
+    import numpy as np
     import torch
     import torch.distributed as dist
-    from ultraquant_b200 import pipeline, shard
+
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if world > 1:
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
-    if args.workload == "llama70b":
-        specs = shard.llama_shapes(layers=args.layers, hidden=8192, kv=1024, ffn=28672,
-                                   k_by_type={t: 2 for t in ("attn_q", "attn_k", "attn_v", "attn_output",
-                                                             "ffn_gate", "ffn_up", "ffn_down")})
-        std = 0.015
-    else:
-        specs = shard.llama_shapes(layers=args.layers)
-        std = 0.02
-    plan = [s for s in shard.plan(specs, world) if s.rank == rank]
-    data = []
-    for sh in plan:
-        g = torch.Generator(device=dev)
-        g.manual_seed(sum(map(ord, sh.tensor.name)) * 1000 + sh.row0)
-        z = torch.randn((sh.rows, sh.tensor.cols), generator=g, device=dev)
-        chi = torch.randn((4, sh.rows, sh.tensor.cols), generator=g, device=dev).pow_(2).sum(0)
-        W = (z / torch.sqrt(chi / 4.0) / (2.0 ** 0.5) * std).float()
-        gh = torch.Generator(device=dev)
-        gh.manual_seed(sum(map(ord, sh.tensor.name)))
-        H = torch.exp(torch.randn(sh.tensor.cols, generator=gh, device=dev, dtype=torch.float64))
-        data.append((sh, W, H))
-        del z, chi
+
+    from ultraquant_b200 import _lib, shard
+    lib = _lib.load()
+
+    specs = [shard.TensorSpec(f"w.k{R}", ROWS, COLS, L=L_BITS, R=R) for R in KS]
+    block = -(-ROWS // world)
+    plan = shard.plan(specs, world, block_rows=block)
+    mine = [s for s in plan if s.rank == rank]
+    W, H = make_inputs(0)
+    r0 = min(s.row0 for s in mine) if mine else 0
+    r1 = max(s.row1 for s in mine) if mine else 0
+    Wd = torch.from_numpy(W[r0:r1]).to(dev)          # this rank's rows (device-resident)
+    Hd = torch.from_numpy(H).to(dev)
+
+    def weights_dev(s):
+        return Wd[s.row0 - r0:s.row1 - r0], Hd
+
+    def step():
+        loc = shard.quantize_shards(plan, rank, weights_dev, SEG, GROUP)
+        return shard.gather_codes(loc, plan, world, SEG, GROUP)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    for _ in range(max(args.warmup, 0)):
+        step()
     torch.cuda.synchronize()
+
+    # ---- timed region (device events, max over ranks) ----------------------
+    lib.uq_profile_reset()
+    lib.uq_profile_enable(1)
+    barrier()
+    torch.cuda.synchronize()
+    launches0 = int(lib.uq_launch_count())
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    with ClockSampler(phys_gpu_index(local)) as clk:
+        e0.record()
+        out = None
+        for _ in range(args.steps):
+            out = step()
+        e1.record()
+        torch.cuda.synchronize()
+    launches = int(lib.uq_launch_count()) - launches0
+    lib.uq_profile_enable(0)
+    ms = e0.elapsed_time(e1)
+    vt, vn = ctypes.c_double(), ctypes.c_int64()
+    _lib.check(lib.uq_profile_read(b"viterbi_fwd", ctypes.addressof(vt), ctypes.addressof(vn)), "profile")
+    lib.uq_profile_reset()
+    ms_t = torch.tensor([ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
+    ms_max = float(ms_t.item())
+    weights = ROWS * COLS * len(KS) * args.steps
+    value = weights / (ms_max / 1e3)
+
+    # ---- Viterbi roofline against the measured FP32 lane peak --------------
+    peak = fp32_lane_peak(lib, dev)
+    props = torch.cuda.get_device_properties(dev)
+    n_sm = props.multi_processor_count
+    clocks = clk.summary()
+    sm_max = (clocks or {}).get("sm_max_mhz") or 1965.0
+    nominal = n_sm * 128 * sm_max * 1e6 / 1e12
+    my_ops = sum(ops_per_weight(L_BITS, s.tensor.R) * s.rows * COLS for s in mine) * args.steps
+    vit_s = vt.value / 1e3
+    achieved = my_ops / vit_s / 1e12 if vit_s > 0 else 0.0
+    my_seqs = sum(s.rows * COLS // SEG for s in mine) * args.steps
+    roofline = {
+        "kernel": "viterbi_fwd_kernel", "bound": "fp32_alu", "achieved": achieved, "peak": peak["packed_f32x2"],
+        "unit": "Tops/s", "frac": achieved / peak["packed_f32x2"],
+        "peak_source": "measured: uq_fp32_lane_probe (packed f32x2 sub/mul/add chains, all SMs, CUDA events, "
+                       "same process, best of 3)",
+        "peak_scalar_f32": peak["scalar_f32"], "nominal_peak": nominal, "frac_of_nominal": achieved / nominal,
+        "ops_per_weight": {f"k{R}": ops_per_weight(L_BITS, R) for R in KS},
+        "launches": int(vn.value), "kernel_ms_total": vt.value, "share_of_step": vt.value / ms if ms else None,
+        # DRAM bytes per launch: one ncu capture of 296 sequences per k
+        # (dram__bytes_read.sum + dram__bytes_write.sum), scaled by the
+        # sequences of this run's launches (the traffic is the backpointers,
+        # proportional to the sequences)
+        "traffic": (sum(NCU_DRAM_BYTES_PER_SEQ[s.tensor.R] * s.rows * COLS // SEG for s in mine) * args.steps
+                    / max(1, int(vn.value))),
+        "traffic_unit": "bytes per launch",
+        "traffic_source": "ncu capture, 296 sequences per k, scaled by the sequences per launch",
+        "algorithmic_bytes_per_launch": my_seqs * (SEG - 1) * (1 << L_BITS) // 16 / max(1, int(vn.value)),
+    }
+    if clocks and clocks.get("sm_mhz"):
+        roofline["sm_mhz_median"] = clocks["sm_mhz"]
+
+    # ---- end to end through the public API with host buffers ---------------
+    e2e = None
+    if not args.no_e2e:
+        Wp = torch.from_numpy(W[r0:r1]).pin_memory()
+        Hp = torch.from_numpy(H)
+
+        def weights_host(s):
+            return Wp[s.row0 - r0:s.row1 - r0], Hp
+
+        what_host = {(s.tensor.name, s.row0): torch.empty((s.rows, COLS), dtype=torch.float32, pin_memory=True)
+                     for s in mine}
+        ref = step()
+        code_host = {k: (torch.empty(v.codes.shape, dtype=torch.int32, pin_memory=True),
+                         torch.empty(v.sc.shape, dtype=torch.float32, pin_memory=True),
+                         torch.empty(2, dtype=torch.float64, pin_memory=True)) for k, v in ref.items()}
+
+        def e2e_step():
+            loc = shard.quantize_shards(plan, rank, weights_host, SEG, GROUP, keep_what=True)
+            res = shard.gather_codes(loc, plan, world, SEG, GROUP)
+            for c in loc:
+                what_host[(c.shard.tensor.name, c.shard.row0)].copy_(c.What, non_blocking=True)
+            if rank == 0:
+                for k, v in res.items():
+                    hc, hs, he = code_host[k]
+                    hc.copy_(v.codes, non_blocking=True)
+                    hs.copy_(v.sc, non_blocking=True)
+                    he.copy_(v.err, non_blocking=True)
+            torch.cuda.current_stream(dev).synchronize()
+
+        e2e_step()
+        barrier()
+        torch.cuda.synchronize()
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        t0.record()
+        for _ in range(args.steps):
+            e2e_step()
+        t1.record()
+        torch.cuda.synchronize()
+        ems = torch.tensor([t0.elapsed_time(t1)], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(ems, op=dist.ReduceOp.MAX)
+        h2d = sum(s.rows * COLS * 4 + H.nbytes for s in mine)
+        d2h = sum(s.rows * COLS * 4 for s in mine)
+        if rank == 0:
+            d2h += sum(hc.numel() * 4 + hs.numel() * 4 + 16 for hc, hs, _ in code_host.values())
+        e2e = {"value": weights / (float(ems.item()) / 1e3), "unit": UNIT,
+               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+               "api": "ultraquant_b200.shard.quantize_shards(pinned host rows) + gather_codes -> "
+                      "pinned host What rows and (rank 0) packed codes, scales, error sums"}
+        # the e2e outputs equal the device-resident step's
+        for k, v in ref.items():
+            if rank == 0:
+                assert torch.equal(code_host[k][0], v.codes.cpu()), "e2e codes differ from the device-resident run"
+
+    cpu = None
+    kern_roof = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        threads = use_all_host_threads()
+        w, t, _ = cpu_reference_sample(W, H, args.cpu_rows)
+        cpu = {"value": w / t, "unit": UNIT, "cores": threads, "kind": "port",
+               "sample": f"first {args.cpu_rows} rows ({args.cpu_rows * COLS} weights) at k=3 and k=2, "
+                         "oracle restatement of the reference torch CPU path", **host_info()}
+    if rank == 0 and not args.no_kernel_rooflines:
+        kern_roof = hbm_kernel_rooflines()
+
     if world > 1:
         dist.barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    results = []
-    for sh, W, H in data:
-        r = pipeline.quant_trellis_device(W, H, L=16, R=sh.tensor.R, seg=SEG, scale_group=GROUP, keep_codes=False)
-        results.append(shard.ShardResult(sh, r.What, r.err))
-    e1.record()
-    torch.cuda.synchronize()
-    ms = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
-    wn = shard.gather_errors(results, specs)
-    weights = sum(s.rows * s.cols for s in specs)
     if rank == 0:
-        model = "Llama-3-70B" if args.workload == "llama70b" else "Llama-3.1-8B"
-        line = {"metric": f"{model}-shaped weight set trellis-quantized, wall time on device",
-                "value": float(ms.item()) / 1e3, "unit": "s", "n_gpus": world, "steps": 1, "warmup": 0,
-                "higher_is_better": False, "scaling": "strong", "weights": weights,
-                "weights_per_s": weights / (float(ms.item()) / 1e3), "layers": args.layers,
-                "wnmse_mean": {k: sum(v for n, v in wn.items() if f".{k}." in n) / max(1, sum(1 for n in wn if f".{k}." in n))
-                               for k in ("attn_q", "attn_k", "attn_v", "attn_output", "ffn_gate", "ffn_up", "ffn_down")},
-                "dtype": "f32", "data": "synthetic"}
+        cfg = workload_config(world)
+        cfg["wnmse"] = {k: v.wnmse for k, v in out.items()}
+        cfg["packed_code_bytes"] = {k: v.codes.numel() * 4 for k, v in out.items()}
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": cfg,
+            "roofline": roofline, "roofline_kernels": kern_roof, "cpu_baseline": cpu, "e2e": e2e,
+            "gpu_launches": launches, "clocks": clocks,
+        }
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
 
 
-def workload_config(world: int):
-    return {
-        "workload": ("4096x4096 f32 N(0,0.02^2)+0.1% 8-sigma outliers (seed=rank), lognormal(0,1) imatrix; "
-                     "importance-weighted RHT(fp64) + bitshift-trellis Viterbi L=16 T=256 at k=2 and k=3, "
-                     "scale group 256, decode, iRHT"),
-        "rows": ROWS, "cols": COLS, "L": L_BITS, "k": list(KS), "T": SEG, "scale_group": GROUP,
-        "weights_per_step_per_gpu": ROWS * COLS * len(KS),
-        "parallelism": f"one tensor per rank x{world}",
-        "l2": "working set > L2: 4 KiB of backpointers per weight written each step",
-    }
+# ---------------------------------------------------------------------------
+# whole weight sets: Llama-3.1-8B (config 4) and Llama-3-70B (config 5)
+# ---------------------------------------------------------------------------
+def _student_t_block(g, rows, cols, std, dev):
+    import torch
+    z = torch.randn((rows, cols), generator=g, device=dev)
+    chi = torch.randn((4, rows, cols), generator=g, device=dev).pow_(2).sum(0)
+    return (z / torch.sqrt(chi / 4.0) / (2.0 ** 0.5) * std).float()
+
+
+def run_weight_set(args, rank: int, world: int, local: int):
+    """Whole Llama-shaped weight sets, sharded by tensor and row block
+    (strong scaling: the set is fixed), trellis L=16 T=256; the run ends
+    with every rank holding every tensor's packed codes, scales and error
+    sums (one NCCL all-gather).
+
+    llama8b : 32 x {q, o 4096 x 4096, k, v 1024 x 4096, gate, up 14336 x 4096,
+              down 4096 x 14336}, Student-t(4) std 0.02, log-normal imatrix,
+              k=3 on ffn_down / attn_q / attn_output, k=2 elsewhere.  Weights
+              are generated on the device before the timed region.
+    llama70b: 80 x {q, o 8192 x 8192, k, v 1024 x 8192, gate, up 28672 x 8192,
+              down 8192 x 28672}, std 0.015, uniform k=2.  The set (274 GB in
+              f32) does not fit the GPUs at 2 ranks, so each rank streams its
+              row blocks: a block's weights are generated on the device just
+              before the block is quantized (standing in for the read from
+              host memory) and freed after it, inside the timed region."""
+    import ctypes
+    import torch
+    import torch.distributed as dist
+    from ultraquant_b200 import _lib, shard
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=dev)
+    lib = _lib.load()
+    stream_blocks = args.workload == "llama70b"
+    if args.workload == "llama70b":
+        specs = shard.llama_shapes(layers=args.layers, hidden=8192, kv=1024, ffn=28672,
+                                   k_by_type={t: 2 for t in ("attn_q", "attn_k", "attn_v", "attn_output",
+                                                             "ffn_gate", "ffn_up", "ffn_down")})
+        std = 0.015
+        model = "Llama-3-70B"
+    else:
+        specs = shard.llama_shapes(layers=args.layers)
+        std = 0.02
+        model = "Llama-3.1-8B"
+    plan = shard.plan(specs, world)
+    mine = [s for s in plan if s.rank == rank]
+    Hs = {}
+
+    def H_of(spec):
+        if spec.name not in Hs:
+            gh = torch.Generator(device=dev)
+            gh.manual_seed(sum(map(ord, spec.name)))
+            Hs[spec.name] = torch.exp(torch.randn(spec.cols, generator=gh, device=dev, dtype=torch.float64))
+        return Hs[spec.name]
+
+    def gen(s):
+        g = torch.Generator(device=dev)
+        g.manual_seed(sum(map(ord, s.tensor.name)) * 1000 + s.row0)
+        return _student_t_block(g, s.rows, s.tensor.cols, std, dev)
+
+    data = {} if stream_blocks else {(s.tensor.name, s.row0): gen(s) for s in mine}
+    for s in mine:
+        H_of(s.tensor)
+    torch.cuda.synchronize()
+
+    def weights(s):
+        W = gen(s) if stream_blocks else data[(s.tensor.name, s.row0)]
+        return W, Hs[s.tensor.name]
+
+    if world > 1:
+        dist.barrier()
+    lib.uq_profile_reset()
+    lib.uq_profile_enable(1)
+    launches0 = int(lib.uq_launch_count())
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(phys_gpu_index(local)) as clk:
+        e0.record()
+        loc = shard.quantize_shards(plan, rank, weights, SEG, GROUP)
+        out = shard.gather_codes(loc, plan, world, SEG, GROUP)
+        e1.record()
+        torch.cuda.synchronize()
+    launches = int(lib.uq_launch_count()) - launches0
+    lib.uq_profile_enable(0)
+    vt, vn = ctypes.c_double(), ctypes.c_int64()
+    _lib.check(lib.uq_profile_read(b"viterbi_fwd", ctypes.addressof(vt), ctypes.addressof(vn)), "profile")
+    lib.uq_profile_reset()
+    ms = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+    wall = float(ms.item()) / 1e3
+    weights_n = sum(s.rows * s.cols for s in specs)
+    peak = fp32_lane_peak(lib, dev)
+    my_ops = sum(ops_per_weight(s.tensor.L, s.tensor.R) * s.rows * s.tensor.padded_cols for s in mine)
+    achieved = my_ops / (vt.value / 1e3) / 1e12 if vt.value > 0 else 0.0
+    roofline = {"kernel": "viterbi_fwd_kernel", "bound": "fp32_alu", "achieved": achieved,
+                "peak": peak["packed_f32x2"], "unit": "Tops/s", "frac": achieved / peak["packed_f32x2"],
+                "peak_source": "measured: uq_fp32_lane_probe (packed f32x2), rank 0",
+                "launches": int(vn.value), "kernel_ms_total": vt.value,
+                "share_of_step": vt.value / (wall * 1e3) if wall else None}
+    if world > 1:
+        dist.barrier()
+    if rank == 0:
+        wn = {k: v.wnmse for k, v in out.items()}
+        line = {"metric": f"{model}-shaped weight set trellis-quantized weights/sec (L=16, T=256)",
+                "value": weights_n / wall, "unit": UNIT, "n_gpus": world, "steps": 1, "warmup": 0,
+                "ms_per_step": wall * 1e3, "wall_s": wall, "higher_is_better": True, "scaling": "strong",
+                "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+                "config": {"workload": f"{model}-shaped weight set, {args.layers} layers, {len(specs)} tensors"
+                                       + (", row blocks streamed (generated per block on the device)"
+                                          if stream_blocks else ", weights resident before timing"),
+                           "weights": weights_n, "layers": args.layers, "L": 16, "T": SEG,
+                           "parallelism": f"tensor x row-block plan over {world} ranks + all-gather of packed codes",
+                           "target": "< 60 s on 8 B200 for the Llama-3.1-8B set" if model == "Llama-3.1-8B" else None},
+                "wnmse_mean": {t: sum(v for n, v in wn.items() if f".{t}." in n) /
+                               max(1, sum(1 for n in wn if f".{t}." in n))
+                               for t in ("attn_q", "attn_k", "attn_v", "attn_output", "ffn_gate", "ffn_up",
+                                         "ffn_down")},
+                "packed_code_bytes": sum(v.codes.numel() * 4 for v in out.values()),
+                "roofline": roofline, "e2e": None,
+                "e2e_note": "weights generated on the device (no host copy of the set)",
+                "gpu_launches": launches, "clocks": clk.summary()}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
 
 
 def main():
@@ -252,8 +615,9 @@ def main():
     ap.add_argument("--cpu-rows", type=int, default=8, help="rows of the CPU baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-kernel-rooflines", action="store_true", help="skip the RHT / E8 roofline entries")
     ap.add_argument("--workload", default="tensor", choices=["tensor", "llama8b", "llama70b"],
-                    help="tensor: the 4096x4096 L=16 k=2+3 step (default); llama8b / llama70b: the "
+                    help="tensor: the 4096x4096 L=16 k=3+2 step (default); llama8b / llama70b: the "
                          "whole Llama-3.1-8B- / Llama-3-70B-shaped weight set sharded over the ranks (one step)")
     ap.add_argument("--layers", type=int, default=None,
                     help="layers of the llama workloads (default 32 for llama8b, 80 for llama70b)")
@@ -268,148 +632,8 @@ def main():
     if args.workload in ("llama8b", "llama70b"):
         if args.layers is None:
             args.layers = 80 if args.workload == "llama70b" else 32
-        return run_llama8b(args, rank, world, local)
-
-    import numpy as np
-    import torch
-    import torch.distributed as dist
-
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world > 1:
-        from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
-
-    from ultraquant_b200 import _lib, pipeline
-    lib = _lib.load()
-
-    W, H = make_inputs(rank)
-    Wd = torch.from_numpy(W).to(dev)
-    Hd = torch.from_numpy(H).to(dev)
-
-    def step():
-        errs = []
-        for R in KS:
-            r = pipeline.quant_trellis_device(Wd, Hd, L=L_BITS, R=R, seg=SEG, scale_group=GROUP)
-            errs.append(r.err)
-        return errs
-
-    def barrier():
-        if world > 1:
-            dist.barrier()
-
-    for _ in range(max(args.warmup, 0)):
-        step()
-    torch.cuda.synchronize()
-
-    # ---- timed region (device events, max over ranks) ----------------------
-    lib.uq_profile_reset()
-    lib.uq_profile_enable(1)
-    phys = os.environ.get("CUDA_VISIBLE_DEVICES", "")
-    phys_idx = int(phys.split(",")[local]) if phys and phys.split(",")[local].strip().isdigit() else local
-    barrier()
-    torch.cuda.synchronize()
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
-    with ClockSampler(phys_idx) as clk:
-        e0.record()
-        errs = None
-        for _ in range(args.steps):
-            errs = step()
-        e1.record()
-        torch.cuda.synchronize()
-    barrier()
-    lib.uq_profile_enable(0)
-    launches = int(lib.uq_launch_count())
-    ms = e0.elapsed_time(e1)
-    import ctypes
-    vt, vn = ctypes.c_double(), ctypes.c_int64()
-    _lib.check(lib.uq_profile_read(b"viterbi_fwd", ctypes.addressof(vt), ctypes.addressof(vn)), "profile")
-    lib.uq_profile_reset()
-    ms_t = torch.tensor([ms], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
-        # the path's only exchange: per-tensor error statistics of every rank
-        gathered = [torch.zeros(2 * len(KS), dtype=torch.float64, device=dev) for _ in range(world)]
-        dist.all_gather(gathered, torch.cat(errs))
-    ms_max = float(ms_t.item())
-    weights = ROWS * COLS * len(KS) * args.steps * world
-    value = weights / (ms_max / 1e3)
-
-    # ---- roofline of the Viterbi forward kernel ---------------------------
-    props = torch.cuda.get_device_properties(dev)
-    n_sm = props.multi_processor_count
-    clocks = clk.summary()
-    sm_max = (clocks or {}).get("sm_max_mhz") or 1965.0
-    peak_tops = n_sm * 128 * sm_max * 1e6 / 1e12
-    vit_ops = sum(ops_per_weight(L_BITS, R) for R in KS) * ROWS * COLS * args.steps
-    vit_s = vt.value / 1e3
-    achieved = vit_ops / vit_s / 1e12 if vit_s > 0 else 0.0
-    roofline = {
-        "kernel": "viterbi_fwd_kernel", "bound": "fp32_alu", "achieved": achieved, "peak": peak_tops,
-        "unit": "Tops/s", "frac": achieved / peak_tops,
-        "peak_source": f"nominal FP32 lanes: {n_sm} SMs x 128 x {sm_max:.0f} MHz (no measured FP32 peak on file)",
-        "ops_per_weight": {f"k{R}": ops_per_weight(L_BITS, R) for R in KS},
-        "launches": int(vn.value), "kernel_ms_total": vt.value, "share_of_step": vt.value / ms if ms else None,
-        # DRAM bytes per launch: one ncu capture of 296 sequences per k
-        # (dram__bytes_read.sum + dram__bytes_write.sum), scaled by the
-        # sequences of the bench's launches (the traffic is the backpointers,
-        # proportional to the sequences)
-        "traffic": (sum(NCU_DRAM_BYTES_PER_SEQ[R] for R in KS) / len(KS)
-                    * (ROWS * COLS // SEG) * len(KS) * args.steps / max(1, int(vn.value))),
-        "traffic_unit": "bytes per launch",
-        "traffic_source": "ncu capture, 296 sequences per k, scaled by sequences per launch",
-    }
-    if clocks and clocks.get("sm_mhz"):
-        roofline["frac_at_measured_clock"] = achieved / (n_sm * 128 * clocks["sm_mhz"] * 1e6 / 1e12)
-
-    # ---- end to end through the public host API ---------------------------
-    e2e = None
-    if not args.no_e2e:
-        Wp = torch.from_numpy(W).pin_memory()
-        Hp = torch.from_numpy(H)
-        pipeline.quant_trellis(Wp, Hp, L=L_BITS, R=KS[0], seg=SEG, scale_group=GROUP)
-        barrier()
-        torch.cuda.synchronize()
-        t0 = torch.cuda.Event(enable_timing=True)
-        t1 = torch.cuda.Event(enable_timing=True)
-        t0.record()
-        for _ in range(args.steps):
-            for R in KS:
-                pipeline.quant_trellis(Wp, Hp, L=L_BITS, R=R, seg=SEG, scale_group=GROUP)
-        t1.record()
-        torch.cuda.synchronize()
-        ems = torch.tensor([t0.elapsed_time(t1)], dtype=torch.float64, device=dev)
-        if world > 1:
-            dist.all_reduce(ems, op=dist.ReduceOp.MAX)
-        e2e = {"value": weights / (float(ems.item()) / 1e3), "unit": UNIT,
-               "h2d_bytes_per_step": len(KS) * (W.nbytes + H.nbytes),
-               "d2h_bytes_per_step": len(KS) * W.nbytes,
-               "api": "ultraquant_b200.pipeline.quant_trellis(pinned host W, host H) -> pinned host What"}
-
-    cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        w, t, cores = cpu_reference_sample(W, H, args.cpu_rows)
-        cpu = {"value": w / t, "unit": UNIT, "cores": cores, "kind": "port",
-               "sample": f"first {args.cpu_rows} rows ({args.cpu_rows * COLS} weights) at k=2 and k=3, "
-                         "oracle restatement of the reference torch CPU path"}
-
-    if world > 1:
-        dist.barrier()
-    if rank == 0:
-        err = torch.cat(errs).double().cpu().numpy()
-        cfg = workload_config(world)
-        cfg["wnmse"] = {f"k{R}": float(err[2 * i] / err[2 * i + 1]) for i, R in enumerate(KS)}
-        line = {
-            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": cfg,
-            "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches,
-            "clocks": clocks,
-        }
-        print(json.dumps(line), flush=True)
-    if world > 1:
-        dist.destroy_process_group()
+        return run_weight_set(args, rank, world, local)
+    return run_tensor(args, rank, world, local)
 
 
 if __name__ == "__main__":

@@ -6,8 +6,7 @@
  * The reference exposes this path as plain Python module functions on numpy
  * arrays (qlab.py, trellis.py, qat.py).  Each entry point below names the
  * reference function it replaces.  The Python package ``ultraquant_b200``
- * wraps these calls in the reference's exact signatures; a ctypes binding is
- * shown in INTEGRATION.md.
+ * wraps these calls in the reference's exact signatures through ctypes.
  *
  * Conventions
  *  - All array pointers are DEVICE pointers unless the name ends in _host.
@@ -337,15 +336,25 @@ int uq_quant_e8_b28(const void *W, int w_dtype, int64_t rows, int64_t n0, int64_
  * ------------------------------------------------------------------- */
 
 /* Synchronises `stream` and reports (and clears) a timeout of a bounded
- * device wait in the cluster-split Viterbi kernel (UQ_ERR_TIMEOUT) or a
- * state outside the codebook given to the QAT decoder (UQ_ERR_INVALID)
- * since the last call; else UQ_OK. */
+ * device wait in the cluster-split Viterbi kernel or the tensor-map RHT / E8
+ * kernels (UQ_ERR_TIMEOUT) or a state outside the codebook given to the QAT
+ * decoder (UQ_ERR_INVALID) since the last call; else UQ_OK.  A timed-out
+ * wait lets its kernel run to the end with wrong results, so callers of
+ * uq_quant_trellis / uq_quant_e8 / uq_trellis_viterbi / uq_rht_rows check
+ * this before using the outputs (the Python layer does so after every
+ * call). */
 int uq_device_errors(void *stream);
 
 /* Runs a one-warp kernel that waits on an mbarrier phase nothing completes;
  * the bounded wait gives up after limit_ms (<= 2000).  Returns
  * UQ_ERR_TIMEOUT when the bound worked (the expected outcome). */
 int uq_wait_timeout_selftest(double limit_ms, void *stream);
+
+/* Fault injection on the host: sets the timeout flag that a bounded device
+ * wait sets when it gives up (which = 0: the cluster-split Viterbi exchange,
+ * 1: the tensor-map RHT, 2: the tensor-map E8 quantizer), so that tests can
+ * check that the next uq_device_errors reports it.  No kernel runs. */
+int uq_inject_device_flag(int which);
 
 /* ---------------------------------------------------------------------
  * Instrumentation (no counterpart in the reference; used by bench.py)
@@ -360,6 +369,13 @@ int64_t uq_launch_count(void);
 /* Synchronises the recorded events of `kernel`; returns the number of
  * launches and their summed device time in milliseconds. */
 int uq_profile_read(const char *kernel, double *total_ms, int64_t *launches);
+
+/* Measured denominator of the Viterbi forward's roofline: one launch of a
+ * kernel that runs only independent float32 sub / mul / add chains (mode 0:
+ * the packed f32x2 forms the Viterbi uses; mode 1: scalar forms) with every
+ * SM fully occupied.  Writes the lane operations the launch performs to
+ * *lane_ops_host; the caller times the launch with CUDA events on `stream`. */
+int uq_fp32_lane_probe(int mode, int64_t iters, double *lane_ops_host, void *stream);
 
 #ifdef __cplusplus
 }

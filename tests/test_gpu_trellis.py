@@ -220,3 +220,49 @@ def test_viterbi_small_workspace_batches(L, R, nseq, fit):
     torch.cuda.synchronize()
     assert torch.equal(small, full)
     assert int(full.min()) >= 0 and int(full.max()) < (1 << L)
+
+
+def test_pipeline_reports_injected_device_timeouts():
+    """A bounded device wait that gave up leaves its kernel's outputs wrong;
+    the production wrappers must raise instead of returning them.  The flag
+    is set on the host (no kernel is made to time out here), and the next
+    call after the report runs clean."""
+    import torch
+    from ultraquant_b200 import _lib, pipeline as P, qlab as Q
+    lib = _lib.load()
+    rng = np.random.RandomState(3)
+    W = torch.from_numpy(rng.normal(0, 0.02, size=(8, 4096)).astype(np.float32)).cuda()
+    H = torch.from_numpy(np.exp(rng.normal(0, 1, size=4096))).cuda()
+    calls = [lambda: P.quant_trellis_device(W, H, 16, 2, 256, 256),
+             lambda: P.quant_step_device(W, H, 0.48),
+             lambda: Q.rht_rows(W.double())]
+    for which in (0, 1, 2):
+        for call in calls:
+            assert lib.uq_inject_device_flag(which) == _lib.UQ_OK
+            with pytest.raises(_lib.UQError, match="timed out"):
+                call()
+            call()   # flag cleared by the report
+    assert lib.uq_inject_device_flag(7) == _lib.UQ_ERR_INVALID
+
+
+def test_sharded_codes_match_whole_tensor():
+    """shard.quantize_shards + gather_codes over several row blocks (one
+    process) give the packed codes, scales and weighted NMSE of the whole
+    tensor quantized in one call, and the codes unpack to its states."""
+    import torch
+    from ultraquant_b200 import pipeline as P, shard as S, trellis as Tr
+    rng = np.random.RandomState(5)
+    rows, cols = 1536, 4096
+    W = torch.from_numpy(rng.normal(0, 0.02, size=(rows, cols)).astype(np.float32)).cuda()
+    H = torch.from_numpy(np.exp(rng.normal(0, 1, size=cols))).cuda()
+    for R in (2, 3):
+        spec = S.TensorSpec(f"t{R}", rows, cols, L=16, R=R)
+        plan = S.plan([spec], 1, block_rows=512)
+        assert len(plan) == 3
+        loc = S.quantize_shards(plan, 0, lambda s: (W[s.row0:s.row1], H), 256, 256)
+        out = S.gather_codes(loc, plan, 1, 256, 256)[spec.name]
+        whole = P.quant_trellis_device(W, H, 16, R, 256, 256)
+        assert torch.equal(out.codes, Tr.pack_states(whole.states, 16, R))
+        assert torch.equal(Tr.unpack_states(out.codes, 256, 16, R), whole.states)
+        assert torch.equal(out.sc.view(torch.int32), whole.sc.view(torch.int32))
+        assert abs(out.wnmse - whole.wnmse) <= 1e-12 * whole.wnmse

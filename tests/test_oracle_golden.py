@@ -77,6 +77,52 @@ def test_trellis_fast_and_encode(g_trellis, tag):
     assert same_bits(O.trellis_decode(st, cw, sc_g, meta), rec)
 
 
+@pytest.mark.parametrize("tag", TQ)
+def test_c_viterbi_golden(g_trellis, tag):
+    """The C restatement of the Viterbi (oracle/uq_viterbi_ref.c) returns the
+    reference's state paths on every golden configuration."""
+    from oracle import cviterbi as CV
+    from oracle.uq_oracle import _flat_normalise
+    A = g_trellis[f"tq_{tag}_in"]
+    L, R, seg, group = (int(v) for v in g_trellis[f"tq_{tag}_cfg"])
+    xn, _, _, _ = _flat_normalise(A, seg, group)
+    assert np.array_equal(CV.viterbi_segments_c(xn, L, R), g_trellis[f"tq_{tag}_states"])
+
+
+@pytest.mark.parametrize("L,R,T", [(6, 1, 32), (8, 4, 64), (11, 3, 256), (12, 2, 1), (12, 2, 2), (14, 2, 64),
+                                   (16, 2, 64), (16, 3, 32)])
+def test_c_viterbi_vs_torch_restatement(L, R, T):
+    """C and torch restatements agree on random and tie-provoking sequences;
+    the fp32 path cost of the C path equals the minimum final cost."""
+    from oracle import cviterbi as CV
+    rng = np.random.RandomState(L * 100 + R * 10 + T)
+    x = rng.randn(6, T).astype(np.float32)
+    x[:3] = np.round(x[:3] * 2) / 2
+    st = CV.viterbi_segments_c(x, L, R, threads=2)
+    assert np.array_equal(st, O.viterbi_segments(x, L, R))
+    # the path cost matches an independent evaluation of the same recurrence
+    cw = O.codebook(L)
+    acc = np.zeros(6, np.float32)
+    for t in range(T):
+        d = (x[:, t] - cw[st[:, t]]).astype(np.float32)
+        acc = (d * d + acc).astype(np.float32) if t else (d * d).astype(np.float32)
+    assert np.array_equal(CV.path_costs(x, st, L).view(np.int32), acc.view(np.int32))
+
+
+def test_product_pred_table(g_trellis):
+    """ultraquant_b200.trellis.pred_table (trellis.py:21-25) against the
+    reference's table and the oracle, for every (L, R) the Viterbi builds."""
+    from ultraquant_b200 import trellis as T
+    assert np.array_equal(T.pred_table(8, 2), g_trellis["pred_8_2"])
+    for L, R in [(6, 1), (8, 3), (10, 2), (12, 2), (12, 4), (16, 2), (16, 3)]:
+        p = T.pred_table(L, R)
+        assert p.shape == (1 << L, 1 << R)
+        assert np.array_equal(p, O.pred_table(L, R))
+        # every state's predecessors shift into it: ((pred << R) | (s & mask)) mod 2^L == s
+        s = np.arange(1 << L)[:, None]
+        assert np.array_equal(((p << R) | (s & ((1 << R) - 1))) & ((1 << L) - 1), np.broadcast_to(s, p.shape))
+
+
 @pytest.mark.parametrize("tag", ["r8", "r10"])
 def test_trellis_full_row(g_trellis, tag):
     A = g_trellis[f"tr_{tag}_in"]

@@ -174,3 +174,62 @@ def test_gloo_sharded_e8_calibration_matches_single_process(tmp_path):
                        start_method="spawn")
     for r in range(2):
         assert torch.load(tmp_path / f"step{r}.pt") == cache["k"]
+
+
+# ---- packed trellis codes of row-sharded tensors (qat.py:11-33 codes) ---------
+CODE_SPECS = [S.TensorSpec("c0", 24, 256, L=8, R=2), S.TensorSpec("c1", 16, 300, L=8, R=3),
+              S.TensorSpec("c2", 8, 512, L=6, R=1)]
+SEG, GROUP = 64, 256
+
+
+def _oracle_codes(spec, W, H):
+    """Oracle trellis recipe on a block of rows: packed codes, scales, error sums."""
+    Hc = np.maximum(H, H.max() * 1e-3)
+    sH = np.sqrt(Hc)[None, :]
+    A = W * sH
+    Ar = O.rht_rows(A)
+    st, sc_g, cw, meta = O.trellis_encode(Ar, L=spec.L, R=spec.R, seg=SEG, scale_group=GROUP)
+    Ah = O.irht_rows(O.trellis_decode(st, cw, sc_g, meta), W.shape[1])
+    err = torch.tensor([np.sum((A - Ah) ** 2), np.sum(A ** 2)], dtype=torch.float64)
+    codes = torch.from_numpy(O.pack_states(st, spec.L, spec.R).view(np.int32))
+    return st, codes, torch.from_numpy(sc_g.reshape(-1).astype(np.float32)), err
+
+
+def _codes_worker(rank, world, port, out_dir):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    import datetime
+    import torch.distributed as dist
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=30))
+    try:
+        shards = S.plan(CODE_SPECS, world, block_rows=8)
+        local = []
+        for s in shards:
+            if s.rank == rank:
+                W, H = _weights(s.tensor, s.row0, s.row1)
+                _, codes, sc, err = _oracle_codes(s.tensor, W, H)
+                local.append(S.ShardCodes(s, codes, sc, err))
+        out = S.gather_codes(local, shards, world, seg=SEG, group=GROUP)
+        torch.save({k: (v.codes, v.sc, v.err) for k, v in out.items()}, os.path.join(out_dir, f"codes{rank}.pt"))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_gloo_gathered_codes_unpack_to_single_process_states(tmp_path):
+    """Two ranks quantize interleaved row blocks of three tensors; after the
+    one all-gather, both ranks hold packed codes that unpack to the states of
+    the whole tensor quantized in one process, with its scales, and the
+    block error sums add up to its weighted NMSE."""
+    mp.start_processes(_codes_worker, args=(2, _free_port(), str(tmp_path)), nprocs=2, join=True,
+                       start_method="spawn")
+    shards = S.plan(CODE_SPECS, 2, block_rows=8)
+    assert {s.rank for s in shards} == {0, 1}
+    for r in range(2):
+        got = torch.load(tmp_path / f"codes{r}.pt")
+        for spec in CODE_SPECS:
+            W, H = _weights(spec, 0, spec.rows)
+            st, codes, sc, err = _oracle_codes(spec, W, H)
+            gc, gsc, gerr = got[spec.name]
+            assert torch.equal(gc, codes), spec.name
+            assert np.array_equal(O.unpack_states(gc.numpy().view(np.uint32), SEG, spec.L, spec.R), st)
+            assert torch.equal(gsc.view(torch.int32), sc.view(torch.int32))
+            assert abs(float(gerr[0] / gerr[1]) - float(err[0] / err[1])) <= 1e-12 * float(err[0] / err[1])

@@ -78,10 +78,12 @@ SIGNATURES = {
     "uq_quant_e8_b28": (_i32, [_p, _i32, _i64, _i64, _i64, _p, _f64, _p, _p, _p, _p, _p, _sz, _p]),
     "uq_device_errors": (_i32, [_p]),
     "uq_wait_timeout_selftest": (_i32, [_f64, _p]),
+    "uq_inject_device_flag": (_i32, [_i32]),
     "uq_profile_enable": (None, [_i32]),
     "uq_profile_reset": (None, []),
     "uq_launch_count": (_i64, []),
     "uq_profile_read": (_i32, [ctypes.c_char_p, _p, _p]),
+    "uq_fp32_lane_probe": (_i32, [_i32, _i64, _p, _p]),
 }
 
 _lock = threading.Lock()

@@ -21,7 +21,7 @@ CSRC = os.path.join(HERE, "csrc")
 OUT = os.path.join(HERE, "_build")
 LIB = os.path.join(HERE, "libuq_b200.so")
 
-SOURCES = ["uq_host.cpp", "uq_rht.cu", "uq_e8.cu", "uq_trellis.cu", "uq_pipeline.cu", "uq_qat.cu", "uq_q8.cu", "uq_qe8.cu"]
+SOURCES = ["uq_host.cpp", "uq_rht.cu", "uq_e8.cu", "uq_trellis.cu", "uq_pipeline.cu", "uq_qat.cu", "uq_q8.cu", "uq_qe8.cu", "uq_peak.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-fmad=false", "-Xcompiler", "-fPIC",
               "-Xcompiler", "-O2", "--expt-relaxed-constexpr"]
@@ -45,7 +45,7 @@ def build(verbose: bool = False, ptxas_info: bool = False) -> str:
     os.makedirs(OUT, exist_ok=True)
     headers = [os.path.join(CSRC, f) for f in os.listdir(CSRC) if f.endswith((".h", ".cuh"))]
     headers.append(os.path.join(HERE, "..", "include", "uq_b200.h"))
-    objs = []
+    objs, jobs = [], []
     for src in SOURCES:
         path = os.path.join(CSRC, src)
         obj = os.path.join(OUT, src + ".o")
@@ -57,11 +57,21 @@ def build(verbose: bool = False, ptxas_info: bool = False) -> str:
             cmd.insert(1, "-Xptxas=-v")
         if verbose:
             print(" ".join(cmd), flush=True)
+        jobs.append((src, cmd))
+
+    def compile_one(job):
+        src, cmd = job
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"nvcc failed for {src}:\n{r.stdout}\n{r.stderr}")
-        if ptxas_info:
-            sys.stderr.write(r.stderr)
+        return r.stderr
+
+    # one nvcc per translation unit, in parallel
+    from concurrent.futures import ThreadPoolExecutor
+    with ThreadPoolExecutor(max_workers=max(1, min(len(jobs), os.cpu_count() or 1))) as ex:
+        for err in ex.map(compile_one, jobs):
+            if ptxas_info:
+                sys.stderr.write(err)
     if _stale(LIB, objs):
         cmd = [nvcc(), *ARCH, "-shared", "-cudart", "static", "-o", LIB, *objs]
         r = subprocess.run(cmd, capture_output=True, text=True)

@@ -22,6 +22,8 @@ int num_sms();
 int qat_take_bad_state();   // uq_qat.cu
 int rht_take_timeout();     // uq_rht.cu
 int e8_take_timeout();      // uq_e8.cu
+int rht_set_timeout();      // uq_rht.cu (fault injection)
+int e8_set_timeout();       // uq_e8.cu (fault injection)
 
 // Launch accounting / optional per-launch event timing (see uq_profile_*).
 void count_launch();

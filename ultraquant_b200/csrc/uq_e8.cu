@@ -580,6 +580,12 @@ int e8_take_timeout() {
     return flag;
 }
 
+// Sets the flag as a timed-out wait would (host-side fault injection).
+int e8_set_timeout() {
+    const int one = 1;
+    return cudaMemcpyToSymbol(g_e8_timeout, &one, sizeof(int)) == cudaSuccess ? 0 : -1;
+}
+
 int e8_quant(const void *A, int a_dtype, int64_t size, int64_t group, double step, double *rec,
              int16_t *idx, double *rms_out, cudaStream_t st) {
     E8Args a{};

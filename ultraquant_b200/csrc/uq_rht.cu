@@ -1133,6 +1133,12 @@ int rht_take_timeout() {
     return flag;
 }
 
+// Sets the flag as a timed-out wait would (host-side fault injection).
+int rht_set_timeout() {
+    const int one = 1;
+    return cudaMemcpyToSymbol(g_rht_timeout, &one, sizeof(int)) == cudaSuccess ? 0 : -1;
+}
+
 int64_t rht_tiles(int64_t rows, int64_t n) {
     const int b = ilog2(n);
     if (b >= 13) return 4 * rows;   // at most one partial per CTA of a row's cluster

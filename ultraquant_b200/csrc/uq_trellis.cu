@@ -1156,6 +1156,21 @@ int uq_device_errors(void *stream) {
     return UQ_OK;
 }
 
+int uq_inject_device_flag(int which) {
+    int rc = -1;
+    if (which == 0) {
+        const int one = 1;
+        rc = cudaMemcpyToSymbol(g_vit_timeout, &one, sizeof(int)) == cudaSuccess ? 0 : -1;
+    } else if (which == 1) {
+        rc = uq::rht_set_timeout();
+    } else if (which == 2) {
+        rc = uq::e8_set_timeout();
+    } else {
+        return uq::fail(UQ_ERR_INVALID, "uq_inject_device_flag: which=%d not in {0, 1, 2}", which);
+    }
+    return rc ? uq::check_cuda("uq_inject_device_flag") : UQ_OK;
+}
+
 int uq_wait_timeout_selftest(double limit_ms, void *stream) {
     if (!(limit_ms > 0.0) || limit_ms > 2000.0) return uq::fail(UQ_ERR_INVALID, "limit_ms must be in (0, 2000]");
     cudaStream_t st = UQ_STREAM(stream);

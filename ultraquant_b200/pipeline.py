@@ -31,9 +31,17 @@ class QuantResult:
         return float(e[0] / e[1])
 
 
+def _device_status(lib, dev, what):
+    """Raise if a bounded device wait of the kernels just launched gave up
+    (their outputs would be wrong).  Synchronises the stream."""
+    _lib.check(lib.uq_device_errors(D.stream_handle(dev)), what)
+
+
 def quant_trellis_device(W: torch.Tensor, H: torch.Tensor, L=12, R=2, seg=64, scale_group=256, seed=0,
-                         keep_codes=True) -> QuantResult:
-    """Device-resident buildtrellis recipe (W float32/float64, H float64)."""
+                         keep_codes=True, check_errors=True) -> QuantResult:
+    """Device-resident buildtrellis recipe (W float32/float64, H float64).
+    ``check_errors``: after the launch, synchronise and raise UQError if a
+    bounded device wait timed out (their results would be wrong)."""
     lib = _lib.load()
     dev = W.device
     rows, n0 = W.shape
@@ -53,11 +61,13 @@ def quant_trellis_device(W: torch.Tensor, H: torch.Tensor, L=12, R=2, seg=64, sc
                                     scale_group, d.data_ptr(), cw.data_ptr(), What.data_ptr(), D.ptr(states),
                                     D.ptr(sc), err.data_ptr(), ws.data_ptr(), ws.numel(), D.stream_handle(dev)),
                "uq_quant_trellis")
+    if check_errors:
+        _device_status(lib, dev, "uq_quant_trellis")
     return QuantResult(What, err, states, sc)
 
 
 def quant_step_device(W: torch.Tensor, H: torch.Tensor, step: float, group=256, seed=0,
-                      keep_codes=False, block28=False) -> QuantResult:
+                      keep_codes=False, block28=False, check_errors=True) -> QuantResult:
     """Device-resident buildalloc recipe (E8 at a fixed step).  ``block28``
     (opt-in, widths 28 x 512 / 28 x 1024, groups of 256): the unpadded
     block-factorised transform, error sums in the rotated domain."""
@@ -77,6 +87,8 @@ def quant_step_device(W: torch.Tensor, H: torch.Tensor, step: float, group=256, 
         _lib.check(lib.uq_quant_e8_b28(W.data_ptr(), D.dtype_code(W), rows, n0, n0, H.data_ptr(), float(step),
                                        d.data_ptr(), What.data_ptr(), D.ptr(idx), err.data_ptr(), ws.data_ptr(),
                                        ws.numel(), D.stream_handle(dev)), "uq_quant_e8_b28")
+        if check_errors:
+            _device_status(lib, dev, "uq_quant_e8_b28")
         return QuantResult(What, err, idx=idx)
     n = int(lib.uq_next_pow2(n0))
     H = H.to(device=dev, dtype=torch.float64).contiguous()
@@ -90,6 +102,8 @@ def quant_step_device(W: torch.Tensor, H: torch.Tensor, step: float, group=256, 
     _lib.check(lib.uq_quant_e8(W.data_ptr(), D.dtype_code(W), rows, n0, n0, H.data_ptr(), float(step), group,
                                d.data_ptr(), What.data_ptr(), D.ptr(idx), err.data_ptr(), ws.data_ptr(),
                                ws.numel(), D.stream_handle(dev)), "uq_quant_e8")
+    if check_errors:
+        _device_status(lib, dev, "uq_quant_e8")
     return QuantResult(What, err, idx=idx)
 
 

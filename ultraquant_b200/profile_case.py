@@ -158,6 +158,66 @@ def build_case(args, lib, st):
     raise SystemExit(f"unknown kernel {k}")
 
 
+def measure(kernel: str, rows: int = 4096, n: int = 4096, n0: int = 0, L: int = 16, R: int = 2, bpw: float = 2.0,
+            iters: int = 10, hbm_peak: float | None = None) -> dict:
+    """Time one case: a warm-up launch, then ``iters`` runs with a buffer
+    larger than L2 rewritten before each (cold inputs), CUDA events around
+    every launch of the case's kernel.  Returns the JSON record of main()."""
+    args = argparse.Namespace(kernel=kernel, rows=rows, n=n, n0=n0, L=L, R=R, bpw=bpw, iters=iters)
+    lib = _lib.load()
+    dev = D.device()
+    st = D.stream_handle(dev)
+    run, units, unit = build_case(args, lib, st)
+    run()
+    torch.cuda.synchronize()
+    if iters <= 0:
+        return {"kernel": kernel, "ok": True}
+    # a buffer larger than L2 rewritten between launches keeps the inputs cold
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    lib.uq_profile_enable(1)
+    lib.uq_profile_reset()
+    for _ in range(iters):
+        flush.fill_(1)
+        run()
+    torch.cuda.synchronize()
+    tot = _lib.ctypes.c_double(0.0)
+    cnt = _lib.ctypes.c_int64(0)
+    _lib.check(lib.uq_profile_read(SCOPE[kernel].encode(), _lib.ctypes.byref(tot), _lib.ctypes.byref(cnt)),
+               "profile")
+    rec = {"kernel": kernel, "rows": rows, "n": n0 or n, "runs": iters, "launches": cnt.value}
+    if kernel == "qe8":
+        # every kernel of the call, and the call as a whole (events on the stream)
+        for scope in ("e8_quant", "qe8_cb_norm", "qe8_classify", "qe8_search", "qe8_exact"):
+            t, c = _lib.ctypes.c_double(0.0), _lib.ctypes.c_int64(0)
+            _lib.check(lib.uq_profile_read(scope.encode(), _lib.ctypes.byref(t), _lib.ctypes.byref(c)), "profile")
+            rec[f"ms_{scope}"] = t.value / iters
+        lib.uq_profile_enable(0)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        flush.fill_(1)
+        e0.record()
+        run()
+        e1.record()
+        torch.cuda.synchronize()
+        rec["ms_call"] = e0.elapsed_time(e1)
+        rec["bpw"] = bpw
+        rec["weights_per_s"] = rows * n / (rec["ms_call"] * 1e-3)
+    lib.uq_profile_enable(0)
+    lib.uq_profile_reset()
+    _lib.check(lib.uq_device_errors(st), kernel)
+    ms = tot.value / iters            # device time of the kernel per run (all its launches)
+    rec["ms_per_run"] = ms
+    if unit == "bytes":
+        peak, kind = (hbm_peak, "given") if hbm_peak else _peaks()
+        gbs = units / (ms * 1e-3) / 1e9
+        rec.update(algorithmic_bytes=units, achieved_gbs=gbs, peak_gbs=peak, frac=gbs / peak, peak_kind=kind)
+    else:
+        props = torch.cuda.get_device_properties(dev)
+        nominal = props.multi_processor_count * 128 * 1965e6
+        tops = units / (ms * 1e-3)
+        rec.update(lane_ops=units, achieved_tops=tops / 1e12, frac_of_nominal_fp32=tops / nominal, L=L, R=R)
+    return rec
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("kernel", choices=sorted(SCOPE))
@@ -169,59 +229,7 @@ def main(argv=None):
     ap.add_argument("--bpw", type=float, default=2.0, help="rate of the qe8 case")
     ap.add_argument("--iters", type=int, default=10)
     args = ap.parse_args(argv)
-    lib = _lib.load()
-    dev = D.device()
-    st = D.stream_handle(dev)
-    run, units, unit = build_case(args, lib, st)
-    run()
-    torch.cuda.synchronize()
-    if args.iters <= 0:
-        print(json.dumps({"kernel": args.kernel, "ok": True}))
-        return
-    # a buffer larger than L2 rewritten between launches keeps the inputs cold
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
-    lib.uq_profile_enable(1)
-    lib.uq_profile_reset()
-    for _ in range(args.iters):
-        flush.fill_(1)
-        run()
-    torch.cuda.synchronize()
-    tot = _lib.ctypes.c_double(0.0)
-    cnt = _lib.ctypes.c_int64(0)
-    _lib.check(lib.uq_profile_read(SCOPE[args.kernel].encode(), _lib.ctypes.byref(tot), _lib.ctypes.byref(cnt)),
-               "profile")
-    rec = {"kernel": args.kernel, "rows": args.rows, "n": args.n0 or args.n, "runs": args.iters,
-           "launches": cnt.value}
-    if args.kernel == "qe8":
-        # every kernel of the call, and the call as a whole (events on the stream)
-        for scope in ("e8_quant", "qe8_cb_norm", "qe8_classify", "qe8_search", "qe8_exact"):
-            t, c = _lib.ctypes.c_double(0.0), _lib.ctypes.c_int64(0)
-            _lib.check(lib.uq_profile_read(scope.encode(), _lib.ctypes.byref(t), _lib.ctypes.byref(c)), "profile")
-            rec[f"ms_{scope}"] = t.value / args.iters
-        lib.uq_profile_enable(0)
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        flush.fill_(1)
-        e0.record()
-        run()
-        e1.record()
-        torch.cuda.synchronize()
-        rec["ms_call"] = e0.elapsed_time(e1)
-        rec["bpw"] = args.bpw
-        rec["weights_per_s"] = args.rows * args.n / (rec["ms_call"] * 1e-3)
-    lib.uq_profile_enable(0)
-    ms = tot.value / args.iters            # device time of the kernel per run (all its launches)
-    rec["ms_per_run"] = ms
-    if unit == "bytes":
-        peak, kind = _peaks()
-        gbs = units / (ms * 1e-3) / 1e9
-        rec.update(algorithmic_bytes=units, achieved_gbs=gbs, peak_gbs=peak, frac=gbs / peak, peak_kind=kind)
-    else:
-        props = torch.cuda.get_device_properties(dev)
-        nominal = props.multi_processor_count * 128 * 1965e6
-        tops = units / (ms * 1e-3)
-        rec.update(lane_ops=units, achieved_tops=tops / 1e12, frac_of_nominal_fp32=tops / nominal,
-                   L=args.L, R=args.R)
-    print(json.dumps(rec))
+    print(json.dumps(measure(args.kernel, args.rows, args.n, args.n0, args.L, args.R, args.bpw, args.iters)))
 
 
 if __name__ == "__main__":

@@ -29,6 +29,10 @@ def _is_dev(a) -> bool:
 
 
 def _ret(t: torch.Tensor, like):
+    """Result in the caller's form, after checking that no bounded device
+    wait of the tensor-map kernels timed out (that would leave ``t`` wrong;
+    the check synchronises the stream, as the host copy does anyway)."""
+    _lib.check(_lib.load().uq_device_errors(D.stream_handle(t.device)), "qlab")
     return t if _is_dev(like) else D.to_host(t)
 
 

@@ -7,10 +7,12 @@ tensor and, for large tensors, by row block; each rank quantizes its share
 with the fused device pipelines and no collective runs on the data path.  The
 only exchanges are
 
-* an all-gather of the per-tensor error statistics {sum (A-Ah)^2, sum A^2}
-  (weighted NMSE per tensor, whichever ranks held its row blocks), and
-* optionally, assembling a tensor's outputs (What, states, scales) on one
-  rank with NCCL gathers, and
+* one all-gather of every rank's packed trellis codes (the L + R(T-1) bits
+  of each sequence), per-256 scales and per-block error sums
+  {sum (A-Ah)^2, sum A^2} (``quantize_shards`` + ``gather_codes``): after it
+  every rank holds every tensor's codes and weighted NMSE,
+* an all-gather of the error statistics alone (``gather_errors``), and,
+  optionally, assembling a tensor's What on one rank (``assemble_rows``),
 * for the calibrated E8 step (qlab.py:171-180), whose 600k-vector sample
   spans the whole tensor: a gather of the sampled normalised vectors to one
   rank, which bisects, and a broadcast of the step.
@@ -25,7 +27,7 @@ from dataclasses import dataclass, field
 import torch
 
 __all__ = ["TensorSpec", "Shard", "plan", "llama_shapes", "run_shards", "gather_errors", "assemble_rows",
-           "calibrate_e8"]
+           "calibrate_e8", "ShardCodes", "PackedTrellis", "quantize_shards", "gather_codes", "shard_words"]
 
 
 @dataclass(frozen=True)
@@ -108,6 +110,131 @@ class ShardResult:
     What: torch.Tensor
     err: torch.Tensor                     # [2] fp64
     extras: dict = field(default_factory=dict)
+
+
+@dataclass
+class ShardCodes:
+    """One row block's trellis output on its rank: packed state paths
+    (nseq, words) int32 holding uint32 bit strings, per-group scales (float32),
+    error sums [sum (A-Ah)^2, sum A^2] (fp64) and, if kept, What."""
+    shard: Shard
+    codes: torch.Tensor
+    sc: torch.Tensor
+    err: torch.Tensor
+    What: torch.Tensor | None = None
+
+
+@dataclass
+class PackedTrellis:
+    """A whole tensor's trellis codes assembled from its row blocks (row
+    order): codes (nseq, words), scales (G,), error sums (2,) summed over the
+    blocks in row order, and the weighted NMSE."""
+    spec: TensorSpec
+    codes: torch.Tensor
+    sc: torch.Tensor
+    err: torch.Tensor
+    seg: int
+    group: int
+
+    @property
+    def wnmse(self) -> float:
+        e = self.err.double().cpu()
+        return float(e[0] / e[1])
+
+
+def shard_words(shard: Shard, seg: int = 256, group: int = 256) -> tuple[int, int, int]:
+    """32-bit words of a block's packed codes, scales and error sums in the
+    gathered buffer (the padded width is a power of two >= seg and group,
+    so blocks of whole rows hold whole sequences and scale groups)."""
+    t = shard.tensor
+    n = t.padded_cols
+    if n % seg or n % group:
+        raise ValueError(f"{t.name}: padded width {n} is not a multiple of seg {seg} and group {group}")
+    nseq = shard.rows * n // seg
+    words = (t.L + t.R * (seg - 1) + 31) // 32
+    return nseq * words, shard.rows * n // group, 4
+
+
+def quantize_shards(shards, rank: int, weights, seg: int = 256, group: int = 256,
+                    keep_what: bool = False) -> list[ShardCodes]:
+    """Quantize this rank's row blocks with the fused device recipe
+    (buildtrellis.py:16-20 around trellis.py:62-108) and pack each block's
+    state paths.  ``weights(shard) -> (W rows, H)``: device tensors, or host
+    tensors (pinned for asynchronous copies), which are copied in."""
+    from . import _device as D
+    from . import pipeline, trellis
+    out = []
+    for s in shards:
+        if s.rank != rank:
+            continue
+        W, H = weights(s)
+        if not W.is_cuda:
+            W = D.as_device(W)
+        res = pipeline.quant_trellis_device(W, H, L=s.tensor.L, R=s.tensor.R, seg=seg, scale_group=group,
+                                            keep_codes=True)
+        codes = trellis.pack_states(res.states, s.tensor.L, s.tensor.R)
+        out.append(ShardCodes(s, codes, res.sc, res.err, res.What if keep_what else None))
+    return out
+
+
+def gather_codes(local, shards, world: int, seg: int = 256, group: int = 256, pg=None) -> dict:
+    """All-gather every rank's packed codes, scales and error sums (one
+    collective) and assemble them per tensor in row order on every rank.
+
+    ``shards`` is the whole plan (every rank computes it), so each block's
+    place in the gathered buffer is known without exchanging sizes; each rank
+    contributes its blocks in plan order, padded to the largest rank's size.
+    Error sums are added in row order (deterministic on every rank)."""
+    import torch.distributed as dist
+    mine = {(c.shard.tensor.name, c.shard.row0): c for c in local}
+    by_rank = [[s for s in shards if s.rank == r] for r in range(world)]
+    sizes = [sum(sum(shard_words(s, seg, group)) for s in blk) for blk in by_rank]
+    cap = max(sizes) if sizes else 0
+    dev = local[0].codes.device if local else torch.device("cpu")
+    rank = dist.get_rank(pg) if (world > 1 and dist.is_available() and dist.is_initialized()) else 0
+    buf = torch.zeros(max(cap, 1), dtype=torch.int32, device=dev)
+    off = 0
+    for s in by_rank[rank]:
+        c = mine[(s.tensor.name, s.row0)]
+        nc, ns, ne = shard_words(s, seg, group)
+        buf[off:off + nc] = c.codes.reshape(-1)
+        buf[off + nc:off + nc + ns] = c.sc.reshape(-1).view(torch.int32)
+        buf[off + nc + ns:off + nc + ns + ne] = c.err.reshape(-1).to(torch.float64).view(torch.int32)
+        off += nc + ns + ne
+    if world > 1:
+        allb = torch.empty(world * buf.numel(), dtype=torch.int32, device=dev)
+        dist.all_gather_into_tensor(allb, buf, group=pg)
+    else:
+        allb = buf
+    # place every block of every tensor
+    specs = {}
+    for s in shards:
+        specs.setdefault(s.tensor.name, s.tensor)
+    out = {}
+    for name, t in specs.items():
+        words = (t.L + t.R * (seg - 1) + 31) // 32
+        nseq = t.rows * t.padded_cols // seg
+        ng = t.rows * t.padded_cols // group
+        out[name] = PackedTrellis(t, torch.empty((nseq, words), dtype=torch.int32, device=dev),
+                                  torch.empty(ng, dtype=torch.float32, device=dev),
+                                  torch.zeros(2, dtype=torch.float64, device=dev), seg, group)
+    errs = {}
+    for r in range(world):
+        off = r * buf.numel()
+        for s in by_rank[r]:
+            nc, ns, ne = shard_words(s, seg, group)
+            p = out[s.tensor.name]
+            q0 = s.row0 * s.tensor.padded_cols // seg
+            g0 = s.row0 * s.tensor.padded_cols // group
+            p.codes.view(-1)[q0 * p.codes.shape[1]:q0 * p.codes.shape[1] + nc] = allb[off:off + nc]
+            p.sc[g0:g0 + ns] = allb[off + nc:off + nc + ns].view(torch.float32)
+            errs.setdefault(s.tensor.name, []).append((s.row0, allb[off + nc + ns:off + nc + ns + ne]))
+            off += nc + ns + ne
+    for name, lst in errs.items():
+        acc = out[name].err
+        for _, e in sorted(lst, key=lambda v: v[0]):
+            acc += e.view(torch.float64)
+    return out
 
 
 def run_shards(shards, rank: int, make_weights, quantize) -> list[ShardResult]:
