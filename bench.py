@@ -112,8 +112,11 @@ def host_info():
 
 
 class ClockSampler:
-    """nvidia-smi clock / throttle samples during the timed region."""
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    """nvidia-smi clock / throttle samples (every 200 ms).  Started before
+    the warm-up, so that nvidia-smi's start-up does not fall into the timed
+    region; mark() brackets the timed region and summary() keeps only the
+    samples taken inside it."""
+    FIELDS = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
@@ -121,6 +124,13 @@ class ClockSampler:
         self.idx = gpu_index
         self.proc = None
         self.f = None
+        self.t0 = self.t1 = None
+
+    def mark(self, start: bool):
+        if start:
+            self.t0 = time.time()
+        else:
+            self.t1 = time.time()
 
     def __enter__(self):
         try:
@@ -148,17 +158,28 @@ class ClockSampler:
             os.unlink(self.f.name)
         except Exception:
             return None
+        import datetime
         sm, mx, pw, reasons = [], [], [], set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for r in rows:
-            r = [x.strip() for x in r]
+        def stamp(r):
             try:
-                sm.append(float(r[1]))
-                mx.append(float(r[2]))
-                pw.append(float(r[3]))
+                return datetime.datetime.strptime(r[0].strip(), "%Y/%m/%d %H:%M:%S.%f").timestamp()
+            except (ValueError, IndexError):
+                return None
+        stamped = self.t0 is not None and any(stamp(r) is not None for r in rows)
+        for r in rows:
+            ts = stamp(r)
+            r = [x.strip() for x in r]
+            # samples inside the timed region (a quarter period of slack)
+            if stamped and (ts is None or not (self.t0 - 0.05 <= ts <= (self.t1 or ts) + 0.05)):
+                continue
+            try:
+                sm.append(float(r[2]))
+                mx.append(float(r[3]))
+                pw.append(float(r[4]))
             except (ValueError, IndexError):
                 continue
-            for nm, v in zip(names, r[5:9]):
+            for nm, v in zip(names, r[6:10]):
                 if v.lower().startswith("active"):
                     reasons.add(nm)
         if not sm:
@@ -329,6 +350,7 @@ def run_tensor(args, rank: int, world: int, local: int):
         if world > 1:
             dist.barrier()
 
+    clk = ClockSampler(phys_gpu_index(local)).__enter__()
     for _ in range(max(args.warmup, 0)):
         step()
     torch.cuda.synchronize()
@@ -341,13 +363,15 @@ def run_tensor(args, rank: int, world: int, local: int):
     launches0 = int(lib.uq_launch_count())
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
-    with ClockSampler(phys_gpu_index(local)) as clk:
-        e0.record()
-        out = None
-        for _ in range(args.steps):
-            out = step()
-        e1.record()
-        torch.cuda.synchronize()
+    clk.mark(True)
+    e0.record()
+    out = None
+    for _ in range(args.steps):
+        out = step()
+    e1.record()
+    torch.cuda.synchronize()
+    clk.mark(False)
+    clk.__exit__(None, None, None)
     launches = int(lib.uq_launch_count()) - launches0
     lib.uq_profile_enable(0)
     ms = e0.elapsed_time(e1)
@@ -549,18 +573,23 @@ def run_weight_set(args, rank: int, world: int, local: int):
         W = gen(s) if stream_blocks else data[(s.tensor.name, s.row0)]
         return W, Hs[s.tensor.name]
 
+    clk = ClockSampler(phys_gpu_index(local)).__enter__()
+    time.sleep(2.0)                       # nvidia-smi start-up outside the timed region
     if world > 1:
         dist.barrier()
+    torch.cuda.synchronize()
     lib.uq_profile_reset()
     lib.uq_profile_enable(1)
     launches0 = int(lib.uq_launch_count())
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(phys_gpu_index(local)) as clk:
-        e0.record()
-        loc = shard.quantize_shards(plan, rank, weights, SEG, GROUP)
-        out = shard.gather_codes(loc, plan, world, SEG, GROUP)
-        e1.record()
-        torch.cuda.synchronize()
+    clk.mark(True)
+    e0.record()
+    loc = shard.quantize_shards(plan, rank, weights, SEG, GROUP)
+    out = shard.gather_codes(loc, plan, world, SEG, GROUP)
+    e1.record()
+    torch.cuda.synchronize()
+    clk.mark(False)
+    clk.__exit__(None, None, None)
     launches = int(lib.uq_launch_count()) - launches0
     lib.uq_profile_enable(0)
     vt, vn = ctypes.c_double(), ctypes.c_int64()

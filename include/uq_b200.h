@@ -200,10 +200,16 @@ int uq_trellis_viterbi(const float *xn, int64_t nseq, int T, int L, int R, const
  * array (uq_trellis_noalloc_scratch_bytes()) that each GPU loading the
  * library holds until exit; sequences are processed in batches that fit it.
  * A sequence needing more than that array (T * 2^L / 16 bytes) is rejected
- * with UQ_ERR_INVALID.  Nothing is allocated or freed.  The first call on a
- * device looks up the array's device address (cudaGetSymbolAddress); make
- * that first call before any stream capture.  Every call shares the array:
- * calls that overlap on the GPU (other streams, other host threads) race. */
+ * with UQ_ERR_INVALID.  Nothing is allocated or freed.  The first call in
+ * each CUDA context of a device (the primary context, a new one after
+ * cudaDeviceReset, or a caller's own) looks up the array's device address in
+ * that context (cudaGetSymbolAddress); make that first call before any
+ * stream capture.  Every call shares the array: calls that overlap on the
+ * GPU (other streams, other host threads) race.  Throughput: at L = 16,
+ * T = 256 one sequence needs ~1 MiB, so a batch is 64 sequences, under half
+ * of the 148 that one wave of the cluster kernel runs, and each batch ends
+ * with a latency-bound traceback launch -- expect well under half the
+ * throughput of uq_trellis_viterbi with a workspace at that size. */
 size_t uq_trellis_noalloc_scratch_bytes(void);
 int uq_trellis_viterbi_noalloc(const float *xn, int64_t nseq, int T, int L, int R,
                                const float *cw, int32_t *states, void *stream);

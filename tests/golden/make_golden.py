@@ -7,10 +7,10 @@ and outputs in ``tests/golden/*.npz``.  The reference has no test suite and no
 committed golden vectors; these fixtures pin the oracle and the CUDA path.
 
 Usage (in a container that has the reference checkout):
-    python tests/golden/make_golden.py [/path/to/reference [rht e8 trellis pipeline qat]]
+    python tests/golden/make_golden.py /path/to/reference [rht e8 trellis pipeline qat ...]
+or with UQ_REFERENCE=/path/to/reference and no positional path.
 
-The reference directory defaults to /root/reference.  Nothing at test or bench
-time reads the reference; only this generator does.
+Nothing at test or bench time reads the reference; only this generator does.
 """
 from __future__ import annotations
 
@@ -20,7 +20,9 @@ import sys
 import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-REF = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+REF = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("UQ_REFERENCE", "")
+if not REF and __name__ == "__main__":
+    sys.exit("usage: make_golden.py /path/to/reference [makers...]  (or set UQ_REFERENCE)")
 
 
 def _import_reference():

@@ -19,6 +19,15 @@ inline bool is_pow2(int64_t n) { return n > 0 && (n & (n - 1)) == 0; }
 inline int ilog2(int64_t n) { int b = 0; while ((int64_t(1) << b) < n) ++b; return b; }
 inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 int num_sms();
+
+// Launch-configuration queries, cached per (kernel, arguments, device, CUDA
+// context): the dynamic shared-memory attribute and the occupancy queries are
+// host-side driver calls of up to milliseconds each, and every pipeline call
+// made several of them.  Without a context ID from the driver they call
+// straight through.
+cudaError_t set_smem_attr(const void *kernel, int smem);
+cudaError_t occupancy_blocks(int *per_sm, const void *kernel, int threads, size_t smem);
+cudaError_t occupancy_clusters(int *clusters, const void *kernel, const cudaLaunchConfig_t *cfg);
 int qat_take_bad_state();   // uq_qat.cu
 int rht_take_timeout();     // uq_rht.cu
 int e8_take_timeout();      // uq_e8.cu

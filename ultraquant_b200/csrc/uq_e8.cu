@@ -329,12 +329,12 @@ int64_t launch_e8_tma(const E8Args &a, cudaStream_t st) {
         !uq::tma::encode_lines(&mo, true, 2, a.rec, dims, strides, box))
         return 0;
     const size_t smem = size_t(8) * 2 * kE8ChunkBytes + 1024;
-    if (cudaFuncSetAttribute(e8_tma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess) {
+    if (uq::set_smem_attr(reinterpret_cast<const void *>(e8_tma_kernel), int(smem)) != cudaSuccess) {
         uq::check_cuda("e8 tma: set smem attribute");
         return -1;
     }
     int per_sm = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, e8_tma_kernel, 256, smem) != cudaSuccess || per_sm < 1) {
+    if (uq::occupancy_blocks(&per_sm, reinterpret_cast<const void *>(e8_tma_kernel), 256, smem) != cudaSuccess || per_sm < 1) {
         uq::check_cuda("e8 tma: occupancy");
         return -1;
     }
@@ -404,7 +404,7 @@ int launch_e8_quant(const E8Args &a0, cudaStream_t st) {
     const int64_t padded = (a.size + a.group - 1) / a.group * a.group;
     const int64_t grid = (padded + a.tile - 1) / a.tile;
     auto kern = e8_quant_kernel<TIn>;
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess)
+    if (uq::set_smem_attr(reinterpret_cast<const void *>(kern), int(smem)) != cudaSuccess)
         return uq::check_cuda("e8: set smem attribute");
     if (grid > 0) { uq::ProfScope _p("e8_quant", st); kern<<<unsigned(grid), threads, smem, st>>>(a); }
     return uq::check_cuda("e8_quant_kernel launch");

@@ -63,6 +63,95 @@ ProfScope::~ProfScope() {
     cudaEventRecord(g_prof[size_t(slot)].b, st);
 }
 
+namespace {
+typedef int (*CtxGetCurrentFn)(void **);
+typedef int (*CtxGetIdFn)(void *, unsigned long long *);
+
+// ID of the context current on this thread (unique for the life of the
+// process), 0 if none is bound or the driver cannot say.
+unsigned long long context_id() {
+    static std::once_flag once;
+    static CtxGetCurrentFn cur = nullptr;
+    static CtxGetIdFn getid = nullptr;
+    std::call_once(once, [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult r = cudaDriverEntryPointSymbolNotFound;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &r) == cudaSuccess &&
+            r == cudaDriverEntryPointSuccess)
+            cur = reinterpret_cast<CtxGetCurrentFn>(p);
+        p = nullptr;
+        r = cudaDriverEntryPointSymbolNotFound;
+        if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &r) == cudaSuccess &&
+            r == cudaDriverEntryPointSuccess)
+            getid = reinterpret_cast<CtxGetIdFn>(p);
+        cudaGetLastError();
+    });
+    void *ctx = nullptr;
+    unsigned long long id = 0;
+    if (!cur || !getid || cur(&ctx) != 0 || !ctx || getid(ctx, &id) != 0) return 0;
+    return id;
+}
+
+struct LaunchQuery {
+    int kind;                     // 0 smem attribute, 1 blocks per SM, 2 clusters
+    const void *kernel;
+    long long a, b, c, d;         // the query's arguments
+    int dev;
+    unsigned long long ctx;
+    int value;
+};
+std::mutex g_lq_mu;
+std::vector<LaunchQuery> g_lq;
+
+template <class F>
+cudaError_t cached_query(int kind, const void *kernel, long long a, long long b, long long c, long long d, int *out,
+                         F query) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return cudaGetLastError();
+    const unsigned long long ctx = context_id();
+    if (ctx) {
+        std::lock_guard<std::mutex> g(g_lq_mu);
+        for (const LaunchQuery &q : g_lq)
+            if (q.kind == kind && q.kernel == kernel && q.a == a && q.b == b && q.c == c && q.d == d &&
+                q.dev == dev && q.ctx == ctx) {
+                if (out) *out = q.value;
+                return cudaSuccess;
+            }
+    }
+    int v = 0;
+    const cudaError_t e = query(&v);
+    if (e != cudaSuccess) return e;
+    if (out) *out = v;
+    if (ctx) {
+        std::lock_guard<std::mutex> g(g_lq_mu);
+        if (g_lq.size() > 4096) g_lq.clear();
+        g_lq.push_back(LaunchQuery{kind, kernel, a, b, c, d, dev, ctx, v});
+    }
+    return cudaSuccess;
+}
+}  // namespace
+
+cudaError_t set_smem_attr(const void *kernel, int smem) {
+    return cached_query(0, kernel, smem, 0, 0, 0, nullptr, [&](int *v) {
+        *v = 0;
+        return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    });
+}
+
+cudaError_t occupancy_blocks(int *per_sm, const void *kernel, int threads, size_t smem) {
+    return cached_query(1, kernel, threads, (long long)smem, 0, 0, per_sm, [&](int *v) {
+        return cudaOccupancyMaxActiveBlocksPerMultiprocessor(v, kernel, threads, smem);
+    });
+}
+
+cudaError_t occupancy_clusters(int *clusters, const void *kernel, const cudaLaunchConfig_t *cfg) {
+    long long cl = 0;
+    for (unsigned i = 0; i < cfg->numAttrs; ++i)
+        if (cfg->attrs[i].id == cudaLaunchAttributeClusterDimension) cl = cfg->attrs[i].val.clusterDim.x;
+    return cached_query(2, kernel, cfg->blockDim.x, (long long)cfg->dynamicSmemBytes, cl, cfg->gridDim.x, clusters,
+                        [&](int *v) { return cudaOccupancyMaxActiveClusters(v, kernel, cfg); });
+}
+
 int num_sms() {
     int dev = 0, n = 148;
     if (cudaGetDevice(&dev) == cudaSuccess)

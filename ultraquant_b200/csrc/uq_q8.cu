@@ -177,7 +177,7 @@ __global__ void __launch_bounds__(256) q8_decode_kernel(const uint8_t *q8, int64
 template <typename K>
 int grid_for(K kern, int64_t work, int per_block) {
     int per_sm = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, 256, 0) != cudaSuccess || per_sm < 1) per_sm = 1;
+    if (uq::occupancy_blocks(&per_sm, reinterpret_cast<const void *>(kern), 256, 0) != cudaSuccess || per_sm < 1) per_sm = 1;
     return int(std::max<int64_t>(1, std::min<int64_t>((work + per_block - 1) / per_block,
                                                       int64_t(uq::num_sms()) * per_sm)));
 }

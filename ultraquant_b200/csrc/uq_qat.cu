@@ -576,10 +576,10 @@ int launch_rows(const FwhtArgs &a, cudaStream_t st, const char *what) {
         (codes && a.cw_smem ? ((size_t(a.ncw) * 4 + 15) & ~size_t(15)) + (DST == DST_GRADS ? size_t(a.ncw) * 8 : 0) : 0) +
         (SRC == SRC_RECON && NB == 12 && a.cw_smem && a.colscale ? size_t(a.ncols_out) * 4 : 0);
     auto kern = qat_rows_kernel<DIR, SRC, DST, NB>;
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess)
+    if (uq::set_smem_attr(reinterpret_cast<const void *>(kern), int(smem)) != cudaSuccess)
         return uq::check_cuda("qat rows: set smem attribute");
     int per_sm = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, 1 << (NB - 5), smem) != cudaSuccess || per_sm < 1)
+    if (uq::occupancy_blocks(&per_sm, reinterpret_cast<const void *>(kern), 1 << (NB - 5), smem) != cudaSuccess || per_sm < 1)
         return uq::check_cuda("qat rows: occupancy query");
     const int64_t grid = std::min<int64_t>(a.rows, int64_t(uq::num_sms()) * per_sm);
     if (grid > 0) { uq::ProfScope _p(what, st); kern<<<unsigned(grid), 1 << (NB - 5), smem, st>>>(a); }
@@ -620,10 +620,10 @@ int launch_fwht(const FwhtArgs &a, cudaStream_t st, const char *what) {
             else if (a.b == 13) kern = fwht_kernel<T, DIR, SRC, DST, 256, 13, 2>;
         }
     }
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess)
+    if (uq::set_smem_attr(reinterpret_cast<const void *>(kern), int(smem)) != cudaSuccess)
         return uq::check_cuda("fwht: set smem attribute");
     int per_sm = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, nthr, smem) != cudaSuccess || per_sm < 1)
+    if (uq::occupancy_blocks(&per_sm, reinterpret_cast<const void *>(kern), nthr, smem) != cudaSuccess || per_sm < 1)
         return uq::check_cuda("fwht: occupancy query");
     const int64_t ntiles = (a.rows + (int64_t(1) << (NB - a.b)) - 1) >> (NB - a.b);
     const int64_t grid = std::min<int64_t>(ntiles, int64_t(uq::num_sms()) * per_sm);

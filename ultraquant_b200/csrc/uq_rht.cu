@@ -891,7 +891,7 @@ template <typename TIn, typename TOut, int MODE>
 int launch_rht28(const R28Args &a, cudaStream_t st) {
     auto kern = rht28_kernel<TIn, TOut, MODE>;
     const size_t smem = size_t(28) * (size_t(8) << a.m);
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess)
+    if (uq::set_smem_attr(reinterpret_cast<const void *>(kern), int(smem)) != cudaSuccess)
         return uq::check_cuda("rht28: set smem attribute");
     const int64_t grid = std::min<int64_t>(a.rows, uq::num_sms());
     if (grid > 0) { uq::ProfScope _p("rht", st); kern<<<unsigned(grid), 512, smem, st>>>(a); }
@@ -963,7 +963,7 @@ int launch_tma_v(const CUtensorMap &mi, const CUtensorMap &mo, const RhtArgs &a,
     // two fp64 tiles (+ one inbox of 2^(LB-1) values per cross-CTA stage) + alignment slack
     const size_t smem = size_t(2) * (size_t(8) << LB) + ((CL == 2 || CL == 4) ? size_t(CL / 2) * (size_t(8) << (LB - 1)) : 0) +
                         1024;
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess)
+    if (uq::set_smem_attr(reinterpret_cast<const void *>(kern), int(smem)) != cudaSuccess)
         return uq::check_cuda("rht tma: set smem attribute");
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute attr[1];
@@ -975,12 +975,12 @@ int launch_tma_v(const CUtensorMap &mi, const CUtensorMap &mo, const RhtArgs &a,
     if (CL > 1) {
         cfg.gridDim = dim3(CL, 1, 1);
         int clusters = 0;
-        if (cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg) != cudaSuccess || clusters < 1)
+        if (uq::occupancy_clusters(&clusters, reinterpret_cast<const void *>(kern), &cfg) != cudaSuccess || clusters < 1)
             return uq::check_cuda("rht tma: cluster occupancy");
         slots = clusters;
     } else {
         int per_sm = 0;
-        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, nt, smem) != cudaSuccess || per_sm < 1)
+        if (uq::occupancy_blocks(&per_sm, reinterpret_cast<const void *>(kern), nt, smem) != cudaSuccess || per_sm < 1)
             return uq::check_cuda("rht tma: occupancy");
         slots = int64_t(per_sm) * uq::num_sms();
     }
@@ -1016,7 +1016,7 @@ template <typename TIn, typename TOut, int MODE>
 int launch_rht_split(const RhtArgs &a, cudaStream_t st) {
     auto kern = rht_split_kernel<TIn, TOut, MODE>;
     const size_t smem = sizeof(double) << kTileBits;
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess)
+    if (uq::set_smem_attr(reinterpret_cast<const void *>(kern), int(smem)) != cudaSuccess)
         return uq::check_cuda("rht split: set smem attribute");
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute attr[1];
@@ -1025,7 +1025,7 @@ int launch_rht_split(const RhtArgs &a, cudaStream_t st) {
     cfg.gridDim = dim3(2, 1, 1); cfg.blockDim = dim3(1024, 1, 1); cfg.dynamicSmemBytes = smem; cfg.stream = st;
     cfg.attrs = attr; cfg.numAttrs = 1;
     int clusters = 0;
-    if (cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg) != cudaSuccess || clusters < 1)
+    if (uq::occupancy_clusters(&clusters, reinterpret_cast<const void *>(kern), &cfg) != cudaSuccess || clusters < 1)
         return uq::check_cuda("rht split: cluster occupancy");
     const int64_t ncl = std::min<int64_t>(a.rows, clusters);
     if (ncl > 0) { uq::ProfScope _p("rht", st); kern<<<unsigned(2 * ncl), 1024, smem, st>>>(a); }
@@ -1056,7 +1056,7 @@ int launch_rht(const RhtArgs &a, cudaStream_t st, int64_t *nparts) {
     // 16 fp64 values per thread; 256-thread tiles (n <= 4096) run 3 CTAs per SM
     auto kern = nthr <= 256 ? rht_tile_kernel<TIn, TOut, MODE, 256, 3>
               : (nthr <= 512 ? rht_tile_kernel<TIn, TOut, MODE, 512, 1> : rht_tile_kernel<TIn, TOut, MODE, 1024, 1>);
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess)
+    if (uq::set_smem_attr(reinterpret_cast<const void *>(kern), int(smem)) != cudaSuccess)
         return uq::check_cuda("rht: set smem attribute");
     const int per_sm = nthr <= 256 ? 3 : 1;
     const int64_t grid = std::min<int64_t>(ntiles, int64_t(uq::num_sms()) * per_sm);

@@ -233,7 +233,7 @@ int launch_normalize(NormArgs a, cudaStream_t st) {
     const size_t smem = sizeof(float) * (size_t(a.tile) + ng + size_t(ng) * 32);
     const int64_t total = a.nrow * a.Tp;
     const int64_t grid = (total + a.tile - 1) / a.tile;
-    if (cudaFuncSetAttribute(normalize_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess)
+    if (uq::set_smem_attr(reinterpret_cast<const void *>(normalize_kernel), int(smem)) != cudaSuccess)
         return uq::check_cuda("normalize: set smem attribute");
     if (grid > 0) { uq::ProfScope _p("normalize", st); normalize_kernel<<<unsigned(grid), 256, smem, st>>>(a); }
     return uq::check_cuda("normalize_kernel launch");
@@ -913,7 +913,7 @@ int launch_viterbi(const VitArgs &a, cudaStream_t st) {
     using C = VitCfg<L, R, CL>;
     const size_t smem = size_t(C::NSET) * C::NBUF * (C::FLOATS + C::OFLOATS) * sizeof(float);
     auto kern = viterbi_fwd_kernel<C>;
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess)
+    if (uq::set_smem_attr(reinterpret_cast<const void *>(kern), int(smem)) != cudaSuccess)
         return uq::check_cuda("viterbi: set smem attribute");
     int64_t ctas;
     if (CL == 1) ctas = (a.nbatch + C::SPS - 1) / C::SPS;
@@ -932,13 +932,13 @@ int64_t viterbi_wave() {
     using C = VitCfg<L, R, CL>;
     const size_t smem = size_t(C::NSET) * C::NBUF * (C::FLOATS + C::OFLOATS) * sizeof(float);
     auto kern = viterbi_fwd_kernel<C>;
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess) {
+    if (uq::set_smem_attr(reinterpret_cast<const void *>(kern), int(smem)) != cudaSuccess) {
         cudaGetLastError();
         return 0;
     }
     if (CL == 1) {
         int per_sm = 0;
-        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, smem) != cudaSuccess) {
+        if (uq::occupancy_blocks(&per_sm, reinterpret_cast<const void *>(kern), kThreads, smem) != cudaSuccess) {
             cudaGetLastError();
             return 0;
         }
@@ -949,7 +949,7 @@ int64_t viterbi_wave() {
     cfg.blockDim = dim3(kThreads, 1, 1);
     cfg.dynamicSmemBytes = smem;
     int ncl = 0;
-    if (cudaOccupancyMaxActiveClusters(&ncl, kern, &cfg) != cudaSuccess) {
+    if (uq::occupancy_clusters(&ncl, reinterpret_cast<const void *>(kern), &cfg) != cudaSuccess) {
         cudaGetLastError();
         return 0;
     }
@@ -1092,27 +1092,89 @@ int trellis_decode(const int32_t *states, const float *cw, const float *sc, int6
 // ---------------------------------------------------------------------------
 namespace {
 constexpr size_t kNoAllocScratchBytes = size_t(64) << 20;   // 64 MiB per device
+// Cached device addresses of the scratch array, one per (device, context).
+// The array lives in the library's module, which the runtime loads into every
+// context that uses it, so a new context on the same device (after
+// cudaDeviceReset, or a caller's own context) has its own copy.  Contexts are
+// told apart by the driver's context ID, which is unique for the life of the
+// process (a context handle may be reused after its context is destroyed).
+struct NoAllocSlot {
+    int dev = -1;
+    unsigned long long ctx_id = 0;
+    void *ptr = nullptr;
+};
+constexpr int kNoAllocSlots = 64;
 std::mutex g_noalloc_mu;
-void *g_noalloc_ptr[256] = {};
+NoAllocSlot g_noalloc_slot[kNoAllocSlots];
+int g_noalloc_next = 0;
+
+// cuCtxGetCurrent / cuCtxGetId from the driver, fetched through the runtime
+// (the library links only the CUDA runtime); null if the driver lacks them.
+typedef int (*CtxGetCurrentFn)(void **);
+typedef int (*CtxGetIdFn)(void *, unsigned long long *);
+struct CtxQuery {
+    CtxGetCurrentFn current = nullptr;
+    CtxGetIdFn id = nullptr;
+};
+const CtxQuery &ctx_query() {
+    static std::once_flag once;
+    static CtxQuery q;
+    std::call_once(once, [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult r = cudaDriverEntryPointSymbolNotFound;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &r) == cudaSuccess &&
+            r == cudaDriverEntryPointSuccess)
+            q.current = reinterpret_cast<CtxGetCurrentFn>(p);
+        p = nullptr;
+        r = cudaDriverEntryPointSymbolNotFound;
+        if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &r) == cudaSuccess &&
+            r == cudaDriverEntryPointSuccess)
+            q.id = reinterpret_cast<CtxGetIdFn>(p);
+        cudaGetLastError();
+    });
+    return q;
+}
+
+// ID of the context current on this thread, 0 if none is bound or the
+// driver cannot say.
+unsigned long long current_ctx_id() {
+    const CtxQuery &q = ctx_query();
+    void *ctx = nullptr;
+    unsigned long long id = 0;
+    if (!q.current || !q.id || q.current(&ctx) != 0 || !ctx || q.id(ctx, &id) != 0) return 0;
+    return id;
+}
 }  // namespace
 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
-// Device address of the scratch array for the current device, looked up once
-// per device (host code may not use the symbol itself as a device address).
+// Device address of the scratch array in the current context, looked up with
+// cudaGetSymbolAddress on the first call per (device, context) and cached
+// (host code may not use the symbol itself as a device address).
 static int noalloc_scratch(void **out) {
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return uq::check_cuda("noalloc: cudaGetDevice");
-    if (dev < 0 || dev >= 256) return uq::fail(UQ_ERR_UNSUPPORTED, "noalloc: device ordinal %d", dev);
-    std::lock_guard<std::mutex> g(g_noalloc_mu);
-    if (!g_noalloc_ptr[dev]) {
-        void *p = nullptr;
-        const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-        if (e != cudaSuccess || !p)
-            return uq::fail(UQ_ERR_CUDA, "noalloc: cudaGetSymbolAddress failed: %s", cudaGetErrorString(e));
-        g_noalloc_ptr[dev] = p;
+    unsigned long long id = current_ctx_id();
+    if (id) {
+        std::lock_guard<std::mutex> g(g_noalloc_mu);
+        for (const NoAllocSlot &s : g_noalloc_slot)
+            if (s.ptr && s.dev == dev && s.ctx_id == id) {
+                *out = s.ptr;
+                return UQ_OK;
+            }
     }
-    *out = g_noalloc_ptr[dev];
+    // first call in this context (or no context bound to the thread yet: the
+    // lookup binds the runtime's context, whose ID is then cached)
+    void *p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || !p)
+        return uq::fail(UQ_ERR_CUDA, "noalloc: cudaGetSymbolAddress failed: %s", cudaGetErrorString(e));
+    id = current_ctx_id();
+    if (id) {   // without a context ID nothing is cached: every call looks the address up
+        std::lock_guard<std::mutex> g(g_noalloc_mu);
+        g_noalloc_slot[g_noalloc_next++ % kNoAllocSlots] = NoAllocSlot{dev, id, p};
+    }
+    *out = p;
     return UQ_OK;
 }
 

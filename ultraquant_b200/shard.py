@@ -160,20 +160,28 @@ def quantize_shards(shards, rank: int, weights, seg: int = 256, group: int = 256
     """Quantize this rank's row blocks with the fused device recipe
     (buildtrellis.py:16-20 around trellis.py:62-108) and pack each block's
     state paths.  ``weights(shard) -> (W rows, H)``: device tensors, or host
-    tensors (pinned for asynchronous copies), which are copied in."""
+    tensors (pinned for asynchronous copies), which are copied in.
+
+    The blocks are launched back to back; the bounded-wait status of all of
+    them is checked once at the end (one stream synchronisation), before any
+    result leaves the rank, and a timed-out wait raises UQError."""
     from . import _device as D
-    from . import pipeline, trellis
+    from . import _lib, pipeline, trellis
     out = []
+    dev = None
     for s in shards:
         if s.rank != rank:
             continue
         W, H = weights(s)
         if not W.is_cuda:
             W = D.as_device(W)
+        dev = W.device
         res = pipeline.quant_trellis_device(W, H, L=s.tensor.L, R=s.tensor.R, seg=seg, scale_group=group,
-                                            keep_codes=True)
+                                            keep_codes=True, check_errors=False)
         codes = trellis.pack_states(res.states, s.tensor.L, s.tensor.R)
         out.append(ShardCodes(s, codes, res.sc, res.err, res.What if keep_what else None))
+    if dev is not None:
+        _lib.check(_lib.load().uq_device_errors(D.stream_handle(dev)), "quantize_shards")
     return out
 
 
