@@ -608,6 +608,47 @@ def run_weight_set(args, rank: int, world: int, local: int):
                 "peak_source": "measured: uq_fp32_lane_probe (packed f32x2), rank 0",
                 "launches": int(vn.value), "kernel_ms_total": vt.value,
                 "share_of_step": vt.value / (wall * 1e3) if wall else None}
+    # ---- end to end (llama8b): the rank's blocks from pinned host memory,
+    # the gathered codes, scales and error sums read back on rank 0 ---------
+    e2e = None
+    if not stream_blocks and not args.no_e2e:
+        host = {key: W.cpu().pin_memory() for key, W in data.items()}
+        data.clear()
+        torch.cuda.empty_cache()
+        code_host = {k: (torch.empty(v.codes.shape, dtype=torch.int32, pin_memory=True),
+                         torch.empty(v.sc.shape, dtype=torch.float32, pin_memory=True),
+                         torch.empty(2, dtype=torch.float64, pin_memory=True)) for k, v in out.items()} \
+            if rank == 0 else {}
+
+        def weights_host(s):
+            return host[(s.tensor.name, s.row0)], Hs[s.tensor.name]
+
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record()
+        loc2 = shard.quantize_shards(plan, rank, weights_host, SEG, GROUP)
+        out2 = shard.gather_codes(loc2, plan, world, SEG, GROUP)
+        for k, (hc, hs, he) in code_host.items():
+            hc.copy_(out2[k].codes, non_blocking=True)
+            hs.copy_(out2[k].sc, non_blocking=True)
+            he.copy_(out2[k].err, non_blocking=True)
+        t1.record()
+        torch.cuda.synchronize()
+        ems = torch.tensor([t0.elapsed_time(t1)], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(ems, op=dist.ReduceOp.MAX)
+        h2d = sum(s.rows * s.tensor.cols * 4 for s in mine)        # the imatrix stays on the device
+        d2h = sum(hc.numel() * 4 + hs.numel() * 4 + 16 for hc, hs, _ in code_host.values())
+        e2e = {"value": weights_n / (float(ems.item()) / 1e3), "unit": UNIT, "wall_s": float(ems.item()) / 1e3,
+               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+               "api": "ultraquant_b200.shard.quantize_shards(pinned host blocks) + gather_codes -> (rank 0) "
+                      "pinned host packed codes, scales, error sums"}
+        if rank == 0:
+            for k in list(out)[:4]:
+                assert torch.equal(code_host[k][0], out[k].codes.cpu()), "e2e codes differ from the resident run"
+        del loc2, out2
     if world > 1:
         dist.barrier()
     if rank == 0:
@@ -627,8 +668,9 @@ def run_weight_set(args, rank: int, world: int, local: int):
                                for t in ("attn_q", "attn_k", "attn_v", "attn_output", "ffn_gate", "ffn_up",
                                          "ffn_down")},
                 "packed_code_bytes": sum(v.codes.numel() * 4 for v in out.values()),
-                "roofline": roofline, "e2e": None,
-                "e2e_note": "weights generated on the device (no host copy of the set)",
+                "roofline": roofline, "e2e": e2e,
+                "e2e_note": None if e2e else "row blocks generated on the device per block (no host copy of the "
+                                             "274 GB set)",
                 "gpu_launches": launches, "clocks": clk.summary()}
         print(json.dumps(line), flush=True)
     if world > 1:
