@@ -310,7 +310,7 @@ def workload_config(world: int):
         "rows": ROWS, "cols": COLS, "L": L_BITS, "k": list(KS), "T": SEG, "scale_group": GROUP,
         "weights_per_step": ROWS * COLS * len(KS),
         "parallelism": f"row blocks of {ROWS // world} rows x{world} ranks" + (" + all-gather" if world > 1 else ""),
-        "l2": "working set > L2: 4 KiB of backpointers per weight written each step",
+        "l2": "working set > L2: 8 KiB of backpointers per weight written each step",
     }
 
 

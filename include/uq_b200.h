@@ -199,7 +199,8 @@ int uq_trellis_viterbi(const float *xn, int64_t nseq, int T, int L, int R, const
  * synchronisation).  Backpointers go to a fixed 64 MiB file-scope device
  * array (uq_trellis_noalloc_scratch_bytes()) that each GPU loading the
  * library holds until exit; sequences are processed in batches that fit it.
- * A sequence needing more than that array (T * 2^L / 16 bytes) is rejected
+ * A sequence needing more than that array ((T - 1) * 2^L / 8 bytes at R = 2,
+ * 3; half that at R = 1, 4) is rejected
  * with UQ_ERR_INVALID.  Nothing is allocated or freed.  The first call in
  * each CUDA context of a device (the primary context, a new one after
  * cudaDeviceReset, or a caller's own) looks up the array's device address in

@@ -2,11 +2,20 @@
 
 The model follows ``ultraquant_b200/csrc/uq_trellis.cu`` index by index:
 thread v owns q in [NQ*v, NQ*v + NQ) (64 states), reads
-m_{t-1}[k*Rn + r] for its r-range, derives the first-index argmin from the
-sign bits of candidate differences (tournament), packs the R-bit fields with
-jq's field at bits [jq*R, jq*R + R), and the traceback decodes them.  It also
-checks that the shared-memory swizzles are bijections and bank-conflict free
-for the access patterns of every (L, R) the kernel is built for.
+m_{t-1}[k*Rn + r] for its r-range and writes one decision record per step,
+which the traceback decodes:
+
+* R = 1, 4: the tournament's first-index argmin from sign bits of candidate
+  differences, R-bit field of q-local jq at bits [jq*R, jq*R + R) of one
+  32-bit word;
+* R = 2, 3: m = min_k c_k and the raw signs s_k = signbit(m - c_k), k < K-1
+  (the first clear one is the first-index argmin), in two 32-bit words: word
+  jq // HQ, pair pw = (jq % HQ) // 2 at bits 2F*pw .. 2F*pw + 2F, s_k at bit
+  2F*pw + 2k + (jq & 1), F = K - 1, HQ = NQ / 2.
+
+It also checks that the shared-memory swizzles are bijections and
+bank-conflict free for the access patterns of every (L, R) the kernel is
+built for.
 """
 import numpy as np
 import pytest
@@ -39,6 +48,29 @@ def _tourney(c):
     return val[0], k
 
 
+def record_layout(R):
+    """(raw, F, words per record, q per word) of the kernel's decision record."""
+    K = 1 << R
+    NQ = 64 // K
+    raw = R in (2, 3)
+    F = K - 1 if raw else R
+    bpw = (NQ * F + 31) // 32
+    return raw, F, bpw, NQ // bpw
+
+
+def _gpu_signbit(d):
+    """Sign bit of a float32 difference as the GPU produces it: inf - inf is
+    the canonical NaN 0x7FFFFFFF (sign clear), not x86's 0xFFC00000."""
+    return False if np.isnan(d) else bool(np.signbit(d))
+
+
+def _raw_signs(c):
+    """min of the candidates and s_k = signbit(m - c_k) for k < K - 1."""
+    m = np.float32(min(c))
+    with np.errstate(invalid="ignore"):
+        return m, [_gpu_signbit(np.float32(m - ck)) for ck in c[:-1]]
+
+
 def model_viterbi(x, L, R, cw):
     """One sequence x (T,) float32 through the kernel's decomposition."""
     K = 1 << R
@@ -48,8 +80,9 @@ def model_viterbi(x, L, R, cw):
     TPS = Q // NQ
     NR = NQ // K if NQ >= K else 1
     T = len(x)
+    raw, F, bpw, HQ = record_layout(R)
     m_prev = None
-    words = np.zeros((max(T - 1, 0), TPS), np.uint32)
+    words = np.zeros((max(T - 1, 0), TPS, bpw), np.uint64)
     for t in range(T - 1):
         m_new = np.empty(Q, np.float32)
         for v in range(TPS):
@@ -57,7 +90,7 @@ def model_viterbi(x, L, R, cw):
             mloc = None
             if m_prev is not None:
                 mloc = [[m_prev[k * Rn + r0 + i] for i in range(NR)] for k in range(K)]
-            word = 0
+            rec = [0] * bpw
             for jq in range(NQ - 1, -1, -1):
                 i = (jq >> R) if NQ >= K else 0
                 q = NQ * v + jq
@@ -68,10 +101,19 @@ def model_viterbi(x, L, R, cw):
                     if mloc is not None:
                         d = np.float32(d + mloc[k][i])
                     c.append(d)
-                mn, kk = _tourney(c)
+                w = jq // HQ
+                if raw:
+                    mn, s = _raw_signs(c)
+                    base = 2 * F * ((jq % HQ) // 2) + (jq & 1)
+                    for k in range(F):
+                        rec[w] |= int(s[k]) << (base + 2 * k)
+                else:
+                    mn, kk = _tourney(c)
+                    rec[w] |= kk << (F * (jq % HQ))
                 m_new[q] = mn
-                word = ((word << R) | kk) & 0xFFFFFFFF
-            words[t, v] = word
+            for w in range(bpw):
+                assert rec[w] < (1 << 32)
+                words[t, v, w] = rec[w]
         m_prev = m_new
     # final argmin over all states (first index)
     best_v, best_s = None, None
@@ -89,14 +131,19 @@ def model_viterbi(x, L, R, cw):
     st[T - 1] = s
     for t in range(T - 1, 0, -1):
         q = s >> R
-        w = int(words[t - 1, q // NQ])
-        k = (w >> ((q % NQ) * R)) & (K - 1)
+        jq = q % NQ
+        w = int(words[t - 1, q // NQ, jq // HQ])
+        if raw:
+            bits = w >> (2 * F * ((jq % HQ) // 2) + (jq & 1))
+            k = next((j for j in range(F) if not (bits >> (2 * j)) & 1), F)
+        else:
+            k = (w >> (F * (jq % HQ))) & ((1 << F) - 1)
         s = k * Q + q
         st[t - 1] = s
     return st
 
 
-@pytest.mark.parametrize("L,R", [(6, 1), (6, 2), (6, 3), (8, 4), (7, 2), (8, 3)])
+@pytest.mark.parametrize("L,R", [(6, 1), (6, 2), (6, 3), (8, 4), (7, 2), (8, 3), (9, 2), (10, 3)])
 def test_model_matches_oracle(L, R):
     rng = np.random.RandomState(L * 10 + R)
     cw = O.codebook(L)
@@ -115,6 +162,31 @@ def test_tourney_first_index():
             c = np.round(rng.rand(K) * 3).astype(np.float32)  # many ties
             mn, k = _tourney(c)
             assert mn == c.min() and k == int(np.argmin(c))
+
+
+def test_raw_signs_first_index():
+    """The lowest clear s_k = signbit(m - c_k) is torch's first-index argmin,
+    on ties, zeros, infinities and values a few ulps apart."""
+    rng = np.random.RandomState(1)
+    specials = np.array([0.0, np.inf, 1.0, np.nextafter(np.float32(1), np.float32(2)), 3e-39, 1e-45],
+                        np.float32)
+    for K in (4, 8):
+        for it in range(2000):
+            if it % 2:
+                c = np.round(rng.rand(K) * 3).astype(np.float32)
+            else:
+                c = rng.choice(specials, K).astype(np.float32)
+            mn, s = _raw_signs(list(c))
+            k = next((j for j, b in enumerate(s) if not b), K - 1)
+            assert mn == c.min() and k == int(np.argmin(c))
+
+
+@pytest.mark.parametrize("R", [1, 2, 3, 4])
+def test_record_fits(R):
+    raw, F, bpw, HQ = record_layout(R)
+    NQ = 64 // (1 << R)
+    assert bpw in (1, 2) and HQ * bpw == NQ and HQ * F <= 32
+    assert raw == (R in (2, 3))
 
 
 def _conflict_ways_128(chunks):

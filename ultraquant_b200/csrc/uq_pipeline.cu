@@ -31,7 +31,7 @@ int e8_quant(const void *A, int a_dtype, int64_t size, int64_t group, double ste
              double *rms_out, cudaStream_t st);
 int trellis_normalize(const void *A, int dtype, int64_t nrow, int64_t T, int64_t lda, int64_t Tp, int64_t group,
                       float *xn, float *sc, cudaStream_t st);
-size_t trellis_ws_bytes(int64_t nseq, int T, int L);
+size_t trellis_ws_bytes(int64_t nseq, int T, int L, int R);
 int trellis_viterbi(const float *xn, int64_t nseq, int T, int L, int R, const float *cw, int32_t *states,
                     void *ws, size_t ws_bytes, cudaStream_t st);
 int trellis_decode(const int32_t *states, const float *cw, const float *sc, int64_t group, int64_t ntot,
@@ -63,7 +63,7 @@ struct TrellisPlan {
     size_t vit_ws;
 };
 
-TrellisPlan plan_trellis(int64_t rows, int64_t n0, int L, int seg, int group) {
+TrellisPlan plan_trellis(int64_t rows, int64_t n0, int L, int R, int seg, int group) {
     TrellisPlan p{};
     p.n = uq_next_pow2(n0);
     p.ntot = rows * p.n;
@@ -71,7 +71,7 @@ TrellisPlan plan_trellis(int64_t rows, int64_t n0, int L, int seg, int group) {
     p.nseq = seg > 0 ? p.padded / seg : 0;
     p.ngroups = p.padded / group;
     p.tiles = uq::rht_tiles(rows, p.n);
-    p.vit_ws = uq::trellis_ws_bytes(p.nseq, seg, L);
+    p.vit_ws = uq::trellis_ws_bytes(p.nseq, seg, L, R);
     return p;
 }
 
@@ -144,9 +144,8 @@ int uq_irht28_rows(const void *X, int x_dtype, int64_t rows, int64_t n0, int64_t
                    const double *signs, void *out, int out_dtype, int64_t ld_out, void *stream);
 
 size_t uq_quant_trellis_workspace_bytes(int64_t rows, int64_t n0, int L, int R, int seg, int group) {
-    (void)R;
     if (rows < 0 || n0 < 1 || seg < 1 || group < 8) return 0;
-    const TrellisPlan p = plan_trellis(rows, n0, L, seg, group);
+    const TrellisPlan p = plan_trellis(rows, n0, L, R, seg, group);
     double *a, *a2; float *b; int32_t *c; float *d; double *e; void *f;
     return carve_trellis(p, n0, true, true, nullptr, &a, &a2, &b, &c, &d, &e, &f);
 }
@@ -160,7 +159,7 @@ int uq_quant_trellis(const void *W, int w_dtype, int64_t rows, int64_t n0, int64
         return uq::fail(UQ_ERR_UNSUPPORTED, "uq_quant_trellis: (L=%d, R=%d, seg=%d) not built", L, R, seg);
     if (rows == 0) return UQ_OK;
     if (!W || !H || !signs || !cw || !What || !workspace) return uq::fail(UQ_ERR_INVALID, "uq_quant_trellis: null pointer");
-    const TrellisPlan p = plan_trellis(rows, n0, L, seg, group);
+    const TrellisPlan p = plan_trellis(rows, n0, L, R, seg, group);
     if (p.padded % seg) return uq::fail(UQ_ERR_INVALID, "uq_quant_trellis: padded size %lld not divisible by seg %d",
                                         (long long)p.padded, seg);
     double *sH, *pre, *part;

@@ -269,6 +269,13 @@ __device__ __forceinline__ u64 add2(u64 a, u64 b) {
     asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
     return r;
 }
+// min of three float32 values (the 3-input form of min.f32, sm_100): exact,
+// so the order of the operands does not matter for non-NaN costs
+__device__ __forceinline__ float min3f(float a, float b, float c) {
+    float r;
+    asm("min.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+    return r;
+}
 // bitwise select by the mask word: (m & a) | (~m & b); only bit 31 is used.
 __device__ __forceinline__ unsigned sel_bits(unsigned m, unsigned a, unsigned b) {
     unsigned r;
@@ -355,6 +362,20 @@ template <int L_, int R_, int CL_> struct VitCfg {
     // measured faster; R = 1 and 4 spill when unrolled
     static constexpr int UNROLL = R_ == 2 || R_ == 3 ? 2 : 1;
     static constexpr int SPS = CL == 1 ? kThreads / TPS : 1;   // sequences per set per CTA
+    // Decision record per q.  R = 2, 3: the raw signs s_k = signbit(m - c_k)
+    // for k < K - 1 (F = K - 1 bits; s_k = 0 iff c_k is the minimum m, so the
+    // first-index argmin is the lowest clear bit, K - 1 if none).  This saves
+    // the tournament's subtree selects, and m takes 3-input mins.  R = 1, 4:
+    // the tournament's R-bit index.  A thread's record of one step is BPW
+    // 32-bit words; word w holds q-local jq in [w HQ, (w+1) HQ).  R = 1, 4:
+    // field at bits F (jq % HQ) .. + F.  R = 2, 3: pair pw = (jq % HQ) / 2 of
+    // the word occupies bits 2F pw .. + 2F, s_k of jq at bit 2F pw + 2k +
+    // (jq & 1).
+    static constexpr bool RAW = R_ == 2 || R_ == 3;
+    static constexpr int F = RAW ? K - 1 : R_;
+    static constexpr int BPW = (NQ * F + 31) / 32;
+    static constexpr int HQ = NQ / BPW;
+    static_assert(!RAW || (HQ % 4 == 0 && 4 * F <= 32), "a 4-q chunk fits one word");
     static constexpr int FLOATS = kThreads * NQ;         // floats per (set, buffer) per CTA
     static constexpr int A = Swz<R>::A, M = Swz<R>::M;
     // k-strides (Rn floats per CTA, Rn/2 in a cluster) and slot strides leave
@@ -524,13 +545,15 @@ struct VitThread {
 
     // One step for the owned q: writes m_t (at wbase + offset - wshift: the
     // local buffer, or the outbox for values the peer reads), returns the
-    // backpointer word (field of q-local index jq at bits [jq*R, jq*R + R)).
+    // thread's decision record (BPW words, low word first; the F-bit field
+    // of q-local index jq in word jq / HQ at bits F (jq % HQ) .. + F).
     template <bool PREV>
-    __device__ __forceinline__ unsigned step(float x, const float (&m)[K][NR], unsigned wbase, unsigned wshift) const {
+    __device__ __forceinline__ u64 step(float x, const float (&m)[K][NR], unsigned wbase, unsigned wshift) const {
+        constexpr int F = C::F, CPW = C::HQ / 4;    // decision bits per q, 4-q chunks per word
         const u64 xx = pk2(x, x);
-        unsigned word = 0;
+        unsigned word[C::BPW];
         // chunks of 4 new m values (2 pairs) are stored as soon as they are
-        // complete; each chunk packs its 4*R decision bits in its own word
+        // complete; each chunk packs its 4*F decision bits in its own word
         // (independent shift chains), merged with bit-field inserts
 #pragma unroll
         for (int c4 = NQ / 4 - 1; c4 >= 0; --c4) {
@@ -546,20 +569,55 @@ struct VitThread {
                     d = mul2(d, d);
                     c[k] = PREV ? add2(d, pk2(m[k][i], m[k][i])) : d;
                 }
-                unsigned blo[R], bhi[R];
-                const u64 mn = tourney<R>(c, blo, bhi);
-                up2(mn, mo[2 * (p - 2 * c4)], mo[2 * (p - 2 * c4) + 1]);
+                if constexpr (C::RAW) {
+                    // m = min over k (3-input mins), then s_k = sign(m - c_k):
+                    // m - c_k is +0 exactly when c_k == m, negative otherwise
+                    // (costs are never -0), so the lowest clear bit is the
+                    // first-index argmin of trellis.py's torch.min; all-inf
+                    // candidates give inf - inf = the canonical NaN (sign
+                    // clear), i.e. k = 0 as torch picks
+                    float lo[K], hi[K];
 #pragma unroll
-                for (int j = R - 1; j >= 0; --j) cw_bits = shift_in_sign(cw_bits, bhi[j]);
+                    for (int k = 0; k < K; ++k) up2(c[k], lo[k], hi[k]);
+                    float mlo, mhi;
+                    if constexpr (K == 4) {
+                        mlo = min3f(lo[0], lo[1], fminf(lo[2], lo[3]));
+                        mhi = min3f(hi[0], hi[1], fminf(hi[2], hi[3]));
+                    } else {
+                        mlo = min3f(min3f(lo[0], lo[1], lo[2]), min3f(lo[3], lo[4], lo[5]), fminf(lo[6], lo[7]));
+                        mhi = min3f(min3f(hi[0], hi[1], hi[2]), min3f(hi[3], hi[4], hi[5]), fminf(hi[6], hi[7]));
+                    }
+                    mo[2 * (p - 2 * c4)] = mlo;
+                    mo[2 * (p - 2 * c4) + 1] = mhi;
+                    // the pair's 2F bits interleave its two q: bit 2k holds s_k of
+                    // the even q (low half), bit 2k + 1 that of the odd q, so
+                    // each difference is packed as soon as it exists
+                    const u64 mn = pk2(mlo, mhi);
 #pragma unroll
-                for (int j = R - 1; j >= 0; --j) cw_bits = shift_in_sign(cw_bits, blo[j]);
+                    for (int k = F - 1; k >= 0; --k) {
+                        float el, eh;
+                        up2(sub2(mn, c[k]), el, eh);
+                        cw_bits = shift_in_sign(cw_bits, __float_as_uint(eh));
+                        cw_bits = shift_in_sign(cw_bits, __float_as_uint(el));
+                    }
+                } else {
+                    unsigned blo[R], bhi[R];
+                    const u64 mn = tourney<R>(c, blo, bhi);
+                    up2(mn, mo[2 * (p - 2 * c4)], mo[2 * (p - 2 * c4) + 1]);
+#pragma unroll
+                    for (int j = R - 1; j >= 0; --j) cw_bits = shift_in_sign(cw_bits, bhi[j]);
+#pragma unroll
+                    for (int j = R - 1; j >= 0; --j) cw_bits = shift_in_sign(cw_bits, blo[j]);
+                }
             }
-            if (c4 == NQ / 4 - 1) word = cw_bits << (4 * R * c4);
-            else word = bfi(cw_bits, word, 4 * R * c4, 4 * R);
+            const int w = c4 / CPW, sub = c4 % CPW;
+            if (sub == CPW - 1) word[w] = cw_bits << (4 * F * sub);
+            else word[w] = bfi(cw_bits, word[w], 4 * F * sub, 4 * F);
             const unsigned o = C::FAST ? (wr0 ^ (unsigned(c4) << 4)) : off(NQ * v + 4 * c4);
             sts4(wbase + o - wshift, mo[0], mo[1], mo[2], mo[3]);
         }
-        return word;
+        if constexpr (C::BPW == 1) return u64(word[0]);
+        else return u64(word[0]) | (u64(word[1]) << 32);
     }
 
     // Final step: costs of all owned states, first-index argmin.
@@ -672,7 +730,9 @@ viterbi_fwd_kernel(VitArgs a) {
 #pragma unroll
     for (int X = 0; X < NSET; ++X) vmask |= (first + X < a.nbatch ? 1u : 0u) << X;
     const float *xcur = a.xn + (a.seq0 + (vmask & 1u ? first : 0)) * int64_t(a.T);
-    uint32_t *bcur = a.bp + (vmask & 1u ? first : 0) * int64_t(bstride) + th.v;
+    // one record (BPW words, low word first) per thread and step
+    using Rec = typename std::conditional<C::BPW == 2, u64, uint32_t>::type;
+    Rec *bcur = reinterpret_cast<Rec *>(a.bp) + (vmask & 1u ? first : 0) * int64_t(bstride) + th.v;
     float xv[NSET];
 #pragma unroll
     for (int X = 0; X < NSET; ++X) xv[X] = (vmask >> X) & 1u ? __ldg(xcur + Off(X) * Off(a.T)) : 0.f;
@@ -704,14 +764,14 @@ viterbi_fwd_kernel(VitArgs a) {
                 xv[X] = (vmask >> X) & 1u ? __ldg(xcur + X * int64_t(a.T) + t + 1) : 0.f;
             else
                 xv[X] = (vmask >> X) & 1u ? __ldg(xcur + (Off(X) * Off(a.T) + Off(t + 1))) : 0.f;
-            unsigned word;
+            Rec word;
             if (CL == 1) {
                 const unsigned wb = smem0 + unsigned(X * NBUF + (t & 1)) * BUF;
                 if (t == 0) {
-                    word = th.template step<false>(x, m, wb, 0u);
+                    word = Rec(th.template step<false>(x, m, wb, 0u));
                 } else {
                     th.load_prev(smem0 + unsigned(X * NBUF + ((t - 1) & 1)) * BUF, m);
-                    word = th.template step<true>(x, m, wb, 0u);
+                    word = Rec(th.template step<true>(x, m, wb, 0u));
                 }
                 seq_sync<C>(th.slot);
             } else {
@@ -720,13 +780,13 @@ viterbi_fwd_kernel(VitArgs a) {
                 const unsigned wb = wbase0 + unsigned(X * NBUF + jw) * wstep;
                 const unsigned wsh = 0u;
                 if (t == 0) {
-                    word = th.template step<false>(x, m, wb, wsh);
+                    word = Rec(th.template step<false>(x, m, wb, wsh));
                 } else {
                     const int jr = (t - 1) & 1;
                     const unsigned mbr = full0 + unsigned(X * NBUF + jr) * 8u;
                     vit_wait(mbr, unsigned(((t - 1) >> 1) & 1), fail);
                     th.load_prev(smem0 + unsigned(X * NBUF + jr) * BUF, m);
-                    word = th.template step<true>(x, m, wb, wsh);
+                    word = Rec(th.template step<true>(x, m, wb, wsh));
                 }
                 if (wremote) fence_proxy_async_smem();   // outbox writes -> async proxy
                 // no CTA barrier: the last warp to finish the step ships the
@@ -885,23 +945,37 @@ __global__ void wait_timeout_probe_kernel(unsigned long long limit_ns, int *stat
     if (threadIdx.x == 0) mbar_arrive(addr);   // complete the phase before exit
 }
 
-// Traceback: one thread per sequence walks the backpointer words.
+// Traceback: one thread per sequence walks the decision records (the
+// record layout of VitCfg: F-bit field of q-local jq in word jq / HQ).
 template <int R>
 __global__ void traceback_kernel(const uint32_t *bp, const int32_t *fin, int64_t nbatch, int T, int L,
                                  int32_t *states, int64_t seq0) {
-    constexpr int K = 1 << R, NQ = 64 / K;
+    using C = VitCfg<(2 * R > 6 ? 2 * R : 6), R, 1>;     // record constants depend on R only
+    constexpr int K = 1 << R, NQ = C::NQ, F = C::F, BPW = C::BPW, HQ = C::HQ;
     const int64_t sq = blockIdx.x * int64_t(blockDim.x) + threadIdx.x;
     if (sq >= nbatch) return;
     const int Q = 1 << (L - R);
     const int TPS = Q / NQ;
-    const uint32_t *b = bp + sq * int64_t(T - 1) * TPS;
+    const uint32_t *b = bp + sq * int64_t(T - 1) * TPS * BPW;
     int32_t *out = states + (seq0 + sq) * int64_t(T);
     int s = fin[sq] & ((1 << L) - 1);
     out[T - 1] = s;
     for (int t = T - 1; t >= 1; --t) {
         const int q = s >> R;
-        const uint32_t w = __ldg(b + int64_t(t - 1) * TPS + q / NQ);
-        const int k = (w >> ((q % NQ) * R)) & (K - 1);
+        const int jq = q % NQ;
+        const uint32_t w = __ldg(b + (int64_t(t - 1) * TPS + q / NQ) * BPW + jq / HQ);
+        int k;
+        if constexpr (C::RAW) {
+            // s_k at bit 2k of the shifted pair bits; the lowest clear one is
+            // the first minimum (K - 1 if none)
+            const unsigned bits = w >> (2 * F * ((jq % HQ) >> 1) + (jq & 1));
+            k = F;
+#pragma unroll
+            for (int j = F - 1; j >= 0; --j)
+                if (!((bits >> (2 * j)) & 1u)) k = j;
+        } else {
+            k = int((w >> (F * (jq % HQ))) & ((1u << F) - 1u));
+        }
         s = k * Q + q;
         out[t - 1] = s;
     }
@@ -1024,19 +1098,31 @@ int vit_check(int64_t nseq, int T, int L, int R) {
 
 namespace uq {
 
-int64_t vit_seq_bytes(int T, int L) {
-    // backpointer words per sequence: (T-1) * 2^L / 64, plus the final state
-    return int64_t(T - 1) * ((int64_t(1) << L) / 64) * 4 + 4;
+int vit_record_words(int R) {
+    switch (R) {
+        case 1: return VitCfg<6, 1, 1>::BPW;
+        case 2: return VitCfg<6, 2, 1>::BPW;
+        case 3: return VitCfg<6, 3, 1>::BPW;
+        case 4: return VitCfg<8, 4, 1>::BPW;
+    }
+    return 1;
 }
 
-size_t trellis_ws_bytes(int64_t nseq, int T, int L) {
-    // cap the backpointer batch at ~8 GiB (whole sequences, at least one
-    // launch worth of sequences): each batch ends with a traceback launch
-    // that is latency bound (~0.19 ms whatever its size), so larger batches
-    // mean fewer of them (at L = 16, T = 256: 7,900 sequences per batch)
-    const int64_t per = vit_seq_bytes(T, L);
+int64_t vit_seq_bytes(int T, int L, int R) {
+    // decision records per sequence: (T-1) * 2^L / 64 of vit_record_words(R)
+    // 32-bit words, plus the final state
+    return int64_t(T - 1) * ((int64_t(1) << L) / 64) * 4 * vit_record_words(R) + 4;
+}
+
+size_t trellis_ws_bytes(int64_t nseq, int T, int L, int R) {
+    // cap the backpointer batch at ~8 GiB per record word (whole sequences,
+    // at least one launch worth of sequences): each batch ends with a
+    // traceback launch that is latency bound (~0.19 ms whatever its size),
+    // so larger batches mean fewer of them (at L = 16, T = 256: ~8,200
+    // sequences per batch)
+    const int64_t per = vit_seq_bytes(T, L, R);
     int64_t want = nseq;
-    const int64_t cap = (int64_t(8) << 30) / per;
+    const int64_t cap = (int64_t(8) << 30) * vit_record_words(R) / per;
     const int64_t min_batch = 2 * 148;
     if (want > cap) want = std::max<int64_t>(cap, min_batch);
     return size_t(std::max<int64_t>(want, 1) * per) + 512;
@@ -1044,14 +1130,14 @@ size_t trellis_ws_bytes(int64_t nseq, int T, int L) {
 
 int trellis_viterbi(const float *xn, int64_t nseq, int T, int L, int R, const float *cw, int32_t *states,
                     void *ws, size_t ws_bytes, cudaStream_t st) {
-    const int64_t per = vit_seq_bytes(T, L);
+    const int64_t per = vit_seq_bytes(T, L, R);
     int64_t batch = int64_t((ws_bytes > 512 ? ws_bytes - 512 : 0) / size_t(per));
     if (batch < 1) return fail(UQ_ERR_WORKSPACE, "viterbi: workspace %zu too small (need %lld per sequence)",
                                ws_bytes, (long long)per);
     if (batch > nseq) batch = nseq;
     Carver c(ws, ws_bytes);
     int32_t *fin = c.take<int32_t>(size_t(batch));
-    uint32_t *bp = c.take<uint32_t>(size_t(batch) * size_t(T - 1) * ((size_t(1) << L) / 64));
+    uint32_t *bp = c.take<uint32_t>(size_t(batch) * size_t(T - 1) * ((size_t(1) << L) / 64) * vit_record_words(R));
     switch (R) {
         case 1: return run_viterbi_r<1>(xn, nseq, T, L, cw, states, bp, fin, batch, st);
         case 2: return run_viterbi_r<2>(xn, nseq, T, L, cw, states, bp, fin, batch, st);
@@ -1186,7 +1272,7 @@ int uq_trellis_viterbi_noalloc(const float *xn, int64_t nseq, int T, int L, int 
                                int32_t *states, void *stream) {
     int rc = vit_check(nseq, T, L, R);
     if (rc) return rc;
-    const int64_t per = uq::vit_seq_bytes(T, L);
+    const int64_t per = uq::vit_seq_bytes(T, L, R);
     if (size_t(per) + 512 > kNoAllocScratchBytes)
         return uq::fail(UQ_ERR_INVALID,
                         "uq_trellis_viterbi_noalloc: one sequence (T=%d, L=%d) needs %lld bytes of backpointer "
@@ -1283,7 +1369,7 @@ int uq_trellis_normalize_rows(const void *A, int a_dtype, int64_t nrow, int64_t 
 
 size_t uq_trellis_workspace_bytes(int64_t nseq, int T, int L, int R) {
     if (vit_check(nseq, T, L, R) != UQ_OK) return 0;
-    return uq::trellis_ws_bytes(nseq, T, L);
+    return uq::trellis_ws_bytes(nseq, T, L, R);
 }
 
 int uq_trellis_viterbi(const float *xn, int64_t nseq, int T, int L, int R, const float *cw, int32_t *states,
