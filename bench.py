@@ -56,7 +56,7 @@ HBM_FALLBACK_GBS = 6650.0
 
 # ncu (L=16, T=256, one launch of 296 sequences per k): DRAM read + write
 # bytes of viterbi_fwd_kernel per sequence (the traffic is the backpointers)
-NCU_DRAM_BYTES_PER_SEQ = {2: (1.252352e6 + 251.667968e6) / 296, 3: (1.233152e6 + 251.116544e6) / 296}
+NCU_DRAM_BYTES_PER_SEQ = {2: (0.899072e6 + 559.365888e6) / 296, 3: (0.901888e6 + 561.186304e6) / 296}
 
 
 def make_inputs(seed: int):
@@ -412,7 +412,8 @@ def run_tensor(args, rank: int, world: int, local: int):
                     / max(1, int(vn.value))),
         "traffic_unit": "bytes per launch",
         "traffic_source": "ncu capture, 296 sequences per k, scaled by the sequences per launch",
-        "algorithmic_bytes_per_launch": my_seqs * (SEG - 1) * (1 << L_BITS) // 16 / max(1, int(vn.value)),
+        # backpointer bytes: 2^L / 64 two-word records (8 B) per step and sequence
+        "algorithmic_bytes_per_launch": my_seqs * (SEG - 1) * (1 << L_BITS) // 8 / max(1, int(vn.value)),
     }
     if clocks and clocks.get("sm_mhz"):
         roofline["sm_mhz_median"] = clocks["sm_mhz"]
