@@ -568,6 +568,12 @@ def run_weight_set(args, rank: int, world: int, local: int):
     data = {} if stream_blocks else {(s.tensor.name, s.row0): gen(s) for s in mine}
     for s in mine:
         H_of(s.tensor)
+    # untimed warm-up: one block of every (padded width, k) this rank holds,
+    # so the pipeline's workspace and the allocator's pools exist before timing
+    warm = {}
+    for s in mine:
+        warm.setdefault((s.tensor.padded_cols, s.tensor.R), s)
+    shard.quantize_shards(list(warm.values()), rank, lambda s: (gen(s), H_of(s.tensor)), SEG, GROUP)
     torch.cuda.synchronize()
 
     def weights(s):

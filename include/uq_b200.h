@@ -207,10 +207,10 @@ int uq_trellis_viterbi(const float *xn, int64_t nseq, int T, int L, int R, const
  * that context (cudaGetSymbolAddress); make that first call before any
  * stream capture.  Every call shares the array: calls that overlap on the
  * GPU (other streams, other host threads) race.  Throughput: at L = 16,
- * T = 256 one sequence needs ~1 MiB, so a batch is 64 sequences, under half
- * of the 148 that one wave of the cluster kernel runs, and each batch ends
- * with a latency-bound traceback launch -- expect well under half the
- * throughput of uq_trellis_viterbi with a workspace at that size. */
+ * T = 256 one sequence needs ~2 MiB (R = 2, 3), so a batch is 32 sequences,
+ * under a quarter of the 148 that one wave of the cluster kernel runs, and
+ * each batch ends with a latency-bound traceback launch -- expect about a
+ * fifth of the throughput of uq_trellis_viterbi with a workspace there. */
 size_t uq_trellis_noalloc_scratch_bytes(void);
 int uq_trellis_viterbi_noalloc(const float *xn, int64_t nseq, int T, int L, int R,
                                const float *cw, int32_t *states, void *stream);
