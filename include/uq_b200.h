@@ -159,6 +159,22 @@ size_t uq_e8_calibrate_sample_workspace_bytes(int64_t ns);
 int uq_e8_calibrate_sample(const double *sub, int64_t ns, double target_bpw, double *step_host,
                            void *workspace, size_t workspace_bytes, void *stream);
 
+/* Opt-in per-row scale search over 16 candidate steps (no counterpart in the
+ * reference, whose q_e8_fast uses one global step, qlab.py:159-183).  A:
+ * rotated matrix (rows, n) fp64, 16-byte aligned, n a multiple of 256 in
+ * [256, 2^17]; groups of 256.  Candidates step_c = step * 2^((c - 8) / 8),
+ * c = 0..15.  For each row and candidate: D = sum (A - rec)^2 (numpy order)
+ * and H = the bits of the row's lattice coordinates z = 2p under their own
+ * histogram.  Row r takes the first argmin of D + lam * H at the smallest
+ * lam whose total H does not exceed the global step's (c = 8).  Outputs
+ * (nullable): rec (rows * n, may equal A), idx = 2p int16, choice (rows)
+ * int32 candidate per row, *lam_host.  Synchronises the stream (lam is
+ * chosen on the host).  UQ_ERR_UNSUPPORTED if some |2p| exceeds 255. */
+size_t uq_e8_scale_search_workspace_bytes(int64_t rows, int64_t n);
+int uq_e8_scale_search(const double *A, int64_t rows, int64_t n, double step, double *rec, int16_t *idx,
+                       int32_t *choice, double *lam_host, void *workspace, size_t workspace_bytes,
+                       void *stream);
+
 /* ---------------------------------------------------------------------
  * Bitshift trellis (trellis.py:14-108, qat.py:11-59)
  * ------------------------------------------------------------------- */
@@ -337,6 +353,16 @@ size_t uq_quant_e8_b28_workspace_bytes(int64_t rows, int64_t n0);
 int uq_quant_e8_b28(const void *W, int w_dtype, int64_t rows, int64_t n0, int64_t ldw,
                     const double *H, double step, const double *signs, float *What, int16_t *idx,
                     double *err, void *workspace, size_t workspace_bytes, void *stream);
+
+/* Opt-in variant of uq_quant_e8 (buildalloc.py:21-24) with the per-row
+ * scale search (uq_e8_scale_search) in place of the single step, groups of
+ * 256; choice (rows, nullable) and *lam_host as there.  No counterpart in
+ * the reference.  Synchronises the stream. */
+size_t uq_quant_e8_search_workspace_bytes(int64_t rows, int64_t n0);
+int uq_quant_e8_search(const void *W, int w_dtype, int64_t rows, int64_t n0, int64_t ldw,
+                       const double *H, double step, const double *signs, float *What, int16_t *idx,
+                       int32_t *choice, double *lam_host, double *err, void *workspace,
+                       size_t workspace_bytes, void *stream);
 
 /* ---------------------------------------------------------------------
  * Device status (no counterpart in the reference)

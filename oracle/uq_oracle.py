@@ -31,6 +31,7 @@ __all__ = [
     "group_rms_f32", "viterbi_segments", "pack_states", "unpack_states", "enc_q8", "deq_q8",
     "hadamard28", "rht28_rows", "irht28_rows", "quant_step_b28", "q_uniform",
     "e8_codebook", "nearest_exact", "q_e8", "e8_bisect", "group_gn",
+    "E8_SEARCH_FACTORS", "log2_table", "e8_scale_search_tables", "e8_scale_search_select", "e8_scale_search",
 ]
 
 
@@ -174,6 +175,106 @@ def q_e8_fast(A, target_bpw=2.0, group=256, calib_key="g", fixed_step=None,
         step = cache[calib_key]
     rec = (e8_decode(gn / step) * step).reshape(-1, group) * rms
     return rec.ravel()[:A.size].reshape(A.shape)
+
+
+# ---------------------------------------------------------------------------
+# Opt-in per-row scale search for the fixed-step E8 quantizer.  No counterpart
+# in the reference (qlab.py:159-183 has one global step); this restatement
+# DEFINES its parity.  For every row and each of 16 candidate steps
+# step_c = step * 2^((c - 8) / 8) the row is decoded as q_e8_fast does it
+# (per-256 group RMS, e8_decode(gn / step_c), rec = (p * step_c) * rms), and
+#   D[r, c] = sum over the row of (A - rec)^2      (numpy order: per group,
+#                                                   then over the row's groups)
+#   H[r, c] = N log2 N - sum_v cnt_v log2 cnt_v     (bits of the row's N
+#             lattice coordinates z = 2p under their own histogram; the sum
+#             runs over z = -255 .. 255 in order, log2 from a table of the C
+#             library's log2 of integers)
+# Each row then takes c_r = first argmin_c D[r, c] + lam * H[r, c], with the
+# smallest lam (bisection in exact midpoints) at which the total rate
+# sum_r H[r, c_r] does not exceed that of the global step (c = 8): the same
+# modelled rate, spent where it removes the most squared error.
+# ---------------------------------------------------------------------------
+E8_SEARCH_FACTORS = [float.fromhex(h) for h in (
+    "0x1.0000000000000p-1", "0x1.172b83c7d517bp-1", "0x1.306fe0a31b715p-1", "0x1.4bfdad5362a27p-1",
+    "0x1.6a09e667f3bcdp-1", "0x1.8ace5422aa0dbp-1", "0x1.ae89f995ad3adp-1", "0x1.d5818dcfba487p-1",
+    "0x1.0000000000000p+0", "0x1.172b83c7d517bp+0", "0x1.306fe0a31b715p+0", "0x1.4bfdad5362a27p+0",
+    "0x1.6a09e667f3bcdp+0", "0x1.8ace5422aa0dbp+0", "0x1.ae89f995ad3adp+0", "0x1.d5818dcfba487p+0")]
+E8_SEARCH_BASE = 8            # the candidate equal to the given step
+E8_SEARCH_ZMAX = 255          # |2p| bound of the rate histogram
+
+
+def log2_table(n: int) -> np.ndarray:
+    """log2(i) for i = 0 .. n from the C library (math.log2), 0 at i = 0."""
+    import math
+    return np.array([0.0] + [math.log2(i) for i in range(1, n + 1)], np.float64)
+
+
+def e8_scale_search_tables(A, step, group=256):
+    """(D, H) of shape (rows, 16) for the rotated matrix A (rows, n) fp64, n a
+    multiple of `group`."""
+    A = np.asarray(A, np.float64)
+    rows, n = A.shape
+    g = A.reshape(rows, n // group, group)
+    rms = np.sqrt((g ** 2).mean(2, keepdims=True)) + 1e-12
+    gn = g / rms
+    LG = log2_table(n)
+    D = np.empty((rows, 16))
+    H = np.empty((rows, 16))
+    for c, f in enumerate(E8_SEARCH_FACTORS):
+        s = step * f
+        p = e8_decode((gn / s).reshape(-1, 8)).reshape(g.shape)
+        rec = (p * s) * rms
+        D[:, c] = ((g - rec) ** 2).sum(axis=2).sum(axis=1)
+        z = (p * 2).astype(np.int64).reshape(rows, n)
+        if np.abs(z).max() > E8_SEARCH_ZMAX:
+            raise ValueError("lattice coordinate beyond the rate histogram")
+        for r in range(rows):
+            cnt = np.bincount(z[r] + E8_SEARCH_ZMAX, minlength=2 * E8_SEARCH_ZMAX + 1)
+            H[r, c] = n * LG[n] - np.cumsum(cnt * LG[cnt])[-1]
+    return D, H
+
+
+def e8_scale_search_select(D, H):
+    """(choice per row, lam): the per-row candidates at the smallest lam whose
+    total rate is at most the base step's (sequential sums over rows)."""
+    def pick(lam):
+        return np.argmin(D + lam * H, axis=1)
+
+    def rate(c):
+        return float(np.cumsum(H[np.arange(H.shape[0]), c])[-1])
+
+    r0 = float(np.cumsum(H[:, E8_SEARCH_BASE])[-1])
+    if rate(pick(0.0)) <= r0:
+        return pick(0.0), 0.0
+    hi = 1.0
+    for _ in range(400):
+        if rate(pick(hi)) <= r0:
+            break
+        hi *= 2.0
+    lo = 0.0
+    for _ in range(64):
+        mid = (lo + hi) * 0.5
+        if rate(pick(mid)) <= r0:
+            hi = mid
+        else:
+            lo = mid
+    return pick(hi), hi
+
+
+def e8_scale_search(A, step, group=256):
+    """Opt-in per-row scale search on the rotated matrix A: returns (rec fp64,
+    choice per row, lam) with rec the q_e8_fast reconstruction at each row's
+    chosen step."""
+    A = np.asarray(A, np.float64)
+    rows, n = A.shape
+    D, H = e8_scale_search_tables(A, step, group)
+    choice, lam = e8_scale_search_select(D, H)
+    g = A.reshape(rows, n // group, group)
+    rms = np.sqrt((g ** 2).mean(2, keepdims=True)) + 1e-12
+    s = (step * np.array(E8_SEARCH_FACTORS))[choice][:, None, None]
+    p = e8_decode(((g / rms) / s).reshape(-1, 8)).reshape(g.shape)
+    rec = ((p * s) * rms).reshape(rows, n)
+    return rec, choice, lam
 
 
 # ---------------------------------------------------------------------------

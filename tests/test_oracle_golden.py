@@ -309,3 +309,24 @@ def test_q_e8_oracle(g_qe8, case):
 def test_q_e8_oracle_group64(g_qe8):
     A = g_qe8["qe_A"][:8]
     assert qe8_same_or_tie(O.q_e8(A, 2.0, group_scale=64), g_qe8["qe_A_g64_2.0"], A, 2.0, 64) == 0
+
+
+def test_e8_scale_search_restatement():
+    """The opt-in per-row scale search (no reference counterpart): every row
+    is the reference's q_e8_fast at its chosen step (pinned by the goldens
+    above), the total rate does not exceed the global step's, the choice is
+    the argmin at the returned lam, and any smaller lam breaks the rate."""
+    rng = np.random.RandomState(11)
+    A = O.rht_rows(rng.standard_t(4, size=(24, 1024)) / np.sqrt(2) * 0.015)
+    step = 0.48
+    rec, choice, lam = O.e8_scale_search(A, step)
+    D, H = O.e8_scale_search_tables(A, step)
+    steps = step * np.array(O.E8_SEARCH_FACTORS)
+    for r in range(A.shape[0]):
+        assert same_bits(rec[r], O.q_e8_fast(A[r:r + 1], fixed_step=steps[choice[r]]).ravel())
+    rows = np.arange(A.shape[0])
+    assert H[rows, choice].sum() <= H[:, 8].sum() * (1 + 1e-15)
+    assert np.array_equal(choice, np.argmin(D + lam * H, axis=1))
+    if lam > 0:
+        lower = np.argmin(D + (lam * (1 - 1e-9)) * H, axis=1)
+        assert np.cumsum(H[rows, lower])[-1] >= np.cumsum(H[rows, choice])[-1]

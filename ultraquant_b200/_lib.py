@@ -48,6 +48,10 @@ SIGNATURES = {
     "uq_e8_sample_gn": (_i32, [_p, _i32, _i64, _i64, _p, _i64, _p, _p, _sz, _p]),
     "uq_e8_calibrate_sample_workspace_bytes": (_sz, [_i64]),
     "uq_e8_calibrate_sample": (_i32, [_p, _i64, _f64, _p, _p, _sz, _p]),
+    "uq_e8_scale_search_workspace_bytes": (_sz, [_i64, _i64]),
+    "uq_e8_scale_search": (_i32, [_p, _i64, _i64, _f64, _p, _p, _p, _p, _p, _sz, _p]),
+    "uq_quant_e8_search_workspace_bytes": (_sz, [_i64, _i64]),
+    "uq_quant_e8_search": (_i32, [_p, _i32, _i64, _i64, _i64, _p, _f64, _p, _p, _p, _p, _p, _p, _p, _sz, _p]),
     "uq_trellis_codebook": (_i32, [_i32, _p, _p]),
     "uq_trellis_normalize": (_i32, [_p, _i32, _i64, _i64, _i64, _p, _p, _p]),
     "uq_trellis_normalize_rows": (_i32, [_p, _i32, _i64, _i64, _i64, _i64, _p, _p, _p]),

@@ -21,7 +21,7 @@ CSRC = os.path.join(HERE, "csrc")
 OUT = os.path.join(HERE, "_build")
 LIB = os.path.join(HERE, "libuq_b200.so")
 
-SOURCES = ["uq_host.cpp", "uq_rht.cu", "uq_e8.cu", "uq_trellis.cu", "uq_pipeline.cu", "uq_qat.cu", "uq_q8.cu", "uq_qe8.cu", "uq_peak.cu"]
+SOURCES = ["uq_host.cpp", "uq_rht.cu", "uq_e8.cu", "uq_trellis.cu", "uq_pipeline.cu", "uq_qat.cu", "uq_q8.cu", "uq_qe8.cu", "uq_peak.cu", "uq_e8search.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-fmad=false", "-Xcompiler", "-fPIC",
               "-Xcompiler", "-O2", "--expt-relaxed-constexpr"]

@@ -29,6 +29,9 @@ int rht_prescale(const double *colscale, const double *signs, int64_t n0, int64_
 int64_t rht_tiles(int64_t rows, int64_t n);
 int e8_quant(const void *A, int a_dtype, int64_t size, int64_t group, double step, double *rec, int16_t *idx,
              double *rms_out, cudaStream_t st);
+size_t e8_search_ws_bytes(int64_t rows, int64_t n);
+int e8_scale_search(const double *A, int64_t rows, int64_t n, double step, double *rec, int16_t *idx,
+                    int32_t *choice_out, double *lam_host, void *ws, size_t ws_bytes, cudaStream_t st);
 int trellis_normalize(const void *A, int dtype, int64_t nrow, int64_t T, int64_t lda, int64_t Tp, int64_t group,
                       float *xn, float *sc, cudaStream_t st);
 size_t trellis_ws_bytes(int64_t nseq, int T, int L, int R);
@@ -216,6 +219,52 @@ int uq_quant_e8(const void *W, int w_dtype, int64_t rows, int64_t n0, int64_t ld
     if ((rc = uq::rht_prescale(sH, signs, n0, n, pre, st))) return rc;
     if ((rc = uq::rht_forward(W, w_dtype, rows, n0, ldw, sH, pre, signs, X, UQ_F64, n, st))) return rc;
     if ((rc = uq::e8_quant(X, UQ_F64, rows * n, group, step, X, idx, nullptr, st))) return rc;
+    return uq::rht_inverse(X, UQ_F64, rows, n, n, n0, signs, sH, pre, What, UQ_F32, n0, W, w_dtype, ldw, part, err,
+                           st);
+}
+
+// Opt-in: the buildalloc recipe with the per-row scale search over 16
+// candidate steps (uq_e8_scale_search) in place of the single fixed step.
+size_t uq_quant_e8_search_workspace_bytes(int64_t rows, int64_t n0) {
+    if (rows < 0 || n0 < 1) return 0;
+    const int64_t n = uq_next_pow2(n0);
+    if (n < 256) return 0;
+    uq::Carver c(nullptr, ~size_t(0));
+    c.take<double>(size_t(n0));
+    c.take<double>(size_t(n));
+    c.take<double>(size_t(rows * n));
+    c.take<double>(size_t(2 * uq::rht_tiles(rows, n)));
+    c.take<char>(uq::e8_search_ws_bytes(rows, n));
+    return c.off;
+}
+
+int uq_quant_e8_search(const void *W, int w_dtype, int64_t rows, int64_t n0, int64_t ldw, const double *H,
+                       double step, const double *signs, float *What, int16_t *idx, int32_t *choice,
+                       double *lam_host, double *err, void *workspace, size_t workspace_bytes, void *stream) {
+    int rc = check_common(rows, n0, ldw, w_dtype, 256, "uq_quant_e8_search");
+    if (rc) return rc;
+    const int64_t n = uq_next_pow2(n0);
+    if (n < 256) return uq::fail(UQ_ERR_INVALID, "uq_quant_e8_search: padded width %lld below one group", (long long)n);
+    if (!(step > 0.0)) return uq::fail(UQ_ERR_INVALID, "uq_quant_e8_search: step must be > 0");
+    if (rows == 0) {
+        if (lam_host) *lam_host = 0.0;
+        return UQ_OK;
+    }
+    if (!W || !H || !signs || !What || !workspace) return uq::fail(UQ_ERR_INVALID, "uq_quant_e8_search: null pointer");
+    uq::Carver c(workspace, workspace_bytes);
+    double *sH = c.take<double>(size_t(n0));
+    double *pre = c.take<double>(size_t(n));
+    double *X = c.take<double>(size_t(rows * n));
+    double *part = c.take<double>(size_t(2 * uq::rht_tiles(rows, n)));
+    const size_t sws = uq::e8_search_ws_bytes(rows, n);
+    void *swsp = c.take<char>(sws);
+    if (!c.ok()) return uq::fail(UQ_ERR_WORKSPACE, "uq_quant_e8_search: workspace %zu < %zu", workspace_bytes, c.off);
+    cudaStream_t st = UQ_STREAM(stream);
+    { uq::ProfScope _p("importance_scale", st); importance_scale_kernel<<<1, 1024, 0, st>>>(H, n0, sH); }
+    if ((rc = uq::check_cuda("importance_scale_kernel launch"))) return rc;
+    if ((rc = uq::rht_prescale(sH, signs, n0, n, pre, st))) return rc;
+    if ((rc = uq::rht_forward(W, w_dtype, rows, n0, ldw, sH, pre, signs, X, UQ_F64, n, st))) return rc;
+    if ((rc = uq::e8_scale_search(X, rows, n, step, X, idx, choice, lam_host, swsp, sws, st))) return rc;
     return uq::rht_inverse(X, UQ_F64, rows, n, n, n0, signs, sH, pre, What, UQ_F32, n0, W, w_dtype, ldw, part, err,
                            st);
 }

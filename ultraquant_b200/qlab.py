@@ -18,7 +18,8 @@ from . import _lib
 from .q8 import deq_q8  # noqa: F401  (qlab.py:27-32, used by load_WH)
 
 __all__ = ["wnmse", "_next_pow2", "rht_rows", "irht_rows", "_d8_decode", "e8_decode",
-           "_entropy_bpw", "q_e8_fast", "_E8_SCALE", "deq_q8", "q_uniform", "e8_codebook", "q_e8"]
+           "_entropy_bpw", "q_e8_fast", "_E8_SCALE", "deq_q8", "q_uniform", "e8_codebook", "q_e8",
+           "e8_scale_search"]
 
 # qlab.py:158 -- calibrated E8 step per calib_key, reused across tensors
 _E8_SCALE: dict = {}
@@ -264,3 +265,29 @@ def q_e8_fast(A, target_bpw=2.0, group=256, calib_key="g", fixed_step=None):
         _lib.check(lib.uq_e8_quant(a.data_ptr(), D.dtype_code(a), size, int(group), step, rec.data_ptr(), None, st),
                    "q_e8_fast")
     return _ret(rec, A)
+
+
+def e8_scale_search(A, step, group=256):
+    """Opt-in per-row scale search (no counterpart in the reference, whose
+    q_e8_fast uses one global step, qlab.py:159-183): each row of the rotated
+    matrix A (rows, n), n a multiple of 256, is quantized like
+    q_e8_fast(fixed_step=s) at the one of 16 steps s = step * 2^((c-8)/8)
+    picked by the rate-constrained search of uq_e8_scale_search.  Returns
+    (rec fp64 like A, choice int32 per row, lam)."""
+    if group != 256:
+        raise ValueError("e8_scale_search quantizes groups of 256")
+    lib = _lib.load()
+    a = D.as_device(A, torch.float64)
+    if a.dim() != 2:
+        raise ValueError("e8_scale_search: A must be (rows, n)")
+    rows, n = a.shape
+    rec = torch.empty_like(a)
+    choice = torch.empty(rows, dtype=torch.int32, device=a.device)
+    lam = ctypes.c_double()
+    ws = D.workspace(lib.uq_e8_scale_search_workspace_bytes(rows, n) if n >= 256 else 0, a.device)
+    _lib.check(lib.uq_e8_scale_search(a.data_ptr(), rows, n, float(step), rec.data_ptr(), None, choice.data_ptr(),
+                                      ctypes.addressof(lam), ws.data_ptr(), ws.numel(), D.stream_handle(a.device)),
+               "e8_scale_search")
+    if _is_dev(A):
+        return rec, choice, float(lam.value)
+    return D.to_host(rec), D.to_host(choice), float(lam.value)
