@@ -298,6 +298,53 @@ def hbm_kernel_rooflines():
     return out
 
 
+def scale_search_timing():
+    """Config 3's opt-in per-row search over 16 E8 steps (uq_e8_scale_search)
+    on the rotated ffn_down shape 4096 x 16384 fp64 at base step 0.48: CUDA
+    events around the whole call (search kernel, host choice of lam, per-row
+    decode) and per kernel."""
+    import ctypes
+    import torch
+    from ultraquant_b200 import _device as D, _lib
+    lib = _lib.load()
+    dev = D.device()
+    st = D.stream_handle(dev)
+    rows, n = 4096, 16384
+    g = torch.Generator(device=dev).manual_seed(0)
+    A = torch.randn(rows, n, dtype=torch.float64, device=dev, generator=g) * 0.015
+    rec = torch.empty_like(A)
+    ch = torch.empty(rows, dtype=torch.int32, device=dev)
+    lam = ctypes.c_double()
+    ws = D.workspace(lib.uq_e8_scale_search_workspace_bytes(rows, n), dev)
+
+    def run():
+        _lib.check(lib.uq_e8_scale_search(A.data_ptr(), rows, n, 0.48, rec.data_ptr(), None, ch.data_ptr(),
+                                          ctypes.addressof(lam), ws.data_ptr(), ws.numel(), st), "scale search")
+    run()
+    torch.cuda.synchronize()
+    lib.uq_profile_reset()
+    lib.uq_profile_enable(1)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(3):
+        run()
+    e1.record()
+    torch.cuda.synchronize()
+    lib.uq_profile_enable(0)
+    per = {}
+    for scope in ("e8_search", "e8_rowstep"):
+        t, c = ctypes.c_double(), ctypes.c_int64()
+        _lib.check(lib.uq_profile_read(scope.encode(), ctypes.byref(t), ctypes.byref(c)), "profile")
+        per[scope] = t.value / 3
+    lib.uq_profile_reset()
+    ms = e0.elapsed_time(e1) / 3
+    del A, rec
+    return {"shape": f"{rows}x{n} fp64 (rotated ffn_down)", "candidates": 16, "base_step": 0.48,
+            "ms_per_call": ms, "ms_search_kernel": per["e8_search"], "ms_rowstep_kernel": per["e8_rowstep"],
+            "weights_per_s": rows * n / (ms * 1e-3),
+            "candidate_decodes_per_s": 16 * rows * n / (per["e8_search"] * 1e-3)}
+
+
 # ---------------------------------------------------------------------------
 # default workload: the 4096 x 4096 tensor at k=3 and k=2, row-split
 # ---------------------------------------------------------------------------
@@ -481,8 +528,10 @@ def run_tensor(args, rank: int, world: int, local: int):
         cpu = {"value": w / t, "unit": UNIT, "cores": threads, "kind": "port",
                "sample": f"first {args.cpu_rows} rows ({args.cpu_rows * COLS} weights) at k=3 and k=2, "
                          "oracle restatement of the reference torch CPU path", **host_info()}
+    search = None
     if rank == 0 and not args.no_kernel_rooflines:
         kern_roof = hbm_kernel_rooflines()
+        search = scale_search_timing()
 
     if world > 1:
         dist.barrier()
@@ -494,7 +543,8 @@ def run_tensor(args, rank: int, world: int, local: int):
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": cfg,
-            "roofline": roofline, "roofline_kernels": kern_roof, "cpu_baseline": cpu, "e2e": e2e,
+            "roofline": roofline, "roofline_kernels": kern_roof, "e8_scale_search": search,
+            "cpu_baseline": cpu, "e2e": e2e,
             "gpu_launches": launches, "clocks": clocks,
         }
         print(json.dumps(line), flush=True)
