@@ -51,22 +51,27 @@ def load() -> ctypes.CDLL:
             lib.uq_oracle_viterbi.restype = ctypes.c_int
             lib.uq_oracle_viterbi.argtypes = [ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_int,
                                               ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int]
+            lib.uq_oracle_viterbi_fused.restype = ctypes.c_int
+            lib.uq_oracle_viterbi_fused.argtypes = lib.uq_oracle_viterbi.argtypes
             lib.uq_oracle_path_cost.restype = ctypes.c_float
             lib.uq_oracle_path_cost.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p]
             _lib = lib
         return _lib
 
 
-def viterbi_segments_c(xn, L: int, R: int, cw=None, threads: int = 0) -> np.ndarray:
-    """Same contract as ``uq_oracle.viterbi_segments`` (int64 states, (nseq, T))."""
+def viterbi_segments_c(xn, L: int, R: int, cw=None, threads: int = 0, fused: bool = False) -> np.ndarray:
+    """Same contract as ``uq_oracle.viterbi_segments`` (int64 states, (nseq, T)).
+    ``fused=True`` forms each cost with one fused multiply-add instead of the
+    reference's two roundings: not the reference, only a probe that finds
+    the sequences on which contraction changes the path."""
     from .uq_oracle import codebook
     x = np.ascontiguousarray(xn, np.float32)
     if x.ndim != 2:
         raise ValueError("xn must be (nseq, T)")
     c = np.ascontiguousarray(codebook(L) if cw is None else cw, np.float32)
     out = np.empty(x.shape, np.int32)
-    rc = load().uq_oracle_viterbi(x.ctypes.data, x.shape[0], x.shape[1], L, R, c.ctypes.data, out.ctypes.data,
-                                  int(threads))
+    fn = load().uq_oracle_viterbi_fused if fused else load().uq_oracle_viterbi
+    rc = fn(x.ctypes.data, x.shape[0], x.shape[1], L, R, c.ctypes.data, out.ctypes.data, int(threads))
     if rc != 0:
         raise RuntimeError("uq_oracle_viterbi failed")
     return out.astype(np.int64)

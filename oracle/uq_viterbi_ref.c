@@ -21,6 +21,7 @@
  */
 #include <stdint.h>
 #include <stdlib.h>
+#include <math.h>
 #include <string.h>
 
 #ifdef _OPENMP
@@ -136,4 +137,78 @@ float uq_oracle_path_cost(const float *x, const int32_t *st, int T, const float 
         acc = t == 0 ? sq : sq + acc;
     }
     return acc;
+}
+
+/* The same Viterbi with each cost formed by one fused multiply-add,
+ * fmaf(d, d, m) -- NOT the reference's arithmetic.  Test infrastructure for
+ * the checker only: sequences on which it and uq_oracle_viterbi disagree are
+ * the ones that expose a device whose compiler contracted the square and the
+ * add into one rounding. */
+static void viterbi_one_fused(const float *x, int T, int L, int R, const float *cw, int32_t *out,
+                              float *cost, float *m, uint8_t *bp) {
+    const int S = 1 << L, Q = 1 << (L - R), K = 1 << R;
+    for (int s = 0; s < S; ++s) {
+        const float d = x[0] - cw[s];
+        cost[s] = d * d;
+    }
+    for (int t = 1; t < T; ++t) {
+        uint8_t *b = bp + (size_t)(t - 1) * (size_t)Q;
+        for (int q = 0; q < Q; ++q) {
+            m[q] = cost[q];
+            b[q] = 0;
+        }
+        for (int k = 1; k < K; ++k) {
+            const float *c = cost + (size_t)k * (size_t)Q;
+            for (int q = 0; q < Q; ++q) {
+                const int lt = c[q] < m[q];
+                m[q] = lt ? c[q] : m[q];
+                b[q] = lt ? (uint8_t)k : b[q];
+            }
+        }
+        const float xt = x[t];
+        for (int s = 0; s < S; ++s) {
+            const float d = xt - cw[s];
+            cost[s] = fmaf(d, d, m[s >> R]);
+        }
+    }
+    int best = 0;
+    float bv = cost[0];
+    for (int s = 1; s < S; ++s)
+        if (cost[s] < bv) { bv = cost[s]; best = s; }
+    out[T - 1] = best;
+    int s = best;
+    for (int t = T - 1; t >= 1; --t) {
+        const int q = s >> R;
+        s = (int)bp[(size_t)(t - 1) * (size_t)Q + (size_t)q] * Q + q;
+        out[t - 1] = s;
+    }
+}
+
+int uq_oracle_viterbi_fused(const float *xn, int64_t nseq, int T, int L, int R, const float *cw, int32_t *states,
+                            int threads) {
+    if (nseq < 0 || T < 1 || L < 1 || L > 20 || R < 1 || R > 8 || R > L || !xn || !cw || !states) return -1;
+    const int S = 1 << L, Q = 1 << (L - R);
+    int failed = 0;
+#ifdef _OPENMP
+    if (threads <= 0) threads = omp_get_max_threads();
+#pragma omp parallel num_threads(threads) reduction(| : failed)
+#endif
+    {
+        float *cost = (float *)malloc(sizeof(float) * (size_t)S);
+        float *m = (float *)malloc(sizeof(float) * (size_t)Q);
+        uint8_t *bp = (uint8_t *)malloc((size_t)(T > 1 ? T - 1 : 1) * (size_t)Q);
+        if (!cost || !m || !bp) {
+            failed = 1;
+        } else {
+#ifdef _OPENMP
+#pragma omp for schedule(dynamic, 1)
+#endif
+            for (int64_t i = 0; i < nseq; ++i)
+                viterbi_one_fused(xn + i * (int64_t)T, T, L, R, cw, states + i * (int64_t)T, cost, m, bp);
+        }
+        free(cost);
+        free(m);
+        free(bp);
+    }
+    return failed ? -1 : 0;
 }

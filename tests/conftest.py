@@ -136,3 +136,15 @@ def qe8_same_or_tie(got, ref, A, bpw, group=256, max_ties=4):
         d = ((gn[v][None, :] - cb) ** 2).sum(1)
         assert float(exact[0]) <= d.min() * (1 + 1e-12), f"vector {v}: not a nearest codeword"
     return int(vecs.size)
+
+
+def near_tie_codebook(L, seed):
+    """A codebook of 2^L float32 entries that are four base values each
+    moved by at most 3 * 2^-22 relative: the candidate costs of a Viterbi
+    step then lie within a few ulps of one another, so a cost formed with a
+    single rounding instead of the reference's two (a contracted
+    multiply-add) changes the chosen path on many sequences."""
+    rng = np.random.RandomState(seed)
+    base = rng.randn(4).astype(np.float32)
+    pert = rng.randint(-3, 4, size=1 << L).astype(np.float32)
+    return (base[np.arange(1 << L) % 4] * (1 + pert * np.float32(2 ** -22))).astype(np.float32)

@@ -266,3 +266,48 @@ def test_sharded_codes_match_whole_tensor():
         assert torch.equal(Tr.unpack_states(out.codes, 256, 16, R), whole.states)
         assert torch.equal(out.sc.view(torch.int32), whole.sc.view(torch.int32))
         assert abs(out.wnmse - whole.wnmse) <= 1e-12 * whole.wnmse
+
+
+@pytest.mark.parametrize("L,R,T,n", [(6, 1, 32, 2000), (6, 3, 32, 2000), (8, 2, 64, 2000), (8, 4, 64, 2000),
+                                     (12, 2, 64, 2000), (12, 3, 64, 2000), (14, 2, 64, 400), (15, 3, 64, 400),
+                                     (16, 1, 32, 64), (16, 2, 32, 128), (16, 3, 32, 128), (16, 4, 32, 64)])
+def test_viterbi_two_roundings_on_near_ties(T, L, R, n):
+    """Every cost is RN(RN((x - cw)^2) + m) like trellis.py's separate torch
+    ops, never a fused multiply-add: on the near-tie codebook (entries a few
+    ulps apart) contraction changes the path on many sequences, and the
+    device must return the separately rounded oracle's states on all."""
+    import torch
+    from conftest import near_tie_codebook
+    from oracle import cviterbi as CV
+    cb = near_tie_codebook(L, L * 10 + R)
+    x = np.random.RandomState(L + R + T).randn(n, T).astype(np.float32)
+    ref = CV.viterbi_segments_c(x, L, R, cw=cb)
+    fused = CV.viterbi_segments_c(x, L, R, cw=cb, fused=True)
+    assert (ref != fused).any(1).sum() >= 1, "the case does not separate the rounding modes"
+    got = T_viterbi(torch.from_numpy(x).cuda(), L, R, torch.from_numpy(cb).cuda())
+    bad = np.flatnonzero((got != ref).any(1))
+    assert bad.size == 0, f"{bad.size} of {n} sequences differ from the two-rounding oracle (first {bad[:5]})"
+
+
+def T_viterbi(x, L, R, cw):
+    import ultraquant_b200.trellis as Tr
+    return Tr.viterbi_states(x, L, R, cw).cpu().numpy()
+
+
+def test_bench_tensor_sequence_with_one_ulp_best_paths():
+    """The one sequence of the benchmarked tensor (seed 0, row 30, segment 7,
+    L = 16, k = 3) whose two best final costs are one fp32 ulp apart: a
+    contracted multiply-add picked the second."""
+    import torch
+    import bench
+    from oracle.uq_oracle import _flat_normalise
+    from oracle import cviterbi as CV
+    W, H = bench.make_inputs(0)
+    Hc = np.maximum(H, H.max() * 1e-3)
+    A = W[30:31].astype(np.float64) * np.sqrt(Hc)[None, :]
+    xn, _, _, _ = _flat_normalise(O.rht_rows(A), 256, 256)
+    x = np.ascontiguousarray(xn[7:8])
+    ref = CV.viterbi_segments_c(x, 16, 3)
+    assert not np.array_equal(ref, CV.viterbi_segments_c(x, 16, 3, fused=True))
+    import ultraquant_b200.trellis as Tr
+    assert np.array_equal(Tr.viterbi_states(torch.from_numpy(x).cuda(), 16, 3).cpu().numpy(), ref)

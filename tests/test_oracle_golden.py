@@ -330,3 +330,19 @@ def test_e8_scale_search_restatement():
     if lam > 0:
         lower = np.argmin(D + (lam * (1 - 1e-9)) * H, axis=1)
         assert np.cumsum(H[rows, lower])[-1] >= np.cumsum(H[rows, choice])[-1]
+
+
+@pytest.mark.parametrize("L,R,T", [(6, 1, 32), (6, 3, 32), (8, 2, 64), (8, 4, 64), (12, 2, 64)])
+def test_near_tie_codebook_separates_rounding_modes(L, R, T):
+    """On the near-tie codebook the reference's two roundings (sub, square,
+    add) and a fused multiply-add give different paths on many sequences,
+    so a device test on it detects contraction; the C restatement keeps the
+    two roundings, like the torch restatement of trellis.py."""
+    from conftest import near_tie_codebook
+    from oracle import cviterbi as CV
+    cb = near_tie_codebook(L, L * 10 + R)
+    x = np.random.RandomState(L + R).randn(400, T).astype(np.float32)
+    sep = CV.viterbi_segments_c(x, L, R, cw=cb)
+    fused = CV.viterbi_segments_c(x, L, R, cw=cb, fused=True)
+    assert (sep != fused).any(1).sum() >= 2
+    assert np.array_equal(sep[:40], O.viterbi_segments(x[:40], L, R, cb))

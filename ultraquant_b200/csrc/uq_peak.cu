@@ -5,7 +5,8 @@
 // sub / mul / add (sub.rn.f32x2, mul.rn.f32x2, add.rn.f32x2; never fused), so
 // the probe runs exactly that instruction mix: every thread carries eight
 // independent chains a <- (a - c) * h + c, each link one packed sub, one packed
-// multiply and one packed add (6 lane operations), with enough resident warps
+// multiply (an FMA with a +0 addend, as the Viterbi forms its squares) and one
+// packed add (6 lane operations), with enough resident warps
 // and independent chains that no dependency latency is exposed.  The caller
 // times one launch with CUDA events on `stream`; lane operations / time is the
 // achievable FP32 lane rate of this GPU at its current clocks.  Mode 1 runs
@@ -30,9 +31,14 @@ __device__ __forceinline__ u64 p_sub2(u64 a, u64 b) {
     asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
     return r;
 }
+// RN(a * b) as a packed FMA with a +0 addend, the Viterbi's form of its
+// squares: ptxas fuses a mul.rn.f32x2 feeding an add.rn.f32x2 into one FMA
+// (even with -fmad=false), which would make each link two instructions and
+// overstate the rate of three separately rounded operations by 1.5x.
 __device__ __forceinline__ u64 p_mul2(u64 a, u64 b) {
     u64 r;
-    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    const u64 zero = 0ull;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(zero));
     return r;
 }
 __device__ __forceinline__ u64 p_add2(u64 a, u64 b) {

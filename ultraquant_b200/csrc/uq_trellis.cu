@@ -259,9 +259,17 @@ __device__ __forceinline__ u64 sub2(u64 a, u64 b) {
     asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
     return r;
 }
-__device__ __forceinline__ u64 mul2(u64 a, u64 b) {
+// RN(d * d) for both halves, as a packed FMA with a +0 addend.  ptxas
+// contracts a mul.rn.f32x2 whose result feeds an add.rn.f32x2 into a single
+// fma.rn.f32x2 -- one rounding where the reference rounds the square and
+// then the sum -- even with -fmad=false (observed on sm_100a: m values one
+// ulp off, and one path in 65,536 of a 4096 x 4096 tensor changed).  An
+// FMA's rounded result cannot be fused any further, and d*d + (+0) rounds
+// exactly like d*d (a zero square stays +0).
+__device__ __forceinline__ u64 sq2(u64 d) {
     u64 r;
-    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    const u64 zero = 0ull;
+    asm("fma.rn.f32x2 %0, %1, %1, %2;" : "=l"(r) : "l"(d), "l"(zero));
     return r;
 }
 __device__ __forceinline__ u64 add2(u64 a, u64 b) {
@@ -566,7 +574,7 @@ struct VitThread {
 #pragma unroll
                 for (int k = 0; k < K; ++k) {
                     u64 d = sub2(xx, cwp[k][p]);
-                    d = mul2(d, d);
+                    d = sq2(d);
                     c[k] = PREV ? add2(d, pk2(m[k][i], m[k][i])) : d;
                 }
                 if constexpr (C::RAW) {
@@ -631,7 +639,7 @@ struct VitThread {
             for (int p = 0; p < NP; ++p) {
                 const int i = (NQ >= K) ? ((2 * p) >> R) : 0;
                 u64 d = sub2(xx, cwp[k][p]);
-                d = mul2(d, d);
+                d = sq2(d);
                 if (PREV) d = add2(d, pk2(m[k][i], m[k][i]));
                 float lo, hi;
                 up2(d, lo, hi);

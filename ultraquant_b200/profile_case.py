@@ -12,7 +12,8 @@ kernel once, which is the form to put under ``ncu -k <kernel> -c 1``.
 Kernels: viterbi (segments of 256, L / R), rht and irht (fp64), e8,
 normalize, fwht (fp32), recon and recon_bwd (the QAT decoder, fp32), q8enc and
 q8dec (Q8_0 blocks, fp32 side), rht28 (opt-in unpadded 28 x P transform, --n0),
-qe8 (finite-codebook E8, fp64, --bpw; all of its kernels).
+qe8 (finite-codebook E8, fp64, --bpw; all of its kernels), e8search (the opt-in
+per-row search over 16 E8 steps at base step 0.48, fp64; the search kernel).
 """
 from __future__ import annotations
 
@@ -27,7 +28,8 @@ from . import _lib
 # profiler scope name of each case's kernel
 SCOPE = {"viterbi": "viterbi_fwd", "rht": "rht", "irht": "rht", "e8": "e8_quant",
          "normalize": "normalize", "fwht": "fwht", "recon": "qat_recon", "recon_bwd": "qat_recon_bwd",
-         "q8enc": "q8_encode", "q8dec": "q8_decode", "rht28": "rht", "qe8": "qe8_search"}
+         "q8enc": "q8_encode", "q8dec": "q8_decode", "rht28": "rht", "qe8": "qe8_search",
+         "e8search": "e8_search"}
 
 
 def _peaks():
@@ -132,6 +134,19 @@ def build_case(args, lib, st):
         def run():
             _lib.check(lib.uq_rht28_rows(A.data_ptr(), 1, rows, n0, n0, None, d28.data_ptr(), out.data_ptr(), st), "rht28")
         return run, rows * n0 * 16, "bytes"
+    if k == "e8search":
+        import ctypes
+        A = torch.randn(rows, n, dtype=torch.float64, device=dev, generator=g) * 0.015
+        rec = torch.empty_like(A)
+        ch = torch.empty(rows, dtype=torch.int32, device=dev)
+        lam = ctypes.c_double()
+        ws = D.workspace(lib.uq_e8_scale_search_workspace_bytes(rows, n), dev)
+
+        def run():
+            _lib.check(lib.uq_e8_scale_search(A.data_ptr(), rows, n, 0.48, rec.data_ptr(), None, ch.data_ptr(),
+                                              ctypes.addressof(lam), ws.data_ptr(), ws.numel(), st), "e8search")
+        # the search kernel reads the row once per candidate (16 x 8 B per weight)
+        return run, A.numel() * 8 * 16, "bytes"
     if k == "qe8":
         from . import qlab as Q
         A = torch.randn(rows, n, dtype=torch.float64, device=dev, generator=g) * 0.02
