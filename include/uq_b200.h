@@ -395,7 +395,13 @@ int uq_inject_device_flag(int which);
 
 /* Count every kernel launch and, when enabled, bracket the launches of the
  * named hot kernels ("viterbi_fwd", "rht", "e8_quant", "traceback") with
- * CUDA events on their launch stream. */
+ * CUDA events on their launch stream.
+ *
+ * Independently of this switch, the pipeline entry points, their stages
+ * ("rht_forward", "trellis_normalize", "trellis_viterbi", "trellis_decode",
+ * "rht_inverse", "e8_quant", "e8_scale_search") and every launch open NVTX
+ * ranges in the "ultraquant_b200" domain, for a tracer attached through
+ * NVTX_INJECTION64_PATH (no cost beyond a null-pointer check without one). */
 void uq_profile_enable(int on);
 void uq_profile_reset(void);
 int64_t uq_launch_count(void);

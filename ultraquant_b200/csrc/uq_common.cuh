@@ -34,11 +34,24 @@ int e8_take_timeout();      // uq_e8.cu
 int rht_set_timeout();      // uq_rht.cu (fault injection)
 int e8_set_timeout();       // uq_e8.cu (fault injection)
 
-// Launch accounting / optional per-launch event timing (see uq_profile_*).
+// NVTX range in the "ultraquant_b200" domain, open for the object's lifetime
+// (host time; a tool such as Nsight Systems attributes the kernels launched
+// inside it).  Without an attached tool each push / pop is one call through
+// a null function pointer.
+struct NvtxRange {
+    explicit NvtxRange(const char *name);
+    ~NvtxRange();
+    NvtxRange(const NvtxRange &) = delete;
+    NvtxRange &operator=(const NvtxRange &) = delete;
+};
+
+// Launch accounting, an NVTX range named after the kernel, and optional
+// per-launch event timing (see uq_profile_*).
 void count_launch();
 struct ProfScope {
     int slot = -1;
     cudaStream_t st;
+    NvtxRange range;
     ProfScope(const char *kernel, cudaStream_t s);  // records a start event if profiling
     ~ProfScope();                                   // records the stop event
 };

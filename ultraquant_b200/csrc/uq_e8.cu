@@ -588,6 +588,7 @@ int e8_set_timeout() {
 
 int e8_quant(const void *A, int a_dtype, int64_t size, int64_t group, double step, double *rec,
              int16_t *idx, double *rms_out, cudaStream_t st) {
+    NvtxRange _r("e8_quant");
     E8Args a{};
     a.A = A; a.size = size; a.group = int(group); a.step = step; a.rec = rec; a.idx = idx; a.rms_out = rms_out;
     if (a_dtype == UQ_F64) return launch_e8_quant<double>(a, st);

@@ -212,6 +212,7 @@ size_t e8_search_ws_bytes(int64_t rows, int64_t n) { return carve_search(nullptr
 // Synchronises the stream (the choice of lam is made on the host).
 int e8_scale_search(const double *A, int64_t rows, int64_t n, double step, double *rec, int16_t *idx,
                     int32_t *choice_out, double *lam_host, void *ws, size_t ws_bytes, cudaStream_t st) {
+    NvtxRange _r("e8_scale_search");
     if (rows == 0) {
         if (lam_host) *lam_host = 0.0;
         return UQ_OK;

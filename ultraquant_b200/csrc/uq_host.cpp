@@ -10,6 +10,7 @@
 #include <vector>
 
 #include <cuda_runtime.h>
+#include <nvtx3/nvToolsExt.h>
 
 #include "uq_common.cuh"
 #include "uq_mt19937.h"
@@ -45,7 +46,25 @@ int check_cuda(const char *what) {
 
 void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 
-ProfScope::ProfScope(const char *kernel, cudaStream_t s) : st(s) {
+namespace {
+nvtxDomainHandle_t nvtx_domain() {
+    static const nvtxDomainHandle_t d = nvtxDomainCreateA("ultraquant_b200");
+    return d;
+}
+}  // namespace
+
+NvtxRange::NvtxRange(const char *name) {
+    nvtxEventAttributes_t a = {};
+    a.version = NVTX_VERSION;
+    a.size = NVTX_EVENT_ATTRIB_STRUCT_SIZE;
+    a.messageType = NVTX_MESSAGE_TYPE_ASCII;
+    a.message.ascii = name;
+    nvtxDomainRangePushEx(nvtx_domain(), &a);
+}
+
+NvtxRange::~NvtxRange() { nvtxDomainRangePop(nvtx_domain()); }
+
+ProfScope::ProfScope(const char *kernel, cudaStream_t s) : st(s), range(kernel) {
     count_launch();
     if (!g_prof_on.load(std::memory_order_relaxed)) return;
     ProfEntry e;

@@ -156,6 +156,7 @@ size_t uq_quant_trellis_workspace_bytes(int64_t rows, int64_t n0, int L, int R, 
 int uq_quant_trellis(const void *W, int w_dtype, int64_t rows, int64_t n0, int64_t ldw, const double *H, int L,
                      int R, int seg, int group, const double *signs, const float *cw, float *What, int32_t *states,
                      float *sc, double *err, void *workspace, size_t workspace_bytes, void *stream) {
+    uq::NvtxRange _r("uq_quant_trellis");
     int rc = check_common(rows, n0, ldw, w_dtype, group, "uq_quant_trellis");
     if (rc) return rc;
     if (R < 1 || R > 4 || L < 6 || L > 16 || L < 2 * R || seg < 1)
@@ -202,6 +203,7 @@ size_t uq_quant_e8_workspace_bytes(int64_t rows, int64_t n0, int group) {
 int uq_quant_e8(const void *W, int w_dtype, int64_t rows, int64_t n0, int64_t ldw, const double *H, double step,
                 int group, const double *signs, float *What, int16_t *idx, double *err, void *workspace,
                 size_t workspace_bytes, void *stream) {
+    uq::NvtxRange _r("uq_quant_e8");
     int rc = check_common(rows, n0, ldw, w_dtype, group, "uq_quant_e8");
     if (rc) return rc;
     if (rows == 0) return UQ_OK;
@@ -241,6 +243,7 @@ size_t uq_quant_e8_search_workspace_bytes(int64_t rows, int64_t n0) {
 int uq_quant_e8_search(const void *W, int w_dtype, int64_t rows, int64_t n0, int64_t ldw, const double *H,
                        double step, const double *signs, float *What, int16_t *idx, int32_t *choice,
                        double *lam_host, double *err, void *workspace, size_t workspace_bytes, void *stream) {
+    uq::NvtxRange _r("uq_quant_e8_search");
     int rc = check_common(rows, n0, ldw, w_dtype, 256, "uq_quant_e8_search");
     if (rc) return rc;
     const int64_t n = uq_next_pow2(n0);
@@ -315,6 +318,7 @@ size_t uq_quant_e8_b28_workspace_bytes(int64_t rows, int64_t n0) {
 int uq_quant_e8_b28(const void *W, int w_dtype, int64_t rows, int64_t n0, int64_t ldw, const double *H, double step,
                     const double *signs, float *What, int16_t *idx, double *err, void *workspace,
                     size_t workspace_bytes, void *stream) {
+    uq::NvtxRange _r("uq_quant_e8_b28");
     int rc = check_common(rows, n0, ldw, w_dtype, 256, "uq_quant_e8_b28");
     if (rc) return rc;
     if (n0 != 28 * 512 && n0 != 28 * 1024)

@@ -1075,6 +1075,7 @@ int64_t rht_tiles(int64_t rows, int64_t n);
 int rht_forward(const void *in, int in_dtype, int64_t rows, int64_t n0, int64_t ld_in,
                 const double *colscale, const double *pre, const double *signs, void *out, int out_dtype,
                 int64_t ld_out, cudaStream_t st) {
+    NvtxRange _r("rht_forward");
     RhtArgs a{};
     a.in = in; a.rows = rows; a.n0 = n0; a.ld_in = ld_in;
     const int64_t n = uq_next_pow2(n0);
@@ -1097,6 +1098,7 @@ int rht_inverse(const void *in, int in_dtype, int64_t rows, int64_t n, int64_t l
                 int64_t n0, const double *signs, const double *colscale, const double *pre, void *out,
                 int out_dtype, int64_t ld_out, const void *ref_w, int ref_dtype,
                 int64_t ld_w, double *err_partial, double *err, cudaStream_t st) {
+    NvtxRange _r("rht_inverse");
     RhtArgs a{};
     a.in = in; a.rows = rows; a.n0 = n; a.ld_in = ld_in;
     a.b = ilog2(n);

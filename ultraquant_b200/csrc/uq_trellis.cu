@@ -1138,6 +1138,7 @@ size_t trellis_ws_bytes(int64_t nseq, int T, int L, int R) {
 
 int trellis_viterbi(const float *xn, int64_t nseq, int T, int L, int R, const float *cw, int32_t *states,
                     void *ws, size_t ws_bytes, cudaStream_t st) {
+    NvtxRange _r("trellis_viterbi");
     const int64_t per = vit_seq_bytes(T, L, R);
     int64_t batch = int64_t((ws_bytes > 512 ? ws_bytes - 512 : 0) / size_t(per));
     if (batch < 1) return fail(UQ_ERR_WORKSPACE, "viterbi: workspace %zu too small (need %lld per sequence)",
@@ -1157,6 +1158,7 @@ int trellis_viterbi(const float *xn, int64_t nseq, int T, int L, int R, const fl
 
 int trellis_normalize(const void *A, int dtype, int64_t nrow, int64_t T, int64_t lda, int64_t Tp, int64_t group,
                       float *xn, float *sc, cudaStream_t st) {
+    NvtxRange _r("trellis_normalize");
     NormArgs a{};
     a.A = A; a.dtype = dtype; a.nrow = nrow; a.T = T; a.lda = lda; a.Tp = Tp; a.group = int(group);
     a.xn = xn; a.sc = sc;
@@ -1165,6 +1167,7 @@ int trellis_normalize(const void *A, int dtype, int64_t nrow, int64_t T, int64_t
 
 int trellis_decode(const int32_t *states, const float *cw, const float *sc, int64_t group, int64_t ntot,
                    float *out, cudaStream_t st) {
+    NvtxRange _r("trellis_decode");
     const int grid = int(std::max<int64_t>(1, std::min<int64_t>((ntot + 255) / 256, int64_t(num_sms()) * 16)));
     if (ntot > 0) { uq::ProfScope _p("decode", st); decode_kernel<<<grid, 256, 0, st>>>(states, cw, sc, group, ntot, out); }
     return check_cuda("decode_kernel launch");
