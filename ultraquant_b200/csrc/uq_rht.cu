@@ -759,6 +759,210 @@ rht_tma_kernel(const __grid_constant__ CUtensorMap tin, const __grid_constant__ 
 }
 
 // ---------------------------------------------------------------------------
+// n = 16384 in one CTA.  The two 8192-element halves of a row are transformed
+// one after the other exactly as the single-CTA rows of 8192 are (index bits
+// 0..11 in three passes, bit 12 by lane shuffles), so after each half
+// register j of thread t holds element elem12(j) of that half.  The first
+// half's 16 values stay in registers while the second is transformed; the
+// last stage (index bit 13, pairs (e, e + 8192)) then pairs register j of
+// the two halves inside the thread: lower = a + b, upper = a - b, the
+// operations of the cluster form, without a cluster or an exchange.
+// Halves arrive by tensor-map loads into NBUF rotating 64 KB buffers (half q
+// in buffer q % NBUF; the load of half q + NBUF is issued as soon as half q's
+// passes are done with the buffer).  Results leave by coalesced stores from
+// registers: for each register a half warp writes 16 consecutive columns.
+// ---------------------------------------------------------------------------
+template <typename TIn, typename TOut, int MODE, bool COLS, int NBUF>
+__global__ void __launch_bounds__(512, 1)
+rht_halves_kernel(const __grid_constant__ CUtensorMap tin, RhtArgs a) {
+    constexpr int NT = 512, HALF = 8192;
+    constexpr unsigned BUFB = HALF * 8;                     // one fp64 tile
+    constexpr int NBOX = HALF / 4096;                       // input boxes of 4096 elements per half
+    constexpr unsigned INB = 4096 * unsigned(sizeof(TIn));
+    constexpr int EPL = 128 / int(sizeof(TIn));             // elements per 128-byte line
+    constexpr int CH_IN = 4096 / EPL, LPH = HALF / EPL;     // lines per box, per half
+    extern __shared__ __align__(1024) unsigned char smem_raw_h[];
+    __shared__ __align__(8) unsigned long long full[NBUF];
+    __shared__ double red[2 * (NT / 32)];
+    const int tid = threadIdx.x;
+    unsigned char *smem_h = smem_raw_h + ((1024u - (unsigned(__cvta_generic_to_shared(smem_raw_h)) & 1023u)) & 1023u);
+    const unsigned sbase = unsigned(__cvta_generic_to_shared(smem_h));
+    const unsigned bar0 = unsigned(__cvta_generic_to_shared(&full[0]));
+    const int64_t nctas = gridDim.x, first = blockIdx.x;
+    // halves q = 0 .. nq-1 of this CTA: row first + (q >> 1) * nctas, half q & 1
+    const int64_t nq = first < a.rows ? 2 * ((a.rows - first + nctas - 1) / nctas) : 0;
+    auto issue = [&](int64_t q) {   // (one thread) load half q into buffer q % NBUF
+        const unsigned bi = unsigned(q % NBUF);
+        mbar_arrive_expect_tx(bar0 + 8u * bi, unsigned(NBOX) * INB);
+#pragma unroll
+        for (int bx = 0; bx < NBOX; ++bx)
+            load3d(sbase + bi * BUFB + unsigned(bx) * INB, &tin, 0, int(q & 1) * LPH + bx * CH_IN,
+                   int(first + (q >> 1) * nctas), bar0 + 8u * bi);
+    };
+    auto elem12 = [&](int j) -> int {
+        return (tid & 15) | (((tid >> 5) & 15) << 4) | (j << 8) | (((tid >> 4) & 1) << 12);
+    };
+    if (tid == 0) {
+        for (int i = 0; i < NBUF; ++i) mbar_init(bar0 + 8u * unsigned(i), 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+    if (tid == 0)
+        for (int64_t q = 0; q < NBUF && q < nq; ++q) issue(q);
+    // sign bits: forward, pass-0 column h 8192 + 16 tid + j at bit 16 h + j;
+    // inverse, output column h 8192 + elem12(j) at bit 16 h + j
+    unsigned smask = 0;
+    if (MODE == MODE_FWD) {
+        if (!COLS)
+#pragma unroll
+            for (int h = 0; h < 2; ++h)
+#pragma unroll
+                for (int j = 0; j < 16; ++j)
+                    smask |= (__ldg(a.signs + h * HALF + 16 * tid + j) < 0.0 ? 1u : 0u) << (16 * h + j);
+    } else {
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+                smask |= (__ldg(a.signs + h * HALF + elem12(j)) < 0.0 ? 1u : 0u) << (16 * h + j);
+    }
+    const double inv_mul = ldexp(1.0, -14);
+    const double fwd_mul = ldexp(1.0, -7);
+    bool fail = false;
+    double xa[16];
+    for (int64_t q = 0; q < nq; ++q) {
+        const int h = int(q & 1);
+        const int64_t r = first + (q >> 1) * nctas;
+        const unsigned bi = unsigned(q % NBUF);
+        const unsigned buf = sbase + bi * BUFB;
+        double *tile = reinterpret_cast<double *>(smem_h + bi * BUFB);
+        double pre_r[COLS && MODE == MODE_FWD ? 16 : 1];
+        if (COLS && MODE == MODE_FWD) {
+            // issued before the wait, so their latency overlaps it
+#pragma unroll
+            for (int j = 0; j < 16; ++j) pre_r[j] = __ldg(a.pre + h * HALF + 16 * tid + j);
+        }
+        rmb_wait(bar0 + 8u * bi, unsigned((q / NBUF) & 1), fail);
+        double x[16];
+        // ---- pass 0: 16 consecutive elements from the swizzled lines ----------
+        if (sizeof(TIn) == 8) {
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+                const double2 v = lds128d(buf + unsigned(tid * 128 + ((c ^ (tid & 7)) << 4)));
+                x[2 * c] = v.x;
+                x[2 * c + 1] = v.y;
+            }
+        } else {
+            const int ln = tid >> 1, hl = tid & 1;
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                const float4 v = lds128f(buf + unsigned(ln * 128 + (((4 * hl + c) ^ (ln & 7)) << 4)));
+                x[4 * c] = v.x; x[4 * c + 1] = v.y; x[4 * c + 2] = v.z; x[4 * c + 3] = v.w;
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            if (MODE == MODE_FWD) x[j] = COLS ? d_mul(x[j], pre_r[j]) : flip_if(x[j], (smask >> (16 * h + j)) & 1u);
+            else x[j] = d_mul(x[j], a.sqrt_n);
+        }
+        stages16(x, 0, 0, 4);
+        __syncthreads();   // everyone has its raw values: the buffer becomes the work tile
+        // ---- pass over bits 4..7 ------------------------------------------------
+        {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) tile[swz((tid << 4) + j)] = x[j];
+            __syncthreads();
+            const int base = (tid & 15) | ((tid >> 4) << 8);
+#pragma unroll
+            for (int j = 0; j < 16; ++j) x[j] = tile[swz(base + (j << 4))];
+            stages16(x, 4, 4, 12);
+            __syncthreads();
+        }
+        // ---- pass over bits 8..11; lane bit 4 reads element bit 12 ----------------
+        {
+            const int pb = (tid & 15) | ((tid >> 4) << 8);
+#pragma unroll
+            for (int j = 0; j < 16; ++j) tile[swz(pb + (j << 4))] = x[j];
+            __syncthreads();
+            const int base = elem12(0);
+#pragma unroll
+            for (int j = 0; j < 16; ++j) x[j] = tile[swz(base + (j << 8))];
+            stages16(x, 8, 8, 12);
+            fence_proxy_async();   // this thread's tile accesses before the next tensor-map load
+            __syncthreads();
+        }
+        // the buffer is free: load the half NBUF ahead into it
+        if (tid == 0 && q + NBUF < nq) issue(q + NBUF);
+        // stage h = 4096: lanes l and l ^ 16 hold the pair (lower: bit 4 clear)
+        {
+            const bool upper = (tid >> 4) & 1;
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+                const double o = __shfl_xor_sync(0xffffffffu, x[j], 16);
+                x[j] = upper ? d_sub(o, x[j]) : d_add(x[j], o);
+            }
+        }
+        if (h == 0) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) xa[j] = x[j];
+            continue;
+        }
+        // ---- stage h = 8192: element e of the first half with e of the second ----
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            const double lo = xa[j], hi = x[j];
+            xa[j] = d_add(lo, hi);
+            x[j] = d_sub(lo, hi);
+        }
+        // ---- epilogue: scale and store (columns elem12(j), 8192 + elem12(j)) ----
+        TOut *orow = static_cast<TOut *>(a.out) + r * a.ld_out;
+        double se = 0.0, sa = 0.0;
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+                const double v = hh ? x[j] : xa[j];
+                const int64_t e = int64_t(hh * HALF + elem12(j));
+                double y;
+                if (MODE == MODE_FWD) {
+                    y = d_mul(v, fwd_mul);
+                } else {
+                    const double xs = d_mul(v, inv_mul);
+                    y = flip_if(xs, (smask >> (16 * hh + j)) & 1u);
+                    if (COLS && e < a.ncols_out) {
+                        if (a.err_partial) {
+                            const double w = a.ref_dtype == UQ_F32
+                                ? double(__ldg(static_cast<const float *>(a.ref_w) + r * a.ld_w + e))
+                                : __ldg(static_cast<const double *>(a.ref_w) + r * a.ld_w + e);
+                            const double A = d_mul(w, __ldg(a.colscale + e));
+                            const double dd = d_sub(A, y);
+                            se = d_add(se, d_mul(dd, dd));
+                            sa = d_add(sa, d_mul(A, A));
+                        }
+                        y = xs / __ldg(a.pre + e);
+                    }
+                }
+                if (MODE == MODE_FWD || e < a.ncols_out) orow[e] = TOut(y);
+            }
+        }
+        if (MODE == MODE_INV && COLS && a.err_partial) {
+            for (int o = 16; o > 0; o >>= 1) {
+                se = d_add(se, __shfl_xor_sync(0xffffffffu, se, o));
+                sa = d_add(sa, __shfl_xor_sync(0xffffffffu, sa, o));
+            }
+            if ((tid & 31) == 0) { red[2 * (tid >> 5)] = se; red[2 * (tid >> 5) + 1] = sa; }
+            __syncthreads();
+            if (tid == 0) {
+                double s0 = 0.0, s1 = 0.0;
+                for (int i = 0; i < NT / 32; ++i) { s0 = d_add(s0, red[2 * i]); s1 = d_add(s1, red[2 * i + 1]); }
+                a.err_partial[2 * r] = s0;
+                a.err_partial[2 * r + 1] = s1;
+            }
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
 // Opt-in block-factorised transform for n0 = 28 * P (P = 512 or 1024: the
 // ffn_down widths 14336 and 28672 without padding).  No counterpart in the
 // reference (it pads to a power of two); the operation order is the one of
@@ -995,6 +1199,25 @@ int launch_tma_v(const CUtensorMap &mi, const CUtensorMap &mo, const RhtArgs &a,
 }
 
 template <typename TIn, typename TOut, int MODE, bool COLS>
+int launch_tma_halves(const CUtensorMap &mi, const RhtArgs &a, cudaStream_t st, int64_t *nparts) {
+    constexpr int NBUF = 3;
+    auto kern = rht_halves_kernel<TIn, TOut, MODE, COLS, NBUF>;
+    const size_t smem = size_t(NBUF) * (size_t(8) << 13) + 1024;   // + alignment slack
+    if (uq::set_smem_attr(reinterpret_cast<const void *>(kern), int(smem)) != cudaSuccess)
+        return uq::check_cuda("rht halves: set smem attribute");
+    int per_sm = 0;
+    if (uq::occupancy_blocks(&per_sm, reinterpret_cast<const void *>(kern), 512, smem) != cudaSuccess || per_sm < 1)
+        return uq::check_cuda("rht halves: occupancy");
+    const int64_t grid = std::min<int64_t>(a.rows, int64_t(per_sm) * uq::num_sms());
+    *nparts = a.rows;   // one error partial per row
+    if (grid > 0) {
+        uq::ProfScope _p("rht", st);
+        kern<<<unsigned(grid), 512, smem, st>>>(mi, a);
+    }
+    return uq::check_cuda("rht_halves_kernel launch");
+}
+
+template <typename TIn, typename TOut, int MODE, bool COLS>
 int launch_tma(const RhtArgs &a, int64_t ncols_in, cudaStream_t st, int64_t *nparts) {
     CUtensorMap mi, mo;
     if (!make_line_map<TIn>(&mi, a.in, a.rows, ncols_in, a.ld_in, 4096) ||
@@ -1003,11 +1226,12 @@ int launch_tma(const RhtArgs &a, int64_t ncols_in, cudaStream_t st, int64_t *npa
     // n = 2^b as 2^LB-element parts on a cluster of 2^(b - LB) CTAs.  Measured
     // on B200: 8192-element parts beat 4096-element parts with one more
     // cluster stage for n >= 8192 (the distributed-shared-memory stage costs
-    // more than the lower occupancy of the 512-thread tile).
+    // more than the lower occupancy of the 512-thread tile).  n = 16384: one
+    // CTA transforms both 8192-element halves (rht_halves_kernel).
     switch (a.b) {
     case 12: return launch_tma_v<TIn, TOut, MODE, 12, 1, COLS>(mi, mo, a, st, nparts);
     case 13: return launch_tma_v<TIn, TOut, MODE, 13, 1, COLS>(mi, mo, a, st, nparts);
-    case 14: return launch_tma_v<TIn, TOut, MODE, 13, 2, COLS>(mi, mo, a, st, nparts);
+    case 14: return launch_tma_halves<TIn, TOut, MODE, COLS>(mi, a, st, nparts);
     default: return launch_tma_v<TIn, TOut, MODE, 13, 4, COLS>(mi, mo, a, st, nparts);
     }
 }
