@@ -290,7 +290,9 @@ def hbm_kernel_rooflines():
     out = []
     for k, rows, n, n0 in cases:
         rec = PC.measure(k, rows=rows, n=n, n0=n0, iters=5, hbm_peak=peak)
-        kern = {"rht": "rht_tma_kernel (forward)", "irht": "rht_tma_kernel (inverse)", "e8": "e8_tma_kernel"}[k]
+        # rows of 16384 run both halves in one CTA (rht_halves_kernel)
+        base = "rht_halves_kernel" if n == 16384 else "rht_tma_kernel"
+        kern = {"rht": f"{base} (forward)", "irht": f"{base} (inverse)", "e8": "e8_tma_kernel"}[k]
         out.append({"kernel": kern, "shape": f"{rows}x{n0 or n}" + (f" (padded to {n})" if n0 else ""),
                     "dtype": "f64", "bound": "hbm", "achieved": rec["achieved_gbs"], "peak": peak, "unit": "GB/s",
                     "frac": rec["achieved_gbs"] / peak, "peak_source": src,
