@@ -139,3 +139,68 @@ def test_rht_tile_layouts_are_permutations(LB):
         for rank in range(CL):
             idx = sorted(out_idx(t, j, LB, CL, rank) for t in range(NT) for j in range(16))
             assert idx == list(range(n))
+
+
+# ---- rht_halves_kernel: rows of 16384 (one CTA) and 32768 (2-CTA cluster) ----
+
+def _stages(x, bits):
+    """Butterfly stages h = 2^0 .. 2^(bits-1) over the last axis, in order:
+    lower a + b, upper a - b (float64, the kernel's and the reference's order)."""
+    import numpy as np
+    x = np.array(x, np.float64)
+    n = x.shape[-1]
+    for b in range(bits):
+        h = 1 << b
+        y = x.reshape(x.shape[:-1] + (n // (2 * h), 2, h))
+        a, c = y[..., 0, :].copy(), y[..., 1, :].copy()
+        y[..., 0, :], y[..., 1, :] = a + c, a - c
+        x = y.reshape(x.shape)
+    return x
+
+
+def _halves_model(row, CL):
+    """Output of rht_halves_kernel's butterflies for one row (before scaling),
+    following its register map: after a part's bits 0..12, thread t register j
+    holds element elem12(t, j) of the part; bit 13 pairs register j of the
+    CTA's two parts; CL = 2: bit 14 pairs register j of the two CTAs, CTA 0
+    keeping its sums and receiving CTA 1's, CTA 1 keeping its differences and
+    receiving CTA 0's; sums go to out_sum(j), differences to out_dif(j)."""
+    import numpy as np
+    HALF = 8192
+    parts = _stages(np.asarray(row).reshape(-1, HALF), 13)   # each part, bits 0..12
+    regs = {}
+    for rank in range(CL):
+        xa = np.empty((512, 16)); x = np.empty((512, 16))
+        for t in range(512):
+            for j in range(16):
+                xa[t, j] = parts[2 * rank][elem12(t, j)]
+                x[t, j] = parts[2 * rank + 1][elem12(t, j)]
+        regs[rank] = (xa + x, xa - x)                           # bit 13
+    out = np.full(CL * 2 * HALF, np.nan)
+    for rank in range(CL):
+        if CL == 2:
+            own = regs[rank][1] if rank else regs[rank][0]
+            got = regs[rank ^ 1][1] if rank else regs[rank ^ 1][0]   # what the partner pushed
+            lo, hi = (got, own) if rank else (own, got)
+            s, d = lo + hi, lo - hi                               # bit 14
+        else:
+            s, d = regs[rank]
+        for t in range(512):
+            for j in range(16):
+                e = elem12(t, j)
+                out[(0 if CL == 1 else rank * HALF) + e] = s[t, j]
+                out[(HALF if CL == 1 else 2 * HALF + rank * HALF) + e] = d[t, j]
+    return out
+
+
+@pytest.mark.parametrize("n,CL", [(16384, 1), (32768, 2)])
+def test_halves_kernel_data_flow(n, CL):
+    """Every output column written once, bit-identical to the whole-row
+    butterflies in stage order."""
+    import numpy as np
+    rng = np.random.RandomState(n)
+    row = rng.standard_normal(n)
+    got = _halves_model(row, CL)
+    assert not np.isnan(got).any()
+    ref = _stages(row, n.bit_length() - 1)
+    assert np.array_equal(got.view(np.uint64), ref.view(np.uint64))

@@ -771,11 +771,22 @@ rht_tma_kernel(const __grid_constant__ CUtensorMap tin, const __grid_constant__ 
 // in buffer q % NBUF; the load of half q + NBUF is issued as soon as half q's
 // passes are done with the buffer).  Results leave by coalesced stores from
 // registers: for each register a half warp writes 16 consecutive columns.
+// n = 32768 (CL = 2): a 2-CTA cluster per row, CTA r runs the quarters 2r
+// and 2r + 1 (columns r 16384 ..) as above, then the stage of index bit 14
+// pairs element e of the two CTAs' 16384: CTA 0 finishes the pairs of its
+// sums (quarters 0 and 2), CTA 1 those of its differences (quarters 1 and
+// 3), each pushing the other 8192 values into its partner's 64 KB inbox by
+// st.async, which completes on the partner's inbox mbarrier.  A split
+// cluster barrier per row ("inbox read") keeps the next push behind the
+// partner's reads.
 // ---------------------------------------------------------------------------
-template <typename TIn, typename TOut, int MODE, bool COLS, int NBUF>
+template <typename TIn, typename TOut, int MODE, bool COLS, int NBUF, int CL>
 __global__ void __launch_bounds__(512, 1)
 rht_halves_kernel(const __grid_constant__ CUtensorMap tin, RhtArgs a) {
+    static_assert(CL == 1 || CL == 2, "rows of 16384 (one CTA) or 32768 (two)");
     constexpr int NT = 512, HALF = 8192;
+    constexpr int B = CL == 1 ? 14 : 15;                    // log2(n)
+    constexpr unsigned INBOX = 8u * HALF;                   // CL = 2: the partner's 8192 values
     constexpr unsigned BUFB = HALF * 8;                     // one fp64 tile
     constexpr int NBOX = HALF / 4096;                       // input boxes of 4096 elements per half
     constexpr unsigned INB = 4096 * unsigned(sizeof(TIn));
@@ -783,12 +794,18 @@ rht_halves_kernel(const __grid_constant__ CUtensorMap tin, RhtArgs a) {
     constexpr int CH_IN = 4096 / EPL, LPH = HALF / EPL;     // lines per box, per half
     extern __shared__ __align__(1024) unsigned char smem_raw_h[];
     __shared__ __align__(8) unsigned long long full[NBUF];
+    __shared__ __align__(8) unsigned long long ibar;      // CL = 2: inbox filled
     __shared__ double red[2 * (NT / 32)];
     const int tid = threadIdx.x;
+    unsigned rank = 0;
+    if (CL > 1) asm("mov.u32 %0, %%cluster_ctarank;" : "=r"(rank));
     unsigned char *smem_h = smem_raw_h + ((1024u - (unsigned(__cvta_generic_to_shared(smem_raw_h)) & 1023u)) & 1023u);
     const unsigned sbase = unsigned(__cvta_generic_to_shared(smem_h));
     const unsigned bar0 = unsigned(__cvta_generic_to_shared(&full[0]));
-    const int64_t nctas = gridDim.x, first = blockIdx.x;
+    const unsigned ibar0 = unsigned(__cvta_generic_to_shared(&ibar));
+    const unsigned inbox = sbase + unsigned(NBUF) * BUFB;   // CL = 2: after the buffers
+    const int64_t nctas = gridDim.x / CL, first = blockIdx.x / CL;
+    const int col0 = int(rank) * 2 * HALF;                 // this CTA's first column
     // halves q = 0 .. nq-1 of this CTA: row first + (q >> 1) * nctas, half q & 1
     const int64_t nq = first < a.rows ? 2 * ((a.rows - first + nctas - 1) / nctas) : 0;
     auto issue = [&](int64_t q) {   // (one thread) load half q into buffer q % NBUF
@@ -796,7 +813,7 @@ rht_halves_kernel(const __grid_constant__ CUtensorMap tin, RhtArgs a) {
         mbar_arrive_expect_tx(bar0 + 8u * bi, unsigned(NBOX) * INB);
 #pragma unroll
         for (int bx = 0; bx < NBOX; ++bx)
-            load3d(sbase + bi * BUFB + unsigned(bx) * INB, &tin, 0, int(q & 1) * LPH + bx * CH_IN,
+            load3d(sbase + bi * BUFB + unsigned(bx) * INB, &tin, 0, col0 / EPL + int(q & 1) * LPH + bx * CH_IN,
                    int(first + (q >> 1) * nctas), bar0 + 8u * bi);
     };
     auto elem12 = [&](int j) -> int {
@@ -804,13 +821,25 @@ rht_halves_kernel(const __grid_constant__ CUtensorMap tin, RhtArgs a) {
     };
     if (tid == 0) {
         for (int i = 0; i < NBUF; ++i) mbar_init(bar0 + 8u * unsigned(i), 1);
+        // CL = 2: the inbox's phase completes on this CTA's arm (arrive +
+        // expect_tx) and the partner's INBOX bytes of st.async
+        if (CL == 2) mbar_init(ibar0, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     __syncthreads();
     if (tid == 0)
         for (int64_t q = 0; q < NBUF && q < nq; ++q) issue(q);
-    // sign bits: forward, pass-0 column h 8192 + 16 tid + j at bit 16 h + j;
-    // inverse, output column h 8192 + elem12(j) at bit 16 h + j
+    unsigned peer_inbox = 0, peer_ibar = 0;
+    if (CL == 2) {
+        asm("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(peer_inbox) : "r"(inbox), "r"(rank ^ 1u));
+        asm("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(peer_ibar) : "r"(ibar0), "r"(rank ^ 1u));
+        cluster_arrive_rel();   // opens the first "inbox read" phase (and follows the barrier init)
+    }
+    // output columns of the sums / differences of register j (last stage)
+    auto out_sum = [&](int j) -> int { return (CL == 1 ? 0 : int(rank) * HALF) + elem12(j); };
+    auto out_dif = [&](int j) -> int { return (CL == 1 ? HALF : 2 * HALF + int(rank) * HALF) + elem12(j); };
+    // sign bits: forward, pass-0 column col0 + h 8192 + 16 tid + j at bit
+    // 16 h + j; inverse, output column out_sum(j) at bit j, out_dif(j) at 16 + j
     unsigned smask = 0;
     if (MODE == MODE_FWD) {
         if (!COLS)
@@ -818,16 +847,16 @@ rht_halves_kernel(const __grid_constant__ CUtensorMap tin, RhtArgs a) {
             for (int h = 0; h < 2; ++h)
 #pragma unroll
                 for (int j = 0; j < 16; ++j)
-                    smask |= (__ldg(a.signs + h * HALF + 16 * tid + j) < 0.0 ? 1u : 0u) << (16 * h + j);
+                    smask |= (__ldg(a.signs + col0 + h * HALF + 16 * tid + j) < 0.0 ? 1u : 0u) << (16 * h + j);
     } else {
 #pragma unroll
-        for (int h = 0; h < 2; ++h)
-#pragma unroll
-            for (int j = 0; j < 16; ++j)
-                smask |= (__ldg(a.signs + h * HALF + elem12(j)) < 0.0 ? 1u : 0u) << (16 * h + j);
+        for (int j = 0; j < 16; ++j) {
+            smask |= (__ldg(a.signs + out_sum(j)) < 0.0 ? 1u : 0u) << j;
+            smask |= (__ldg(a.signs + out_dif(j)) < 0.0 ? 1u : 0u) << (16 + j);
+        }
     }
-    const double inv_mul = ldexp(1.0, -14);
-    const double fwd_mul = ldexp(1.0, -7);
+    const double inv_mul = ldexp(1.0, -B);
+    const double fwd_mul = ldexp(1.0, -(B >> 1));
     bool fail = false;
     double xa[16];
     for (int64_t q = 0; q < nq; ++q) {
@@ -840,7 +869,7 @@ rht_halves_kernel(const __grid_constant__ CUtensorMap tin, RhtArgs a) {
         if (COLS && MODE == MODE_FWD) {
             // issued before the wait, so their latency overlaps it
 #pragma unroll
-            for (int j = 0; j < 16; ++j) pre_r[j] = __ldg(a.pre + h * HALF + 16 * tid + j);
+            for (int j = 0; j < 16; ++j) pre_r[j] = __ldg(a.pre + col0 + h * HALF + 16 * tid + j);
         }
         rmb_wait(bar0 + 8u * bi, unsigned((q / NBUF) & 1), fail);
         double x[16];
@@ -914,7 +943,27 @@ rht_halves_kernel(const __grid_constant__ CUtensorMap tin, RhtArgs a) {
             xa[j] = d_add(lo, hi);
             x[j] = d_sub(lo, hi);
         }
-        // ---- epilogue: scale and store (columns elem12(j), 8192 + elem12(j)) ----
+        if constexpr (CL == 2) {
+            // ---- stage h = 16384 with the partner: CTA 0 keeps its sums (quarter
+            //      0) and receives CTA 1's (quarter 2); CTA 1 keeps its
+            //      differences (quarter 3) and receives CTA 0's (quarter 1) ----
+            cluster_wait_acq();   // the partner has read its inbox of the previous row
+            if (tid == 0) mbar_arrive_expect_tx(ibar0, INBOX);
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+                st_async_f64(peer_inbox + 8u * unsigned(elem12(j)), rank ? xa[j] : x[j], peer_ibar);
+            rmb_wait(ibar0, unsigned((q >> 1) & 1), fail);   // the partner's values are in the inbox
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+                const double v = lds64d(inbox + 8u * unsigned(elem12(j)));
+                const double own = rank ? x[j] : xa[j];
+                const double lo = rank ? v : own, hi = rank ? own : v;
+                xa[j] = d_add(lo, hi);
+                x[j] = d_sub(lo, hi);
+            }
+            cluster_arrive_rel();   // inbox read
+        }
+        // ---- epilogue: scale and store (sums at out_sum(j), differences at out_dif(j)) ----
         TOut *orow = static_cast<TOut *>(a.out) + r * a.ld_out;
         double se = 0.0, sa = 0.0;
 #pragma unroll
@@ -922,10 +971,10 @@ rht_halves_kernel(const __grid_constant__ CUtensorMap tin, RhtArgs a) {
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
                 const double v = hh ? x[j] : xa[j];
-                const int64_t e = int64_t(hh * HALF + elem12(j));
+                const int64_t e = int64_t(hh ? out_dif(j) : out_sum(j));
                 double y;
                 if (MODE == MODE_FWD) {
-                    y = d_mul(v, fwd_mul);
+                    y = (B & 1) ? div_sqrt_n(v, a) : d_mul(v, fwd_mul);
                 } else {
                     const double xs = d_mul(v, inv_mul);
                     y = flip_if(xs, (smask >> (16 * hh + j)) & 1u);
@@ -955,11 +1004,12 @@ rht_halves_kernel(const __grid_constant__ CUtensorMap tin, RhtArgs a) {
             if (tid == 0) {
                 double s0 = 0.0, s1 = 0.0;
                 for (int i = 0; i < NT / 32; ++i) { s0 = d_add(s0, red[2 * i]); s1 = d_add(s1, red[2 * i + 1]); }
-                a.err_partial[2 * r] = s0;
-                a.err_partial[2 * r + 1] = s1;
+                a.err_partial[2 * (CL * r + rank)] = s0;
+                a.err_partial[2 * (CL * r + rank) + 1] = s1;
             }
         }
     }
+    if (CL == 2) cluster_wait_acq();   // closes the last "inbox read" phase
 }
 
 // ---------------------------------------------------------------------------
@@ -1198,21 +1248,40 @@ int launch_tma_v(const CUtensorMap &mi, const CUtensorMap &mo, const RhtArgs &a,
     return uq::check_cuda("rht_tma_kernel launch");
 }
 
-template <typename TIn, typename TOut, int MODE, bool COLS>
+// Rows of 16384 (CL = 1: three load buffers) or 32768 (CL = 2: a 2-CTA
+// cluster per row, two load buffers and the 64 KB inbox).
+template <typename TIn, typename TOut, int MODE, bool COLS, int CL>
 int launch_tma_halves(const CUtensorMap &mi, const RhtArgs &a, cudaStream_t st, int64_t *nparts) {
-    constexpr int NBUF = 3;
-    auto kern = rht_halves_kernel<TIn, TOut, MODE, COLS, NBUF>;
-    const size_t smem = size_t(NBUF) * (size_t(8) << 13) + 1024;   // + alignment slack
+    constexpr int NBUF = CL == 1 ? 3 : 2;
+    auto kern = rht_halves_kernel<TIn, TOut, MODE, COLS, NBUF, CL>;
+    const size_t smem = size_t(NBUF + (CL == 2 ? 1 : 0)) * (size_t(8) << 13) + 1024;   // + alignment slack
     if (uq::set_smem_attr(reinterpret_cast<const void *>(kern), int(smem)) != cudaSuccess)
         return uq::check_cuda("rht halves: set smem attribute");
-    int per_sm = 0;
-    if (uq::occupancy_blocks(&per_sm, reinterpret_cast<const void *>(kern), 512, smem) != cudaSuccess || per_sm < 1)
-        return uq::check_cuda("rht halves: occupancy");
-    const int64_t grid = std::min<int64_t>(a.rows, int64_t(per_sm) * uq::num_sms());
-    *nparts = a.rows;   // one error partial per row
-    if (grid > 0) {
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = CL; attr[0].val.clusterDim.y = 1; attr[0].val.clusterDim.z = 1;
+    cfg.blockDim = dim3(512, 1, 1); cfg.dynamicSmemBytes = smem; cfg.stream = st;
+    cfg.attrs = attr; cfg.numAttrs = CL > 1 ? 1 : 0;
+    int64_t slots = 0;
+    if (CL > 1) {
+        cfg.gridDim = dim3(CL, 1, 1);
+        int clusters = 0;
+        if (uq::occupancy_clusters(&clusters, reinterpret_cast<const void *>(kern), &cfg) != cudaSuccess || clusters < 1)
+            return uq::check_cuda("rht halves: cluster occupancy");
+        slots = clusters;
+    } else {
+        int per_sm = 0;
+        if (uq::occupancy_blocks(&per_sm, reinterpret_cast<const void *>(kern), 512, smem) != cudaSuccess || per_sm < 1)
+            return uq::check_cuda("rht halves: occupancy");
+        slots = int64_t(per_sm) * uq::num_sms();
+    }
+    const int64_t groups = std::min<int64_t>(a.rows, slots);
+    cfg.gridDim = dim3(unsigned(groups * CL), 1, 1);
+    *nparts = a.rows * CL;   // one error partial per CTA and row
+    if (groups > 0) {
         uq::ProfScope _p("rht", st);
-        kern<<<unsigned(grid), 512, smem, st>>>(mi, a);
+        if (cudaLaunchKernelEx(&cfg, kern, mi, a) != cudaSuccess) return uq::check_cuda("rht_halves_kernel launch");
     }
     return uq::check_cuda("rht_halves_kernel launch");
 }
@@ -1226,13 +1295,14 @@ int launch_tma(const RhtArgs &a, int64_t ncols_in, cudaStream_t st, int64_t *npa
     // n = 2^b as 2^LB-element parts on a cluster of 2^(b - LB) CTAs.  Measured
     // on B200: 8192-element parts beat 4096-element parts with one more
     // cluster stage for n >= 8192 (the distributed-shared-memory stage costs
-    // more than the lower occupancy of the 512-thread tile).  n = 16384: one
-    // CTA transforms both 8192-element halves (rht_halves_kernel).
+    // more than the lower occupancy of the 512-thread tile).  n = 16384 and
+    // 32768: each CTA transforms two 8192-element parts in sequence
+    // (rht_halves_kernel; one CTA, or a 2-CTA cluster, per row).
     switch (a.b) {
     case 12: return launch_tma_v<TIn, TOut, MODE, 12, 1, COLS>(mi, mo, a, st, nparts);
     case 13: return launch_tma_v<TIn, TOut, MODE, 13, 1, COLS>(mi, mo, a, st, nparts);
-    case 14: return launch_tma_halves<TIn, TOut, MODE, COLS>(mi, a, st, nparts);
-    default: return launch_tma_v<TIn, TOut, MODE, 13, 4, COLS>(mi, mo, a, st, nparts);
+    case 14: return launch_tma_halves<TIn, TOut, MODE, COLS, 1>(mi, a, st, nparts);
+    default: return launch_tma_halves<TIn, TOut, MODE, COLS, 2>(mi, a, st, nparts);
     }
 }
 
