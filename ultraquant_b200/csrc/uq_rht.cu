@@ -447,14 +447,12 @@ rht_split_kernel(RhtArgs a) {
 }
 
 // ---------------------------------------------------------------------------
-// TMA form for n = 2^12 .. 2^15.  A row is split into 2^LB-element parts, one
-// per CTA of a cluster of n / 2^LB CTAs (a single CTA for n = 2^LB).  Each
-// part arrives by tensor-map loads into a shared buffer with the 128-byte
-// swizzle (16-byte chunk c of 128-byte line r at c ^ (r & 7)), so that pass
-// 0 -- thread t owns the 16 consecutive elements 16t .. 16t+15 -- reads it
-// with conflict-free 16-byte loads; the CTA's next row is loaded into the
-// second buffer meanwhile.  Index bits above LB are the cluster stages: each
-// CTA reads its partner's part from distributed shared memory.  The result is
+// TMA form for rows of n = 2^LB = 4096 or 8192, one CTA per row (wider rows:
+// rht_halves_kernel below).  The row arrives by tensor-map loads into a
+// shared buffer with the 128-byte swizzle (16-byte chunk c of 128-byte line
+// r at c ^ (r & 7)), so that pass 0 -- thread t owns the 16 consecutive
+// elements 16t .. 16t+15 -- reads it with conflict-free 16-byte loads; the
+// CTA's next row is loaded into the second buffer meanwhile.  The result is
 // written back to the buffer in the same swizzled line layout and leaves by
 // a tensor-map store.  Columns past n0 (padding) and rows past the end are
 // zero-filled by the load and clipped by the store.  Every pass layout is a
@@ -471,88 +469,50 @@ __device__ __forceinline__ double flip_if(double v, unsigned neg) {
     return __longlong_as_double(__double_as_longlong(v) ^ (static_cast<long long>(neg) << 63));
 }
 
-template <typename TIn, typename TOut, int MODE, int LB, int CL, bool COLS>
+template <typename TIn, typename TOut, int MODE, int LB, bool COLS>
 __global__ void __launch_bounds__(1 << (LB - 4), LB == 12 ? 3 : 1)
 rht_tma_kernel(const __grid_constant__ CUtensorMap tin, const __grid_constant__ CUtensorMap tout, RhtArgs a) {
+    static_assert(LB == 12 || LB == 13, "rows of 4096 or 8192");
     constexpr int NT = 1 << (LB - 4);
-    constexpr int HALF = 1 << LB;                  // elements per CTA and row
+    constexpr int HALF = 1 << LB;                  // elements per row
     constexpr int BUFB = HALF * 8;                 // one buffer: the fp64 tile
     constexpr int NBOX = HALF / 4096;              // tensor-map boxes of 4096 elements
-    constexpr int LCL = CL == 1 ? 0 : (CL == 2 ? 1 : 2);
-    static_assert(CL == 1 || CL == 2 || CL == 4, "rows of 1, 2 or 4 CTAs");
-    constexpr bool PUSH_ROWS = CL == 2 || CL == 4;
-    constexpr int B = LB + LCL;                    // log2(n)
-    // loads move 4096-element boxes, stores 2048-element boxes (so that the two
-    // output ranges of a PUSH row, 2^(LB-1) columns each, are whole boxes)
+    constexpr int B = LB;                          // log2(n)
+    // loads move 4096-element boxes, stores 2048-element boxes
     constexpr int OBOX = 2048, NOBOX = HALF / OBOX;
     constexpr int INB = 4096 * int(sizeof(TIn)), OUTB = OBOX * int(sizeof(TOut));
     extern __shared__ __align__(1024) unsigned char smem_raw_r[];
     __shared__ __align__(8) unsigned long long full[2];
-    __shared__ __align__(8) unsigned long long ibar[2];   // PUSH: inbox i filled
     __shared__ double red[2 * (NT / 32)];
     const int tid = threadIdx.x;
-    unsigned rank = 0;
-    if (CL > 1) asm("mov.u32 %0, %%cluster_ctarank;" : "=r"(rank));
-    const int64_t col0 = int64_t(rank) * HALF;
     // the swizzled tensor-map buffers start on a 1024-byte boundary
     unsigned char *smem_r = smem_raw_r + ((1024u - (unsigned(__cvta_generic_to_shared(smem_raw_r)) & 1023u)) & 1023u);
     const unsigned sbase = unsigned(__cvta_generic_to_shared(smem_r));
     const unsigned bar0 = unsigned(__cvta_generic_to_shared(&full[0]));
-    const int64_t nclusters = gridDim.x / CL;
-    const int64_t first = blockIdx.x / CL;
+    const int64_t nctas = gridDim.x;
+    const int64_t first = blockIdx.x;
     constexpr int CH_IN = 4096 / (128 / int(sizeof(TIn)));     // 128-byte lines per input box
     constexpr int CH_OUT = OBOX / (128 / int(sizeof(TOut)));
-    const int lin0 = int(col0 / (128 / int(sizeof(TIn))));
-    const int lout0 = int(col0 / (128 / int(sizeof(TOut))));
-    // Rows over 2 or 4 CTAs (PUSH): the cross-CTA stages are finished by
-    // halves (below), so register j ends up holding column
-    // blk(j) 2^LB + a 2^(LB-1) + tid + ((j & 7) << (LB - 4)), a = rank & 1,
-    // blk(j) = (rank >> 1) + (j < 8 ? 0 : CL / 2): two column ranges of
-    // 2^(LB-1) per CTA.  Otherwise register j holds col0 + tid + (j << (LB-4)).
-    constexpr bool PUSH = CL == 2 || CL == 4;
-    // Single-CTA rows of 8192 (LB = 13): the last index bit (12) is done with
-    // lane shuffles instead of a third transpose through the tile.  The pass
-    // over bits 8..11 reads with lane bit 4 on element bit 12, so register j
-    // then holds element (tid & 15) | ((tid >> 5) & 15) << 4 | j << 8 |
+    // Register j holds column tid + (j << (LB - 4)) after the last pass, except
+    // for rows of 8192 (LB = 13): their last index bit (12) is done with lane
+    // shuffles instead of a third transpose through the tile.  The pass over
+    // bits 8..11 reads with lane bit 4 on element bit 12, so register j then
+    // holds element (tid & 15) | ((tid >> 5) & 15) << 4 | j << 8 |
     // ((tid >> 4) & 1) << 12.
-    // Rows of 16384 / 32768 (2 / 4 CTAs) too: the push stages pair equal
-    // register slots of the parts whatever the layout; CTA rank r then
-    // finishes the slots (r & 1)*8 .. +7, i.e. the elements with bit 11 =
-    // r & 1, of two parts, and stores them as four 2048-column boxes (both
-    // parts, bit 12 = 0 and 1).
     constexpr bool SHFL12 = LB == 13;
-    constexpr bool SHFL12_PUSH = SHFL12 && (CL == 2 || CL == 4);
     auto elem12 = [&](int j) -> int {
         return (tid & 15) | (((tid >> 5) & 15) << 4) | (j << 8) | (((tid >> 4) & 1) << 12);
     };
-    auto out_col = [&](int j) -> int64_t {
-        if (SHFL12_PUSH)
-            return (int64_t((rank >> 1) + (j < 8 ? 0 : CL / 2)) << LB) + elem12(int(rank & 1u) * 8 + (j & 7));
-        if (PUSH)
-            return (int64_t((rank >> 1) + (j < 8 ? 0 : CL / 2)) << LB) + (int64_t(rank & 1u) << (LB - 1)) + tid +
-                   ((j & 7) << (LB - 4));
-        if (SHFL12) return col0 + elem12(j);
-        return col0 + tid + (j << (LB - 4));
-    };
-    // index of register j's output in the store buffer (whole boxes of 4096)
-    auto out_idx = [&](int j) -> int {
-        if (SHFL12_PUSH) {
-            const int e = elem12(int(rank & 1u) * 8 + (j & 7));
-            return (j < 8 ? 0 : (1 << (LB - 1))) + (((e >> 12) & 1) << 11) + (e & 2047);
-        }
-        if (PUSH) return (j < 8 ? 0 : (1 << (LB - 1))) + tid + ((j & 7) << (LB - 4));
+    // column of register j's output, which is also its index in the store
+    // buffer (boxes of 2048 columns)
+    auto out_col = [&](int j) -> int {
         if (SHFL12) return elem12(j);
         return tid + (j << (LB - 4));
     };
 
-    const unsigned ibar0 = unsigned(__cvta_generic_to_shared(&ibar[0]));
     if (tid == 0) {
         mbar_init(bar0, 1);
         mbar_init(bar0 + 8, 1);
-        // an inbox's phase completes on this CTA's arm (arrive + expect_tx)
-        // and the partner's INBOX bytes of st.async
-        if (PUSH_ROWS)
-            for (int i = 0; i < LCL; ++i) mbar_init(ibar0 + 8u * unsigned(i), 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     __syncthreads();
@@ -560,7 +520,7 @@ rht_tma_kernel(const __grid_constant__ CUtensorMap tin, const __grid_constant__ 
         mbar_arrive_expect_tx(bar0, NBOX * INB);
 #pragma unroll
         for (int bx = 0; bx < NBOX; ++bx)
-            load3d(sbase + bx * INB, &tin, 0, lin0 + bx * CH_IN, int(first), bar0);
+            load3d(sbase + bx * INB, &tin, 0, bx * CH_IN, int(first), bar0);
     }
     // per-thread constants: pass-0 columns 16 tid + j, last-pass columns tid + (j << (LB - 4))
     double pre_r[COLS && MODE == MODE_FWD ? 16 : 1];
@@ -568,7 +528,7 @@ rht_tma_kernel(const __grid_constant__ CUtensorMap tin, const __grid_constant__ 
     if (MODE == MODE_FWD) {
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
-            const int64_t e = col0 + 16 * tid + j;
+            const int64_t e = 16 * tid + j;
             if (COLS) pre_r[j] = __ldg(a.pre + e);
             else mask0 |= (__ldg(a.signs + e) < 0.0 ? 1u : 0u) << j;
         }
@@ -579,21 +539,9 @@ rht_tma_kernel(const __grid_constant__ CUtensorMap tin, const __grid_constant__ 
     const double inv_mul = ldexp(1.0, -B);
     const double fwd_mul = ldexp(1.0, -(B >> 1));
     bool fail = false;
-    unsigned peer_base[LCL > 0 ? LCL : 1], peer_ibar[LCL > 0 ? LCL : 1];
-#pragma unroll
-    for (int i = 0; i < LCL; ++i) {
-        asm("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(peer_base[i]) : "r"(sbase), "r"(rank ^ (1u << i)));
-        asm("mapa.shared::cluster.u32 %0, %1, %2;"
-            : "=r"(peer_ibar[i]) : "r"(ibar0 + 8u * unsigned(i)), "r"(rank ^ (1u << i)));
-    }
-    // PUSH rows: a partner's values arrive in an inbox after the two tiles
-    // (inbox i for the stage with rank ^ 2^i)
-    constexpr unsigned INBOX = 8u << (LB - 1);
-    const unsigned inbox = sbase + 2u * unsigned(BUFB);
-    if (PUSH) cluster_arrive_rel();   // opens the first "inbox read" phase
 
     int k = 0;
-    for (int64_t r = first; r < a.rows; r += nclusters, ++k) {
+    for (int64_t r = first; r < a.rows; r += nctas, ++k) {
         const unsigned buf = sbase + unsigned((k & 1) * BUFB);
         double *tile = reinterpret_cast<double *>(smem_r + (k & 1) * BUFB);
         rmb_wait(bar0 + 8u * unsigned(k & 1), unsigned((k >> 1) & 1), fail);
@@ -623,14 +571,13 @@ rht_tma_kernel(const __grid_constant__ CUtensorMap tin, const __grid_constant__ 
         __syncthreads();   // everyone has its raw values: the buffer becomes the work tile
         // prefetch the CTA's next row into the other buffer (its previous store
         // must have finished reading it)
-        if (tid == 0 && r + nclusters < a.rows) {
+        if (tid == 0 && r + nctas < a.rows) {
             bulk_wait_read0();
             const unsigned nb = bar0 + 8u * unsigned((k + 1) & 1);
             mbar_arrive_expect_tx(nb, NBOX * INB);
 #pragma unroll
             for (int bx = 0; bx < NBOX; ++bx)
-                load3d(sbase + unsigned(((k + 1) & 1) * BUFB) + bx * INB, &tin, 0, lin0 + bx * CH_IN,
-                          int(r + nclusters), nb);
+                load3d(sbase + unsigned(((k + 1) & 1) * BUFB) + bx * INB, &tin, 0, bx * CH_IN, int(r + nctas), nb);
         }
         // ---- passes 4, 8, ...: transposes through the element-swizzled tile ----
 #pragma unroll
@@ -660,44 +607,12 @@ rht_tma_kernel(const __grid_constant__ CUtensorMap tin, const __grid_constant__ 
                 x[j] = upper ? d_sub(o, x[j]) : d_add(x[j], o);
             }
         }
-        // registers: elements tid + (j << (LB - 4)) of this CTA's part
-        // ---- stages of index bits LB .. B-1 across the cluster: bit LB + i pairs
-        //      CTA rank with rank ^ 2^i (lower: own + peer, upper: peer - own) --
-        if constexpr (PUSH) {
-            // Stage of bit LB + i with CTA rank ^ 2^i: of the 2^LB pairs at
-            // local index jj (registers jj, 8 + jj: the lower and upper of
-            // this CTA's two ranges), the lower CTA (bit i of rank clear)
-            // finishes those of registers < 8 and the upper those >= 8; each
-            // pushes the other half into the partner's inbox by st.async,
-            // which completes on the partner's inbox mbarrier (no fence and
-            // no cluster barrier on the data path).
-            cluster_wait_acq();   // every inbox of the previous row has been read
-#pragma unroll
-            for (int i = 0; i < LCL; ++i) {
-                const bool up = (rank >> i) & 1u;
-                if (tid == 0) mbar_arrive_expect_tx(ibar0 + 8u * unsigned(i), INBOX);
-#pragma unroll
-                for (int jj = 0; jj < 8; ++jj)
-                    st_async_f64(peer_base[i] + 2u * unsigned(BUFB) + unsigned(i) * INBOX +
-                                     8u * unsigned(tid + (jj << (LB - 4))), up ? x[jj] : x[8 + jj], peer_ibar[i]);
-                rmb_wait(ibar0 + 8u * unsigned(i), unsigned(k & 1), fail);   // the partner's values are in inbox i
-#pragma unroll
-                for (int jj = 0; jj < 8; ++jj) {
-                    const double v = lds64d(inbox + unsigned(i) * INBOX + 8u * unsigned(tid + (jj << (LB - 4))));
-                    const double own = up ? x[8 + jj] : x[jj];
-                    const double lo = up ? v : own, hi = up ? own : v;
-                    x[jj] = d_add(lo, hi);
-                    x[8 + jj] = d_sub(lo, hi);
-                }
-            }
-            cluster_arrive_rel();   // inboxes read
-        }
         // ---- epilogue: scale, write the swizzled output lines, store ---------
         double se = 0.0, sa = 0.0;
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
-            const int E = out_idx(j);
-            const int64_t e = out_col(j);
+            const int E = out_col(j);
+            const int64_t e = E;
             double y;
             if (MODE == MODE_FWD) {
                 y = (B & 1) ? div_sqrt_n(x[j], a) : d_mul(x[j], fwd_mul);
@@ -732,30 +647,17 @@ rht_tma_kernel(const __grid_constant__ CUtensorMap tin, const __grid_constant__ 
         __syncthreads();
         if (tid == 0) {
 #pragma unroll
-            for (int bx = 0; bx < NOBOX; ++bx) {
-                // PUSH: boxes [0, NOBOX/2) hold the first column range
-                // (registers < 8), the rest the second
-                // SHFL12_PUSH: box bx = (column range bx >> 1, bit 12 = bx & 1)
-                // of the columns with bit 11 = rank & 1
-                const int c0 = SHFL12_PUSH
-                    ? ((int(rank >> 1) + (bx >> 1) * (CL / 2)) * (1 << LB) + (bx & 1) * 4096 + int(rank & 1u) * 2048) /
-                          (128 / int(sizeof(TOut)))
-                    : PUSH ? int(out_col((bx / (NOBOX / 2)) * 8) - tid + (bx % (NOBOX / 2)) * OBOX) /
-                                 (128 / int(sizeof(TOut)))
-                           : lout0 + bx * CH_OUT;
-                store3d(&tout, 0, c0, int(r), buf + unsigned(bx * OUTB));
-            }
+            for (int bx = 0; bx < NOBOX; ++bx) store3d(&tout, 0, bx * CH_OUT, int(r), buf + unsigned(bx * OUTB));
             bulk_commit();
             if (MODE == MODE_INV && COLS && a.err_partial) {
                 double s0 = 0.0, s1 = 0.0;
                 for (int i = 0; i < NT / 32; ++i) { s0 = d_add(s0, red[2 * i]); s1 = d_add(s1, red[2 * i + 1]); }
-                a.err_partial[2 * (CL * r + rank)] = s0;
-                a.err_partial[2 * (CL * r + rank) + 1] = s1;
+                a.err_partial[2 * r] = s0;
+                a.err_partial[2 * r + 1] = s1;
             }
         }
     }
     if (tid == 0) bulk_wait0();
-    if (PUSH) cluster_wait_acq();   // closes the last "inbox read" phase
 }
 
 // ---------------------------------------------------------------------------
@@ -1210,40 +1112,21 @@ bool tma_ok(const RhtArgs &a, int64_t ncols_in) {
            a.ncols_out % (128 / int(sizeof(TOut))) == 0 && encode_fn() != nullptr;
 }
 
-template <typename TIn, typename TOut, int MODE, int LB, int CL, bool COLS>
+template <typename TIn, typename TOut, int MODE, int LB, bool COLS>
 int launch_tma_v(const CUtensorMap &mi, const CUtensorMap &mo, const RhtArgs &a, cudaStream_t st, int64_t *nparts) {
-    auto kern = rht_tma_kernel<TIn, TOut, MODE, LB, CL, COLS>;
+    auto kern = rht_tma_kernel<TIn, TOut, MODE, LB, COLS>;
     const int nt = 1 << (LB - 4);
-    // two fp64 tiles (+ one inbox of 2^(LB-1) values per cross-CTA stage) + alignment slack
-    const size_t smem = size_t(2) * (size_t(8) << LB) + ((CL == 2 || CL == 4) ? size_t(CL / 2) * (size_t(8) << (LB - 1)) : 0) +
-                        1024;
+    const size_t smem = size_t(2) * (size_t(8) << LB) + 1024;   // two fp64 tiles + alignment slack
     if (uq::set_smem_attr(reinterpret_cast<const void *>(kern), int(smem)) != cudaSuccess)
         return uq::check_cuda("rht tma: set smem attribute");
-    cudaLaunchConfig_t cfg = {};
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = CL; attr[0].val.clusterDim.y = 1; attr[0].val.clusterDim.z = 1;
-    cfg.blockDim = dim3(nt, 1, 1); cfg.dynamicSmemBytes = smem; cfg.stream = st;
-    cfg.attrs = attr; cfg.numAttrs = CL > 1 ? 1 : 0;
-    int64_t slots = 0;
-    if (CL > 1) {
-        cfg.gridDim = dim3(CL, 1, 1);
-        int clusters = 0;
-        if (uq::occupancy_clusters(&clusters, reinterpret_cast<const void *>(kern), &cfg) != cudaSuccess || clusters < 1)
-            return uq::check_cuda("rht tma: cluster occupancy");
-        slots = clusters;
-    } else {
-        int per_sm = 0;
-        if (uq::occupancy_blocks(&per_sm, reinterpret_cast<const void *>(kern), nt, smem) != cudaSuccess || per_sm < 1)
-            return uq::check_cuda("rht tma: occupancy");
-        slots = int64_t(per_sm) * uq::num_sms();
-    }
-    const int64_t groups = std::min<int64_t>(a.rows, slots);
-    cfg.gridDim = dim3(unsigned(groups * CL), 1, 1);
-    *nparts = a.rows * CL;
-    if (groups > 0) {
+    int per_sm = 0;
+    if (uq::occupancy_blocks(&per_sm, reinterpret_cast<const void *>(kern), nt, smem) != cudaSuccess || per_sm < 1)
+        return uq::check_cuda("rht tma: occupancy");
+    const int64_t grid = std::min<int64_t>(a.rows, int64_t(per_sm) * uq::num_sms());
+    *nparts = a.rows;
+    if (grid > 0) {
         uq::ProfScope _p("rht", st);
-        if (cudaLaunchKernelEx(&cfg, kern, mi, mo, a) != cudaSuccess) return uq::check_cuda("rht_tma_kernel launch");
+        kern<<<unsigned(grid), nt, smem, st>>>(mi, mo, a);
     }
     return uq::check_cuda("rht_tma_kernel launch");
 }
@@ -1292,15 +1175,14 @@ int launch_tma(const RhtArgs &a, int64_t ncols_in, cudaStream_t st, int64_t *npa
     if (!make_line_map<TIn>(&mi, a.in, a.rows, ncols_in, a.ld_in, 4096) ||
         !make_line_map<TOut>(&mo, a.out, a.rows, a.ncols_out, a.ld_out, 2048))
         return uq::fail(UQ_ERR_CUDA, "rht: tensor map encoding failed");
-    // n = 2^b as 2^LB-element parts on a cluster of 2^(b - LB) CTAs.  Measured
-    // on B200: 8192-element parts beat 4096-element parts with one more
-    // cluster stage for n >= 8192 (the distributed-shared-memory stage costs
-    // more than the lower occupancy of the 512-thread tile).  n = 16384 and
-    // 32768: each CTA transforms two 8192-element parts in sequence
-    // (rht_halves_kernel; one CTA, or a 2-CTA cluster, per row).
+    // Rows of 4096 and 8192: one CTA per row (rht_tma_kernel; measured on
+    // B200, a 512-thread CTA per row of 8192 beats two 4096-element parts on
+    // a cluster).  n = 16384 and 32768: each CTA transforms two 8192-element
+    // parts in sequence (rht_halves_kernel; one CTA, or a 2-CTA cluster, per
+    // row).
     switch (a.b) {
-    case 12: return launch_tma_v<TIn, TOut, MODE, 12, 1, COLS>(mi, mo, a, st, nparts);
-    case 13: return launch_tma_v<TIn, TOut, MODE, 13, 1, COLS>(mi, mo, a, st, nparts);
+    case 12: return launch_tma_v<TIn, TOut, MODE, 12, COLS>(mi, mo, a, st, nparts);
+    case 13: return launch_tma_v<TIn, TOut, MODE, 13, COLS>(mi, mo, a, st, nparts);
     case 14: return launch_tma_halves<TIn, TOut, MODE, COLS, 1>(mi, a, st, nparts);
     default: return launch_tma_halves<TIn, TOut, MODE, COLS, 2>(mi, a, st, nparts);
     }
