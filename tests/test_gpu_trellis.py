@@ -268,6 +268,43 @@ def test_sharded_codes_match_whole_tensor():
         assert abs(out.wnmse - whole.wnmse) <= 1e-12 * whole.wnmse
 
 
+def test_quantize_shards_resumes_from_block_store(tmp_path):
+    """A run saves its three row blocks to a BlockStore; a crash that lost the
+    second block's marker is simulated by deleting that marker line.  The
+    re-run quantizes only that block, loads the others, and gathers the codes,
+    scales and weighted NMSE of a run without the store."""
+    import torch
+    from ultraquant_b200 import shard as S
+    rng = np.random.RandomState(6)
+    rows, cols = 1536, 4096
+    W = torch.from_numpy(rng.normal(0, 0.02, size=(rows, cols)).astype(np.float32)).cuda()
+    H = torch.from_numpy(np.exp(rng.normal(0, 1, size=cols))).cuda()
+    spec = S.TensorSpec("w", rows, cols, L=16, R=2)
+    plan = S.plan([spec], 1, block_rows=512)
+    ref = S.gather_codes(S.quantize_shards(plan, 0, lambda s: (W[s.row0:s.row1], H)), plan, 1)[spec.name]
+    root = str(tmp_path)
+    S.quantize_shards(plan, 0, lambda s: (W[s.row0:s.row1], H), store=S.BlockStore(root))
+    marker = tmp_path / "blocks.0.done"
+    lines = marker.read_text().splitlines()
+    assert len(lines) == 3
+    lost = S.BlockStore.key(plan[1], 256, 256)
+    assert lost in lines
+    marker.write_text("\n".join(ln for ln in lines if ln != lost) + "\n")
+    called = []
+
+    def weights(s):
+        called.append(s.row0)
+        return W[s.row0:s.row1], H
+
+    loc = S.quantize_shards(plan, 0, weights, store=S.BlockStore(root))
+    assert called == [plan[1].row0]
+    out = S.gather_codes(loc, plan, 1)[spec.name]
+    assert torch.equal(out.codes, ref.codes)
+    assert torch.equal(out.sc.view(torch.int32), ref.sc.view(torch.int32))
+    assert out.wnmse == ref.wnmse
+    assert len(marker.read_text().splitlines()) == 3
+
+
 @pytest.mark.parametrize("L,R,T,n", [(6, 1, 32, 2000), (6, 3, 32, 2000), (8, 2, 64, 2000), (8, 4, 64, 2000),
                                      (12, 2, 64, 2000), (12, 3, 64, 2000), (14, 2, 64, 400), (15, 3, 64, 400),
                                      (16, 1, 32, 64), (16, 2, 32, 128), (16, 3, 32, 128), (16, 4, 32, 64)])

@@ -233,3 +233,80 @@ def test_gloo_gathered_codes_unpack_to_single_process_states(tmp_path):
             assert np.array_equal(O.unpack_states(gc.numpy().view(np.uint32), SEG, spec.L, spec.R), st)
             assert torch.equal(gsc.view(torch.int32), sc.view(torch.int32))
             assert abs(float(gerr[0] / gerr[1]) - float(err[0] / err[1])) <= 1e-12 * float(err[0] / err[1])
+
+
+# ---- resumable runs: per-row-block completion markers (BlockStore) -------------
+
+def test_block_store_round_trip_and_markers(tmp_path):
+    """Saved blocks load back bit-identically; a block counts as done only
+    with its marker, for the same L, R, seg and group, and a file that does
+    not match the block's plan is not used."""
+    shards = S.plan(CODE_SPECS, 1, block_rows=8)
+    store = S.BlockStore(str(tmp_path), rank=0)
+    saved = {}
+    for s in shards[:-1]:
+        W, H = _weights(s.tensor, s.row0, s.row1)
+        _, codes, sc, err = _oracle_codes(s.tensor, W, H)
+        c = S.ShardCodes(s, codes, sc, err)
+        store.save(c, SEG, GROUP)
+        saved[(s.tensor.name, s.row0)] = c
+    fresh = S.BlockStore(str(tmp_path), rank=1)          # another process, another rank
+    for s in shards[:-1]:
+        assert fresh.done(s, SEG, GROUP)
+        assert not fresh.done(s, SEG * 2, GROUP)          # other parameters: not this block
+        got = fresh.load(s, "cpu", SEG, GROUP)
+        ref = saved[(s.tensor.name, s.row0)]
+        assert torch.equal(got.codes, ref.codes) and torch.equal(got.sc.view(torch.int32), ref.sc.view(torch.int32))
+        assert torch.equal(got.err, ref.err)
+    last = shards[-1]
+    assert not fresh.done(last, SEG, GROUP)
+    # a block file written without its marker (interrupted before the marker) is not done
+    W, H = _weights(last.tensor, last.row0, last.row1)
+    _, codes, sc, err = _oracle_codes(last.tensor, W, H)
+    np.savez(store.path(last), codes=codes.numpy(), sc=sc.numpy(), err=err.numpy())
+    assert not S.BlockStore(str(tmp_path)).done(last, SEG, GROUP)
+    # a marked block whose file does not match its plan is not loaded
+    first = shards[0]
+    np.savez(store.path(first), codes=codes.numpy()[:1], sc=sc.numpy(), err=err.numpy())
+    assert S.BlockStore(str(tmp_path)).load(first, "cpu", SEG, GROUP) is None
+
+
+def _store_worker(rank, world, port, root):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    import datetime
+    import torch.distributed as dist
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=30))
+    try:
+        store = S.BlockStore(root, rank=rank)
+        for s in S.plan(CODE_SPECS, world, block_rows=8):
+            if s.rank == rank:
+                W, H = _weights(s.tensor, s.row0, s.row1)
+                _, codes, sc, err = _oracle_codes(s.tensor, W, H)
+                store.save(S.ShardCodes(s, codes, sc, err), SEG, GROUP)
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_resume_at_another_world_size(tmp_path):
+    """Two gloo ranks quantize and save their row blocks; a re-run in one
+    process takes every block from the store (no block is quantized again:
+    its weight callback raises) and gathers the codes of the whole tensors
+    quantized in one process."""
+    root = str(tmp_path / "store")
+    mp.start_processes(_store_worker, args=(2, _free_port(), root), nprocs=2, join=True, start_method="spawn")
+    assert sorted(f for f in os.listdir(root) if f.endswith(".done")) == ["blocks.0.done", "blocks.1.done"]
+
+    def no_weights(s):
+        raise AssertionError(f"block {s.tensor.name}:{s.row0} quantized again")
+
+    shards = S.plan(CODE_SPECS, 1, block_rows=8)
+    local = S.quantize_shards(shards, 0, no_weights, seg=SEG, group=GROUP, store=S.BlockStore(root), device="cpu")
+    assert len(local) == len(shards)
+    out = S.gather_codes(local, shards, 1, seg=SEG, group=GROUP)
+    for spec in CODE_SPECS:
+        W, H = _weights(spec, 0, spec.rows)
+        st, codes, sc, err = _oracle_codes(spec, W, H)
+        assert torch.equal(out[spec.name].codes, codes), spec.name
+        assert torch.equal(out[spec.name].sc.view(torch.int32), sc.view(torch.int32))
+        assert abs(out[spec.name].wnmse - float(err[0] / err[1])) <= 1e-12 * float(err[0] / err[1])

@@ -17,17 +17,26 @@ only exchanges are
   spans the whole tensor: a gather of the sampled normalised vectors to one
   rank, which bisects, and a broadcast of the step.
 
+Resumable runs: with a ``BlockStore``, each finished row block's packed
+codes, scales and error sums are saved with a completion marker, and a
+re-run (at any world size) loads the finished blocks instead of quantizing
+them again -- the sharded counterpart of the builders' per-tensor
+``OUT.done`` (buildtrellis.py:22-28, 40).
+
 The plan is deterministic (every rank computes it locally) and balances the
 ranks by padded weights x trellis cost per weight.
 """
 from __future__ import annotations
 
+import os
 from dataclasses import dataclass, field
 
+import numpy as np
 import torch
 
 __all__ = ["TensorSpec", "Shard", "plan", "llama_shapes", "run_shards", "gather_errors", "assemble_rows",
-           "calibrate_e8", "ShardCodes", "PackedTrellis", "quantize_shards", "gather_codes", "shard_words"]
+           "calibrate_e8", "ShardCodes", "PackedTrellis", "quantize_shards", "gather_codes", "shard_words",
+           "BlockStore"]
 
 
 @dataclass(frozen=True)
@@ -155,8 +164,80 @@ def shard_words(shard: Shard, seg: int = 256, group: int = 256) -> tuple[int, in
     return nseq * words, shard.rows * n // group, 4
 
 
+class BlockStore:
+    """Completion markers of row blocks for resumable sharded runs.
+
+    ``save`` writes a block's packed codes, scales and error sums to
+    ``<root>/<tensor>.<row0>-<row1>.npz`` under a temporary name, renames it
+    into place and only then appends the block's key to the rank's marker
+    file ``<root>/blocks.<rank>.done`` (flushed and synced), so a marker
+    always names a complete file.  The key also holds L, R, seg and group,
+    so a run with other parameters does not pick up stale blocks.  ``done``
+    reads the markers of every rank (a re-run may use another world size).
+    ``load`` checks the sizes against the block's plan and returns None for
+    a file that does not match (the block is then quantized again)."""
+
+    def __init__(self, root: str, rank: int = 0):
+        self.root = root
+        self.rank = rank
+        os.makedirs(root, exist_ok=True)
+        self._keys = None
+
+    @staticmethod
+    def key(shard: Shard, seg: int, group: int) -> str:
+        t = shard.tensor
+        return f"{t.name}:{shard.row0}:{shard.row1}:L{t.L}:R{t.R}:seg{seg}:g{group}"
+
+    def path(self, shard: Shard) -> str:
+        name = shard.tensor.name.replace(os.sep, "_")
+        return os.path.join(self.root, f"{name}.{shard.row0}-{shard.row1}.npz")
+
+    def _read_keys(self) -> set:
+        keys = set()
+        for fn in os.listdir(self.root):
+            if fn.startswith("blocks.") and fn.endswith(".done"):
+                with open(os.path.join(self.root, fn)) as fh:
+                    keys.update(ln.strip() for ln in fh if ln.strip())
+        return keys
+
+    def done(self, shard: Shard, seg: int = 256, group: int = 256) -> bool:
+        if self._keys is None:
+            self._keys = self._read_keys()
+        return self.key(shard, seg, group) in self._keys
+
+    def save(self, c: ShardCodes, seg: int = 256, group: int = 256) -> None:
+        final = self.path(c.shard)
+        tmp = final + f".{os.getpid()}.tmp"
+        with open(tmp, "wb") as fh:
+            np.savez(fh, codes=c.codes.cpu().numpy(), sc=c.sc.cpu().numpy(),
+                     err=c.err.to(torch.float64).cpu().numpy())
+            fh.flush()
+            os.fsync(fh.fileno())
+        os.replace(tmp, final)
+        k = self.key(c.shard, seg, group)
+        with open(os.path.join(self.root, f"blocks.{self.rank}.done"), "a") as fh:
+            fh.write(k + "\n")
+            fh.flush()
+            os.fsync(fh.fileno())
+        if self._keys is not None:
+            self._keys.add(k)
+
+    def load(self, shard: Shard, device, seg: int = 256, group: int = 256) -> ShardCodes | None:
+        try:
+            with np.load(self.path(shard)) as z:
+                codes, sc, err = z["codes"], z["sc"], z["err"]
+        except (OSError, KeyError, ValueError):
+            return None
+        nc, ns, _ = shard_words(shard, seg, group)
+        if (codes.dtype != np.int32 or codes.size != nc or sc.dtype != np.float32 or sc.size != ns
+                or err.dtype != np.float64 or err.size != 2):
+            return None
+        return ShardCodes(shard, torch.from_numpy(codes).to(device), torch.from_numpy(sc).to(device),
+                          torch.from_numpy(err).to(device))
+
+
 def quantize_shards(shards, rank: int, weights, seg: int = 256, group: int = 256,
-                    keep_what: bool = False) -> list[ShardCodes]:
+                    keep_what: bool = False, store: BlockStore | None = None, device=None) -> list[ShardCodes]:
     """Quantize this rank's row blocks with the fused device recipe
     (buildtrellis.py:16-20 around trellis.py:62-108) and pack each block's
     state paths.  ``weights(shard) -> (W rows, H)``: device tensors, or host
@@ -164,14 +245,27 @@ def quantize_shards(shards, rank: int, weights, seg: int = 256, group: int = 256
 
     The blocks are launched back to back; the bounded-wait status of all of
     them is checked once at the end (one stream synchronisation), before any
-    result leaves the rank, and a timed-out wait raises UQError."""
+    result leaves the rank, and a timed-out wait raises UQError.
+
+    ``store``: blocks it marks done are loaded onto ``device`` (default: the
+    current CUDA device, else the CPU) instead of being quantized; the others
+    are saved to it after the status check (What is not kept for loaded
+    blocks)."""
     from . import _device as D
     from . import _lib, pipeline, trellis
     out = []
     dev = None
+    fresh = []
+    if device is None:
+        device = torch.device("cuda", torch.cuda.current_device()) if torch.cuda.is_available() else torch.device("cpu")
     for s in shards:
         if s.rank != rank:
             continue
+        if store is not None and store.done(s, seg, group):
+            c = store.load(s, device, seg, group)
+            if c is not None:
+                out.append(c)
+                continue
         W, H = weights(s)
         if not W.is_cuda:
             W = D.as_device(W)
@@ -180,8 +274,12 @@ def quantize_shards(shards, rank: int, weights, seg: int = 256, group: int = 256
                                             keep_codes=True, check_errors=False)
         codes = trellis.pack_states(res.states, s.tensor.L, s.tensor.R)
         out.append(ShardCodes(s, codes, res.sc, res.err, res.What if keep_what else None))
+        fresh.append(out[-1])
     if dev is not None:
         _lib.check(_lib.load().uq_device_errors(D.stream_handle(dev)), "quantize_shards")
+    if store is not None:
+        for c in fresh:
+            store.save(c, seg, group)
     return out
 
 
