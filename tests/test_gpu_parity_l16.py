@@ -130,3 +130,21 @@ def test_llama8b_shapes_l16(name, rows, cols, R):
     spr = O.next_pow2(cols) // 256
     nseq, mism, w = _check_tensor(W, H, R, 4096 // spr, seed=7)
     assert nseq >= 4096
+
+
+@pytest.mark.parametrize("name,rows,cols", [
+    ("ffn_down", 8192, 28672),          # padded to 32768 columns (2-CTA transform): 128 sequences per row
+    ("ffn_gate", 28672, 8192),
+    ("attn_k", 1024, 8192),
+])
+def test_llama70b_shapes_l16(name, rows, cols):
+    """Llama-3-70B tensor shapes with Student-t (nu = 4) weights of std 0.015
+    and a log-normal imatrix at the uniform k = 2 of that weight set: 4,096
+    sequences per tensor checked."""
+    rng = np.random.RandomState(sum(map(ord, name)) + 70)
+    W = _student_t(rng, (rows, cols), 0.015)
+    H = np.exp(rng.normal(0.0, 1.0, size=cols))
+    spr = O.next_pow2(cols) // 256
+    nseq, mism, w = _check_tensor(W, H, 2, 4096 // spr, seed=70)
+    assert nseq >= 4096
+    assert 0.0 < w < 0.08
