@@ -268,6 +268,25 @@ def test_sharded_codes_match_whole_tensor():
         assert abs(out.wnmse - whole.wnmse) <= 1e-12 * whole.wnmse
 
 
+def test_sharded_e8_points_match_whole_tensor():
+    """shard.quantize_shards_e8 + gather_e8 over three row blocks give the
+    int16 E8 points and weighted NMSE of the whole tensor quantized in one
+    call (ffn_down width 14336 -> 16384, step 0.48)."""
+    import torch
+    from ultraquant_b200 import pipeline as P, shard as S
+    rng = np.random.RandomState(8)
+    rows, cols = 1536, 14336
+    W = torch.from_numpy((rng.standard_t(4, size=(rows, cols)) / np.sqrt(2) * 0.015).astype(np.float32)).cuda()
+    H = torch.from_numpy(np.exp(rng.normal(0, 1, size=cols))).cuda()
+    spec = S.TensorSpec("d", rows, cols)
+    plan = S.plan([spec], 1, block_rows=512)
+    assert len(plan) == 3
+    out = S.gather_e8(S.quantize_shards_e8(plan, 0, lambda s: (W[s.row0:s.row1], H), 0.48), plan, 1, 0.48)[spec.name]
+    whole = P.quant_step_device(W, H, 0.48, keep_codes=True)
+    assert torch.equal(out.idx.reshape(-1), whole.idx)
+    assert abs(out.wnmse - whole.wnmse) <= 1e-12 * whole.wnmse
+
+
 def test_quantize_shards_resumes_from_block_store(tmp_path):
     """A run saves its three row blocks to a BlockStore; a crash that lost the
     second block's marker is simulated by deleting that marker line.  The

@@ -310,3 +310,58 @@ def test_resume_at_another_world_size(tmp_path):
         assert torch.equal(out[spec.name].codes, codes), spec.name
         assert torch.equal(out[spec.name].sc.view(torch.int32), sc.view(torch.int32))
         assert abs(out[spec.name].wnmse - float(err[0] / err[1])) <= 1e-12 * float(err[0] / err[1])
+
+
+# ---- int16 E8 points of row-sharded tensors (qlab.py:153, 159-183) -------------
+E8_SPECS = [S.TensorSpec("e0", 24, 256), S.TensorSpec("e1", 16, 300), S.TensorSpec("e2", 8, 512)]
+E8_STEP = 0.48
+
+
+def _oracle_e8(spec, W, H):
+    """Oracle fixed-step E8 recipe on a block of rows: int16 points 2p of the
+    padded rotated rows and the error sums."""
+    Hc = np.maximum(H, H.max() * 1e-3)
+    A = W * np.sqrt(Hc)[None, :]
+    Ar = O.rht_rows(A)
+    p = O.e8_decode(O.group_gn(Ar) / E8_STEP)
+    idx = torch.from_numpy((2 * p).reshape(Ar.shape).astype(np.int16))
+    Ah = O.irht_rows(O.q_e8_fast(Ar, fixed_step=E8_STEP), W.shape[1])
+    err = torch.tensor([np.sum((A - Ah) ** 2), np.sum(A ** 2)], dtype=torch.float64)
+    return idx, err
+
+
+def _e8_worker(rank, world, port, out_dir):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    import datetime
+    import torch.distributed as dist
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=30))
+    try:
+        shards = S.plan(E8_SPECS, world, block_rows=8)
+        local = []
+        for s in shards:
+            if s.rank == rank:
+                W, H = _weights(s.tensor, s.row0, s.row1)
+                idx, err = _oracle_e8(s.tensor, W, H)
+                local.append(S.ShardE8(s, idx, err))
+        out = S.gather_e8(local, shards, world, E8_STEP)
+        torch.save({k: (v.idx, v.err) for k, v in out.items()}, os.path.join(out_dir, f"e8_{rank}.pt"))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_gloo_gathered_e8_points_equal_single_process(tmp_path):
+    """Two ranks quantize interleaved row blocks with the fixed-step E8
+    recipe; after the one all-gather both hold the int16 points of the whole
+    tensors quantized in one process and their weighted NMSE."""
+    mp.start_processes(_e8_worker, args=(2, _free_port(), str(tmp_path)), nprocs=2, join=True,
+                       start_method="spawn")
+    assert {s.rank for s in S.plan(E8_SPECS, 2, block_rows=8)} == {0, 1}
+    for r in range(2):
+        got = torch.load(tmp_path / f"e8_{r}.pt")
+        for spec in E8_SPECS:
+            W, H = _weights(spec, 0, spec.rows)
+            idx, err = _oracle_e8(spec, W, H)
+            gidx, gerr = got[spec.name]
+            assert gidx.shape == (spec.rows, spec.padded_cols)
+            assert torch.equal(gidx, idx), spec.name
+            assert abs(float(gerr[0] / gerr[1]) - float(err[0] / err[1])) <= 1e-12 * float(err[0] / err[1])

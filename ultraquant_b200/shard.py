@@ -10,7 +10,9 @@ only exchanges are
 * one all-gather of every rank's packed trellis codes (the L + R(T-1) bits
   of each sequence), per-256 scales and per-block error sums
   {sum (A-Ah)^2, sum A^2} (``quantize_shards`` + ``gather_codes``): after it
-  every rank holds every tensor's codes and weighted NMSE,
+  every rank holds every tensor's codes and weighted NMSE; likewise the
+  int16 E8 lattice points of the fixed-step recipe and their error sums
+  (``quantize_shards_e8`` + ``gather_e8``),
 * an all-gather of the error statistics alone (``gather_errors``), and,
   optionally, assembling a tensor's What on one rank (``assemble_rows``),
 * for the calibrated E8 step (qlab.py:171-180), whose 600k-vector sample
@@ -36,7 +38,7 @@ import torch
 
 __all__ = ["TensorSpec", "Shard", "plan", "llama_shapes", "run_shards", "gather_errors", "assemble_rows",
            "calibrate_e8", "ShardCodes", "PackedTrellis", "quantize_shards", "gather_codes", "shard_words",
-           "BlockStore"]
+           "BlockStore", "ShardE8", "PackedE8", "quantize_shards_e8", "gather_e8", "shard_words_e8"]
 
 
 @dataclass(frozen=True)
@@ -283,6 +285,41 @@ def quantize_shards(shards, rank: int, weights, seg: int = 256, group: int = 256
     return out
 
 
+def _exchange_blocks(parts, shards, world: int, words, dev, pg=None):
+    """The one all-gather of block payloads.  ``parts[(tensor, row0)]``: this
+    rank's blocks as lists of flat 32-bit tensors whose word counts are
+    ``words(shard)``; every rank contributes its blocks in plan order, padded
+    to the largest rank's size (every rank knows the plan, so no sizes are
+    exchanged).  Returns [(shard, [int32 views of its parts])] for every block
+    of every rank."""
+    import torch.distributed as dist
+    by_rank = [[s for s in shards if s.rank == r] for r in range(world)]
+    sizes = [sum(sum(words(s)) for s in blk) for blk in by_rank]
+    cap = max(sizes) if sizes else 0
+    rank = dist.get_rank(pg) if (world > 1 and dist.is_available() and dist.is_initialized()) else 0
+    buf = torch.zeros(max(cap, 1), dtype=torch.int32, device=dev)
+    off = 0
+    for s in by_rank[rank]:
+        for p, nw in zip(parts[(s.tensor.name, s.row0)], words(s)):
+            buf[off:off + nw] = p.reshape(-1).view(torch.int32)
+            off += nw
+    if world > 1:
+        allb = torch.empty(world * buf.numel(), dtype=torch.int32, device=dev)
+        dist.all_gather_into_tensor(allb, buf, group=pg)
+    else:
+        allb = buf
+    out = []
+    for r in range(world):
+        off = r * buf.numel()
+        for s in by_rank[r]:
+            views = []
+            for nw in words(s):
+                views.append(allb[off:off + nw])
+                off += nw
+            out.append((s, views))
+    return out
+
+
 def gather_codes(local, shards, world: int, seg: int = 256, group: int = 256, pg=None) -> dict:
     """All-gather every rank's packed codes, scales and error sums (one
     collective) and assemble them per tensor in row order on every rank.
@@ -291,51 +328,113 @@ def gather_codes(local, shards, world: int, seg: int = 256, group: int = 256, pg
     place in the gathered buffer is known without exchanging sizes; each rank
     contributes its blocks in plan order, padded to the largest rank's size.
     Error sums are added in row order (deterministic on every rank)."""
-    import torch.distributed as dist
-    mine = {(c.shard.tensor.name, c.shard.row0): c for c in local}
-    by_rank = [[s for s in shards if s.rank == r] for r in range(world)]
-    sizes = [sum(sum(shard_words(s, seg, group)) for s in blk) for blk in by_rank]
-    cap = max(sizes) if sizes else 0
     dev = local[0].codes.device if local else torch.device("cpu")
-    rank = dist.get_rank(pg) if (world > 1 and dist.is_available() and dist.is_initialized()) else 0
-    buf = torch.zeros(max(cap, 1), dtype=torch.int32, device=dev)
-    off = 0
-    for s in by_rank[rank]:
-        c = mine[(s.tensor.name, s.row0)]
-        nc, ns, ne = shard_words(s, seg, group)
-        buf[off:off + nc] = c.codes.reshape(-1)
-        buf[off + nc:off + nc + ns] = c.sc.reshape(-1).view(torch.int32)
-        buf[off + nc + ns:off + nc + ns + ne] = c.err.reshape(-1).to(torch.float64).view(torch.int32)
-        off += nc + ns + ne
-    if world > 1:
-        allb = torch.empty(world * buf.numel(), dtype=torch.int32, device=dev)
-        dist.all_gather_into_tensor(allb, buf, group=pg)
-    else:
-        allb = buf
-    # place every block of every tensor
-    specs = {}
-    for s in shards:
-        specs.setdefault(s.tensor.name, s.tensor)
+    parts = {(c.shard.tensor.name, c.shard.row0): [c.codes, c.sc, c.err.to(torch.float64)] for c in local}
+    blocks = _exchange_blocks(parts, shards, world, lambda s: shard_words(s, seg, group), dev, pg)
     out = {}
-    for name, t in specs.items():
+    for s in shards:
+        t = s.tensor
+        if t.name in out:
+            continue
         words = (t.L + t.R * (seg - 1) + 31) // 32
         nseq = t.rows * t.padded_cols // seg
         ng = t.rows * t.padded_cols // group
-        out[name] = PackedTrellis(t, torch.empty((nseq, words), dtype=torch.int32, device=dev),
-                                  torch.empty(ng, dtype=torch.float32, device=dev),
-                                  torch.zeros(2, dtype=torch.float64, device=dev), seg, group)
+        out[t.name] = PackedTrellis(t, torch.empty((nseq, words), dtype=torch.int32, device=dev),
+                                    torch.empty(ng, dtype=torch.float32, device=dev),
+                                    torch.zeros(2, dtype=torch.float64, device=dev), seg, group)
     errs = {}
-    for r in range(world):
-        off = r * buf.numel()
-        for s in by_rank[r]:
-            nc, ns, ne = shard_words(s, seg, group)
-            p = out[s.tensor.name]
-            q0 = s.row0 * s.tensor.padded_cols // seg
-            g0 = s.row0 * s.tensor.padded_cols // group
-            p.codes.view(-1)[q0 * p.codes.shape[1]:q0 * p.codes.shape[1] + nc] = allb[off:off + nc]
-            p.sc[g0:g0 + ns] = allb[off + nc:off + nc + ns].view(torch.float32)
-            errs.setdefault(s.tensor.name, []).append((s.row0, allb[off + nc + ns:off + nc + ns + ne]))
-            off += nc + ns + ne
+    for s, (codes, sc, err) in blocks:
+        p = out[s.tensor.name]
+        q0 = s.row0 * s.tensor.padded_cols // seg
+        g0 = s.row0 * s.tensor.padded_cols // group
+        p.codes.view(-1)[q0 * p.codes.shape[1]:q0 * p.codes.shape[1] + codes.numel()] = codes
+        p.sc[g0:g0 + sc.numel()] = sc.view(torch.float32)
+        errs.setdefault(s.tensor.name, []).append((s.row0, err))
+    for name, lst in errs.items():
+        acc = out[name].err
+        for _, e in sorted(lst, key=lambda v: v[0]):
+            acc += e.view(torch.float64)
+    return out
+
+
+# ---- E8 lattice points of row-sharded tensors (qlab.py:159-183, fixed step) ----
+
+@dataclass
+class ShardE8:
+    """One row block's E8 output on its rank: the int16 lattice coordinates
+    2p of its padded rotated rows (rows, n) -- the integer "indices" of
+    qlab.py:153 -- error sums [sum (A-Ah)^2, sum A^2] (fp64) and, if kept,
+    What."""
+    shard: Shard
+    idx: torch.Tensor
+    err: torch.Tensor
+    What: torch.Tensor | None = None
+
+
+@dataclass
+class PackedE8:
+    """A whole tensor's E8 points assembled from its row blocks (row order):
+    idx (rows, n) int16 = 2p, error sums (2,) summed over the blocks in row
+    order, the step, and the weighted NMSE."""
+    spec: TensorSpec
+    idx: torch.Tensor
+    err: torch.Tensor
+    step: float
+
+    @property
+    def wnmse(self) -> float:
+        e = self.err.double().cpu()
+        return float(e[0] / e[1])
+
+
+def shard_words_e8(shard: Shard) -> tuple[int, int]:
+    """32-bit words of a block's int16 points (two per word: the padded width
+    is a power of two) and error sums in the gathered buffer."""
+    return shard.rows * shard.tensor.padded_cols // 2, 4
+
+
+def quantize_shards_e8(shards, rank: int, weights, step: float, group: int = 256,
+                       keep_what: bool = False) -> list[ShardE8]:
+    """This rank's row blocks through the fixed-step E8 recipe
+    (buildalloc.py:21-24 around qlab.py:159-183), keeping the int16 points.
+    ``weights(shard) -> (W rows, H)`` as for ``quantize_shards``; one
+    bounded-wait check at the end."""
+    from . import _device as D
+    from . import _lib, pipeline
+    out = []
+    dev = None
+    for s in shards:
+        if s.rank != rank:
+            continue
+        W, H = weights(s)
+        if not W.is_cuda:
+            W = D.as_device(W)
+        dev = W.device
+        res = pipeline.quant_step_device(W, H, step, group=group, keep_codes=True, check_errors=False)
+        out.append(ShardE8(s, res.idx.reshape(s.rows, s.tensor.padded_cols), res.err,
+                           res.What if keep_what else None))
+    if dev is not None:
+        _lib.check(_lib.load().uq_device_errors(D.stream_handle(dev)), "quantize_shards_e8")
+    return out
+
+
+def gather_e8(local, shards, world: int, step: float, pg=None) -> dict:
+    """All-gather every rank's E8 points and error sums (one collective) and
+    assemble them per tensor in row order on every rank; error sums are added
+    in row order."""
+    dev = local[0].idx.device if local else torch.device("cpu")
+    parts = {(c.shard.tensor.name, c.shard.row0): [c.idx.contiguous(), c.err.to(torch.float64)] for c in local}
+    blocks = _exchange_blocks(parts, shards, world, shard_words_e8, dev, pg)
+    out = {}
+    for s in shards:
+        t = s.tensor
+        if t.name not in out:
+            out[t.name] = PackedE8(t, torch.empty((t.rows, t.padded_cols), dtype=torch.int16, device=dev),
+                                   torch.zeros(2, dtype=torch.float64, device=dev), step)
+    errs = {}
+    for s, (idx, err) in blocks:
+        out[s.tensor.name].idx[s.row0:s.row1] = idx.view(torch.int16).reshape(s.rows, s.tensor.padded_cols)
+        errs.setdefault(s.tensor.name, []).append((s.row0, err))
     for name, lst in errs.items():
         acc = out[name].err
         for _, e in sorted(lst, key=lambda v: v[0]):
