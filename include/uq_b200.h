@@ -169,7 +169,8 @@ int uq_e8_calibrate_sample(const double *sub, int64_t ns, double target_bpw, dou
  * lam whose total H does not exceed the global step's (c = 8).  Outputs
  * (nullable): rec (rows * n, may equal A), idx = 2p int16, choice (rows)
  * int32 candidate per row, *lam_host.  Synchronises the stream (lam is
- * chosen on the host).  UQ_ERR_UNSUPPORTED if some |2p| exceeds 255. */
+ * chosen on the host).  UQ_ERR_UNSUPPORTED if some |2p| exceeds 255, or
+ * for more than (2^31 - 1) / 16 rows (one CTA per row and candidate). */
 size_t uq_e8_scale_search_workspace_bytes(int64_t rows, int64_t n);
 int uq_e8_scale_search(const double *A, int64_t rows, int64_t n, double step, double *rec, int16_t *idx,
                        int32_t *choice, double *lam_host, void *workspace, size_t workspace_bytes,

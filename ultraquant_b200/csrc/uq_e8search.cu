@@ -90,10 +90,19 @@ __device__ __forceinline__ void load8(const double *row, int64_t e0, int n, doub
     }
 }
 
-// One CTA per (row, candidate): D and H of that pair.  Warps walk units of
-// two groups (the warp layout of WarpGroup<256>); the squared errors of a
-// unit go through a warp slab in shared memory so that their sums take
-// numpy's order.
+// Position of element e of a unit in the warp's slab: e ^ ((e >> 4) & 15).
+// The squared errors are written with lane v at e = 8 v + i (i fixed per
+// store) and read by warp_group_sumsq with four runs of 8 consecutive
+// elements 128 apart; with this swizzle both touch each of the 16 bank pairs
+// exactly twice (two wavefronts per 8-byte warp access, the minimum), where
+// the plain layout took 16 and 4.
+__device__ __forceinline__ int slab_pos(int e) { return e ^ ((e >> 4) & 15); }
+
+// One CTA per (row, candidate): D and H of that pair.  CTA b takes row
+// b / 16 and candidate b % 16, so a row's 16 CTAs run together and read it
+// from L2 once it is there.  Warps walk units of two groups (the warp layout
+// of WarpGroup<256>); the squared errors of a unit go through a warp slab in
+// shared memory so that their sums take numpy's order.
 __global__ void __launch_bounds__(kWarps * 32) e8_search_kernel(const double *A, int n, double step,
                                                                   const double *LG, double *D, double *H,
                                                                   int *bad) {
@@ -101,7 +110,7 @@ __global__ void __launch_bounds__(kWarps * 32) e8_search_kernel(const double *A,
     __shared__ __align__(16) double slab[kWarps][2 * kGroup];
     __shared__ double dg[4096 / kGroup * 32];      // per-group sums (n <= 2^17)
     __shared__ int hist[kBins];
-    const int row = blockIdx.x, c = blockIdx.y;
+    const int row = int(blockIdx.x / kCand), c = int(blockIdx.x % kCand);
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const double s = d_mul(step, c_factor[c]);
     const double *rowA = A + int64_t(row) * n;
@@ -123,7 +132,7 @@ __global__ void __launch_bounds__(kWarps * 32) e8_search_kernel(const double *A,
             decode_at(a, r, s, p);
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
-                slab[warp][8 * vv + i] = d_sub(a[i], d_mul(d_mul(p[i], s), r));
+                slab[warp][slab_pos(8 * vv + i)] = d_sub(a[i], d_mul(d_mul(p[i], s), r));
                 if (e0 < n) {
                     const int z = int((long long)d_mul(p[i], 2.0));
                     if (z < -kZMax || z > kZMax) atomicExch(bad, 1);
@@ -132,7 +141,7 @@ __global__ void __launch_bounds__(kWarps * 32) e8_search_kernel(const double *A,
             }
         }
         __syncwarp();
-        const double dsum = warp_group_sumsq<kGroup, double>([&](int i) -> double { return slab[warp][i]; });
+        const double dsum = warp_group_sumsq<kGroup, double>([&](int i) -> double { return slab[warp][slab_pos(i)]; });
         if (lane == 0) dg[2 * u] = dsum;
         if (lane == W::LPG && 2 * u + 1 < G) dg[2 * u + 1] = dsum;
         __syncwarp();
@@ -217,6 +226,8 @@ int e8_scale_search(const double *A, int64_t rows, int64_t n, double step, doubl
         if (lam_host) *lam_host = 0.0;
         return UQ_OK;
     }
+    if (rows > ((int64_t(1) << 31) - 1) / kCand)
+        return fail(UQ_ERR_UNSUPPORTED, "e8 scale search: %lld rows exceed the grid of 16 CTAs per row", (long long)rows);
     const SearchWs w = carve_search(ws, rows, n);
     if (ws_bytes < w.bytes) return fail(UQ_ERR_WORKSPACE, "e8 scale search: workspace %zu < %zu", ws_bytes, w.bytes);
     // the candidate table lives in each device's constant memory
@@ -230,7 +241,7 @@ int e8_scale_search(const double *A, int64_t rows, int64_t n, double step, doubl
         return check_cuda("e8 scale search: tables");
     {
         ProfScope _p("e8_search", st);
-        e8_search_kernel<<<dim3(unsigned(rows), kCand), kWarps * 32, 0, st>>>(A, int(n), step, w.LG, w.D, w.H, w.bad);
+        e8_search_kernel<<<unsigned(rows * kCand), kWarps * 32, 0, st>>>(A, int(n), step, w.LG, w.D, w.H, w.bad);
     }
     int rc = check_cuda("e8_search_kernel launch");
     if (rc) return rc;
