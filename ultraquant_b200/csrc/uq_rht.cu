@@ -293,6 +293,11 @@ __device__ __forceinline__ void cluster_sync_all() {
 __device__ __forceinline__ void cluster_arrive_rel() {
     asm volatile("barrier.cluster.arrive.release.aligned;\n" ::: "memory");
 }
+// Arrival without release semantics: only for arrivals that publish no
+// writes (the values read before it are already in registers)
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+    asm volatile("barrier.cluster.arrive.relaxed.aligned;\n" ::: "memory");
+}
 __device__ __forceinline__ void cluster_wait_acq() {
     asm volatile("barrier.cluster.wait.acquire.aligned;\n" ::: "memory");
 }
@@ -863,7 +868,10 @@ rht_halves_kernel(const __grid_constant__ CUtensorMap tin, RhtArgs a) {
                 xa[j] = d_add(lo, hi);
                 x[j] = d_sub(lo, hi);
             }
-            cluster_arrive_rel();   // inbox read
+            // inbox read: the partner may push its next row.  Relaxed: this
+            // arrival publishes no writes, and the inbox values it follows
+            // are consumed by the butterflies above, issued before it
+            cluster_arrive_relaxed();
         }
         // ---- epilogue: scale and store (sums at out_sum(j), differences at out_dif(j)) ----
         TOut *orow = static_cast<TOut *>(a.out) + r * a.ld_out;
