@@ -365,3 +365,37 @@ def test_gloo_gathered_e8_points_equal_single_process(tmp_path):
             assert gidx.shape == (spec.rows, spec.padded_cols)
             assert torch.equal(gidx, idx), spec.name
             assert abs(float(gerr[0] / gerr[1]) - float(err[0] / err[1])) <= 1e-12 * float(err[0] / err[1])
+
+
+def _idle_rank_worker(rank, world, port, out_dir):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    import datetime
+    import torch.distributed as dist
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=30))
+    try:
+        spec = CODE_SPECS[2]                               # 8 rows: one block, on rank 0
+        shards = S.plan([spec], world, block_rows=8)
+        local = []
+        for s in shards:
+            if s.rank == rank:
+                W, H = _weights(s.tensor, s.row0, s.row1)
+                _, codes, sc, err = _oracle_codes(s.tensor, W, H)
+                local.append(S.ShardCodes(s, codes, sc, err))
+        out = S.gather_codes(local, shards, world, seg=SEG, group=GROUP)
+        torch.save((len(local), out[spec.name].codes), os.path.join(out_dir, f"idle{rank}.pt"))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_gather_with_a_rank_without_blocks(tmp_path):
+    """More ranks than blocks: the idle rank still takes part in the one
+    all-gather and receives the whole tensor's codes."""
+    mp.start_processes(_idle_rank_worker, args=(2, _free_port(), str(tmp_path)), nprocs=2, join=True,
+                       start_method="spawn")
+    spec = CODE_SPECS[2]
+    W, H = _weights(spec, 0, spec.rows)
+    _, codes, _, _ = _oracle_codes(spec, W, H)
+    n0, c0 = torch.load(tmp_path / "idle0.pt")
+    n1, c1 = torch.load(tmp_path / "idle1.pt")
+    assert (n0, n1) == (1, 0)
+    assert torch.equal(c0, codes) and torch.equal(c1, codes)

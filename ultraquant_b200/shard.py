@@ -285,6 +285,18 @@ def quantize_shards(shards, rank: int, weights, seg: int = 256, group: int = 256
     return out
 
 
+def _exchange_device(local_dev, world: int, pg=None):
+    """Device of the gathered buffer: the rank's blocks' device, or for a
+    rank without blocks the current CUDA device under NCCL (which gathers
+    device tensors only), else the CPU."""
+    if local_dev is not None:
+        return local_dev
+    import torch.distributed as dist
+    if world > 1 and dist.is_available() and dist.is_initialized() and dist.get_backend(pg) == "nccl":
+        return torch.device("cuda", torch.cuda.current_device())
+    return torch.device("cpu")
+
+
 def _exchange_blocks(parts, shards, world: int, words, dev, pg=None):
     """The one all-gather of block payloads.  ``parts[(tensor, row0)]``: this
     rank's blocks as lists of flat 32-bit tensors whose word counts are
@@ -328,7 +340,7 @@ def gather_codes(local, shards, world: int, seg: int = 256, group: int = 256, pg
     place in the gathered buffer is known without exchanging sizes; each rank
     contributes its blocks in plan order, padded to the largest rank's size.
     Error sums are added in row order (deterministic on every rank)."""
-    dev = local[0].codes.device if local else torch.device("cpu")
+    dev = _exchange_device(local[0].codes.device if local else None, world, pg)
     parts = {(c.shard.tensor.name, c.shard.row0): [c.codes, c.sc, c.err.to(torch.float64)] for c in local}
     blocks = _exchange_blocks(parts, shards, world, lambda s: shard_words(s, seg, group), dev, pg)
     out = {}
@@ -422,7 +434,7 @@ def gather_e8(local, shards, world: int, step: float, pg=None) -> dict:
     """All-gather every rank's E8 points and error sums (one collective) and
     assemble them per tensor in row order on every rank; error sums are added
     in row order."""
-    dev = local[0].idx.device if local else torch.device("cpu")
+    dev = _exchange_device(local[0].idx.device if local else None, world, pg)
     parts = {(c.shard.tensor.name, c.shard.row0): [c.idx.contiguous(), c.err.to(torch.float64)] for c in local}
     blocks = _exchange_blocks(parts, shards, world, shard_words_e8, dev, pg)
     out = {}
