@@ -293,11 +293,6 @@ __device__ __forceinline__ void cluster_sync_all() {
 __device__ __forceinline__ void cluster_arrive_rel() {
     asm volatile("barrier.cluster.arrive.release.aligned;\n" ::: "memory");
 }
-// Arrival without release semantics: only for arrivals that publish no
-// writes (the values read before it are already in registers)
-__device__ __forceinline__ void cluster_arrive_relaxed() {
-    asm volatile("barrier.cluster.arrive.relaxed.aligned;\n" ::: "memory");
-}
 __device__ __forceinline__ void cluster_wait_acq() {
     asm volatile("barrier.cluster.wait.acquire.aligned;\n" ::: "memory");
 }
@@ -868,10 +863,11 @@ rht_halves_kernel(const __grid_constant__ CUtensorMap tin, RhtArgs a) {
                 xa[j] = d_add(lo, hi);
                 x[j] = d_sub(lo, hi);
             }
-            // inbox read: the partner may push its next row.  Relaxed: this
-            // arrival publishes no writes, and the inbox values it follows
-            // are consumed by the butterflies above, issued before it
-            cluster_arrive_relaxed();
+            // inbox read: the partner may push its next row.  The release
+            // orders this thread's inbox reads before the partner's next
+            // writes (a relaxed arrival measured 5 % faster, but nothing
+            // would then keep those reads ahead of it)
+            cluster_arrive_rel();
         }
         // ---- epilogue: scale and store (sums at out_sum(j), differences at out_dif(j)) ----
         TOut *orow = static_cast<TOut *>(a.out) + r * a.ld_out;
